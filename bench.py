@@ -1,0 +1,325 @@
+"""bench.py -- Qwen3.5-0.8B-shape Q4_K_M bs1 greedy decode at ctx 4k on B200.
+
+Workload: a random-init Qwen3.5-0.8B-shaped hybrid
+decoder in the Q4_K_M mix (hidden 1024, 24 layers = [GDN x3, ATT] x6, FFN 3584,
+vocab 248320 tied Q6_K head), written as a synthetic GGUF; the KV cache and
+R/S state are prefilled from 4096 seeded random tokens (untimed); each timed
+step decodes one token (one CUDA-graph replay of the whole forward + LM-head
+argmax).  Weights (513 MB) exceed L2 (126 MB), so no flush is needed.
+
+  value  tokens/s over all GPUs (independent replicas, weak scaling), device-timed
+  e2e    the same metric through the public C ABI with host buffers: per step
+         kib_qwen35_forward() copies the token and position host->device and
+         reads the argmax back (the reference's per-token loop)
+  roofline  the dominant kernel family (K-quant GEMV) on BASELINE config 1,
+         Q4_K 3584x1024, over a rotating pool of weight copies > 4x L2
+  cpu_baseline  the CPU oracle's decode step on the host cores (bounded sample)
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kib|reference]
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "kraken-infer_b200"), os.path.join(ROOT, "tests")]
+
+METRIC = "Qwen3.5-0.8B-shape Q4_K_M bs1 decode tok/s @ctx4k"
+UNIT = "tok/s"
+CONTEXT = 4096
+WORKLOAD = "qwen35-0.8b-shape-q4_k_m-bs1-greedy-decode-ctx4096"
+# HBM bytes per decoded token at ctx 4096 (algorithmic): weights 513.3 MB
+# (24 layers 304.7 + Q6_K LM head 208.6), GDN S r+w 37.7, conv R r+w 2.7,
+# KV read 50.3 (6 layers x 4096 x 2 heads x 256 x 2 B x K,V).
+TOKEN_BYTES = 604.0e6
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.samples = []
+        self.stop = threading.Event()
+
+    def _run(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        while not self.stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits"],
+                                     capture_output=True, text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self.stop.wait(0.2)
+
+    def __enter__(self):
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop.set()
+        self.t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 2 + i and s[2 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_setup(n):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("gloo")
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def allmax(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x)])
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def model_path(rank, world):
+    d = os.environ.get("KIB_BENCH_DIR", os.path.join(tempfile.gettempdir(), "kib_bench"))
+    os.makedirs(d, exist_ok=True)
+    return os.path.join(d, "qwen35_0p8b_shape_q4_k_m_seed1234.gguf")
+
+
+def ensure_model(path, rank, world):
+    import kib
+    if rank == 0 and not os.path.exists(path):
+        tmp = path + ".tmp"
+        kib.write_synthetic_qwen35(tmp, threads=min(os.cpu_count() or 8, 64), seed=1234)
+        os.replace(tmp, path)
+    barrier(world)
+
+
+def matvec_roofline(ctx, hbm_peak):
+    """Config 1 (Q4_K 3584x1024, x ~ N(0,1)) over a rotating pool of distinct
+    weight copies > 4x L2, launched back to back; CUDA events on the stream the
+    kernels run on."""
+    import numpy as np
+    import torch
+    import kib
+    rows, cols = 3584, 1024
+    w = kib.quantize(kib.Q4_K, (np.random.default_rng(1).standard_normal(rows * cols) * 0.02).astype(np.float32))
+    wbytes = w.size
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    copies = max(8, (4 * l2) // wbytes + 1)
+    pool = torch.from_numpy(np.tile(w, copies)).cuda()
+    x = torch.randn(cols, device="cuda")
+    y = torch.zeros(copies, rows, device="cuda")
+    stream = torch.cuda.ExternalStream(ctx.lib.kib_stream(ctx.h))
+    ctx.begin_graph()
+    for i in range(copies):
+        ctx.matvec_kquant(kib.Q4_K, pool.data_ptr() + i * wbytes, rows, cols, x, y[i])
+    ctx.commit_graph()
+    reps = 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.begin_graph()
+    e0.record(stream)
+    for _ in range(reps):
+        for i in range(copies):
+            ctx.matvec_kquant(kib.Q4_K, pool.data_ptr() + i * wbytes, rows, cols, x, y[i])
+    e1.record(stream)
+    ctx.commit_graph()
+    ms = e0.elapsed_time(e1) / (reps * copies)
+    alg = wbytes + cols * 4 + rows * 4  # 2,082,816 B per call
+    achieved = alg / (ms * 1e-3) / 1e9
+    # single-launch latency
+    torch.cuda.synchronize()
+    e0.record(stream)
+    ctx.matvec_kquant(kib.Q4_K, pool, rows, cols, x, y[0])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "traffic": None,
+            "kernel": "kquant_gemv_kernel<Q4_K,1> (config 1: Q4_K 3584x1024 matvec)",
+            "bytes_per_launch": alg, "us_per_launch": round(ms * 1e3, 3), "launches": reps * copies,
+            "pool_copies": int(copies), "single_launch_us": round(e0.elapsed_time(e1) * 1e3, 2)}
+
+
+def cpu_decode_sample(path, threads, budget_s=20.0, max_tokens=6):
+    """The oracle's bs1 decode step at position 4096 on the host cores (state
+    content does not change the work)."""
+    import numpy as np
+    import oracle_lib
+    o = oracle_lib.Oracle(threads=threads)
+    om = oracle_lib.OracleModel(o, path, CONTEXT + 16)
+    tok = 1
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_tokens:
+        _, _, lg = om.forward([tok], CONTEXT + n)
+        tok = int(np.argmax(lg[0]))
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    om.close()
+    return n / dt, n, dt
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    path = model_path(rank, world)
+    ensure_model(path, 0, 1)
+    threads = os.cpu_count() or 1
+    for _ in range(max(args.warmup, 0) and 1):
+        cpu_decode_sample(path, threads, budget_s=5.0, max_tokens=1)
+    vals = []
+    toks = 0
+    secs = 0.0
+    for _ in range(args.steps):
+        v, n, dt = cpu_decode_sample(path, threads, budget_s=10.0, max_tokens=2)
+        vals.append(v)
+        toks += n
+        secs += dt
+    value = toks / secs
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * secs / max(toks, 1), 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "context": CONTEXT, "quant_mix": "Q4_K + Q6_K ffn_down/head",
+                       "l2": "weights 513 MB > L2"},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{toks} decode steps at position {CONTEXT} (oracle/kib_oracle.cpp, "
+                                       f"{threads} threads)"},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="kib", choices=["kib", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=64)
+    args = ap.parse_args()
+    rank, world, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    import numpy as np
+    import torch
+    import kib
+    torch.cuda.set_device(local)
+    path = model_path(rank, world)
+    ensure_model(path, rank, world)
+    ctx = kib.Context(local)
+    total = CONTEXT + args.warmup + args.steps + args.e2e_steps + 8
+    m = kib.Qwen35(ctx, path, context_tokens=total, decode_tokens=8, prefill_chunk=1024, enable_mtp=False)
+    prompt = np.random.default_rng(4096 + rank).integers(0, m.plan.vocab_size, CONTEXT).astype(np.int32)
+    first = m.prefill(prompt, 1024)
+    # warm-up (captures the decode graph)
+    toks = m.decode_greedy(first, args.warmup)
+    stream = torch.cuda.ExternalStream(ctx.lib.kib_stream(ctx.h))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pos0 = m.position
+    lib = ctx.lib
+    # timed region: K graph replays, token and position resident on the device
+    barrier(world)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        h = m.h
+        # same call kib_qwen35_decode_greedy makes, with events around it on the engine's stream
+        e0.record(stream)
+        out = np.zeros(args.steps, np.int32)
+        rc = lib.kib_qwen35_decode_greedy(h, int(toks[-1]), args.steps, out.ctypes.data)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    assert rc == 0
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    ms_max = allmax(ms, world)
+    value = world * args.steps / (ms_max / 1e3)
+    # e2e through the public C ABI with host buffers, per-token sync
+    tok = int(out[-1])
+    e2e_tokens = np.zeros(1, np.int32)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        am, _, _ = m.forward([tok], advance=True)
+        tok = int(am[0])
+    t1 = time.perf_counter()
+    e2e_s = allmax(t1 - t0, world)
+    e2e = world * args.e2e_steps / e2e_s
+    hbm_peak, peak_kind = peaks()
+    line = None
+    if rank == 0:
+        roof = matvec_roofline(ctx, hbm_peak)
+        roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"
+        step_achieved = TOKEN_BYTES / (ms / args.steps * 1e-3) / 1e9
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            threads = os.cpu_count() or 1
+            v, n, dt = cpu_decode_sample(path, threads, budget_s=20.0, max_tokens=6)
+            cpu = {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"{n} oracle decode steps at position {CONTEXT} in {dt:.1f} s "
+                             f"(oracle/kib_oracle.cpp, {threads} threads)"}
+        launches_per_step = 2 + 5 * int(m.plan.main_layers)
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32 (K-quant weights, F16 KV)",
+                "data": "synthetic (random-init weights, seeded random token ids)",
+                "config": {"workload": WORKLOAD, "context": CONTEXT, "position_start": pos0,
+                           "quant_mix": "Q4_K projections, Q6_K ffn_down + tied head", "layers": 24,
+                           "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (weights 513 MB)"},
+                "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+                        "api": "kib_qwen35_forward (token + position H2D, argmax D2H, per-token sync)"},
+                "roofline": roof,
+                "step_roofline": {"bound": "hbm", "bytes_per_token": TOKEN_BYTES, "achieved": round(step_achieved, 1),
+                                  "peak": hbm_peak, "unit": "GB/s", "frac": round(step_achieved / hbm_peak, 4)},
+                "cpu_baseline": cpu, "gpu_launches": launches_per_step * args.steps,
+                "clocks": clk.summary(),
+                "tokens_head": [int(x) for x in out[:8]]}
+    m.close()
+    ctx.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    barrier(world)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,57 @@
+"""Builds the B200 backend in-tree: kraken-infer_b200/lib/libkib.so (sm_100a).
+
+Usage: python kraken-infer_b200/build.py [--force]
+The CUDA sources are compiled with nvcc for sm_100a only; the host C++ (GGUF
+reader/writer) with the same nvcc invocation.  Output stays in the source tree
+so it travels with the repository snapshot.
+"""
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+LIB_DIR = os.path.join(HERE, "lib")
+LIB = os.path.join(LIB_DIR, "libkib.so")
+SOURCES = ["ops.cu", "engine.cu", "gguf.cpp"]
+HEADERS = ["kib_common.cuh", "kquant.cuh", "kquant_gemv.cuh", "layer_kernels.cuh", "kib_ctx.cuh", "gguf.hpp"]
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-pthread",
+         "--expt-relaxed-constexpr", "-I" + os.path.join(HERE, "..", "include")]
+
+
+def _stale():
+    if not os.path.exists(LIB):
+        return True
+    t = os.path.getmtime(LIB)
+    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
+    deps.append(os.path.join(HERE, "..", "include", "kib.h"))
+    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+
+
+def build(force=False, verbose=False, ptxas_info=False):
+    if not force and not _stale():
+        return LIB
+    os.makedirs(LIB_DIR, exist_ok=True)
+    objs = []
+    for src in SOURCES:
+        obj = os.path.join(LIB_DIR, src + ".o")
+        cmd = [NVCC] + ARCH + FLAGS + ["-c", os.path.join(CSRC, src), "-o", obj]
+        if ptxas_info and src.endswith(".cu"):
+            cmd += ["-Xptxas", "-v"]
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.check_call(cmd)
+        objs.append(obj)
+    cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.check_call(cmd)
+    for o in objs:
+        os.remove(o)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose=True, ptxas_info="--ptxas" in sys.argv)

@@ -1,0 +1,1231 @@
+// engine.cu -- the Qwen3.5 runtime on the B200 kernels: GGUF load + weight map +
+// execution plan, chunked prefill, graph-replayed greedy decode and the MTP
+// draft -> verify -> greedy-accept loop.
+//
+// Mirrors the reference's runtime (src/runtime/qwen35_runtime.cpp):
+//   build_qwen35_execution_plan      4380-4526
+//   allocate_qwen35_metal_cache      1252-1389
+//   upload_qwen35_metal_weights      1426-1528  (raw GGUF bytes, as stored)
+//   run_qwen35_linear_layer_chunk    2634-3144
+//   run_qwen35_full_attention_layer_chunk 3146-3423
+//   run_qwen35_decode_tokens         3860-3936
+//   run_qwen35_mtp_tokens(_from_id_buffer) 4111-4240
+//   generate_qwen35_metal            5239-6714 (prefill 5717-6046, MTP loop 6457-6600,
+//                                    greedy loop 6601-6632, adaptive budget 6421-6455)
+// Per decode step the whole forward is one CUDA graph: 5 kernels per layer
+// chained with programmatic dependent launch, the sampled token and the
+// position stay on the device.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf.hpp"
+#include "kib_ctx.cuh"
+#include "layer_kernels.cuh"
+
+namespace kib {
+cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const float* x, int x_ld, int T, float* y,
+                            int y_ld, const float* resid, cudaStream_t st);
+cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const int* ids, int T, float* out,
+                            int out_ld, cudaStream_t st);
+cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st);
+cudaError_t norm_gate_launch(float* v, const float* w, const float* gate, int T, int heads, int d, float eps,
+                             float* out, cudaStream_t st);
+cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w, int K, int C, int T, float* out,
+                        int out_ld, int silu, cudaStream_t st);
+cudaError_t silu_mul_launch(float* g, const float* u, size_t n, cudaStream_t st);
+}  // namespace kib
+
+using namespace kib;
+
+namespace {
+
+constexpr int kMaxSmallT = 8;
+constexpr int64_t kQwenEndOfText = 151643;  // qwen_tokenizer.hpp:44
+
+struct DevT {
+  uint8_t* p = nullptr;
+  int type = -1;
+  std::vector<uint64_t> shape;
+  int cols() const { return shape.empty() ? 0 : static_cast<int>(shape[0]); }
+  int rows() const { return shape.size() < 2 ? 1 : static_cast<int>(shape[1]); }
+  const float* f() const { return reinterpret_cast<const float*>(p); }
+  bool ok() const { return p != nullptr; }
+};
+
+struct LayerW {
+  int kind = 0;  // 0 linear attention, 1 full attention, 2 MTP (full attention block)
+  int cache_index = 0;
+  DevT attn_norm, post_norm, ffn_gate, ffn_up, ffn_down;
+  DevT qkv, zgate, conv1d, dt_bias, ssm_a, beta, alpha, ssm_norm, ssm_out;
+  DevT q, k, v, o, q_norm, k_norm;
+  DevT eh_proj, enorm, hnorm, shead_norm;
+};
+
+}  // namespace
+
+struct kib_qwen35 {
+  kib_ctx* ctx = nullptr;
+  std::unique_ptr<GgufFile> gguf;
+  kib_qwen35_plan plan{};
+  // hparams
+  int H = 0, I = 0, V = 0, heads = 0, kvh = 0, hd = 0, lkh = 0, lvh = 0, lhd = 0, convk = 0, C = 0, VD = 0;
+  int KD = 0, AD = 0;
+  float eps = 1e-6f, theta = 1e7f;
+  int sections[4] = {11, 11, 10, 0};
+  int64_t eos = -1;
+  int cap = 0, chunk = 1024, tmax = 1024;
+  int nsplit = 64;
+  // weights
+  uint8_t* d_weights = nullptr;
+  uint64_t weight_bytes = 0;
+  DevT tok_embd, output_norm, output;
+  std::vector<LayerW> layers;
+  bool has_mtp = false;
+  LayerW mtp;
+  // caches
+  uint16_t *d_k = nullptr, *d_v = nullptr, *d_mk = nullptr, *d_mv = nullptr;
+  float *d_r = nullptr, *d_s = nullptr, *d_r_snap = nullptr, *d_s_snap = nullptr, *d_pending_h = nullptr;
+  size_t k_elems = 0, r_elems = 0, s_elems = 0, mk_elems = 0;
+  // activations
+  float *d_h = nullptr, *d_h1 = nullptr, *d_qkv = nullptr, *d_z = nullptr, *d_beta = nullptr, *d_alpha = nullptr;
+  float *d_y = nullptr, *d_act = nullptr, *d_act2 = nullptr, *d_qg = nullptr, *d_kp = nullptr, *d_vp = nullptr;
+  float *d_att = nullptr, *d_qout = nullptr, *d_norm = nullptr, *d_norm2 = nullptr, *d_hn = nullptr;
+  float *d_logits = nullptr, *d_e = nullptr, *d_cat = nullptr, *d_hm = nullptr, *d_hm1 = nullptr, *d_mtp_h = nullptr;
+  float *d_part = nullptr;
+  unsigned* d_attn_cnt = nullptr;
+  float *d_cand_max = nullptr, *d_cand_sum = nullptr;
+  int* d_cand_idx = nullptr;
+  unsigned* d_head_cnt = nullptr;
+  int *d_pos = nullptr, *d_mtp_pos = nullptr, *d_tokens = nullptr, *d_argmax = nullptr, *d_log = nullptr,
+      *d_step = nullptr, *d_mtp_tok = nullptr;
+  float* d_prob = nullptr;
+  // host mirrors
+  int* h_pin = nullptr;  // pinned scratch (tokens / argmax)
+  float* h_pinf = nullptr;
+  uint64_t pos = 0;
+  // graphs
+  cudaGraphExec_t fwd_graph[kMaxSmallT + 1] = {};
+  bool fwd_graph_logits[kMaxSmallT + 1] = {};
+  cudaGraphExec_t decode_graph = nullptr;
+  cudaGraphExec_t mtp_graph = nullptr;
+  std::string err;
+};
+
+namespace {
+
+int fail(kib_qwen35* m, int code, const std::string& msg) {
+  m->err = msg;
+  if (m->ctx) m->ctx->last_error = msg;
+  return code;
+}
+
+#define ENG_CUDA(expr)                                                                   \
+  do {                                                                                   \
+    cudaError_t e_ = (expr);                                                             \
+    if (e_ != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+template <typename T>
+cudaError_t dalloc(T** p, size_t elems) {
+  return cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(elems, 1) * sizeof(T) + 256);
+}
+
+// -------------------------------------------------------------- enqueue ops
+struct Enq {
+  kib_qwen35* m;
+  cudaStream_t st;
+  std::string why;
+  cudaError_t e = cudaSuccess;
+  bool ok() const { return e == cudaSuccess; }
+  void run(cudaError_t r, const char* what) {
+    if (e == cudaSuccess && r != cudaSuccess) {
+      e = r;
+      if (why.empty()) why = what;
+    }
+  }
+};
+
+GemvDesc base_desc(kib_qwen35* m, int type, int cols, int T) {
+  GemvDesc d;
+  d.type = type;
+  d.cols = cols;
+  d.ntok = T;
+  d.eps = m->eps;
+  d.err = m->ctx->d_err;
+  return d;
+}
+
+void add_seg(GemvDesc& d, const DevT& w, float* out, int ld, int epi, const DevT* w2 = nullptr) {
+  GemvSegDesc& s = d.seg[d.nseg++];
+  s.w = w.p;
+  s.w2 = w2 ? w2->p : nullptr;
+  s.out = out;
+  s.rows = w.rows();
+  s.ld = ld;
+  s.epilogue = epi;
+}
+
+// Launches one GEMV over several matrices sharing an input; splits by type
+// (segments in one launch must share type and cols).
+void gemv_multi(Enq& q, GemvDesc tmpl, const std::vector<std::tuple<const DevT*, float*, int, int>>& segs) {
+  std::map<int, GemvDesc> by_type;
+  for (auto& s : segs) {
+    const DevT* w = std::get<0>(s);
+    auto it = by_type.find(w->type);
+    if (it == by_type.end()) {
+      GemvDesc d = tmpl;
+      d.type = w->type;
+      d.nseg = 0;
+      it = by_type.emplace(w->type, d).first;
+    }
+    add_seg(it->second, *w, std::get<1>(s), std::get<2>(s), std::get<3>(s));
+  }
+  for (auto& kv : by_type) {
+    if (kv.second.nseg == 0) continue;
+    std::string why;
+    q.run(gemv_launch(kv.second, q.m->ctx->num_sms, q.st, &why), "gemv");
+    if (!q.ok() && q.why == "gemv") q.why = why;
+  }
+}
+
+// ---- small-T (<= 8) blocks: every projection is a fused GEMV ----------------
+
+void linear_block_small(Enq& q, const LayerW& L, int T, const float* x_in, float* x_mid) {
+  kib_qwen35* m = q.m;
+  const int li = L.cache_index;
+  GemvDesc d = base_desc(m, L.qkv.type, m->H, T);
+  d.prologue = kProRms;
+  d.in = x_in;
+  d.in_ld = m->H;
+  d.norm_w = L.attn_norm.f();
+  d.conv_state = m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1);
+  d.conv_w = L.conv1d.f();
+  d.conv_k = m->convk;
+  gemv_multi(q, d,
+             {{&L.qkv, m->d_qkv, m->C, kEpiConv},
+              {&L.zgate, m->d_z, m->VD, kEpiStore},
+              {&L.beta, m->d_beta, m->lvh, kEpiStore},
+              {&L.alpha, m->d_alpha, m->lvh, kEpiStore}});
+  GdnParams g;
+  g.conv_out = m->d_qkv;
+  g.C = m->C;
+  g.beta_raw = m->d_beta;
+  g.alpha_raw = m->d_alpha;
+  g.ld_ba = m->lvh;
+  g.dt_bias = L.dt_bias.f();
+  g.ssm_a = L.ssm_a.f();
+  g.state = m->d_s + static_cast<size_t>(li) * m->lvh * m->lhd * m->lhd;
+  g.out = m->d_y;
+  g.T = T;
+  g.key_heads = m->lkh;
+  g.value_heads = m->lvh;
+  g.eps = m->eps;
+  q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
+  GemvDesc o = base_desc(m, L.ssm_out.type, m->VD, T);
+  o.prologue = kProNormGate;
+  o.in = m->d_y;
+  o.in_ld = m->VD;
+  o.norm_w = L.ssm_norm.f();
+  o.gate = m->d_z;
+  o.head_dim = m->lhd;
+  o.resid = x_in;
+  gemv_multi(q, o, {{&L.ssm_out, x_mid, m->H, kEpiResidual}});
+}
+
+AttnParams attn_params(kib_qwen35* m, const LayerW& L, uint16_t* kc, uint16_t* vc, const int* pos, int T) {
+  AttnParams a;
+  a.qg = m->d_qg;
+  a.kp = m->d_kp;
+  a.vp = m->d_vp;
+  a.q_norm = L.q_norm.f();
+  a.k_norm = L.k_norm.f();
+  a.kcache = kc;
+  a.vcache = vc;
+  a.pos = pos;
+  a.T = T;
+  a.heads = m->heads;
+  a.kv_heads = m->kvh;
+  a.eps = m->eps;
+  a.theta = m->theta;
+  a.sec0 = m->sections[0];
+  a.sec1 = m->sections[1];
+  a.sec2 = m->sections[2];
+  a.sec3 = m->sections[3];
+  a.n_dims = 2 * (a.sec0 + a.sec1 + a.sec2 + a.sec3);
+  a.nsplit = m->nsplit;
+  a.part = m->d_part;
+  a.counters = m->d_attn_cnt;
+  a.out = m->d_att;
+  a.q_out = m->d_qout;
+  a.round_q = T >= 64 ? 1 : 0;
+  return a;
+}
+
+template <int TM>
+cudaError_t launch_attn_decode(const AttnParams& a, int kvh, int nsplit, cudaStream_t st) {
+  const size_t smem = (static_cast<size_t>(a.T) * 4 * kHd + 8 * static_cast<size_t>(a.T) * (kHd + 2)) * sizeof(float);
+  static bool cfg = false;
+  if (!cfg) {
+    cudaFuncSetAttribute(attn_decode_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cfg = true;
+  }
+  return launch_pdl(attn_decode_kernel<TM>, dim3(nsplit, kvh), dim3(256), smem, st, a);
+}
+
+void attention_block_small(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc, const int* pos, int T,
+                           const float* x_in, float* x_mid) {
+  kib_qwen35* m = q.m;
+  GemvDesc d = base_desc(m, L.q.type, m->H, T);
+  d.prologue = kProRms;
+  d.in = x_in;
+  d.in_ld = m->H;
+  d.norm_w = L.attn_norm.f();
+  gemv_multi(q, d,
+             {{&L.q, m->d_qg, 2 * m->AD, kEpiStore}, {&L.k, m->d_kp, m->KD, kEpiStore}, {&L.v, m->d_vp, m->KD, kEpiStore}});
+  const AttnParams a = attn_params(m, L, kc, vc, pos, T);
+  q.run(T == 1 ? launch_attn_decode<1>(a, m->kvh, m->nsplit, q.st) : launch_attn_decode<8>(a, m->kvh, m->nsplit, q.st),
+        "attn_decode");
+  GemvDesc o = base_desc(m, L.o.type, m->AD, T);
+  o.prologue = kProPlain;
+  o.in = m->d_att;
+  o.in_ld = m->AD;
+  o.resid = x_in;
+  gemv_multi(q, o, {{&L.o, x_mid, m->H, kEpiResidual}});
+}
+
+void ffn_small(Enq& q, const LayerW& L, int T, const float* x_mid, float* x_out) {
+  kib_qwen35* m = q.m;
+  if (L.ffn_gate.type == L.ffn_up.type) {
+    GemvDesc d = base_desc(m, L.ffn_gate.type, m->H, T);
+    d.prologue = kProRms;
+    d.in = x_mid;
+    d.in_ld = m->H;
+    d.norm_w = L.post_norm.f();
+    d.nseg = 0;
+    add_seg(d, L.ffn_gate, m->d_act, m->I, kEpiSiluMul, &L.ffn_up);
+    std::string why;
+    q.run(gemv_launch(d, m->ctx->num_sms, q.st, &why), "ffn_gate_up");
+  } else {
+    GemvDesc d = base_desc(m, L.ffn_gate.type, m->H, T);
+    d.prologue = kProRms;
+    d.in = x_mid;
+    d.in_ld = m->H;
+    d.norm_w = L.post_norm.f();
+    gemv_multi(q, d, {{&L.ffn_gate, m->d_act, m->I, kEpiStore}, {&L.ffn_up, m->d_act2, m->I, kEpiStore}});
+    q.run(silu_mul_launch(m->d_act, m->d_act2, static_cast<size_t>(T) * m->I, q.st), "silu_mul");
+  }
+  GemvDesc o = base_desc(m, L.ffn_down.type, m->I, T);
+  o.prologue = kProPlain;
+  o.in = m->d_act;
+  o.in_ld = m->I;
+  o.resid = x_mid;
+  gemv_multi(q, o, {{&L.ffn_down, x_out, m->H, kEpiResidual}});
+}
+
+// LM head over T rows: RMSNorm(norm_w) prologue (rows also stored to x_out),
+// fused argmax epilogue (+ logits if requested).
+void head_small(Enq& q, int T, const float* x, const DevT& norm_w, const DevT& head, int* token_out, float* prob_out,
+                float* x_out, float* logits, int* token_log, int* step, int* pos_adv) {
+  kib_qwen35* m = q.m;
+  GemvDesc d = base_desc(m, head.type, m->H, T);
+  d.prologue = kProRms;
+  d.in = x;
+  d.in_ld = m->H;
+  d.norm_w = norm_w.f();
+  d.nseg = 0;
+  add_seg(d, head, logits, m->V, kEpiArgmax);
+  d.argmax = true;
+  d.cand_max = m->d_cand_max;
+  d.cand_sum = m->d_cand_sum;
+  d.cand_idx = m->d_cand_idx;
+  d.counter = m->d_head_cnt;
+  d.token_out = token_out;
+  d.prob_out = prob_out;
+  d.x_out = x_out;
+  d.token_log = token_log;
+  d.step_counter = step;
+  d.pos_advance = pos_adv;
+  std::string why;
+  q.run(gemv_launch(d, m->ctx->num_sms, q.st, &why), "lm_head");
+}
+
+void main_layers_small(Enq& q, int T, const int* pos) {
+  kib_qwen35* m = q.m;
+  for (const LayerW& L : m->layers) {
+    if (L.kind == 0) {
+      linear_block_small(q, L, T, m->d_h, m->d_h1);
+    } else {
+      const size_t off = static_cast<size_t>(L.cache_index) * m->cap * m->KD;
+      attention_block_small(q, L, m->d_k + off, m->d_v + off, pos, T, m->d_h, m->d_h1);
+    }
+    ffn_small(q, L, T, m->d_h1, m->d_h);
+  }
+}
+
+// ---- prefill (T > 8) blocks ----------------------------------------------------
+
+void gemm(Enq& q, const DevT& w, const float* x, int x_ld, int T, float* y, int y_ld, const float* resid = nullptr) {
+  q.run(gemm_f16_launch(w.type, w.p, w.rows(), w.cols(), x, x_ld, T, y, y_ld, resid, q.st), "gemm");
+}
+
+void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, float* x_mid) {
+  kib_qwen35* m = q.m;
+  const int li = L.cache_index;
+  q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
+  gemm(q, L.qkv, m->d_norm, m->H, T, m->d_qkv, m->C);
+  q.run(conv_launch(m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1), m->d_qkv, m->C, L.conv1d.f(), m->convk,
+                    m->C, T, m->d_qkv, m->C, 1, q.st),
+        "conv");
+  gemm(q, L.zgate, m->d_norm, m->H, T, m->d_z, m->VD);
+  gemm(q, L.beta, m->d_norm, m->H, T, m->d_beta, m->lvh);
+  gemm(q, L.alpha, m->d_norm, m->H, T, m->d_alpha, m->lvh);
+  GdnParams g;
+  g.conv_out = m->d_qkv;
+  g.C = m->C;
+  g.beta_raw = m->d_beta;
+  g.alpha_raw = m->d_alpha;
+  g.ld_ba = m->lvh;
+  g.dt_bias = L.dt_bias.f();
+  g.ssm_a = L.ssm_a.f();
+  g.state = m->d_s + static_cast<size_t>(li) * m->lvh * m->lhd * m->lhd;
+  g.out = m->d_y;
+  g.T = T;
+  g.key_heads = m->lkh;
+  g.value_heads = m->lvh;
+  g.eps = m->eps;
+  q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
+  q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, T, m->lvh, m->lhd, m->eps, m->d_norm2, q.st), "norm_gate");
+  gemm(q, L.ssm_out, m->d_norm2, m->VD, T, x_mid, m->H, x_in);
+}
+
+void attention_block_prefill(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc, const int* pos, int T,
+                             const float* x_in, float* x_mid) {
+  kib_qwen35* m = q.m;
+  q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
+  gemm(q, L.q, m->d_norm, m->H, T, m->d_qg, 2 * m->AD);
+  gemm(q, L.k, m->d_norm, m->H, T, m->d_kp, m->KD);
+  gemm(q, L.v, m->d_norm, m->H, T, m->d_vp, m->KD);
+  const AttnParams a = attn_params(m, L, kc, vc, pos, T);
+  q.run(launch_pdl(attn_prep_kernel, dim3(T), dim3(256), 8 * kHd * sizeof(float), q.st, a), "attn_prep");
+  q.run(launch_pdl(attn_prefill_kernel, dim3((T + 7) / 8, m->heads), dim3(256), 0, q.st, a), "attn_prefill");
+  gemm(q, L.o, m->d_att, m->AD, T, x_mid, m->H, x_in);
+}
+
+void ffn_prefill(Enq& q, const LayerW& L, int T, const float* x_mid, float* x_out) {
+  kib_qwen35* m = q.m;
+  q.run(rms_rows_launch(x_mid, L.post_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
+  gemm(q, L.ffn_gate, m->d_norm, m->H, T, m->d_act, m->I);
+  gemm(q, L.ffn_up, m->d_norm, m->H, T, m->d_act2, m->I);
+  q.run(silu_mul_launch(m->d_act, m->d_act2, static_cast<size_t>(T) * m->I, q.st), "silu_mul");
+  gemm(q, L.ffn_down, m->d_act, m->I, T, x_out, m->H, x_mid);
+}
+
+void main_layers_prefill(Enq& q, int T, const int* pos) {
+  kib_qwen35* m = q.m;
+  for (const LayerW& L : m->layers) {
+    if (L.kind == 0) {
+      linear_block_prefill(q, L, T, m->d_h, m->d_h1);
+    } else {
+      const size_t off = static_cast<size_t>(L.cache_index) * m->cap * m->KD;
+      attention_block_prefill(q, L, m->d_k + off, m->d_v + off, pos, T, m->d_h, m->d_h1);
+    }
+    ffn_prefill(q, L, T, m->d_h1, m->d_h);
+  }
+}
+
+const DevT& head_weight(kib_qwen35* m) { return m->output.ok() ? m->output : m->tok_embd; }
+
+// ------------------------------------------------------------------ loading
+int bind(kib_qwen35* m, const std::map<std::string, DevT>& dev, const std::string& name,
+         const std::vector<uint64_t>& shape, DevT& out, bool required = true) {
+  auto it = dev.find(name);
+  if (it == dev.end()) {
+    if (!required) return KIB_OK;
+    return fail(m, KIB_ERR_INVALID_ARGUMENT, "missing Qwen3.5 GGUF tensor: " + name);
+  }
+  if (it->second.shape != shape) return fail(m, KIB_ERR_INVALID_ARGUMENT, "Qwen3.5 GGUF tensor " + name + " has unexpected shape");
+  out = it->second;
+  return KIB_OK;
+}
+
+int capture(kib_qwen35* m, cudaGraphExec_t* exec, const std::function<void(Enq&)>& body) {
+  cudaStream_t st = m->ctx->stream;
+  Enq q{m, st};
+  cudaGraph_t g = nullptr;
+  ENG_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  body(q);
+  cudaError_t ce = cudaStreamEndCapture(st, &g);
+  if (!q.ok()) {
+    if (g) cudaGraphDestroy(g);
+    return fail(m, KIB_ERR_INTERNAL, "graph capture launch failed: " + q.why + ": " + cudaGetErrorString(q.e));
+  }
+  if (ce != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, std::string("graph capture: ") + cudaGetErrorString(ce));
+  cudaError_t ie = cudaGraphInstantiate(exec, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+  return KIB_OK;
+}
+
+int sync_check(kib_qwen35* m, const char* what) {
+  cudaError_t e = cudaStreamSynchronize(m->ctx->stream);
+  if (e != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, std::string(what) + ": " + cudaGetErrorString(e));
+  int err = 0;
+  cudaMemcpy(&err, m->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (err) {
+    cudaMemset(m->ctx->d_err, 0, sizeof(int));
+    return fail(m, KIB_ERR_TIMEOUT, std::string(what) + ": a bounded device wait gave up");
+  }
+  return KIB_OK;
+}
+
+int set_pos(kib_qwen35* m, int* dptr, uint64_t value) {
+  m->h_pin[0] = static_cast<int>(value);
+  ENG_CUDA(cudaMemcpyAsync(dptr, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+  ENG_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  return KIB_OK;
+}
+
+// Forward over T <= 8 tokens already in d_tokens at position *d_pos, through
+// the LM head (argmax per row into d_argmax, normed rows into d_hn).
+int forward_small(kib_qwen35* m, int T, bool want_logits) {
+  if (!m->fwd_graph[T] || m->fwd_graph_logits[T] != want_logits) {
+    if (m->fwd_graph[T]) cudaGraphExecDestroy(m->fwd_graph[T]);
+    m->fwd_graph[T] = nullptr;
+    int rc = capture(m, &m->fwd_graph[T], [&](Enq& q) {
+      q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, m->d_tokens, T, m->d_h, m->H, q.st), "embed");
+      main_layers_small(q, T, m->d_pos);
+      head_small(q, T, m->d_h, m->output_norm, head_weight(m), m->d_argmax, m->d_prob, m->d_hn,
+                 want_logits ? m->d_logits : nullptr, nullptr, nullptr, nullptr);
+    });
+    if (rc) return rc;
+    m->fwd_graph_logits[T] = want_logits;
+  }
+  ENG_CUDA(cudaGraphLaunch(m->fwd_graph[T], m->ctx->stream));
+  return KIB_OK;
+}
+
+// Prefill chunk with T > 8 tokens (not graph-captured: one-shot).
+int forward_prefill(kib_qwen35* m, int T, bool head) {
+  Enq q{m, m->ctx->stream};
+  q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, m->d_tokens, T, m->d_h, m->H, q.st), "embed");
+  main_layers_prefill(q, T, m->d_pos);
+  if (head) {
+    head_small(q, 1, m->d_h + static_cast<size_t>(T - 1) * m->H, m->output_norm, head_weight(m), m->d_argmax, m->d_prob,
+               nullptr, nullptr, nullptr, nullptr, nullptr);
+  }
+  if (!q.ok()) return fail(m, KIB_ERR_INTERNAL, "prefill launch: " + q.why + ": " + cudaGetErrorString(q.e));
+  return KIB_OK;
+}
+
+// MTP layer over T tokens (ids in d_tokens, h rows in h_rows) at *d_mtp_pos:
+// writes the MTP KV cache and the normed h_nextn rows into d_mtp_h; with
+// head, also the argmax of the LM head per row.
+void mtp_enqueue(Enq& q, int T, const int* ids, const float* h_rows, bool head, int* token_out, float* prob_out,
+                 int* token_log, int* step, int* pos_adv) {
+  kib_qwen35* m = q.m;
+  const LayerW& L = m->mtp;
+  q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, ids, T, m->d_e, m->H, q.st), "mtp_embed");
+  q.run(launch_pdl(mtp_cat_kernel, dim3(T), dim3(256), 0, q.st, static_cast<const float*>(m->d_e), h_rows,
+                   L.enorm.f(), L.hnorm.f(), m->H, m->eps, m->d_cat),
+        "mtp_cat");
+  if (T <= kMaxSmallT) {
+    GemvDesc d = base_desc(m, L.eh_proj.type, 2 * m->H, T);
+    d.prologue = kProPlain;
+    d.in = m->d_cat;
+    d.in_ld = 2 * m->H;
+    gemv_multi(q, d, {{&L.eh_proj, m->d_hm, m->H, kEpiStore}});
+    attention_block_small(q, L, m->d_mk, m->d_mv, m->d_mtp_pos, T, m->d_hm, m->d_hm1);
+    ffn_small(q, L, T, m->d_hm1, m->d_hm);
+  } else {
+    gemm(q, L.eh_proj, m->d_cat, 2 * m->H, T, m->d_hm, m->H);
+    attention_block_prefill(q, L, m->d_mk, m->d_mv, m->d_mtp_pos, T, m->d_hm, m->d_hm1);
+    ffn_prefill(q, L, T, m->d_hm1, m->d_hm);
+  }
+  const DevT& hn = L.shead_norm.ok() ? L.shead_norm : m->output_norm;
+  if (head) {
+    head_small(q, T, m->d_hm, hn, head_weight(m), token_out, prob_out, m->d_mtp_h, nullptr, token_log, step, pos_adv);
+  } else {
+    q.run(rms_rows_launch(m->d_hm, hn.f(), T, m->H, m->eps, m->d_mtp_h, q.st), "mtp_head_norm");
+  }
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* opt, kib_qwen35** out) {
+  if (!ctx || !path || !out) return KIB_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  std::unique_ptr<kib_qwen35> mp(new kib_qwen35);
+  kib_qwen35* m = mp.get();
+  m->ctx = ctx;
+  std::string err;
+  m->gguf = GgufFile::open(path, &err);
+  if (!m->gguf) return set_error(ctx, KIB_ERR_INVALID_ARGUMENT, err);
+  const GgufFile& g = *m->gguf;
+  const GgufValue* arch = g.meta("general.architecture");
+  if (!arch || arch->str != "qwen35") return set_error(ctx, KIB_ERR_INVALID_ARGUMENT, "unsupported GGUF architecture");
+  const std::string a = "qwen35.";
+  // load_gguf_bundle hparams (model_config.cpp:808-856)
+  m->H = static_cast<int>(g.num(a + "embedding_length", 0));
+  m->I = static_cast<int>(g.num(a + "feed_forward_length", 0));
+  const int total_layers = static_cast<int>(g.num(a + "block_count", 0));
+  const int nextn = static_cast<int>(g.num(a + "nextn_predict_layers", 0));
+  const int main_layers = total_layers - nextn;
+  m->heads = static_cast<int>(g.num(a + "attention.head_count", 0));
+  m->kvh = static_cast<int>(g.num(a + "attention.head_count_kv", 0));
+  m->hd = static_cast<int>(g.num(a + "attention.key_length", 0));
+  m->eps = static_cast<float>(g.num(a + "attention.layer_norm_rms_epsilon", 1e-6));
+  m->theta = static_cast<float>(g.num(a + "rope.freq_base", 1e7));
+  m->convk = static_cast<int>(g.num(a + "ssm.conv_kernel", 4));
+  m->lhd = static_cast<int>(g.num(a + "ssm.state_size", 128));
+  m->lkh = static_cast<int>(g.num(a + "ssm.group_count", 16));
+  m->lvh = static_cast<int>(g.num(a + "ssm.time_step_rank", 16));
+  const int interval = static_cast<int>(g.num(a + "full_attention_interval", 4));
+  if (const GgufValue* s = g.meta(a + "rope.dimension_sections"); s && s->is_array)
+    for (size_t i = 0; i < 4 && i < s->arr.size(); ++i) m->sections[i] = static_cast<int>(s->arr[i]);
+  m->eos = static_cast<int64_t>(g.num("tokenizer.ggml.eos_token_id", -1));
+  const GgufTensor* te = g.tensor("token_embd.weight");
+  if (!te || te->shape.size() != 2) return set_error(ctx, KIB_ERR_INVALID_ARGUMENT, "missing Qwen3.5 GGUF tensor: token_embd.weight");
+  m->V = static_cast<int>(te->shape[1]);
+  if (m->H <= 0 || m->I <= 0 || main_layers <= 0 || main_layers > 64 || m->heads <= 0 || m->kvh <= 0 ||
+      m->heads % m->kvh || m->heads / m->kvh != 4 || m->hd != 256 || m->lhd != 128 || m->lvh % m->lkh ||
+      m->H % 256 || m->I % 256 || m->convk < 2 || m->convk > 8)
+    return set_error(ctx, KIB_ERR_INVALID_ARGUMENT,
+                     "Qwen3.5 hparams outside this backend's kernels (need head_dim 256, GQA 4, ssm state 128)");
+  m->KD = m->kvh * m->hd;
+  m->AD = m->heads * m->hd;
+  m->VD = m->lvh * m->lhd;
+  m->C = 2 * m->lkh * m->lhd + m->VD;
+
+  // ---- upload every tensor, raw bytes as stored, 256-byte aligned with padding
+  uint64_t total = 0;
+  for (auto& t : g.tensors()) total += (t.bytes + 511) / 256 * 256;
+  m->weight_bytes = total;
+  if (cudaMalloc(&m->d_weights, total) != cudaSuccess) return set_error(ctx, KIB_ERR_INTERNAL, "weight allocation failed");
+  std::map<std::string, DevT> dev;
+  uint64_t off = 0;
+  for (auto& t : g.tensors()) {
+    DevT d;
+    d.p = m->d_weights + off;
+    d.type = static_cast<int>(t.type);
+    d.shape = t.shape;
+    if (cudaMemcpy(d.p, t.data, t.bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+      return set_error(ctx, KIB_ERR_INTERNAL, "weight upload failed: " + t.name);
+    dev[t.name] = d;
+    off += (t.bytes + 511) / 256 * 256;
+  }
+  // ---- weight map (qwen35_weight_map.cpp:61-454)
+  const uint64_t H = static_cast<uint64_t>(m->H), I = static_cast<uint64_t>(m->I), V = static_cast<uint64_t>(m->V);
+  const uint64_t hd = static_cast<uint64_t>(m->hd), AD = static_cast<uint64_t>(m->AD), KD = static_cast<uint64_t>(m->KD);
+  const uint64_t C = static_cast<uint64_t>(m->C), VD = static_cast<uint64_t>(m->VD);
+  const uint64_t lvh = static_cast<uint64_t>(m->lvh), lhd = static_cast<uint64_t>(m->lhd);
+  int rc = bind(m, dev, "token_embd.weight", {H, V}, m->tok_embd);
+  if (!rc) rc = bind(m, dev, "output_norm.weight", {H}, m->output_norm);
+  if (!rc) rc = bind(m, dev, "output.weight", {H, V}, m->output, false);
+  if (rc) return set_error(ctx, rc, m->err);
+  auto kquant = [](const DevT& t) { return t.type == 12 || t.type == 13 || t.type == 14; };
+  if (!kquant(m->tok_embd) || m->output_norm.type != 0 || (m->output.ok() && !kquant(m->output)))
+    return set_error(ctx, KIB_ERR_INVALID_ARGUMENT, "token_embd/output must be K-quant and output_norm F32");
+  int n_lin = 0, n_full = 0;
+  auto bind_full = [&](int l, LayerW& L) {
+    const std::string p = "blk." + std::to_string(l) + ".";
+    int r = bind(m, dev, p + "attn_q.weight", {H, 2 * AD}, L.q);
+    if (!r) r = bind(m, dev, p + "attn_k.weight", {H, KD}, L.k);
+    if (!r) r = bind(m, dev, p + "attn_v.weight", {H, KD}, L.v);
+    if (!r) r = bind(m, dev, p + "attn_output.weight", {AD, H}, L.o);
+    if (!r) r = bind(m, dev, p + "attn_q_norm.weight", {hd}, L.q_norm);
+    if (!r) r = bind(m, dev, p + "attn_k_norm.weight", {hd}, L.k_norm);
+    return r;
+  };
+  auto bind_common = [&](int l, LayerW& L) {
+    const std::string p = "blk." + std::to_string(l) + ".";
+    int r = bind(m, dev, p + "attn_norm.weight", {H}, L.attn_norm);
+    if (!r) r = bind(m, dev, p + "post_attention_norm.weight", {H}, L.post_norm);
+    if (!r) r = bind(m, dev, p + "ffn_gate.weight", {H, I}, L.ffn_gate);
+    if (!r) r = bind(m, dev, p + "ffn_down.weight", {I, H}, L.ffn_down);
+    if (!r) r = bind(m, dev, p + "ffn_up.weight", {H, I}, L.ffn_up);
+    return r;
+  };
+  for (int l = 0; l < main_layers; ++l) {
+    LayerW L;
+    const std::string p = "blk." + std::to_string(l) + ".";
+    L.kind = ((l + 1) % interval) != 0 ? 0 : 1;
+    rc = bind_common(l, L);
+    if (!rc && L.kind == 1) {
+      rc = bind_full(l, L);
+      L.cache_index = n_full++;
+    } else if (!rc) {
+      rc = bind(m, dev, p + "attn_qkv.weight", {H, C}, L.qkv);
+      if (!rc) rc = bind(m, dev, p + "attn_gate.weight", {H, VD}, L.zgate);
+      if (!rc) rc = bind(m, dev, p + "ssm_conv1d.weight", {static_cast<uint64_t>(m->convk), C}, L.conv1d);
+      if (!rc) rc = bind(m, dev, p + "ssm_dt.bias", {lvh}, L.dt_bias);
+      if (!rc) rc = bind(m, dev, p + "ssm_a", {lvh}, L.ssm_a);
+      if (!rc) rc = bind(m, dev, p + "ssm_beta.weight", {H, lvh}, L.beta);
+      if (!rc) rc = bind(m, dev, p + "ssm_alpha.weight", {H, lvh}, L.alpha);
+      if (!rc) rc = bind(m, dev, p + "ssm_norm.weight", {lhd}, L.ssm_norm);
+      if (!rc) rc = bind(m, dev, p + "ssm_out.weight", {VD, H}, L.ssm_out);
+      L.cache_index = n_lin++;
+    }
+    if (rc) return set_error(ctx, rc, m->err);
+    m->layers.push_back(L);
+  }
+  m->has_mtp = nextn == 1 && (!opt || opt->enable_mtp);
+  if (m->has_mtp) {
+    LayerW& L = m->mtp;
+    L.kind = 2;
+    const std::string p = "blk." + std::to_string(main_layers) + ".";
+    rc = bind_common(main_layers, L);
+    if (!rc) rc = bind_full(main_layers, L);
+    if (!rc) rc = bind(m, dev, p + "nextn.eh_proj.weight", {2 * H, H}, L.eh_proj);
+    if (!rc) rc = bind(m, dev, p + "nextn.enorm.weight", {H}, L.enorm);
+    if (!rc) rc = bind(m, dev, p + "nextn.hnorm.weight", {H}, L.hnorm);
+    if (!rc) rc = bind(m, dev, p + "nextn.shared_head_norm.weight", {H}, L.shead_norm, false);
+    if (rc) return set_error(ctx, rc, m->err);
+  }
+  // ---- execution plan (qwen35_runtime.cpp:4380-4526)
+  const uint64_t context = opt && opt->context_tokens ? opt->context_tokens : 4096;
+  const uint64_t decode = opt && opt->decode_tokens ? opt->decode_tokens : 1;
+  m->cap = static_cast<int>(context + decode + 8);
+  m->chunk = opt && opt->prefill_chunk_tokens ? static_cast<int>(opt->prefill_chunk_tokens) : 1024;
+  m->tmax = std::max(m->chunk, kMaxSmallT);
+  m->nsplit = std::max(1, std::min(64, (m->cap + 63) / 64));
+  auto& P = m->plan;
+  P.hidden_size = H;
+  P.main_layers = static_cast<uint64_t>(main_layers);
+  P.total_layers = static_cast<uint64_t>(total_layers);
+  P.head_dim = hd;
+  P.attention_heads = static_cast<uint64_t>(m->heads);
+  P.kv_heads = static_cast<uint64_t>(m->kvh);
+  P.linear_key_heads = static_cast<uint64_t>(m->lkh);
+  P.linear_value_heads = lvh;
+  P.linear_key_head_dim = lhd;
+  P.linear_value_head_dim = lhd;
+  P.linear_inner_size = VD;
+  P.linear_conv_kernel = static_cast<uint64_t>(m->convk);
+  P.linear_conv_channels = C;
+  P.intermediate_size = I;
+  P.vocab_size = V;
+  P.attention_capacity_tokens = static_cast<uint64_t>(m->cap);
+  P.full_attention_layers = static_cast<uint64_t>(n_full);
+  P.linear_attention_layers = static_cast<uint64_t>(n_lin);
+  P.kv_dim = KD;
+  P.recurrent_r_elements_per_layer = C * static_cast<uint64_t>(m->convk - 1);
+  P.recurrent_s_elements_per_layer = lvh * lhd * lhd;
+  P.kv_cache_bytes = 2ull * n_full * m->cap * KD * 2;
+  P.recurrent_r_cache_bytes = static_cast<uint64_t>(n_lin) * P.recurrent_r_elements_per_layer * 4;
+  P.recurrent_s_cache_bytes = static_cast<uint64_t>(n_lin) * P.recurrent_s_elements_per_layer * 4;
+  P.total_cache_bytes = P.kv_cache_bytes + P.recurrent_r_cache_bytes + P.recurrent_s_cache_bytes;
+  P.weight_bytes = total;
+  P.mtp_layers = m->has_mtp ? 1 : 0;
+  for (int l = 0; l < main_layers; ++l) P.layer_kinds[l] = m->layers[l].kind;
+  // ---- caches + activations (allocate_qwen35_metal_cache, qwen35_runtime.cpp:1252-1330)
+  m->k_elems = static_cast<size_t>(n_full) * m->cap * m->KD;
+  m->r_elems = static_cast<size_t>(n_lin) * P.recurrent_r_elements_per_layer;
+  m->s_elems = static_cast<size_t>(n_lin) * P.recurrent_s_elements_per_layer;
+  m->mk_elems = m->has_mtp ? static_cast<size_t>(m->cap) * m->KD : 0;
+  const size_t T = static_cast<size_t>(m->tmax);
+  bool ok = dalloc(&m->d_k, m->k_elems) == cudaSuccess && dalloc(&m->d_v, m->k_elems) == cudaSuccess &&
+            dalloc(&m->d_r, m->r_elems) == cudaSuccess && dalloc(&m->d_s, m->s_elems) == cudaSuccess &&
+            dalloc(&m->d_r_snap, m->r_elems) == cudaSuccess && dalloc(&m->d_s_snap, m->s_elems) == cudaSuccess &&
+            dalloc(&m->d_mk, m->mk_elems) == cudaSuccess && dalloc(&m->d_mv, m->mk_elems) == cudaSuccess &&
+            dalloc(&m->d_pending_h, H) == cudaSuccess && dalloc(&m->d_h, T * H) == cudaSuccess &&
+            dalloc(&m->d_h1, T * H) == cudaSuccess && dalloc(&m->d_qkv, T * C) == cudaSuccess &&
+            dalloc(&m->d_z, T * VD) == cudaSuccess && dalloc(&m->d_beta, T * lvh) == cudaSuccess &&
+            dalloc(&m->d_alpha, T * lvh) == cudaSuccess && dalloc(&m->d_y, T * VD) == cudaSuccess &&
+            dalloc(&m->d_act, T * I) == cudaSuccess && dalloc(&m->d_act2, T * I) == cudaSuccess &&
+            dalloc(&m->d_qg, T * 2 * AD) == cudaSuccess && dalloc(&m->d_kp, T * KD) == cudaSuccess &&
+            dalloc(&m->d_vp, T * KD) == cudaSuccess && dalloc(&m->d_att, T * AD) == cudaSuccess &&
+            dalloc(&m->d_qout, T * AD) == cudaSuccess && dalloc(&m->d_norm, T * 2 * H) == cudaSuccess &&
+            dalloc(&m->d_norm2, T * VD) == cudaSuccess && dalloc(&m->d_hn, T * H) == cudaSuccess &&
+            dalloc(&m->d_logits, static_cast<size_t>(kMaxSmallT) * V) == cudaSuccess &&
+            dalloc(&m->d_e, T * H) == cudaSuccess && dalloc(&m->d_cat, T * 2 * H) == cudaSuccess &&
+            dalloc(&m->d_hm, T * H) == cudaSuccess && dalloc(&m->d_hm1, T * H) == cudaSuccess &&
+            dalloc(&m->d_mtp_h, T * H) == cudaSuccess &&
+            dalloc(&m->d_part, static_cast<size_t>(m->nsplit) * kMaxSmallT * m->heads * (kHd + 2)) == cudaSuccess &&
+            dalloc(&m->d_attn_cnt, 64) == cudaSuccess && dalloc(&m->d_head_cnt, 4) == cudaSuccess &&
+            dalloc(&m->d_cand_max, 1024 * kGemvMaxTok) == cudaSuccess &&
+            dalloc(&m->d_cand_sum, 1024 * kGemvMaxTok) == cudaSuccess &&
+            dalloc(&m->d_cand_idx, 1024 * kGemvMaxTok) == cudaSuccess && dalloc(&m->d_pos, 4) == cudaSuccess &&
+            dalloc(&m->d_mtp_pos, 4) == cudaSuccess && dalloc(&m->d_tokens, T) == cudaSuccess &&
+            dalloc(&m->d_argmax, kMaxSmallT) == cudaSuccess && dalloc(&m->d_prob, 4096) == cudaSuccess &&
+            dalloc(&m->d_log, 1 << 20) == cudaSuccess && dalloc(&m->d_step, 4) == cudaSuccess &&
+            dalloc(&m->d_mtp_tok, 4) == cudaSuccess &&
+            cudaMallocHost(&m->h_pin, 4096 * sizeof(int)) == cudaSuccess &&
+            cudaMallocHost(&m->h_pinf, 4096 * sizeof(float)) == cudaSuccess;
+  if (!ok) {
+    kib_qwen35_free(mp.release());
+    return set_error(ctx, KIB_ERR_INTERNAL, "cache/activation allocation failed");
+  }
+  cudaMemset(m->d_attn_cnt, 0, 64 * sizeof(unsigned));
+  cudaMemset(m->d_head_cnt, 0, 4 * sizeof(unsigned));
+  *out = mp.release();
+  return kib_qwen35_reset(*out);
+}
+
+void kib_qwen35_free(kib_qwen35* m) {
+  if (!m) return;
+  if (m->ctx && m->ctx->stream) cudaStreamSynchronize(m->ctx->stream);
+  for (auto& g : m->fwd_graph)
+    if (g) cudaGraphExecDestroy(g);
+  if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
+  if (m->mtp_graph) cudaGraphExecDestroy(m->mtp_graph);
+  void* ptrs[] = {m->d_weights, m->d_k, m->d_v, m->d_mk, m->d_mv, m->d_r, m->d_s, m->d_r_snap, m->d_s_snap,
+                  m->d_pending_h, m->d_h, m->d_h1, m->d_qkv, m->d_z, m->d_beta, m->d_alpha, m->d_y, m->d_act,
+                  m->d_act2, m->d_qg, m->d_kp, m->d_vp, m->d_att, m->d_qout, m->d_norm, m->d_norm2, m->d_hn,
+                  m->d_logits, m->d_e, m->d_cat, m->d_hm, m->d_hm1, m->d_mtp_h, m->d_part, m->d_attn_cnt,
+                  m->d_head_cnt, m->d_cand_max, m->d_cand_sum, m->d_cand_idx, m->d_pos, m->d_mtp_pos,
+                  m->d_tokens, m->d_argmax, m->d_prob, m->d_log, m->d_step, m->d_mtp_tok};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  if (m->h_pin) cudaFreeHost(m->h_pin);
+  if (m->h_pinf) cudaFreeHost(m->h_pinf);
+  delete m;
+}
+
+int kib_qwen35_get_plan(const kib_qwen35* m, kib_qwen35_plan* plan) {
+  if (!m || !plan) return KIB_ERR_INVALID_ARGUMENT;
+  *plan = m->plan;
+  return KIB_OK;
+}
+
+int kib_qwen35_reset(kib_qwen35* m) {
+  if (!m) return KIB_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = m->ctx->stream;
+  ENG_CUDA(cudaMemsetAsync(m->d_k, 0, m->k_elems * 2, st));
+  ENG_CUDA(cudaMemsetAsync(m->d_v, 0, m->k_elems * 2, st));
+  ENG_CUDA(cudaMemsetAsync(m->d_r, 0, m->r_elems * 4, st));
+  ENG_CUDA(cudaMemsetAsync(m->d_s, 0, m->s_elems * 4, st));
+  if (m->mk_elems) {
+    ENG_CUDA(cudaMemsetAsync(m->d_mk, 0, m->mk_elems * 2, st));
+    ENG_CUDA(cudaMemsetAsync(m->d_mv, 0, m->mk_elems * 2, st));
+  }
+  ENG_CUDA(cudaMemsetAsync(m->d_pending_h, 0, static_cast<size_t>(m->H) * 4, st));
+  ENG_CUDA(cudaMemsetAsync(m->d_step, 0, 4, st));
+  m->pos = 0;
+  return set_pos(m, m->d_pos, 0);
+}
+
+uint64_t kib_qwen35_position(const kib_qwen35* m) { return m ? m->pos : 0; }
+
+int kib_qwen35_set_position(kib_qwen35* m, uint64_t position) {
+  if (!m || position >= static_cast<uint64_t>(m->cap)) return KIB_ERR_INVALID_ARGUMENT;
+  m->pos = position;
+  return set_pos(m, m->d_pos, position);
+}
+
+int kib_qwen35_forward(kib_qwen35* m, const int32_t* tokens, uint64_t n, int advance, int32_t* argmax_out,
+                       float* logits, float* normed_hidden) {
+  if (!m || !tokens || n < 1 || n > kMaxSmallT) return KIB_ERR_INVALID_ARGUMENT;
+  if (m->pos + n > static_cast<uint64_t>(m->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "forward exceeds cache capacity");
+  cudaStream_t st = m->ctx->stream;
+  std::memcpy(m->h_pin + 16, tokens, n * sizeof(int32_t));
+  m->h_pin[0] = static_cast<int>(m->pos);
+  ENG_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, st));
+  ENG_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_pin + 16, n * sizeof(int), cudaMemcpyHostToDevice, st));
+  int rc = forward_small(m, static_cast<int>(n), logits != nullptr);
+  if (rc) return rc;
+  if (argmax_out) ENG_CUDA(cudaMemcpyAsync(m->h_pin + 32, m->d_argmax, n * sizeof(int), cudaMemcpyDeviceToHost, st));
+  if (logits)
+    ENG_CUDA(cudaMemcpyAsync(logits, m->d_logits, n * static_cast<size_t>(m->V) * 4, cudaMemcpyDeviceToHost, st));
+  if (normed_hidden)
+    ENG_CUDA(cudaMemcpyAsync(normed_hidden, m->d_hn, n * static_cast<size_t>(m->H) * 4, cudaMemcpyDeviceToHost, st));
+  rc = sync_check(m, "forward");
+  if (rc) return rc;
+  if (argmax_out) std::memcpy(argmax_out, m->h_pin + 32, n * sizeof(int32_t));
+  if (advance) m->pos += n;
+  return KIB_OK;
+}
+
+int kib_qwen35_prefill(kib_qwen35* m, const int32_t* tokens, uint64_t n, uint64_t chunk, int32_t* next_token) {
+  if (!m || !tokens || n == 0) return KIB_ERR_INVALID_ARGUMENT;
+  if (m->pos + n > static_cast<uint64_t>(m->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "prefill exceeds cache capacity");
+  if (chunk == 0) chunk = static_cast<uint64_t>(m->chunk);
+  if (chunk > static_cast<uint64_t>(m->tmax)) chunk = static_cast<uint64_t>(m->tmax);
+  cudaStream_t st = m->ctx->stream;
+  std::vector<int32_t> staging;
+  for (uint64_t s = 0; s < n; s += chunk) {
+    const uint64_t T = std::min<uint64_t>(chunk, n - s);
+    const bool last = s + T == n;
+    m->h_pin[0] = static_cast<int>(m->pos);
+    ENG_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, st));
+    ENG_CUDA(cudaMemcpyAsync(m->d_tokens, tokens + s, T * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    int rc;
+    if (T <= static_cast<uint64_t>(kMaxSmallT)) {
+      rc = forward_small(m, static_cast<int>(T), false);
+    } else {
+      rc = forward_prefill(m, static_cast<int>(T), last);
+    }
+    if (rc) return rc;
+    if (m->has_mtp) {
+      // MTP layer over the chunk (qwen35_runtime.cpp:5894-5961): normed rows,
+      // shifted by one with pending_h in front.
+      Enq q{m, st};
+      if (T > static_cast<uint64_t>(kMaxSmallT))
+        q.run(rms_rows_launch(m->d_h, m->output_norm.f(), static_cast<int>(T), m->H, m->eps, m->d_hn, st), "norm_rows");
+      // shifted rows: [pending_h, normed rows 0..T-2]
+      q.run(cudaMemcpyAsync(m->d_norm, m->d_pending_h, static_cast<size_t>(m->H) * 4, cudaMemcpyDeviceToDevice, st),
+            "shift");
+      if (T > 1)
+        q.run(cudaMemcpyAsync(m->d_norm + m->H, m->d_hn, (T - 1) * static_cast<size_t>(m->H) * 4,
+                              cudaMemcpyDeviceToDevice, st),
+              "shift");
+      q.run(cudaMemcpyAsync(m->d_pending_h, m->d_hn + (T - 1) * static_cast<size_t>(m->H),
+                            static_cast<size_t>(m->H) * 4, cudaMemcpyDeviceToDevice, st),
+            "pending_h");
+      q.run(cudaMemcpyAsync(m->d_mtp_pos, m->d_pos, sizeof(int), cudaMemcpyDeviceToDevice, st), "mtp_pos");
+      mtp_enqueue(q, static_cast<int>(T), m->d_tokens, m->d_norm, false, nullptr, nullptr, nullptr, nullptr, nullptr);
+      if (!q.ok()) return fail(m, KIB_ERR_INTERNAL, "mtp prefill: " + q.why);
+    }
+    m->pos += T;
+    if (last && next_token) {
+      // the small path's head ran over all T rows; the last row's argmax is the sample
+      const int row = T <= static_cast<uint64_t>(kMaxSmallT) ? static_cast<int>(T) - 1 : 0;
+      ENG_CUDA(cudaMemcpyAsync(m->h_pin + 32, m->d_argmax + row, sizeof(int), cudaMemcpyDeviceToHost, st));
+    }
+    int rc2 = sync_check(m, "prefill");
+    if (rc2) return rc2;
+    if (last && next_token) *next_token = m->h_pin[32];
+  }
+  return KIB_OK;
+}
+
+int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps, int32_t* tokens_out) {
+  if (!m || steps == 0) return KIB_ERR_INVALID_ARGUMENT;
+  if (m->pos + steps > static_cast<uint64_t>(m->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "decode exceeds cache capacity");
+  if (steps > (1u << 20)) return KIB_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = m->ctx->stream;
+  if (!m->decode_graph) {
+    int rc = capture(m, &m->decode_graph, [&](Enq& q) {
+      q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, m->d_tokens, 1, m->d_h, m->H, q.st), "embed");
+      main_layers_small(q, 1, m->d_pos);
+      head_small(q, 1, m->d_h, m->output_norm, head_weight(m), m->d_tokens, nullptr, nullptr, nullptr, m->d_log,
+                 m->d_step, m->d_pos);
+    });
+    if (rc) return rc;
+  }
+  m->h_pin[0] = static_cast<int>(m->pos);
+  m->h_pin[1] = first_token;
+  m->h_pin[2] = 0;
+  ENG_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, st));
+  ENG_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_pin + 1, sizeof(int), cudaMemcpyHostToDevice, st));
+  ENG_CUDA(cudaMemcpyAsync(m->d_step, m->h_pin + 2, sizeof(int), cudaMemcpyHostToDevice, st));
+  for (uint64_t i = 0; i < steps; ++i) ENG_CUDA(cudaGraphLaunch(m->decode_graph, st));
+  if (tokens_out) ENG_CUDA(cudaMemcpyAsync(tokens_out, m->d_log, steps * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  int rc = sync_check(m, "decode");
+  if (rc) return rc;
+  m->pos += steps;
+  return KIB_OK;
+}
+
+int kib_qwen35_state_io(kib_qwen35* m, int into, uint16_t* k, uint16_t* v, float* r, float* s, uint16_t* mk,
+                        uint16_t* mv, float* ph) {
+  if (!m) return KIB_ERR_INVALID_ARGUMENT;
+  auto io = [&](void* dev, void* host, size_t bytes) -> cudaError_t {
+    if (!host || bytes == 0) return cudaSuccess;
+    return into ? cudaMemcpy(dev, host, bytes, cudaMemcpyHostToDevice) : cudaMemcpy(host, dev, bytes, cudaMemcpyDeviceToHost);
+  };
+  cudaStreamSynchronize(m->ctx->stream);
+  ENG_CUDA(io(m->d_k, k, m->k_elems * 2));
+  ENG_CUDA(io(m->d_v, v, m->k_elems * 2));
+  ENG_CUDA(io(m->d_r, r, m->r_elems * 4));
+  ENG_CUDA(io(m->d_s, s, m->s_elems * 4));
+  ENG_CUDA(io(m->d_mk, mk, m->mk_elems * 2));
+  ENG_CUDA(io(m->d_mv, mv, m->mk_elems * 2));
+  ENG_CUDA(io(m->d_pending_h, ph, static_cast<size_t>(m->H) * 4));
+  return KIB_OK;
+}
+
+int kib_qwen35_mtp_forward(kib_qwen35* m, const int32_t* tokens, const float* h_rows, uint64_t n, uint64_t position,
+                           int32_t* argmax_out, float* h_nextn_out) {
+  if (!m || !tokens || !h_rows || n < 1 || n > kMaxSmallT) return KIB_ERR_INVALID_ARGUMENT;
+  if (!m->has_mtp) return fail(m, KIB_ERR_UNAVAILABLE, "model has no MTP/NextN layer");
+  cudaStream_t st = m->ctx->stream;
+  std::memcpy(m->h_pin + 16, tokens, n * sizeof(int32_t));
+  m->h_pin[0] = static_cast<int>(position);
+  ENG_CUDA(cudaMemcpyAsync(m->d_mtp_pos, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, st));
+  ENG_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_pin + 16, n * sizeof(int), cudaMemcpyHostToDevice, st));
+  ENG_CUDA(cudaMemcpyAsync(m->d_norm, h_rows, n * static_cast<size_t>(m->H) * 4, cudaMemcpyHostToDevice, st));
+  Enq q{m, st};
+  mtp_enqueue(q, static_cast<int>(n), m->d_tokens, m->d_norm, true, m->d_argmax, nullptr, nullptr, nullptr, nullptr);
+  if (!q.ok()) return fail(m, KIB_ERR_INTERNAL, "mtp forward: " + q.why);
+  if (argmax_out) ENG_CUDA(cudaMemcpyAsync(m->h_pin + 32, m->d_argmax, n * sizeof(int), cudaMemcpyDeviceToHost, st));
+  if (h_nextn_out)
+    ENG_CUDA(cudaMemcpyAsync(h_nextn_out, m->d_mtp_h, n * static_cast<size_t>(m->H) * 4, cudaMemcpyDeviceToHost, st));
+  int rc = sync_check(m, "mtp_forward");
+  if (rc) return rc;
+  if (argmax_out) std::memcpy(argmax_out, m->h_pin + 32, n * sizeof(int32_t));
+  return KIB_OK;
+}
+
+// generate_qwen35_metal (qwen35_runtime.cpp:5239-6714), greedy decoding.
+int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t* out, uint64_t cap_out,
+                        kib_generation_result* res) {
+  if (!m || !rq || !rq->prompt_tokens || rq->prompt_count == 0 || !res) return KIB_ERR_INVALID_ARGUMENT;
+  std::memset(res, 0, sizeof(*res));
+  const uint64_t max_new = std::min<uint64_t>(rq->max_new_tokens, cap_out);
+  if (rq->prompt_count + max_new + 8 > static_cast<uint64_t>(m->cap))
+    return fail(m, KIB_ERR_INVALID_ARGUMENT, "prompt + max_new_tokens exceeds the attention capacity");
+  auto is_eos = [&](int64_t t) {
+    if (rq->ignore_eos) return false;
+    return t == kQwenEndOfText || t == m->eos ||
+           (rq->eos_token_id != UINT64_MAX && static_cast<uint64_t>(t) == rq->eos_token_id);
+  };
+  cudaEvent_t e0, e1, e2;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventCreate(&e2);
+  cudaStream_t st = m->ctx->stream;
+  int rc = kib_qwen35_reset(m);
+  if (rc) return rc;
+  cudaEventRecord(e0, st);
+  int32_t next = 0;
+  rc = kib_qwen35_prefill(m, rq->prompt_tokens, rq->prompt_count, rq->prefill_chunk_tokens, &next);
+  if (rc) return rc;
+  cudaEventRecord(e1, st);
+  res->prompt_tokens = rq->prompt_count;
+  uint64_t n = 0;
+  bool stop = false;
+  const bool mtp = rq->enable_mtp && m->has_mtp && rq->mtp_draft_tokens > 0;
+  kib_mtp_report& R = res->mtp;
+  R.available = m->has_mtp ? 1 : 0;
+  R.enabled = mtp ? 1 : 0;
+  R.draft_tokens = rq->mtp_draft_tokens;
+  R.p_min = rq->mtp_p_min;
+  if (!mtp) {
+    // greedy loop (6601-6632), replayed in device-side batches; tokens past an
+    // EOS are discarded
+    int32_t tok = next;
+    if (is_eos(tok)) {
+      stop = true;
+    } else if (max_new > 0) {
+      out[n++] = tok;
+    }
+    std::vector<int32_t> buf;
+    while (!stop && n < max_new) {
+      const uint64_t batch = std::min<uint64_t>(32, max_new - n);
+      buf.resize(batch);
+      rc = kib_qwen35_decode_greedy(m, tok, batch, buf.data());
+      if (rc) return rc;
+      for (uint64_t i = 0; i < batch; ++i) {
+        if (is_eos(buf[i])) {
+          stop = true;
+          break;
+        }
+        out[n++] = buf[i];
+      }
+      tok = buf[batch - 1];
+    }
+  } else {
+    // MTP loop (6457-6600) with the adaptive budget (6421-6455)
+    const uint64_t K = std::min<uint64_t>(rq->mtp_draft_tokens, kMaxSmallT - 1);
+    uint64_t budget = rq->mtp_adaptive ? 1 : K;
+    uint64_t win_d = 0, win_a = 0;
+    int32_t next_token = next;
+    while (n < max_new && !stop) {
+      if (is_eos(next_token)) {
+        stop = true;
+        break;
+      }
+      out[n++] = next_token;
+      if (n >= max_new) break;
+      const uint64_t vpos = m->pos;
+      const uint64_t b = std::min<uint64_t>(budget, max_new - n);
+      // draft chain on the device: token and h stay resident
+      m->h_pin[0] = static_cast<int>(vpos);
+      m->h_pin[1] = next_token;
+      m->h_pin[2] = 0;
+      ENG_CUDA(cudaMemcpyAsync(m->d_mtp_pos, m->h_pin, 4, cudaMemcpyHostToDevice, st));
+      ENG_CUDA(cudaMemcpyAsync(m->d_mtp_tok, m->h_pin + 1, 4, cudaMemcpyHostToDevice, st));
+      ENG_CUDA(cudaMemcpyAsync(m->d_step, m->h_pin + 2, 4, cudaMemcpyHostToDevice, st));
+      ENG_CUDA(cudaMemcpyAsync(m->d_mtp_h, m->d_pending_h, static_cast<size_t>(m->H) * 4, cudaMemcpyDeviceToDevice, st));
+      if (!m->mtp_graph) {
+        rc = capture(m, &m->mtp_graph, [&](Enq& q) {
+          // d_mtp_h holds the input h; the head overwrites it with h_nextn
+          q.run(cudaMemcpyAsync(m->d_hn, m->d_mtp_h, static_cast<size_t>(m->H) * 4, cudaMemcpyDeviceToDevice, q.st), "h_in");
+          mtp_enqueue(q, 1, m->d_mtp_tok, m->d_hn, true, m->d_mtp_tok, m->d_prob, m->d_log, m->d_step, m->d_mtp_pos);
+        });
+        if (rc) return rc;
+      }
+      for (uint64_t i = 0; i < b; ++i) ENG_CUDA(cudaGraphLaunch(m->mtp_graph, st));
+      ENG_CUDA(cudaMemcpyAsync(m->h_pin + 64, m->d_log, b * 4, cudaMemcpyDeviceToHost, st));
+      ENG_CUDA(cudaMemcpyAsync(m->h_pinf, m->d_prob, b * 4, cudaMemcpyDeviceToHost, st));
+      rc = sync_check(m, "mtp draft");
+      if (rc) return rc;
+      std::vector<int32_t> drafts;
+      for (uint64_t i = 0; i < b; ++i) {
+        if (rq->mtp_p_min > 0.0 && static_cast<double>(m->h_pinf[i]) < rq->mtp_p_min) {
+          ++R.confidence_stops;
+          break;
+        }
+        drafts.push_back(m->h_pin[64 + i]);
+        ++R.drafted_tokens;
+      }
+      std::vector<int32_t> verify{next_token};
+      verify.insert(verify.end(), drafts.begin(), drafts.end());
+      // snapshot_recurrent_state (6154-6167)
+      ENG_CUDA(cudaMemcpyAsync(m->d_r_snap, m->d_r, m->r_elems * 4, cudaMemcpyDeviceToDevice, st));
+      ENG_CUDA(cudaMemcpyAsync(m->d_s_snap, m->d_s, m->s_elems * 4, cudaMemcpyDeviceToDevice, st));
+      std::vector<int32_t> targets(verify.size());
+      rc = kib_qwen35_forward(m, verify.data(), verify.size(), 0, targets.data(), nullptr, nullptr);
+      if (rc) return rc;
+      uint64_t acc = 0;
+      for (size_t i = 0; i < drafts.size(); ++i) {
+        if (n >= max_new) break;
+        ++R.verify_steps;
+        if (i < 8) ++R.verified_by_position[i];
+        if (is_eos(targets[i])) {
+          stop = true;
+          break;
+        }
+        if (targets[i] != drafts[i]) break;
+        out[n++] = drafts[i];
+        ++acc;
+        ++R.accepted_tokens;
+        if (i < 8) ++R.accepted_by_position[i];
+        if (n >= max_new) break;
+      }
+      if (rq->mtp_adaptive && K > 1 && !drafts.empty()) {
+        win_d += drafts.size();
+        win_a += acc;
+        const uint64_t thr = std::max<uint64_t>(16, budget * 8);
+        if (win_d >= thr) {
+          bool changed = false;
+          if (budget > 1 && win_a * 4 < win_d * 3) {
+            --budget;
+            changed = true;
+          } else if (budget < K && win_a == win_d) {
+            ++budget;
+            changed = true;
+          }
+          if (changed) {
+            ++R.adaptive_changes;
+            win_d = win_a = 0;
+          } else if (win_d >= thr * 2) {
+            win_d = win_a = 0;
+          }
+        }
+      }
+      const uint64_t committed = 1 + acc;
+      if (stop) {
+        m->pos = vpos + committed;
+        break;
+      }
+      if (acc == drafts.size()) {
+        m->pos = vpos + committed;
+        ENG_CUDA(cudaMemcpyAsync(m->d_pending_h, m->d_hn + (committed - 1) * static_cast<size_t>(m->H),
+                                 static_cast<size_t>(m->H) * 4, cudaMemcpyDeviceToDevice, st));
+        next_token = targets[committed - 1];
+      } else {
+        // restore_recurrent_state (6169-6182) and re-run the committed tokens
+        ENG_CUDA(cudaMemcpyAsync(m->d_r, m->d_r_snap, m->r_elems * 4, cudaMemcpyDeviceToDevice, st));
+        ENG_CUDA(cudaMemcpyAsync(m->d_s, m->d_s_snap, m->s_elems * 4, cudaMemcpyDeviceToDevice, st));
+        std::vector<int32_t> commit(verify.begin(), verify.begin() + static_cast<long>(committed));
+        std::vector<int32_t> ct(committed);
+        m->pos = vpos;
+        rc = kib_qwen35_forward(m, commit.data(), committed, 1, ct.data(), nullptr, nullptr);
+        if (rc) return rc;
+        ENG_CUDA(cudaMemcpyAsync(m->d_pending_h, m->d_hn + (committed - 1) * static_cast<size_t>(m->H),
+                                 static_cast<size_t>(m->H) * 4, cudaMemcpyDeviceToDevice, st));
+        next_token = ct[committed - 1];
+      }
+    }
+    R.adaptive_budget = budget;
+  }
+  cudaEventRecord(e2, st);
+  cudaEventSynchronize(e2);
+  float pf = 0, dc = 0;
+  cudaEventElapsedTime(&pf, e0, e1);
+  cudaEventElapsedTime(&dc, e1, e2);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaEventDestroy(e2);
+  res->prefill_ms = pf;
+  res->decode_ms = dc;
+  res->generated_tokens = n;
+  res->finish_reason_stop = stop ? 1 : 0;
+  res->kv_used_tokens = m->pos;
+  return KIB_OK;
+}
+
+// ---------------------------------------------------------------- GGUF tools
+void kib_synth_default(kib_synth_config* c) {
+  if (!c) return;
+  SynthQwen35Config d;
+  c->hidden = static_cast<uint64_t>(d.hidden);
+  c->layers = static_cast<uint64_t>(d.layers);
+  c->intermediate = static_cast<uint64_t>(d.intermediate);
+  c->vocab = static_cast<uint64_t>(d.vocab);
+  c->heads = static_cast<uint64_t>(d.heads);
+  c->kv_heads = static_cast<uint64_t>(d.kv_heads);
+  c->head_dim = static_cast<uint64_t>(d.head_dim);
+  c->ssm_heads = static_cast<uint64_t>(d.ssm_heads);
+  c->ssm_head_dim = static_cast<uint64_t>(d.ssm_head_dim);
+  c->conv_kernel = static_cast<uint64_t>(d.conv_kernel);
+  c->full_attention_interval = static_cast<uint64_t>(d.full_attention_interval);
+  c->nextn_layers = static_cast<uint64_t>(d.nextn_layers);
+  c->proj_type = d.proj_type;
+  c->down_type = d.down_type;
+  c->embd_type = d.embd_type;
+  c->seed = d.seed;
+  c->rope_theta = d.rope_theta;
+  c->rms_eps = d.rms_eps;
+  c->eos_token_id = d.eos_token_id;
+  c->threads = d.threads;
+}
+
+int kib_write_synthetic_qwen35(const char* path, const kib_synth_config* c, char* err, int err_len) {
+  if (!path || !c) return KIB_ERR_INVALID_ARGUMENT;
+  SynthQwen35Config d;
+  d.hidden = static_cast<int64_t>(c->hidden);
+  d.layers = static_cast<int64_t>(c->layers);
+  d.intermediate = static_cast<int64_t>(c->intermediate);
+  d.vocab = static_cast<int64_t>(c->vocab);
+  d.heads = static_cast<int64_t>(c->heads);
+  d.kv_heads = static_cast<int64_t>(c->kv_heads);
+  d.head_dim = static_cast<int64_t>(c->head_dim);
+  d.ssm_heads = static_cast<int64_t>(c->ssm_heads);
+  d.ssm_head_dim = static_cast<int64_t>(c->ssm_head_dim);
+  d.conv_kernel = static_cast<int64_t>(c->conv_kernel);
+  d.full_attention_interval = static_cast<int64_t>(c->full_attention_interval);
+  d.nextn_layers = static_cast<int64_t>(c->nextn_layers);
+  d.proj_type = c->proj_type;
+  d.down_type = c->down_type;
+  d.embd_type = c->embd_type;
+  d.seed = c->seed;
+  d.rope_theta = c->rope_theta;
+  d.rms_eps = c->rms_eps;
+  d.eos_token_id = c->eos_token_id;
+  d.threads = c->threads > 0 ? c->threads : 8;
+  std::string e;
+  if (!write_synthetic_qwen35(path, d, &e)) {
+    if (err && err_len > 0) {
+      std::strncpy(err, e.c_str(), static_cast<size_t>(err_len - 1));
+      err[err_len - 1] = 0;
+    }
+    return KIB_ERR_INVALID_ARGUMENT;
+  }
+  return KIB_OK;
+}
+
+int kib_quantize_kquant(int type, const float* x, uint64_t n, void* out) {
+  if (!x || !out || n == 0 || n % 256) return KIB_ERR_INVALID_ARGUMENT;
+  uint8_t* o = static_cast<uint8_t*>(out);
+  switch (type) {
+    case 12: quantize_q4_k(x, static_cast<int64_t>(n), o); return KIB_OK;
+    case 13: quantize_q5_k(x, static_cast<int64_t>(n), o); return KIB_OK;
+    case 14: quantize_q6_k(x, static_cast<int64_t>(n), o); return KIB_OK;
+    default: return KIB_ERR_INVALID_ARGUMENT;
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,541 @@
+// layer_kernels.cuh -- the non-GEMV kernels of the Qwen3.5 hybrid decoder:
+// fused gated-delta-net core, split-K GQA decode attention with an in-kernel
+// combine, prefill attention, token embedding, MTP input preparation and the
+// multi-token (M > 8) K-quant GEMM used by chunked prefill.
+#pragma once
+
+#include "kib_common.cuh"
+#include "kquant.cuh"
+
+namespace kib {
+
+KIB_DEV float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
+KIB_DEV float softplus20_f(float v) { return v > 20.0f ? v : logf(1.0f + expf(v)); }
+KIB_DEV float silu_k(float v) { return v / (1.0f + expf(-v)); }
+
+// ===================================================================== GDN
+// One CTA per (value head, group of 16 state rows).  Fuses, per token:
+//   split_qkv_l2_norm_f32_qwen35 (mps_backend.mm:2097-2153) for the head's q,k,
+//   prepare_qwen35_gdn_gate_beta_f32 (2588-2605),
+//   gated_delta_net_f32_batched_qwen35 (2307-2374) for 16 rows of S.
+// The conv + silu that precede it run in the qkv GEMV epilogue; the norm-gate
+// that follows runs in the ssm_out GEMV prologue.
+struct GdnParams {
+  const float* conv_out;  // [T][C]: q | k | v after conv+silu
+  int C;
+  const float* beta_raw;  // [T][ld_ba]
+  const float* alpha_raw; // [T][ld_ba]
+  int ld_ba;
+  const float* dt_bias;   // [Hv]
+  const float* ssm_a;     // [Hv]
+  float* state;           // [Hv][128][128] (this layer)
+  float* out;             // [T][Hv*128]
+  int T;
+  int key_heads;
+  int value_heads;
+  float eps;
+};
+
+constexpr int kGdnRows = 16;  // state rows per CTA
+
+static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_constant__ GdnParams p) {
+  constexpr int D = 128;
+  __shared__ __align__(16) float qn[D];
+  __shared__ __align__(16) float kn[D];
+  __shared__ float red[2][4];
+  __shared__ float s_gb[2];
+  const int h = blockIdx.x, grp = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kh = h % p.key_heads;
+  const int key_dim = p.key_heads * D;
+  float* S = p.state + static_cast<size_t>(h) * D * D;
+  // warp w owns rows grp*16 + 4w .. +3; lane owns columns 4*lane .. +3
+  float4 s[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+    s[r] = *reinterpret_cast<const float4*>(S + static_cast<size_t>(grp * kGdnRows + 4 * warp + r) * D + 4 * lane);
+
+  pdl_wait();
+  pdl_launch_dependents();
+  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  for (int t = 0; t < p.T; ++t) {
+    const float* row = p.conv_out + static_cast<size_t>(t) * p.C;
+    const float qv = row[kh * D + tid];
+    const float kv = row[key_dim + kh * D + tid];
+    float q2 = warp_sum(qv * qv), k2 = warp_sum(kv * kv);
+    if (lane == 0) {
+      red[0][warp] = q2;
+      red[1][warp] = k2;
+    }
+    if (tid == 0) {
+      const float a = p.alpha_raw[static_cast<size_t>(t) * p.ld_ba + h];
+      const float b = p.beta_raw[static_cast<size_t>(t) * p.ld_ba + h];
+      s_gb[0] = softplus20_f(a + p.dt_bias[h]) * p.ssm_a[h];
+      s_gb[1] = sigmoid_f(b);
+    }
+    __syncthreads();
+    const float qs = 1.0f / fmaxf(sqrtf((red[0][0] + red[0][1]) + (red[0][2] + red[0][3])), p.eps);
+    const float ks = 1.0f / fmaxf(sqrtf((red[1][0] + red[1][1]) + (red[1][2] + red[1][3])), p.eps);
+    qn[tid] = qv * qs;
+    kn[tid] = kv * ks;
+    const float ge = expf(s_gb[0]);
+    const float beta = s_gb[1];
+    __syncthreads();
+    const float4 k4 = *reinterpret_cast<const float4*>(kn + 4 * lane);
+    const float4 q4 = *reinterpret_cast<const float4*>(qn + 4 * lane);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int vrow = grp * kGdnRows + 4 * warp + r;
+      float4 st = s[r];
+      st.x *= ge;
+      st.y *= ge;
+      st.z *= ge;
+      st.w *= ge;
+      const float sk = warp_sum(st.x * k4.x + st.y * k4.y + st.z * k4.z + st.w * k4.w);
+      const float v = row[2 * key_dim + h * D + vrow];
+      const float delta = (v - sk) * beta;
+      st.x += k4.x * delta;
+      st.y += k4.y * delta;
+      st.z += k4.z * delta;
+      st.w += k4.w * delta;
+      const float y = warp_sum(st.x * q4.x + st.y * q4.y + st.z * q4.z + st.w * q4.w);
+      if (lane == 0) p.out[static_cast<size_t>(t) * p.value_heads * D + h * D + vrow] = y * scale;
+      s[r] = st;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+    *reinterpret_cast<float4*>(S + static_cast<size_t>(grp * kGdnRows + 4 * warp + r) * D + 4 * lane) = s[r];
+}
+
+// =============================================================== attention
+struct AttnParams {
+  const float* qg;        // [T][heads][2*hd]: q | gate per head (joint projection)
+  const float* kp;        // [T][kv_heads*hd]
+  const float* vp;        // [T][kv_heads*hd]
+  const float* q_norm;    // [hd]
+  const float* k_norm;    // [hd]
+  uint16_t* kcache;       // [cap][kv_heads*hd] f16, this layer
+  uint16_t* vcache;
+  const int* pos;         // position of token 0
+  int T;
+  int heads;
+  int kv_heads;
+  float eps;
+  float theta;
+  int n_dims;             // rotated dims (2 * sum of MRoPE sections)
+  int sec0, sec1, sec2, sec3;
+  int nsplit;
+  float* part;            // [nsplit][T][heads][hd + 2]
+  unsigned* counters;     // [kv_heads]
+  float* out;             // [T][heads*hd]
+  float* q_out;           // prefill: normed+roped q [T][heads][hd]
+  int round_q;            // prefill T >= 64: Q rounded to half (flash256 numerics)
+};
+
+constexpr int kHd = 256;
+
+// qk_norm (mps_backend.mm:1991-2024) then mrope_f32_in_place (2482-2527) on one
+// 256-wide head vector held in shared memory; one warp.
+KIB_DEV void norm_rope_head(float* v, const float* in, const float* w, float eps, int position,
+                            const AttnParams& p, int lane) {
+  float ss = 0.0f;
+  for (int i = lane; i < kHd; i += 32) {
+    const float x = in[i];
+    ss += x * x;
+  }
+  ss = warp_sum(ss);
+  const float scale = 1.0f / sqrtf(ss / static_cast<float>(kHd) + p.eps);
+  for (int i = lane; i < kHd; i += 32) v[i] = in[i] * (scale * w[i]);
+  __syncwarp();
+  const int half = p.n_dims / 2;
+  const int total = p.sec0 + p.sec1 + p.sec2 + p.sec3;
+  for (int pi = lane; pi < half; pi += 32) {
+    // text positions: all four MRoPE position streams equal `position`
+    (void)total;
+    const float exponent = static_cast<float>(2 * pi) / static_cast<float>(p.n_dims);
+    const float freq = 1.0f / powf(p.theta, exponent);
+    const float angle = static_cast<float>(position) * freq;
+    float sn, cs;
+    sincosf(angle, &sn, &cs);
+    const float x0 = v[pi], x1 = v[half + pi];
+    v[pi] = x0 * cs - x1 * sn;
+    v[half + pi] = x1 * cs + x0 * sn;
+  }
+  __syncwarp();
+}
+
+// Split-K decode attention for T <= 8 queries over an F16 KV cache.  Grid
+// (nsplit, kv_heads); 8 warps: warp w serves q head (w % 4) of the kv group and
+// key half (w / 4).  The CTA owning a new token's position normalises, rotates
+// and writes its K/V (single writer).  The last CTA of each kv head merges
+// all splits and applies sigmoid(gate) (attention_f32_batched_f16_kv,
+// mps_backend.mm:2943-3008, plus qwen35_runtime.cpp:3347-3351).
+template <int TM>
+__global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant__ AttnParams p) {
+  constexpr int G = 4;  // q heads per kv head
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                        // [T][G][256]
+  float* merge = sm + p.T * G * kHd;     // [8 warps][T][256 + 2]
+  __shared__ bool s_last;
+  const int split = blockIdx.x, kvh = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kvd = p.kv_heads * kHd;
+
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pos0 = *p.pos;
+  const int nkeys = pos0 + p.T;
+  int chunk = (nkeys + p.nsplit - 1) / p.nsplit;
+  chunk = (chunk + 7) & ~7;
+  const int kb = split * chunk, ke = min(kb + chunk, nkeys);
+
+  // q prep: warp -> (head, token)
+  for (int job = warp; job < G * p.T; job += 8) {
+    const int j = job % G, t = job / G;
+    const int head = kvh * G + j;
+    norm_rope_head(qs + (t * G + j) * kHd, p.qg + (static_cast<size_t>(t) * p.heads + head) * 2 * kHd, p.q_norm,
+                   p.eps, pos0 + t, p, lane);
+  }
+  // new keys owned by this split
+  for (int t = warp; t < p.T; t += 8) {
+    const int kpos = pos0 + t;
+    if (kpos < kb || kpos >= ke) continue;
+    float* tmp = merge + warp * (kHd + 2);  // scratch row
+    norm_rope_head(tmp, p.kp + static_cast<size_t>(t) * kvd + kvh * kHd, p.k_norm, p.eps, kpos, p, lane);
+    for (int i = lane; i < kHd; i += 32) {
+      p.kcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] = __half_as_ushort(__float2half_rn(tmp[i]));
+      p.vcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] =
+          __half_as_ushort(__float2half_rn(p.vp[static_cast<size_t>(t) * kvd + kvh * kHd + i]));
+    }
+  }
+  __threadfence_block();
+  __syncthreads();
+
+  // main loop: this warp's head j, keys kb + half, kb + half + 2, ...
+  const int j = warp % G, kh2 = warp / G;
+  const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
+  float m[TM], l[TM], acc[TM][8];
+  float qreg[TM][8];
+#pragma unroll
+  for (int t = 0; t < TM; ++t) {
+    m[t] = -INFINITY;
+    l[t] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc[t][i] = 0.0f;
+      qreg[t][i] = t < p.T ? qs[(t * G + j) * kHd + 8 * lane + i] : 0.0f;
+    }
+  }
+  for (int key = kb + kh2; key < ke; key += 2) {
+    const uint4 kr = __ldcg(reinterpret_cast<const uint4*>(p.kcache + static_cast<size_t>(key) * kvd + kvh * kHd + 8 * lane));
+    const uint4 vr = __ldcg(reinterpret_cast<const uint4*>(p.vcache + static_cast<size_t>(key) * kvd + kvh * kHd + 8 * lane));
+    float kf[8], vf[8];
+    {
+      const __half2* kh = reinterpret_cast<const __half2*>(&kr);
+      const __half2* vh = reinterpret_cast<const __half2*>(&vr);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __half22float2(kh[i]);
+        const float2 b = __half22float2(vh[i]);
+        kf[2 * i] = a.x;
+        kf[2 * i + 1] = a.y;
+        vf[2 * i] = b.x;
+        vf[2 * i + 1] = b.y;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TM; ++t) {
+      if (t >= p.T) break;
+      if (key > pos0 + t) continue;  // causal (uniform across the warp)
+      float d = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) d = fmaf(qreg[t][i], kf[i], d);
+      const float sc = warp_sum(d) * scale;
+      const float nm = fmaxf(m[t], sc);
+      const float ps = expf(m[t] - nm);
+      const float w = expf(sc - nm);
+      l[t] = l[t] * ps + w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[t][i] = acc[t][i] * ps + w * vf[i];
+      m[t] = nm;
+    }
+  }
+  // merge the two key halves of each head inside the CTA, then write the split partial
+  for (int t = 0; t < p.T; ++t) {
+    float* mrow = merge + (warp * p.T + t) * (kHd + 2);
+    for (int i = 0; i < 8; ++i) mrow[8 * lane + i] = acc[t][i];
+    if (lane == 0) {
+      mrow[kHd] = m[t];
+      mrow[kHd + 1] = l[t];
+    }
+  }
+  __syncthreads();
+  for (int job = tid; job < G * p.T * kHd; job += 256) {
+    const int i = job % kHd, jt = job / kHd, jj = jt % G, t = jt / G;
+    const float* a = merge + (jj * p.T + t) * (kHd + 2);        // warp jj   (half 0)
+    const float* b = merge + ((jj + G) * p.T + t) * (kHd + 2);  // warp jj+4 (half 1)
+    const float ma = a[kHd], mb = b[kHd];
+    const float M = fmaxf(ma, mb);
+    const float ea = ma == -INFINITY ? 0.0f : expf(ma - M);
+    const float eb = mb == -INFINITY ? 0.0f : expf(mb - M);
+    float* dst = p.part + ((static_cast<size_t>(split) * p.T + t) * p.heads + kvh * G + jj) * (kHd + 2);
+    dst[i] = a[i] * ea + b[i] * eb;
+    if (i == 0) {
+      dst[kHd] = M;
+      dst[kHd + 1] = a[kHd + 1] * ea + b[kHd + 1] * eb;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&p.counters[kvh], 1u) == static_cast<unsigned>(p.nsplit - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int job = tid; job < G * p.T * kHd; job += 256) {
+    const int i = job % kHd, jt = job / kHd, jj = jt % G, t = jt / G;
+    const int head = kvh * G + jj;
+    float M = -INFINITY;
+    for (int sp = 0; sp < p.nsplit; ++sp)
+      M = fmaxf(M, __ldcg(p.part + ((static_cast<size_t>(sp) * p.T + t) * p.heads + head) * (kHd + 2) + kHd));
+    float num = 0.0f, den = 0.0f;
+    for (int sp = 0; sp < p.nsplit; ++sp) {
+      const float* src = p.part + ((static_cast<size_t>(sp) * p.T + t) * p.heads + head) * (kHd + 2);
+      const float ms = __ldcg(src + kHd);
+      if (ms == -INFINITY) continue;
+      const float e = expf(ms - M);
+      num += __ldcg(src + i) * e;
+      den += __ldcg(src + kHd + 1) * e;
+    }
+    const float o = den == 0.0f ? 0.0f : num / den;
+    const float g = p.qg[(static_cast<size_t>(t) * p.heads + head) * 2 * kHd + kHd + i];
+    p.out[static_cast<size_t>(t) * p.heads * kHd + head * kHd + i] = o * sigmoid_f(g);
+  }
+  if (tid == 0) p.counters[kvh] = 0u;
+}
+
+// Prefill step 1: per token, q norm+rope -> q_out, k norm+rope and v -> f16 cache.
+// grid T; 8 warps over the heads + kv heads.
+static __global__ void __launch_bounds__(256) attn_prep_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ __align__(16) float sm[];
+  const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pos = *p.pos + t;
+  const int kvd = p.kv_heads * kHd;
+  float* tmp = sm + warp * kHd;
+  for (int job = warp; job < p.heads + p.kv_heads; job += 8) {
+    if (job < p.heads) {
+      norm_rope_head(tmp, p.qg + (static_cast<size_t>(t) * p.heads + job) * 2 * kHd, p.q_norm, p.eps, pos, p, lane);
+      for (int i = lane; i < kHd; i += 32) p.q_out[(static_cast<size_t>(t) * p.heads + job) * kHd + i] = tmp[i];
+    } else {
+      const int kh = job - p.heads;
+      norm_rope_head(tmp, p.kp + static_cast<size_t>(t) * kvd + kh * kHd, p.k_norm, p.eps, pos, p, lane);
+      for (int i = lane; i < kHd; i += 32) {
+        p.kcache[static_cast<size_t>(pos) * kvd + kh * kHd + i] = __half_as_ushort(__float2half_rn(tmp[i]));
+        p.vcache[static_cast<size_t>(pos) * kvd + kh * kHd + i] =
+            __half_as_ushort(__float2half_rn(p.vp[static_cast<size_t>(t) * kvd + kh * kHd + i]));
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// Prefill step 2: one warp per (query, head), sequential online softmax over
+// keys <= query position (attention_f32_batched_f16_kv order); Q rounded to
+// half when round_q (flash256 numerics, mps_backend.mm:3450-3460); output
+// multiplied by sigmoid(gate).  grid (ceil(T/8), heads).
+static __global__ void __launch_bounds__(256) attn_prefill_kernel(const __grid_constant__ AttnParams p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * 8 + warp, head = blockIdx.y;
+  pdl_wait();
+  pdl_launch_dependents();
+  if (t >= p.T) return;
+  const int pos0 = *p.pos;
+  const int qpos = pos0 + t;
+  const int kvd = p.kv_heads * kHd;
+  const int kvh = head / (p.heads / p.kv_heads);
+  float q[8], acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float v = p.q_out[(static_cast<size_t>(t) * p.heads + head) * kHd + 8 * lane + i];
+    q[i] = p.round_q ? round_to_half(v) : v;
+    acc[i] = 0.0f;
+  }
+  const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
+  float m = -INFINITY, l = 0.0f;
+  for (int key = 0; key <= qpos; ++key) {
+    const uint4 kr = __ldcg(reinterpret_cast<const uint4*>(p.kcache + static_cast<size_t>(key) * kvd + kvh * kHd + 8 * lane));
+    const uint4 vr = __ldcg(reinterpret_cast<const uint4*>(p.vcache + static_cast<size_t>(key) * kvd + kvh * kHd + 8 * lane));
+    const __half2* kh = reinterpret_cast<const __half2*>(&kr);
+    const __half2* vh = reinterpret_cast<const __half2*>(&vr);
+    float d = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = __half22float2(kh[i]);
+      d = fmaf(q[2 * i], a.x, d);
+      d = fmaf(q[2 * i + 1], a.y, d);
+    }
+    const float sc = warp_sum(d) * scale;
+    const float nm = fmaxf(m, sc);
+    const float ps = expf(m - nm), w = expf(sc - nm);
+    l = l * ps + w;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 b = __half22float2(vh[i]);
+      acc[2 * i] = acc[2 * i] * ps + w * b.x;
+      acc[2 * i + 1] = acc[2 * i + 1] * ps + w * b.y;
+    }
+    m = nm;
+  }
+  const float inv = l == 0.0f ? 0.0f : 1.0f / l;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = 8 * lane + i;
+    const float g = p.qg[(static_cast<size_t>(t) * p.heads + head) * 2 * kHd + kHd + d];
+    p.out[static_cast<size_t>(t) * p.heads * kHd + head * kHd + d] = acc[i] * inv * sigmoid_f(g);
+  }
+}
+
+// =============================================================== embedding
+// q*_k_get_rows (mps_backend.mm:1693-1824): dequantize rows `ids` of a K-quant
+// matrix; out-of-range ids produce zeros.  grid T, 256 threads.
+template <int QT>
+__global__ void __launch_bounds__(256) get_rows_kernel(const uint8_t* w, int nrows, int cols, const int* ids,
+                                                       float* out, int out_ld) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = blockIdx.x;
+  const int id = ids[t];
+  const int units = cols / 64;
+  const int bpr = cols / 256;
+  float* o = out + static_cast<size_t>(t) * out_ld;
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+    const int blk = u >> 2, unit = u & 3;
+    if (id < 0 || id >= nrows) {
+      for (int e = 0; e < 64; ++e) o[256 * blk + unit_col<QT>(unit, e)] = 0.0f;
+      continue;
+    }
+    const uint8_t* b = w + (static_cast<size_t>(id) * bpr + blk) * kquant_block_bytes(QT);
+    float v[64];
+    unit_dequant<QT>(b, unit, v);
+#pragma unroll
+    for (int e = 0; e < 64; ++e) o[256 * blk + unit_col<QT>(unit, e)] = v[e];
+  }
+}
+
+// MTP input (qwen35_runtime.cpp:4156-4195): cat[t] = [rms(e_t)*enorm | rms(h_t)*hnorm].
+static __global__ void __launch_bounds__(256) mtp_cat_kernel(const float* e, const float* h, const float* enorm,
+                                                      const float* hnorm, int H, float eps, float* cat) {
+  __shared__ float red[2][8];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* er = e + static_cast<size_t>(t) * H;
+  const float* hr = h + static_cast<size_t>(t) * H;
+  float se = 0.0f, sh = 0.0f;
+  for (int i = tid; i < H; i += 256) {
+    se += er[i] * er[i];
+    sh += hr[i] * hr[i];
+  }
+  se = warp_sum(se);
+  sh = warp_sum(sh);
+  if (lane == 0) {
+    red[0][warp] = se;
+    red[1][warp] = sh;
+  }
+  __syncthreads();
+  float te = 0.0f, th = 0.0f;
+  for (int w = 0; w < 8; ++w) {
+    te += red[0][w];
+    th += red[1][w];
+  }
+  const float ce = 1.0f / sqrtf(te / static_cast<float>(H) + eps);
+  const float ch = 1.0f / sqrtf(th / static_cast<float>(H) + eps);
+  float* c = cat + static_cast<size_t>(t) * 2 * H;
+  for (int i = tid; i < H; i += 256) {
+    c[i] = er[i] * ce * enorm[i];
+    c[H + i] = hr[i] * ch * hnorm[i];
+  }
+}
+
+// ============================================================ prefill GEMM
+// Y[t][r] (+)= W[r,:] . X[t,:] for M > 8 tokens with the reference's mul_mm_simd
+// numerics (mps_backend.mm:1088-1230): weights rounded to half per weight
+// (dequantize_*_mm), x rounded to half, fp32 accumulation.  Products of two
+// halves are exact in fp32, so CUDA-core FMAs reproduce the MMA up to order.
+// Tile 64 rows x 64 tokens, K step one super-block (256).
+struct GemmParams {
+  const uint8_t* w;
+  int rows, cols;
+  const float* x;   // [T][x_ld]
+  int x_ld;
+  int T;
+  float* y;         // [T][y_ld]
+  int y_ld;
+  const float* resid;  // optional [T][y_ld]
+};
+
+template <int QT>
+__global__ void __launch_bounds__(256) kquant_gemm_f16_kernel(const __grid_constant__ GemmParams p) {
+  extern __shared__ __align__(16) float gsm[];
+  float* Ws = gsm;              // [256 k][64 rows]
+  float* Xs = gsm + 256 * 64;   // [256 k][64 tokens]
+  const int tid = threadIdx.x;
+  const int r0 = blockIdx.x * 64, t0 = blockIdx.y * 64;
+  const int bpr = p.cols / 256;
+  const int tr = tid / 16, tt = tid % 16;  // thread computes rows tr*4..+3, tokens tt*4..+3
+  float acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int kb = 0; kb < bpr; ++kb) {
+    {  // weights: 64 rows x 4 units = 256 units, one per thread
+      const int rl = tid >> 2, unit = tid & 3;
+      const int row = r0 + rl;
+      float v[64];
+      if (row < p.rows) {
+        unit_dequant_f16<QT>(p.w + (static_cast<size_t>(row) * bpr + kb) * kquant_block_bytes(QT), unit, v);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) v[e] = 0.0f;
+      }
+#pragma unroll
+      for (int e = 0; e < 64; ++e) Ws[unit_col<QT>(unit, e) * 64 + rl] = v[e];
+    }
+    for (int i = tid; i < 64 * 256; i += 256) {
+      const int tl = i / 256, k = i % 256;
+      const int t = t0 + tl;
+      Xs[k * 64 + tl] = t < p.T ? round_to_half(p.x[static_cast<size_t>(t) * p.x_ld + kb * 256 + k]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int k = 0; k < 256; ++k) {
+      const float4 wv = *reinterpret_cast<const float4*>(Ws + k * 64 + tr * 4);
+      const float4 xv = *reinterpret_cast<const float4*>(Xs + k * 64 + tt * 4);
+      const float w4[4] = {wv.x, wv.y, wv.z, wv.w}, x4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(w4[a], x4[b], acc[a][b]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int row = r0 + tr * 4 + a, t = t0 + tt * 4 + b;
+      if (row < p.rows && t < p.T) {
+        float v = acc[a][b];
+        if (p.resid) v += p.resid[static_cast<size_t>(t) * p.y_ld + row];
+        p.y[static_cast<size_t>(t) * p.y_ld + row] = v;
+      }
+    }
+}
+
+}  // namespace kib

@@ -1,0 +1,822 @@
+// ops.cu -- op-level C ABI (the MpsContext twin): context lifetime, memory,
+// K-quant matvec/matmul/argmax/get_rows, norms, GDN, conv, MRoPE, attention,
+// element-wise ops and copies.  Shape validation follows the reference's
+// MpsContext checks (mps_backend.mm:4006-4308): invalid shapes return
+// KIB_ERR_INVALID_ARGUMENT with a message, never launch.
+#include <cuda_fp16.h>
+
+#include <cstring>
+#include <string>
+
+#include "kib_ctx.cuh"
+#include "layer_kernels.cuh"
+
+using namespace kib;
+
+// =========================================================== small kernels
+namespace {
+
+__global__ void rms_norm_rows_kernel(const float* in, const float* w, int n, float eps, float* out) {
+  __shared__ float red[32];
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  pdl_launch_dependents();
+  const float* x = in + static_cast<size_t>(t) * n;
+  float ss = 0.0f;
+  for (int i = tid; i < n; i += blockDim.x) ss += x[i] * x[i];
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int i = 0; i < static_cast<int>(blockDim.x) / 32; ++i) tot += red[i];
+  const float scale = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
+  float* y = out + static_cast<size_t>(t) * n;
+  for (int i = tid; i < n; i += blockDim.x) y[i] = x[i] * scale * w[i];
+}
+
+// per-head RMSNorm in place; if gate != null also * silu(gate) (norm_gated)
+__global__ void head_norm_kernel(float* v, const float* w, const float* gate, int heads, int d, float eps,
+                                 float* out) {
+  const int h = blockIdx.x, t = blockIdx.y, lane = threadIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
+  const size_t base = (static_cast<size_t>(t) * heads + h) * d;
+  float ss = 0.0f;
+  for (int i = lane; i < d; i += 32) ss += v[base + i] * v[base + i];
+  ss = warp_sum(ss);
+  const float scale = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
+  float* dst = out ? out : v;
+  for (int i = lane; i < d; i += 32) {
+    // qk_norm: v * (scale * w); norm_gated: v * scale * w * silu(gate)
+    const float r = gate ? v[base + i] * scale * w[i] * silu_k(gate[base + i]) : v[base + i] * (scale * w[i]);
+    dst[base + i] = r;
+  }
+}
+
+__global__ void split_qkv_l2_kernel(const float* src, float* q, float* k, float* v, int key_heads, int value_heads,
+                                    int d, float eps) {
+  const int h = blockIdx.x, t = blockIdx.y, part = blockIdx.z, lane = threadIdx.x;
+  const int key_dim = key_heads * d, C = 2 * key_dim + value_heads * d;
+  const float* row = src + static_cast<size_t>(t) * C;
+  if (part == 2) {
+    if (h >= value_heads) return;
+    for (int i = lane; i < d; i += 32) v[(static_cast<size_t>(t) * value_heads + h) * d + i] = row[2 * key_dim + h * d + i];
+    return;
+  }
+  if (h >= key_heads) return;
+  const float* s = row + part * key_dim + h * d;
+  float ss = 0.0f;
+  for (int i = lane; i < d; i += 32) ss += s[i] * s[i];
+  ss = warp_sum(ss);
+  const float scale = 1.0f / fmaxf(sqrtf(ss), eps);
+  float* dst = part == 0 ? q : k;
+  for (int i = lane; i < d; i += 32) dst[(static_cast<size_t>(t) * key_heads + h) * d + i] = s[i] * scale;
+}
+
+// build_ssm_conv_state_f32 + ssm_conv_f32 (+ optional silu): one thread per
+// channel, sequential over tokens, state updated in place.
+__global__ void conv_stateful_kernel(float* state, const float* in, int in_ld, const float* w, int K, int C, int T,
+                                     float* out, int out_ld, int apply_silu) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float win[16];
+  for (int j = 0; j < K - 1; ++j) win[j] = state[static_cast<size_t>(c) * (K - 1) + j];
+  for (int t = 0; t < T; ++t) {
+    win[K - 1] = in[static_cast<size_t>(t) * in_ld + c];
+    float s = 0.0f;
+    for (int j = 0; j < K; ++j) s += win[j] * w[static_cast<size_t>(c) * K + j];
+    out[static_cast<size_t>(t) * out_ld + c] = apply_silu ? silu_k(s) : s;
+    for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+  }
+  for (int j = 0; j < K - 1; ++j) state[static_cast<size_t>(c) * (K - 1) + j] = win[j];
+}
+
+__global__ void prepare_gate_beta_kernel(float* gate, float* beta, const float* bias, const float* scale, int total,
+                                         int heads) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int c = i % heads;
+  gate[i] = softplus20_f(gate[i] + bias[c]) * scale[c];
+  beta[i] = sigmoid_f(beta[i]);
+}
+
+// Generic delta rule (gated_delta_net_f32_batched_in_place, mps_backend.mm:2225-2305):
+// one thread per state row, any head_dim.
+__global__ void gdn_generic_kernel(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                                   float* state, int T, int key_heads, int value_heads, int d, float* out) {
+  const int h = blockIdx.x, row = threadIdx.x + blockIdx.y * blockDim.x;
+  if (row >= d) return;
+  const int kh = h % key_heads;
+  const float scale = 1.0f / sqrtf(static_cast<float>(d));
+  float* s = state + (static_cast<size_t>(h) * d + row) * d;
+  for (int t = 0; t < T; ++t) {
+    const float* kk = k + (static_cast<size_t>(t) * key_heads + kh) * d;
+    const float* qq = q + (static_cast<size_t>(t) * key_heads + kh) * d;
+    const float ge = expf(g[t * value_heads + h]);
+    float sk = 0.0f;
+    for (int c = 0; c < d; ++c) {
+      s[c] *= ge;
+      sk += s[c] * kk[c];
+    }
+    const float delta = (v[(static_cast<size_t>(t) * value_heads + h) * d + row] - sk) * beta[t * value_heads + h];
+    float y = 0.0f;
+    for (int c = 0; c < d; ++c) {
+      s[c] += kk[c] * delta;
+      y += s[c] * qq[c];
+    }
+    out[(static_cast<size_t>(t) * value_heads + h) * d + row] = y * scale;
+  }
+}
+
+__global__ void mrope_kernel(float* v, const int* positions, int T, int heads, int hd, int n_dims, int s0, int s1,
+                             int s2, int s3, float theta) {
+  const int half = n_dims / 2;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= T * heads * half) return;
+  const int pi = idx % half, h = (idx / half) % heads, t = idx / (half * heads);
+  const int tot = s0 + s1 + s2 + s3;
+  if (tot == 0) return;
+  const int sector = pi % tot;
+  const int sid = sector < s0 ? 0 : (sector < s0 + s1 ? 1 : (sector < s0 + s1 + s2 ? 2 : 3));
+  const float pos = static_cast<float>(positions[t + T * sid]);
+  const float freq = 1.0f / powf(theta, static_cast<float>(2 * pi) / static_cast<float>(n_dims));
+  float sn, cs;
+  sincosf(pos * freq, &sn, &cs);
+  float* b = v + (static_cast<size_t>(t) * heads + h) * hd;
+  const float x0 = b[pi], x1 = b[half + pi];
+  b[pi] = x0 * cs - x1 * sn;
+  b[half + pi] = x1 * cs + x0 * sn;
+}
+
+// attention_f32_batched_f16_kv (mps_backend.mm:2943-3008): warp per (query, head).
+__global__ void attention_generic_kernel(const float* q, const uint16_t* kc, const uint16_t* vc, int start, int T,
+                                         int heads, int kv_heads, int hd, int round_q, float* out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * 8 + warp, h = blockIdx.y;
+  if (t >= T) return;
+  const int kvh = h / (heads / kv_heads), kvd = kv_heads * hd;
+  const int per = (hd + 31) / 32;
+  float qv[8], acc[8];
+  for (int i = 0; i < per && i < 8; ++i) {
+    const int d = lane + 32 * i;
+    const float x = d < hd ? q[(static_cast<size_t>(t) * heads + h) * hd + d] : 0.0f;
+    qv[i] = round_q ? round_to_half(x) : x;
+    acc[i] = 0.0f;
+  }
+  const float scale = 1.0f / sqrtf(static_cast<float>(hd));
+  float m = -INFINITY, l = 0.0f;
+  for (int key = 0; key <= start + t; ++key) {
+    float d0 = 0.0f;
+    for (int i = 0; i < per && i < 8; ++i) {
+      const int d = lane + 32 * i;
+      if (d < hd) d0 += qv[i] * half_bits_to_float(kc[static_cast<size_t>(key) * kvd + kvh * hd + d]);
+    }
+    const float sc = warp_sum(d0) * scale;
+    const float nm = fmaxf(m, sc), ps = expf(m - nm), w = expf(sc - nm);
+    l = l * ps + w;
+    for (int i = 0; i < per && i < 8; ++i) {
+      const int d = lane + 32 * i;
+      if (d < hd) acc[i] = acc[i] * ps + w * half_bits_to_float(vc[static_cast<size_t>(key) * kvd + kvh * hd + d]);
+    }
+    m = nm;
+  }
+  const float inv = l == 0.0f ? 0.0f : 1.0f / l;
+  for (int i = 0; i < per && i < 8; ++i) {
+    const int d = lane + 32 * i;
+    if (d < hd) out[(static_cast<size_t>(t) * heads + h) * hd + d] = acc[i] * inv;
+  }
+}
+
+__global__ void binary_kernel(int op, float* a, const float* b, size_t n, size_t row) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  switch (op) {
+    case 0: a[i] += b[i]; break;
+    case 1: a[i] *= b[i]; break;
+    case 2: a[i] += b[i % row]; break;
+    default: a[i] *= b[i % row]; break;
+  }
+}
+
+__global__ void unary_kernel(int op, float* v, size_t n) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float x = v[i];
+  v[i] = op == 0 ? sigmoid_f(x) : (op == 1 ? softplus20_f(x) : silu_k(x));
+}
+
+__global__ void silu_mul_kernel(float* g, const float* u, size_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) g[i] = silu_k(g[i]) * u[i];
+}
+
+__global__ void copy_rows_kernel(const float* src, float* dst_f, uint16_t* dst_h, size_t rows, size_t rv, size_t ss,
+                                 size_t so, size_t ds, size_t dof) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * rv) return;
+  const size_t r = i / rv, c = i % rv;
+  const float v = src[r * ss + so + c];
+  if (dst_f) dst_f[dof + r * ds + c] = v;
+  else dst_h[dof + r * ds + c] = __half_as_ushort(__float2half_rn(v));
+}
+
+__global__ void argmax_kernel(const float* v, int n, int* tok, float* prob) {
+  __shared__ float bv[256];
+  __shared__ int bi[256];
+  __shared__ float bs[256];
+  const int tid = threadIdx.x;
+  float best = -INFINITY;
+  int idx = n;
+  for (int i = tid; i < n; i += 256)
+    if (v[i] > best || (v[i] == best && i < idx)) {
+      best = v[i];
+      idx = i;
+    }
+  bv[tid] = best;
+  bi[tid] = idx;
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if (tid < s) {
+      if (bv[tid + s] > bv[tid] || (bv[tid + s] == bv[tid] && bi[tid + s] < bi[tid])) {
+        bv[tid] = bv[tid + s];
+        bi[tid] = bi[tid + s];
+      }
+    }
+    __syncthreads();
+  }
+  const float mx = bv[0];
+  float sum = 0.0f;
+  for (int i = tid; i < n; i += 256) sum += expf(v[i] - mx);
+  bs[tid] = sum;
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if (tid < s) bs[tid] += bs[tid + s];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    *tok = bi[0];
+    if (prob) *prob = bs[0] > 0.0f ? 1.0f / bs[0] : 0.0f;
+  }
+}
+
+unsigned blocks_for(size_t n, unsigned t = 256) { return static_cast<unsigned>((n + t - 1) / t); }
+
+bool kquant_type_ok(int type) { return type == kTypeQ4K || type == kTypeQ5K || type == kTypeQ6K; }
+
+}  // namespace
+
+// ============================================================ GEMV planner
+namespace kib {
+
+template <int QT, int NT, bool F16W>
+static cudaError_t gemv_instance(const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kquant_gemv_kernel<QT, NT, F16W>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  return launch_pdl(kquant_gemv_kernel<QT, NT, F16W>, dim3(grid), dim3(kGemvThreads), smem, st, p);
+}
+
+template <int QT>
+static cudaError_t gemv_dispatch(const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
+  switch (p.ntok) {
+    case 1: return gemv_instance<QT, 1, false>(p, grid, smem, st);
+    case 2: return gemv_instance<QT, 2, false>(p, grid, smem, st);
+    case 3: return gemv_instance<QT, 3, false>(p, grid, smem, st);
+    default: return gemv_instance<QT, 8, true>(p, grid, smem, st);
+  }
+}
+
+cudaError_t gemv_launch(const GemvDesc& d, int num_sms, cudaStream_t st, std::string* why) {
+  if (!kquant_type_ok(d.type) || d.cols <= 0 || d.cols % 256 || d.cols > 16384 || d.ntok < 1 ||
+      d.ntok > kGemvMaxTok || d.nseg < 1 || d.nseg > kGemvMaxSegs) {
+    if (why) *why = "GEMV: unsupported type/cols/tokens/segments";
+    return cudaErrorInvalidValue;
+  }
+  GemvParams p = {};
+  const int BB = kquant_block_bytes(d.type);
+  p.cols = d.cols;
+  p.row_bytes = d.cols / 256 * BB;
+  const int units = d.cols / 64;
+  p.rg = units <= 16 ? 16 : (units <= 32 ? 32 : (units <= 64 ? 64 : (units <= 128 ? 128 : 256)));
+  const int groups = kGemvThreads / p.rg;
+  const int m = groups > 8 ? groups : 8;
+  bool paired = false;
+  int total_rows = 0;
+  for (int i = 0; i < d.nseg; ++i) {
+    total_rows += d.seg[i].rows;
+    paired = paired || d.seg[i].epilogue == kEpiSiluMul;
+  }
+  const int mult = paired ? 2 : 1;
+  const int max_stage = 32 * 1024;
+  int tr_max = (max_stage / (p.row_bytes * mult)) / m * m;
+  if (tr_max < m) tr_max = m;
+  int target = (total_rows + num_sms - 1) / num_sms;
+  target = (target + m - 1) / m * m;
+  const int tr = target < tr_max ? target : tr_max;
+  p.tile_rows = tr;
+  int tiles = 0;
+  for (int i = 0; i < d.nseg; ++i) {
+    p.seg[i].w = static_cast<const uint8_t*>(d.seg[i].w);
+    p.seg[i].w2 = static_cast<const uint8_t*>(d.seg[i].w2);
+    p.seg[i].out = d.seg[i].out;
+    p.seg[i].rows = d.seg[i].rows;
+    p.seg[i].ld = d.seg[i].ld;
+    p.seg[i].epilogue = d.seg[i].epilogue;
+    p.seg[i].tile_begin = tiles;
+    tiles += (d.seg[i].rows + tr - 1) / tr;
+  }
+  p.nseg = d.nseg;
+  p.total_tiles = tiles;
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  const int half = ((tr * p.row_bytes) + 15) & ~15;
+  p.stage_bytes = half * mult;
+  const int per_cta = (tiles + grid - 1) / grid;
+  int S = (96 * 1024) / p.stage_bytes;
+  if (S < 1) S = 1;
+  if (S > per_cta) S = per_cta;
+  if (S > 8) S = 8;
+  const size_t xs_bytes = static_cast<size_t>(d.ntok) * d.cols * sizeof(float);
+  while (S > 1 && static_cast<size_t>(S) * p.stage_bytes + xs_bytes > 190 * 1024) --S;
+  if (static_cast<size_t>(S) * p.stage_bytes + xs_bytes > 200 * 1024) {
+    if (why) *why = "GEMV: shared memory plan exceeds 200 KB";
+    return cudaErrorInvalidValue;
+  }
+  p.stages = S;
+  p.ntok = d.ntok;
+  p.prologue = d.prologue;
+  p.paired = paired ? 1 : 0;
+  p.argmax = d.argmax ? 1 : 0;
+  p.in = d.in;
+  p.in_ld = d.in_ld;
+  p.norm_w = d.norm_w;
+  p.eps = d.eps;
+  p.gate = d.gate;
+  p.head_dim = d.head_dim;
+  p.resid = d.resid;
+  p.conv_state = d.conv_state;
+  p.conv_w = d.conv_w;
+  p.conv_k = d.conv_k;
+  p.cand_max = d.cand_max;
+  p.cand_sum = d.cand_sum;
+  p.cand_idx = d.cand_idx;
+  p.counter = d.counter;
+  p.token_out = d.token_out;
+  p.prob_out = d.prob_out;
+  p.token_log = d.token_log;
+  p.step_counter = d.step_counter;
+  p.pos_advance = d.pos_advance;
+  p.x_out = d.x_out;
+  p.err = d.err;
+  const size_t smem = static_cast<size_t>(S) * p.stage_bytes + xs_bytes;
+  switch (d.type) {
+    case kTypeQ4K: return gemv_dispatch<kTypeQ4K>(p, grid, smem, st);
+    case kTypeQ5K: return gemv_dispatch<kTypeQ5K>(p, grid, smem, st);
+    default: return gemv_dispatch<kTypeQ6K>(p, grid, smem, st);
+  }
+}
+
+// M > 8: half-precision GEMM path.
+cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const float* x, int x_ld, int T, float* y,
+                            int y_ld, const float* resid, cudaStream_t st) {
+  GemmParams p;
+  p.w = static_cast<const uint8_t*>(w);
+  p.rows = rows;
+  p.cols = cols;
+  p.x = x;
+  p.x_ld = x_ld;
+  p.T = T;
+  p.y = y;
+  p.y_ld = y_ld;
+  p.resid = resid;
+  const size_t smem = 2 * 256 * 64 * sizeof(float);
+  dim3 grid((rows + 63) / 64, (T + 63) / 64);
+  static bool cfg[3] = {false, false, false};
+  switch (type) {
+    case kTypeQ4K:
+      if (!cfg[0]) { cudaFuncSetAttribute(kquant_gemm_f16_kernel<kTypeQ4K>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); cfg[0] = true; }
+      return launch_pdl(kquant_gemm_f16_kernel<kTypeQ4K>, grid, dim3(256), smem, st, p);
+    case kTypeQ5K:
+      if (!cfg[1]) { cudaFuncSetAttribute(kquant_gemm_f16_kernel<kTypeQ5K>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); cfg[1] = true; }
+      return launch_pdl(kquant_gemm_f16_kernel<kTypeQ5K>, grid, dim3(256), smem, st, p);
+    default:
+      if (!cfg[2]) { cudaFuncSetAttribute(kquant_gemm_f16_kernel<kTypeQ6K>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); cfg[2] = true; }
+      return launch_pdl(kquant_gemm_f16_kernel<kTypeQ6K>, grid, dim3(256), smem, st, p);
+  }
+}
+
+cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const int* ids, int T, float* out,
+                            int out_ld, cudaStream_t st) {
+  const uint8_t* wb = static_cast<const uint8_t*>(w);
+  switch (type) {
+    case kTypeQ4K: return launch_pdl(get_rows_kernel<kTypeQ4K>, dim3(T), dim3(64), 0, st, wb, nrows, cols, ids, out, out_ld);
+    case kTypeQ5K: return launch_pdl(get_rows_kernel<kTypeQ5K>, dim3(T), dim3(64), 0, st, wb, nrows, cols, ids, out, out_ld);
+    default: return launch_pdl(get_rows_kernel<kTypeQ6K>, dim3(T), dim3(64), 0, st, wb, nrows, cols, ids, out, out_ld);
+  }
+}
+
+cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st) {
+  return launch_pdl(rms_norm_rows_kernel, dim3(T), dim3(256), 0, st, in, w, n, eps, out);
+}
+
+cudaError_t norm_gate_launch(float* v, const float* w, const float* gate, int T, int heads, int d, float eps, float* out,
+                             cudaStream_t st) {
+  return launch_pdl(head_norm_kernel, dim3(heads, T), dim3(32), 0, st, v, w, gate, heads, d, eps, out);
+}
+
+cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w, int K, int C, int T, float* out,
+                        int out_ld, int silu, cudaStream_t st) {
+  return launch_pdl(conv_stateful_kernel, dim3(blocks_for(C, 128)), dim3(128), 0, st, state, in, in_ld, w, K, C, T,
+                    out, out_ld, silu);
+}
+
+cudaError_t silu_mul_launch(float* g, const float* u, size_t n, cudaStream_t st) {
+  return launch_pdl(silu_mul_kernel, dim3(blocks_for(n)), dim3(256), 0, st, g, u, n);
+}
+
+int finish_op(kib_ctx* ctx, const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return check_cuda(ctx, e, what);
+  if (ctx->in_graph) return KIB_OK;
+  e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, what);
+  int err = 0;
+  cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (err != 0) {
+    cudaMemset(ctx->d_err, 0, sizeof(int));
+    return set_error(ctx, KIB_ERR_TIMEOUT, std::string(what) + ": a bounded device wait gave up");
+  }
+  return KIB_OK;
+}
+
+}  // namespace kib
+
+// =============================================================== C ABI
+#define KIB_REQUIRE_CTX(ctx)                       \
+  do {                                             \
+    if (!(ctx) || !(ctx)->stream) return KIB_ERR_UNAVAILABLE; \
+  } while (0)
+#define KIB_ARG(cond, msg)                                              \
+  do {                                                                  \
+    if (!(cond)) return set_error(ctx, KIB_ERR_INVALID_ARGUMENT, msg);  \
+  } while (0)
+
+extern "C" {
+
+int kib_create(int device, kib_ctx** out) {
+  if (!out) return KIB_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= device || device < 0) return KIB_ERR_UNAVAILABLE;
+  auto* ctx = new kib_ctx;
+  ctx->device = device;
+  cudaSetDevice(device);
+  cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (major < 10) {
+    delete ctx;
+    return KIB_ERR_UNAVAILABLE;
+  }
+  if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess ||
+      cudaMalloc(&ctx->d_cand_max, sizeof(float) * 1024 * kGemvMaxTok) != cudaSuccess ||
+      cudaMalloc(&ctx->d_cand_sum, sizeof(float) * 1024 * kGemvMaxTok) != cudaSuccess ||
+      cudaMalloc(&ctx->d_cand_idx, sizeof(int) * 1024 * kGemvMaxTok) != cudaSuccess ||
+      cudaMalloc(&ctx->d_counter, sizeof(unsigned)) != cudaSuccess) {
+    kib_destroy(ctx);
+    return KIB_ERR_INTERNAL;
+  }
+  cudaMemset(ctx->d_err, 0, sizeof(int));
+  cudaMemset(ctx->d_counter, 0, sizeof(unsigned));
+  *out = ctx;
+  return KIB_OK;
+}
+
+void kib_destroy(kib_ctx* ctx) {
+  if (!ctx) return;
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  cudaFree(ctx->d_err);
+  cudaFree(ctx->d_cand_max);
+  cudaFree(ctx->d_cand_sum);
+  cudaFree(ctx->d_cand_idx);
+  cudaFree(ctx->d_counter);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+int kib_valid(const kib_ctx* ctx) { return ctx && ctx->stream ? 1 : 0; }
+const char* kib_last_error(const kib_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "no context"; }
+void* kib_stream(kib_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int kib_begin_graph(kib_ctx* ctx) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(!ctx->in_graph, "graph scope already open");
+  ctx->in_graph = true;
+  return KIB_OK;
+}
+int kib_commit_graph(kib_ctx* ctx) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(ctx->in_graph, "no graph scope is open");
+  ctx->in_graph = false;
+  return finish_op(ctx, "commit_graph");
+}
+int kib_abort_graph(kib_ctx* ctx) {
+  KIB_REQUIRE_CTX(ctx);
+  ctx->in_graph = false;
+  cudaStreamSynchronize(ctx->stream);
+  return KIB_OK;
+}
+
+int kib_make_buffer(kib_ctx* ctx, uint64_t bytes, void** dev_out) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(dev_out && bytes > 0, "make_buffer: size must be positive");
+  // 256 bytes of tail padding: bulk weight copies round their size up to 16.
+  return check_cuda(ctx, cudaMalloc(dev_out, bytes + 256), "make_buffer");
+}
+int kib_free_buffer(kib_ctx* ctx, void* dev) {
+  KIB_REQUIRE_CTX(ctx);
+  cudaStreamSynchronize(ctx->stream);
+  return check_cuda(ctx, cudaFree(dev), "free_buffer");
+}
+int kib_copy_to_buffer(kib_ctx* ctx, void* dst, uint64_t off, const void* src, uint64_t bytes) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(dst && src, "copy_to_buffer: null pointer");
+  cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "copy_to_buffer");
+  return finish_op(ctx, "copy_to_buffer");
+}
+int kib_copy_from_buffer(kib_ctx* ctx, const void* src, uint64_t off, void* dst, uint64_t bytes) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(dst && src, "copy_from_buffer: null pointer");
+  cudaError_t e =
+      cudaMemcpyAsync(dst, static_cast<const uint8_t*>(src) + off, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "copy_from_buffer");
+  return check_cuda(ctx, cudaStreamSynchronize(ctx->stream), "copy_from_buffer");
+}
+int kib_copy_buffer_region(kib_ctx* ctx, const void* src, void* dst, uint64_t so, uint64_t dof, uint64_t bytes) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(dst && src, "copy_buffer_region: null pointer");
+  cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(dst) + dof, static_cast<const uint8_t*>(src) + so, bytes,
+                                  cudaMemcpyDeviceToDevice, ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "copy_buffer_region");
+  return finish_op(ctx, "copy_buffer_region");
+}
+int kib_zero_buffer(kib_ctx* ctx, void* dev, uint64_t bytes) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(dev, "zero_buffer: null pointer");
+  cudaError_t e = cudaMemsetAsync(dev, 0, bytes, ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "zero_buffer");
+  return finish_op(ctx, "zero_buffer");
+}
+
+// ---- K-quant
+static int kquant_shape_check(kib_ctx* ctx, int type, const void* w, uint64_t rows, uint64_t cols, uint64_t tokens) {
+  KIB_ARG(kquant_type_ok(type), "K-quant op: type must be Q4_K(12), Q5_K(13) or Q6_K(14)");
+  KIB_ARG(w, "K-quant op: weight buffer is not initialized");
+  KIB_ARG(rows > 0 && cols > 0 && tokens > 0, "K-quant op: dimensions must be positive");
+  KIB_ARG(cols % 256 == 0, "K-quant op: cols must be a multiple of 256");
+  KIB_ARG(rows < (1ull << 31) && cols <= 16384 && tokens < (1ull << 31), "K-quant op: dimensions exceed limits");
+  return KIB_OK;
+}
+
+int kib_matmul_kquant_f32(kib_ctx* ctx, int type, const void* w, uint64_t rows, uint64_t cols, uint64_t tokens,
+                          const float* input, float* output) {
+  KIB_REQUIRE_CTX(ctx);
+  int st = kquant_shape_check(ctx, type, w, rows, cols, tokens);
+  if (st) return st;
+  KIB_ARG(input && output, "K-quant matmul: null input/output");
+  cudaError_t e;
+  if (tokens <= 8) {
+    GemvDesc d;
+    d.type = type;
+    d.cols = static_cast<int>(cols);
+    d.ntok = static_cast<int>(tokens);
+    d.nseg = 1;
+    d.seg[0].w = w;
+    d.seg[0].out = output;
+    d.seg[0].rows = static_cast<int>(rows);
+    d.seg[0].ld = static_cast<int>(rows);
+    d.in = input;
+    d.in_ld = static_cast<int>(cols);
+    d.err = ctx->d_err;
+    std::string why;
+    e = gemv_launch(d, ctx->num_sms, ctx->stream, &why);
+    if (e != cudaSuccess) return set_error(ctx, KIB_ERR_INTERNAL, "matmul: " + why + " " + cudaGetErrorString(e));
+  } else {
+    e = gemm_f16_launch(type, w, static_cast<int>(rows), static_cast<int>(cols), input, static_cast<int>(cols),
+                        static_cast<int>(tokens), output, static_cast<int>(rows), nullptr, ctx->stream);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "matmul");
+  }
+  return finish_op(ctx, "matmul_kquant");
+}
+
+int kib_matvec_kquant_f32(kib_ctx* ctx, int type, const void* w, uint64_t rows, uint64_t cols, const float* in,
+                          float* out) {
+  return kib_matmul_kquant_f32(ctx, type, w, rows, cols, 1, in, out);
+}
+
+int kib_matvec_kquant_f32_argmax(kib_ctx* ctx, int type, const void* w, uint64_t rows, uint64_t cols,
+                                 const float* input, int32_t* token_out, float* prob_out) {
+  KIB_REQUIRE_CTX(ctx);
+  int st = kquant_shape_check(ctx, type, w, rows, cols, 1);
+  if (st) return st;
+  KIB_ARG(input && token_out, "K-quant argmax: null input/output");
+  GemvDesc d;
+  d.type = type;
+  d.cols = static_cast<int>(cols);
+  d.ntok = 1;
+  d.nseg = 1;
+  d.seg[0].w = w;
+  d.seg[0].out = nullptr;
+  d.seg[0].rows = static_cast<int>(rows);
+  d.seg[0].ld = static_cast<int>(rows);
+  d.seg[0].epilogue = kEpiArgmax;
+  d.in = input;
+  d.in_ld = static_cast<int>(cols);
+  d.argmax = true;
+  d.cand_max = ctx->d_cand_max;
+  d.cand_sum = ctx->d_cand_sum;
+  d.cand_idx = ctx->d_cand_idx;
+  d.counter = ctx->d_counter;
+  d.token_out = token_out;
+  d.prob_out = prob_out;
+  d.err = ctx->d_err;
+  std::string why;
+  cudaError_t e = gemv_launch(d, ctx->num_sms, ctx->stream, &why);
+  if (e != cudaSuccess) return set_error(ctx, KIB_ERR_INTERNAL, "argmax: " + why + " " + cudaGetErrorString(e));
+  return finish_op(ctx, "matvec_argmax");
+}
+
+int kib_dequantize_rows_kquant_f32(kib_ctx* ctx, int type, const void* w, uint64_t rows, const int32_t* ids,
+                                   uint64_t count, uint64_t cols, float* out) {
+  KIB_REQUIRE_CTX(ctx);
+  int st = kquant_shape_check(ctx, type, w, rows, cols, count);
+  if (st) return st;
+  KIB_ARG(ids && out, "dequantize_rows: null ids/output");
+  cudaError_t e = get_rows_launch(type, w, static_cast<int>(rows), static_cast<int>(cols), ids,
+                                  static_cast<int>(count), out, static_cast<int>(cols), ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "dequantize_rows");
+  return finish_op(ctx, "dequantize_rows");
+}
+
+#define KIB_NAMED(q, T)                                                                                     \
+  int kib_matvec_##q##_f32_device(kib_ctx* ctx, const void* w, uint64_t r, uint64_t c, const float* i,      \
+                                  float* o) {                                                              \
+    return kib_matvec_kquant_f32(ctx, T, w, r, c, i, o);                                                    \
+  }                                                                                                         \
+  int kib_matmul_##q##_f32_device(kib_ctx* ctx, const void* w, uint64_t r, uint64_t c, uint64_t t,          \
+                                  const float* i, float* o) {                                              \
+    return kib_matmul_kquant_f32(ctx, T, w, r, c, t, i, o);                                                 \
+  }
+KIB_NAMED(q4_k, 12)
+KIB_NAMED(q5_k, 13)
+KIB_NAMED(q6_k, 14)
+
+// ---- norms
+int kib_rms_norm_f32_f32_batched(kib_ctx* ctx, const float* in, const float* w, uint64_t tokens, uint64_t size,
+                                 float eps, float* out) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(in && w && out && tokens > 0 && size > 0, "rms_norm: invalid arguments");
+  cudaError_t e = rms_rows_launch(in, w, static_cast<int>(tokens), static_cast<int>(size), eps, out, ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "rms_norm");
+  return finish_op(ctx, "rms_norm");
+}
+int kib_qk_norm_f32_f32_batched(kib_ctx* ctx, float* v, const float* w, uint64_t tokens, uint64_t heads,
+                                uint64_t hd, float eps) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(v && w && tokens && heads && hd, "qk_norm: invalid arguments");
+  cudaError_t e = norm_gate_launch(v, w, nullptr, static_cast<int>(tokens), static_cast<int>(heads),
+                                   static_cast<int>(hd), eps, nullptr, ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "qk_norm");
+  return finish_op(ctx, "qk_norm");
+}
+int kib_qwen35_norm_gated_f32_in_place(kib_ctx* ctx, float* v, const float* w, const float* gate, uint64_t tokens,
+                                       uint64_t heads, uint64_t hd, float eps) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(v && w && gate && tokens && heads && hd, "norm_gated: invalid arguments");
+  cudaError_t e = norm_gate_launch(v, w, gate, static_cast<int>(tokens), static_cast<int>(heads),
+                                   static_cast<int>(hd), eps, nullptr, ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "norm_gated");
+  return finish_op(ctx, "norm_gated");
+}
+int kib_split_qkv_l2_norm_f32_qwen35(kib_ctx* ctx, const float* src, float* q, float* k, float* v, uint64_t tokens,
+                                     uint64_t kh, uint64_t vh, uint64_t hd, float eps) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(src && q && k && v && tokens && kh && vh && hd, "split_qkv_l2_norm: invalid arguments");
+  const unsigned hmax = static_cast<unsigned>(kh > vh ? kh : vh);
+  split_qkv_l2_kernel<<<dim3(hmax, static_cast<unsigned>(tokens), 3), 32, 0, ctx->stream>>>(
+      src, q, k, v, static_cast<int>(kh), static_cast<int>(vh), static_cast<int>(hd), eps);
+  return finish_op(ctx, "split_qkv_l2_norm");
+}
+
+// ---- GDN pieces
+int kib_ssm_conv_f32_stateful(kib_ctx* ctx, float* state, const float* in, const float* w, uint64_t K, uint64_t C,
+                              uint64_t T, float* out) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(state && in && w && out && K >= 2 && K <= 16 && C && T, "ssm_conv: invalid arguments");
+  cudaError_t e = conv_launch(state, in, static_cast<int>(C), w, static_cast<int>(K), static_cast<int>(C),
+                              static_cast<int>(T), out, static_cast<int>(C), 0, ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "ssm_conv");
+  return finish_op(ctx, "ssm_conv");
+}
+int kib_prepare_qwen35_gdn_gate_beta_f32(kib_ctx* ctx, float* gate, float* beta, const float* bias,
+                                         const float* scale, uint64_t tokens, uint64_t heads) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(gate && beta && bias && scale && tokens && heads, "prepare_gate_beta: invalid arguments");
+  const size_t n = tokens * heads;
+  prepare_gate_beta_kernel<<<blocks_for(n), 256, 0, ctx->stream>>>(gate, beta, bias, scale, static_cast<int>(n),
+                                                                    static_cast<int>(heads));
+  return finish_op(ctx, "prepare_gate_beta");
+}
+int kib_gated_delta_net_f32_batched_in_place(kib_ctx* ctx, const float* q, const float* k, const float* v,
+                                             const float* g, const float* beta, float* state, uint64_t tokens,
+                                             uint64_t kh, uint64_t vh, uint64_t hd, float* out) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(q && k && v && g && beta && state && out && tokens && kh && vh && hd, "gated_delta_net: invalid arguments");
+  KIB_ARG(vh % kh == 0, "gated_delta_net: value heads must be a multiple of key heads");
+  const unsigned th = static_cast<unsigned>(hd < 256 ? hd : 256);
+  gdn_generic_kernel<<<dim3(static_cast<unsigned>(vh), static_cast<unsigned>((hd + th - 1) / th)), th, 0,
+                       ctx->stream>>>(q, k, v, g, beta, state, static_cast<int>(tokens), static_cast<int>(kh),
+                                      static_cast<int>(vh), static_cast<int>(hd), out);
+  return finish_op(ctx, "gated_delta_net");
+}
+
+// ---- attention
+int kib_mrope_f32_in_place(kib_ctx* ctx, float* v, const int32_t* pos, uint64_t T, uint64_t heads, uint64_t hd,
+                           uint64_t n_dims, uint64_t s0, uint64_t s1, uint64_t s2, uint64_t s3, float theta) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(v && pos && T && heads && hd && n_dims && n_dims <= hd && n_dims % 2 == 0, "mrope: invalid arguments");
+  const size_t n = T * heads * (n_dims / 2);
+  mrope_kernel<<<blocks_for(n), 256, 0, ctx->stream>>>(v, pos, static_cast<int>(T), static_cast<int>(heads),
+                                                       static_cast<int>(hd), static_cast<int>(n_dims),
+                                                       static_cast<int>(s0), static_cast<int>(s1),
+                                                       static_cast<int>(s2), static_cast<int>(s3), theta);
+  return finish_op(ctx, "mrope");
+}
+int kib_attention_f32_batched_f16_kv(kib_ctx* ctx, const float* q, const uint16_t* kc, const uint16_t* vc,
+                                     uint64_t layer, uint64_t start, uint64_t T, uint64_t cap, uint64_t heads,
+                                     uint64_t kvh, uint64_t hd, float* out) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(q && kc && vc && out && T && heads && kvh && hd && heads % kvh == 0 && hd <= 256,
+          "attention: invalid arguments");
+  KIB_ARG(start + T <= cap, "attention: positions exceed cache capacity");
+  const size_t off = layer * cap * kvh * hd;
+  const int round_q = (T >= 64 && hd == 256) ? 1 : 0;
+  attention_generic_kernel<<<dim3(static_cast<unsigned>((T + 7) / 8), static_cast<unsigned>(heads)), 256, 0,
+                             ctx->stream>>>(q, kc + off, vc + off, static_cast<int>(start), static_cast<int>(T),
+                                            static_cast<int>(heads), static_cast<int>(kvh), static_cast<int>(hd),
+                                            round_q, out);
+  return finish_op(ctx, "attention");
+}
+
+// ---- element-wise
+int kib_binary_f32_in_place(kib_ctx* ctx, int op, float* a, const float* b, uint64_t total, uint64_t row) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(a && b && total && op >= 0 && op <= 3 && (op < 2 || (row > 0 && total % row == 0)),
+          "binary op: invalid arguments");
+  binary_kernel<<<blocks_for(total), 256, 0, ctx->stream>>>(op, a, b, total, row ? row : 1);
+  return finish_op(ctx, "binary");
+}
+int kib_unary_f32_in_place(kib_ctx* ctx, int op, float* v, uint64_t n) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(v && n && op >= 0 && op <= 2, "unary op: invalid arguments");
+  unary_kernel<<<blocks_for(n), 256, 0, ctx->stream>>>(op, v, n);
+  return finish_op(ctx, "unary");
+}
+int kib_silu_mul_f32_in_place(kib_ctx* ctx, float* g, const float* u, uint64_t n) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(g && u && n, "silu_mul: invalid arguments");
+  cudaError_t e = silu_mul_launch(g, u, n, ctx->stream);
+  if (e != cudaSuccess) return check_cuda(ctx, e, "silu_mul");
+  return finish_op(ctx, "silu_mul");
+}
+int kib_copy_f32_rows(kib_ctx* ctx, const float* src, float* dst, uint64_t rows, uint64_t rv, uint64_t ss,
+                      uint64_t so, uint64_t ds, uint64_t dof) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(src && dst && rows && rv && rv + so <= ss && rv <= ds, "copy_f32_rows: invalid arguments");
+  copy_rows_kernel<<<blocks_for(rows * rv), 256, 0, ctx->stream>>>(src, dst, nullptr, rows, rv, ss, so, ds, dof);
+  return finish_op(ctx, "copy_f32_rows");
+}
+int kib_copy_f32_rows_to_f16(kib_ctx* ctx, const float* src, uint16_t* dst, uint64_t rows, uint64_t rv, uint64_t ss,
+                             uint64_t so, uint64_t ds, uint64_t dof) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(src && dst && rows && rv && rv + so <= ss && rv <= ds, "copy_f32_rows_to_f16: invalid arguments");
+  copy_rows_kernel<<<blocks_for(rows * rv), 256, 0, ctx->stream>>>(src, nullptr, dst, rows, rv, ss, so, ds, dof);
+  return finish_op(ctx, "copy_f32_rows_to_f16");
+}
+int kib_argmax_f32_i32(kib_ctx* ctx, const float* v, uint64_t n, int32_t* tok, float* prob) {
+  KIB_REQUIRE_CTX(ctx);
+  KIB_ARG(v && tok && n > 0 && n < (1ull << 31), "argmax: invalid arguments");
+  argmax_kernel<<<1, 256, 0, ctx->stream>>>(v, static_cast<int>(n), tok, prob);
+  return finish_op(ctx, "argmax");
+}
+
+}  // extern "C"

@@ -1,0 +1,379 @@
+"""kib -- Python binding of the B200 backend's C ABI (include/kib.h).
+
+A thin ctypes layer over kraken-infer_b200/lib/libkib.so, mirroring the
+reference's backend seam toyllm::mps::MpsContext (op level) and its Qwen3.5
+runtime entry points (generate_qwen35_metal and friends).  Device buffers are
+passed as raw pointers; torch tensors are accepted for convenience (their
+data_ptr() is passed, no torch types cross the ABI).
+
+Loading fails loudly: there is no CPU fallback.  On a machine without a
+B200, kib_create() returns KIB_ERR_UNAVAILABLE.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, byref, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_uint16, c_uint32, c_uint64, c_void_p
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libkib.so")
+HEADER_PATH = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "include", "kib.h")
+
+KIB_OK = 0
+KIB_ERR_INVALID_ARGUMENT = 1
+KIB_ERR_UNAVAILABLE = 2
+KIB_ERR_INTERNAL = 3
+KIB_ERR_TIMEOUT = 4
+
+Q4_K, Q5_K, Q6_K = 12, 13, 14
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
+
+
+class KibError(RuntimeError):
+    def __init__(self, code, message):
+        super().__init__(f"kib error {code}: {message}")
+        self.code = code
+
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Loads libkib.so (built by kraken-infer_b200/build.py); raises if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise KibError(KIB_ERR_UNAVAILABLE, f"{path} is missing: run kraken-infer_b200/build.py")
+    lib = ctypes.CDLL(path)
+    _declare(lib)
+    _lib = lib
+    return lib
+
+
+class Qwen35Options(ctypes.Structure):
+    _fields_ = [("context_tokens", c_uint64), ("decode_tokens", c_uint64), ("prefill_chunk_tokens", c_uint64),
+                ("sequence_slots", c_uint64), ("kv_cache_f16", c_int), ("enable_mtp", c_int)]
+
+
+class Qwen35Plan(ctypes.Structure):
+    _fields_ = [(n, c_uint64) for n in (
+        "hidden_size", "main_layers", "total_layers", "head_dim", "attention_heads", "kv_heads",
+        "linear_key_heads", "linear_value_heads", "linear_key_head_dim", "linear_value_head_dim",
+        "linear_inner_size", "linear_conv_kernel", "linear_conv_channels", "intermediate_size", "vocab_size",
+        "attention_capacity_tokens", "full_attention_layers", "linear_attention_layers", "kv_dim",
+        "recurrent_r_elements_per_layer", "recurrent_s_elements_per_layer", "kv_cache_bytes",
+        "recurrent_r_cache_bytes", "recurrent_s_cache_bytes", "total_cache_bytes", "weight_bytes")] + [
+        ("mtp_layers", c_int), ("layer_kinds", c_int * 64)]
+
+
+class MtpReport(ctypes.Structure):
+    _fields_ = [("available", c_int), ("enabled", c_int), ("draft_tokens", c_uint64), ("p_min", c_double),
+                ("drafted_tokens", c_uint64), ("accepted_tokens", c_uint64), ("verify_steps", c_uint64),
+                ("confidence_stops", c_uint64), ("adaptive_budget", c_uint64), ("adaptive_changes", c_uint64),
+                ("verified_by_position", c_uint64 * 8), ("accepted_by_position", c_uint64 * 8)]
+
+
+class GenerationRequest(ctypes.Structure):
+    _fields_ = [("prompt_tokens", POINTER(c_int32)), ("prompt_count", c_uint64), ("max_new_tokens", c_uint64),
+                ("prefill_chunk_tokens", c_uint64), ("enable_mtp", c_int), ("mtp_draft_tokens", c_uint64),
+                ("mtp_p_min", c_double), ("mtp_adaptive", c_int), ("ignore_eos", c_int),
+                ("eos_token_id", c_uint64)]
+
+
+class GenerationResult(ctypes.Structure):
+    _fields_ = [("prompt_tokens", c_uint64), ("generated_tokens", c_uint64), ("finish_reason_stop", c_int),
+                ("mtp", MtpReport), ("kv_used_tokens", c_uint64), ("prefill_ms", c_double), ("decode_ms", c_double)]
+
+
+class SynthConfig(ctypes.Structure):
+    _fields_ = [(n, c_uint64) for n in (
+        "hidden", "layers", "intermediate", "vocab", "heads", "kv_heads", "head_dim", "ssm_heads", "ssm_head_dim",
+        "conv_kernel", "full_attention_interval", "nextn_layers")] + [
+        ("proj_type", c_uint32), ("down_type", c_uint32), ("embd_type", c_uint32), ("seed", c_uint64),
+        ("rope_theta", c_double), ("rms_eps", c_double), ("eos_token_id", c_int64), ("threads", c_int)]
+
+
+_U64 = c_uint64
+_P = c_void_p
+
+
+def _declare(lib):
+    sig = {
+        "kib_create": (c_int, [c_int, POINTER(c_void_p)]),
+        "kib_destroy": (None, [_P]),
+        "kib_valid": (c_int, [_P]),
+        "kib_last_error": (c_char_p, [_P]),
+        "kib_begin_graph": (c_int, [_P]),
+        "kib_commit_graph": (c_int, [_P]),
+        "kib_abort_graph": (c_int, [_P]),
+        "kib_stream": (c_void_p, [_P]),
+        "kib_make_buffer": (c_int, [_P, _U64, POINTER(c_void_p)]),
+        "kib_free_buffer": (c_int, [_P, _P]),
+        "kib_copy_to_buffer": (c_int, [_P, _P, _U64, _P, _U64]),
+        "kib_copy_from_buffer": (c_int, [_P, _P, _U64, _P, _U64]),
+        "kib_copy_buffer_region": (c_int, [_P, _P, _P, _U64, _U64, _U64]),
+        "kib_zero_buffer": (c_int, [_P, _P, _U64]),
+        "kib_matvec_kquant_f32": (c_int, [_P, c_int, _P, _U64, _U64, _P, _P]),
+        "kib_matmul_kquant_f32": (c_int, [_P, c_int, _P, _U64, _U64, _U64, _P, _P]),
+        "kib_matvec_kquant_f32_argmax": (c_int, [_P, c_int, _P, _U64, _U64, _P, _P, _P]),
+        "kib_dequantize_rows_kquant_f32": (c_int, [_P, c_int, _P, _U64, _P, _U64, _U64, _P]),
+        "kib_rms_norm_f32_f32_batched": (c_int, [_P, _P, _P, _U64, _U64, c_float, _P]),
+        "kib_qk_norm_f32_f32_batched": (c_int, [_P, _P, _P, _U64, _U64, _U64, c_float]),
+        "kib_qwen35_norm_gated_f32_in_place": (c_int, [_P, _P, _P, _P, _U64, _U64, _U64, c_float]),
+        "kib_split_qkv_l2_norm_f32_qwen35": (c_int, [_P, _P, _P, _P, _P, _U64, _U64, _U64, _U64, c_float]),
+        "kib_ssm_conv_f32_stateful": (c_int, [_P, _P, _P, _P, _U64, _U64, _U64, _P]),
+        "kib_prepare_qwen35_gdn_gate_beta_f32": (c_int, [_P, _P, _P, _P, _P, _U64, _U64]),
+        "kib_gated_delta_net_f32_batched_in_place": (c_int, [_P, _P, _P, _P, _P, _P, _P, _U64, _U64, _U64, _U64, _P]),
+        "kib_mrope_f32_in_place": (c_int, [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _U64, _U64, _U64, c_float]),
+        "kib_attention_f32_batched_f16_kv": (c_int, [_P, _P, _P, _P, _U64, _U64, _U64, _U64, _U64, _U64, _U64, _P]),
+        "kib_binary_f32_in_place": (c_int, [_P, c_int, _P, _P, _U64, _U64]),
+        "kib_unary_f32_in_place": (c_int, [_P, c_int, _P, _U64]),
+        "kib_silu_mul_f32_in_place": (c_int, [_P, _P, _P, _U64]),
+        "kib_copy_f32_rows": (c_int, [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _U64]),
+        "kib_copy_f32_rows_to_f16": (c_int, [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _U64]),
+        "kib_argmax_f32_i32": (c_int, [_P, _P, _U64, _P, _P]),
+        "kib_qwen35_load": (c_int, [_P, c_char_p, POINTER(Qwen35Options), POINTER(c_void_p)]),
+        "kib_qwen35_free": (None, [_P]),
+        "kib_qwen35_get_plan": (c_int, [_P, POINTER(Qwen35Plan)]),
+        "kib_generate_qwen35": (c_int, [_P, POINTER(GenerationRequest), _P, _U64, POINTER(GenerationResult)]),
+        "kib_qwen35_reset": (c_int, [_P]),
+        "kib_qwen35_prefill": (c_int, [_P, _P, _U64, _U64, _P]),
+        "kib_qwen35_forward": (c_int, [_P, _P, _U64, c_int, _P, _P, _P]),
+        "kib_qwen35_decode_greedy": (c_int, [_P, c_int32, _U64, _P]),
+        "kib_qwen35_position": (c_uint64, [_P]),
+        "kib_qwen35_set_position": (c_int, [_P, _U64]),
+        "kib_qwen35_state_io": (c_int, [_P, c_int, _P, _P, _P, _P, _P, _P, _P]),
+        "kib_qwen35_mtp_forward": (c_int, [_P, _P, _P, _U64, _U64, _P, _P]),
+        "kib_synth_default": (None, [POINTER(SynthConfig)]),
+        "kib_write_synthetic_qwen35": (c_int, [c_char_p, POINTER(SynthConfig), c_char_p, c_int]),
+        "kib_quantize_kquant": (c_int, [c_int, _P, _U64, _P]),
+    }
+    for name in ("q4_k", "q5_k", "q6_k"):
+        sig[f"kib_matvec_{name}_f32_device"] = (c_int, [_P, _P, _U64, _U64, _P, _P])
+        sig[f"kib_matmul_{name}_f32_device"] = (c_int, [_P, _P, _U64, _U64, _U64, _P, _P])
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def header_symbols(header: str = HEADER_PATH):
+    """Names of every function declared in include/kib.h."""
+    import re
+    text = open(header).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kib_[a-z0-9_]+)\s*\(", text)))
+
+
+def ptr(x):
+    """Device/host pointer of a torch tensor, numpy array, int or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):
+        return x.ctypes.data
+    raise TypeError(f"cannot take the address of {type(x)}")
+
+
+class Context:
+    """A device context: one CUDA stream, like MpsContext's one command queue."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load_library()
+        h = c_void_p()
+        rc = self.lib.kib_create(device, byref(h))
+        if rc != KIB_OK:
+            raise KibError(rc, "kib_create failed (no sm_100 device?)")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.kib_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, rc):
+        if rc != KIB_OK:
+            msg = self.lib.kib_last_error(self.h)
+            raise KibError(rc, msg.decode() if msg else "")
+
+    def call(self, name, *args):
+        fn = getattr(self.lib, name)
+        self.check(fn(self.h, *[ptr(a) if not isinstance(a, (float, int)) or isinstance(a, bool) else a for a in args]))
+
+    # graph scope (begin_graph / commit_graph)
+    def begin_graph(self):
+        self.check(self.lib.kib_begin_graph(self.h))
+
+    def commit_graph(self):
+        self.check(self.lib.kib_commit_graph(self.h))
+
+    # K-quant ops
+    def matmul_kquant(self, qtype, weight, rows, cols, tokens, inp, out):
+        self.check(self.lib.kib_matmul_kquant_f32(self.h, qtype, ptr(weight), rows, cols, tokens, ptr(inp), ptr(out)))
+
+    def matvec_kquant(self, qtype, weight, rows, cols, inp, out):
+        self.check(self.lib.kib_matvec_kquant_f32(self.h, qtype, ptr(weight), rows, cols, ptr(inp), ptr(out)))
+
+    def matvec_argmax(self, qtype, weight, rows, cols, inp, token_out, prob_out=None):
+        self.check(self.lib.kib_matvec_kquant_f32_argmax(self.h, qtype, ptr(weight), rows, cols, ptr(inp),
+                                                         ptr(token_out), ptr(prob_out)))
+
+    def dequantize_rows(self, qtype, weight, rows, ids, count, cols, out):
+        self.check(self.lib.kib_dequantize_rows_kquant_f32(self.h, qtype, ptr(weight), rows, ptr(ids), count, cols,
+                                                           ptr(out)))
+
+
+class Qwen35:
+    """The Qwen3.5 runtime over a GGUF file (generate_qwen35_metal's twin)."""
+
+    def __init__(self, ctx: Context, gguf_path: str, context_tokens=4096, decode_tokens=256, prefill_chunk=1024,
+                 enable_mtp=True):
+        self.ctx = ctx
+        self.lib = ctx.lib
+        opt = Qwen35Options(context_tokens, decode_tokens, prefill_chunk, 1, 1, 1 if enable_mtp else 0)
+        h = c_void_p()
+        ctx.check(self.lib.kib_qwen35_load(ctx.h, gguf_path.encode(), byref(opt), byref(h)))
+        self.h = h
+        plan = Qwen35Plan()
+        ctx.check(self.lib.kib_qwen35_get_plan(self.h, byref(plan)))
+        self.plan = plan
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.kib_qwen35_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def position(self):
+        return int(self.lib.kib_qwen35_position(self.h))
+
+    def set_position(self, pos):
+        self.ctx.check(self.lib.kib_qwen35_set_position(self.h, pos))
+
+    def reset(self):
+        self.ctx.check(self.lib.kib_qwen35_reset(self.h))
+
+    def prefill(self, tokens, chunk=0):
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt = c_int32()
+        self.ctx.check(self.lib.kib_qwen35_prefill(self.h, t.ctypes.data, len(t), chunk, byref(nxt)))
+        return int(nxt.value)
+
+    def forward(self, tokens, advance=True, logits=False, normed=False):
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        n = len(t)
+        am = np.zeros(n, dtype=np.int32)
+        lg = np.zeros((n, self.plan.vocab_size), dtype=np.float32) if logits else None
+        hn = np.zeros((n, self.plan.hidden_size), dtype=np.float32) if normed else None
+        self.ctx.check(self.lib.kib_qwen35_forward(self.h, t.ctypes.data, n, 1 if advance else 0, am.ctypes.data,
+                                                   ptr(lg), ptr(hn)))
+        return am, lg, hn
+
+    def decode_greedy(self, first_token, steps):
+        import numpy as np
+        out = np.zeros(steps, dtype=np.int32)
+        self.ctx.check(self.lib.kib_qwen35_decode_greedy(self.h, int(first_token), steps, out.ctypes.data))
+        return out
+
+    def state_sizes(self):
+        p = self.plan
+        return {
+            "kv": p.full_attention_layers * p.attention_capacity_tokens * p.kv_dim,
+            "r": p.linear_attention_layers * p.recurrent_r_elements_per_layer,
+            "s": p.linear_attention_layers * p.recurrent_s_elements_per_layer,
+            "mtp_kv": p.attention_capacity_tokens * p.kv_dim if p.mtp_layers else 0,
+            "h": p.hidden_size,
+        }
+
+    def export_state(self):
+        import numpy as np
+        z = self.state_sizes()
+        st = {"k": np.zeros(z["kv"], np.uint16), "v": np.zeros(z["kv"], np.uint16), "r": np.zeros(z["r"], np.float32),
+              "s": np.zeros(z["s"], np.float32), "mk": np.zeros(z["mtp_kv"], np.uint16),
+              "mv": np.zeros(z["mtp_kv"], np.uint16), "h": np.zeros(z["h"], np.float32)}
+        self.ctx.check(self.lib.kib_qwen35_state_io(self.h, 0, st["k"].ctypes.data, st["v"].ctypes.data,
+                                                    st["r"].ctypes.data, st["s"].ctypes.data,
+                                                    st["mk"].ctypes.data if z["mtp_kv"] else None,
+                                                    st["mv"].ctypes.data if z["mtp_kv"] else None,
+                                                    st["h"].ctypes.data))
+        return st
+
+    def import_state(self, st):
+        self.ctx.check(self.lib.kib_qwen35_state_io(self.h, 1, ptr(st.get("k")), ptr(st.get("v")), ptr(st.get("r")),
+                                                    ptr(st.get("s")),
+                                                    ptr(st.get("mk")) if len(st.get("mk", [])) else None,
+                                                    ptr(st.get("mv")) if len(st.get("mv", [])) else None,
+                                                    ptr(st.get("h"))))
+
+    def mtp_forward(self, tokens, h_rows, position):
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        h = np.ascontiguousarray(h_rows, dtype=np.float32)
+        n = len(t)
+        am = np.zeros(n, np.int32)
+        hn = np.zeros((n, self.plan.hidden_size), np.float32)
+        self.ctx.check(self.lib.kib_qwen35_mtp_forward(self.h, t.ctypes.data, h.ctypes.data, n, position,
+                                                       am.ctypes.data, hn.ctypes.data))
+        return am, hn
+
+    def generate(self, prompt, max_new_tokens, enable_mtp=False, mtp_draft_tokens=3, mtp_p_min=0.0,
+                 mtp_adaptive=True, ignore_eos=False, prefill_chunk=0, eos_token_id=None):
+        import numpy as np
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        rq = GenerationRequest(p.ctypes.data_as(POINTER(c_int32)), len(p), max_new_tokens, prefill_chunk,
+                               1 if enable_mtp else 0, mtp_draft_tokens, mtp_p_min, 1 if mtp_adaptive else 0,
+                               1 if ignore_eos else 0, 2 ** 64 - 1 if eos_token_id is None else eos_token_id)
+        out = np.zeros(max(max_new_tokens, 1), np.int32)
+        res = GenerationResult()
+        self.ctx.check(self.lib.kib_generate_qwen35(self.h, byref(rq), out.ctypes.data, max_new_tokens, byref(res)))
+        return out[: res.generated_tokens].copy(), res
+
+
+def synth_config(**overrides) -> SynthConfig:
+    lib = load_library()
+    cfg = SynthConfig()
+    lib.kib_synth_default(byref(cfg))
+    for k, v in overrides.items():
+        setattr(cfg, k, v)
+    return cfg
+
+
+def write_synthetic_qwen35(path: str, **overrides) -> str:
+    """Writes a random-init Qwen3.5-shaped GGUF (Q4_K_M mix by default)."""
+    lib = load_library()
+    cfg = synth_config(**overrides)
+    err = ctypes.create_string_buffer(512)
+    rc = lib.kib_write_synthetic_qwen35(path.encode(), byref(cfg), err, 512)
+    if rc != KIB_OK:
+        raise KibError(rc, err.value.decode())
+    return path
+
+
+def quantize(qtype: int, x):
+    """K-quant super-blocks of a float32 array (length a multiple of 256)."""
+    import numpy as np
+    lib = load_library()
+    a = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.zeros(a.size // 256 * BLOCK_BYTES[qtype], np.uint8)
+    rc = lib.kib_quantize_kquant(qtype, a.ctypes.data, a.size, out.ctypes.data)
+    if rc != KIB_OK:
+        raise KibError(rc, "quantize failed")
+    return out

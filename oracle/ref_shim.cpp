@@ -1,0 +1,91 @@
+// ref_shim.cpp -- TEST INFRASTRUCTURE ONLY.
+//
+// Exposes a few of the reference's own host routines through a C ABI so the
+// parity tests can call them.  The reference translation unit
+// src/runtime/qwen35_runtime.cpp is compiled in place (included by path from
+// the reference checkout named by -DKIB_REF_ROOT); nothing from it is copied
+// into this repository.  Built by oracle/Makefile into oracle/_ref/libkib_ref.so.
+#define KIB_STR2(x) #x
+#define KIB_STR(x) KIB_STR2(x)
+#include KIB_STR(KIB_REF_RUNTIME_TU)
+
+#include <cstring>
+
+extern "C" {
+
+// dequantize_quantized_transposed_f32 (qwen35_runtime.cpp:1084-1241) on a raw
+// 2-D tensor; the reference returns the transpose [cols][rows], which this
+// wrapper writes back as [rows][cols].
+int ref_dequant_tensor(unsigned type, unsigned long long rows, unsigned long long cols,
+                       const unsigned char* bytes, unsigned long long nbytes, float* out) {
+  toyllm::GgufTensorInfo info;
+  info.name = "probe";
+  info.shape = {cols, rows};
+  info.type = type;
+  toyllm::GgufTensorBytes tb;
+  tb.data = reinterpret_cast<const std::byte*>(bytes);
+  tb.size = static_cast<std::size_t>(nbytes);
+  auto result = toyllm::dequantize_quantized_transposed_f32(info, tb);
+  if (!result.is_ok()) return -1;
+  const auto& t = result.value();
+  for (unsigned long long r = 0; r < rows; ++r)
+    for (unsigned long long c = 0; c < cols; ++c) out[r * cols + c] = t[c * rows + r];
+  return 0;
+}
+
+// f16_to_float_cpu (qwen35_runtime.cpp:934-952)
+float ref_f16_to_float(unsigned short v) {
+  unsigned char b[2] = {static_cast<unsigned char>(v & 0xFF), static_cast<unsigned char>(v >> 8)};
+  return toyllm::f16_to_float_cpu(b);
+}
+
+// Greedy pick of sample_qwen35_next_token (qwen35_runtime.cpp:3777-3858).
+long long ref_greedy_token(const float* logits, unsigned long long n) {
+  std::vector<float> v(logits, logits + n);
+  std::mt19937 rng(0);
+  toyllm::Qwen35EffectiveSamplingConfig cfg;
+  cfg.do_sample = false;
+  cfg.temperature = 0.0;
+  cfg.top_k = 0;
+  cfg.top_p = 1.0;
+  auto r = toyllm::sample_qwen35_next_token(v, rng, cfg);
+  return r.is_ok() ? static_cast<long long>(r.value()) : -1;
+}
+
+// load_model_bundle + read_gguf_file + build_qwen35_weight_map +
+// build_qwen35_execution_plan over a GGUF file: proves that a synthetic model
+// written by this repository is accepted by the reference's own loader.
+// Writes hidden, main layers, linear layers, full layers, mtp layers,
+// attention capacity, R and S elements per layer into dims[0..7].
+int ref_check_gguf(const char* path, unsigned long long context_tokens, long long* dims,
+                   char* err, int err_len) {
+  auto fail = [&](const std::string& m) {
+    if (err && err_len > 0) {
+      std::strncpy(err, m.c_str(), static_cast<size_t>(err_len - 1));
+      err[err_len - 1] = 0;
+    }
+    return -1;
+  };
+  auto bundle = toyllm::load_model_bundle(path);
+  if (!bundle.is_ok()) return fail(bundle.status().message());
+  auto gguf = toyllm::read_gguf_file(path);
+  if (!gguf.is_ok()) return fail(gguf.status().message());
+  auto map = toyllm::build_qwen35_weight_map(bundle.value().model, gguf.value());
+  if (!map.is_ok()) return fail(map.status().message());
+  toyllm::Qwen35RuntimeOptions options;
+  options.context_tokens = static_cast<std::size_t>(context_tokens);
+  auto plan = toyllm::build_qwen35_execution_plan(bundle.value().model, map.value(), 1, options);
+  if (!plan.is_ok()) return fail(plan.status().message());
+  const auto& p = plan.value();
+  dims[0] = static_cast<long long>(p.hidden_size);
+  dims[1] = static_cast<long long>(p.main_layers);
+  dims[2] = static_cast<long long>(p.cache.linear_attention_layers);
+  dims[3] = static_cast<long long>(p.cache.full_attention_layers);
+  dims[4] = static_cast<long long>(map.value().mtp_layers);
+  dims[5] = static_cast<long long>(p.cache.attention_capacity_tokens);
+  dims[6] = static_cast<long long>(p.cache.recurrent_r_elements_per_layer);
+  dims[7] = static_cast<long long>(p.cache.recurrent_s_elements_per_layer);
+  return 0;
+}
+
+}  // extern "C"

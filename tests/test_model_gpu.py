@@ -1,0 +1,144 @@
+"""Whole-model parity: the CUDA runtime (prefill, graph-replayed greedy decode,
+MTP draft/verify/accept) against the CPU oracle's restatement of the
+reference's runtime on the same synthetic GGUF."""
+import numpy as np
+import pytest
+
+import kib
+import oracle_lib
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(hidden=256, layers=8, intermediate=512, vocab=4096, heads=8, kv_heads=2, head_dim=256, ssm_heads=2,
+             ssm_head_dim=128, nextn_layers=1, threads=8, seed=2026)
+LOGIT_RTOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def small_model(tmp_path_factory):
+    path = str(tmp_path_factory.mktemp("m") / "small.gguf")
+    kib.write_synthetic_qwen35(path, **SMALL)
+    return path
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def prompt(n, vocab, seed=0):
+    return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int32)
+
+
+@pytest.mark.parametrize("plen,chunk", [(5, 1024), (40, 16), (70, 1024)])
+def test_prefill_logits_match_oracle(ctx, oracle, small_model, plen, chunk):
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=64, prefill_chunk=1024)
+    om = oracle_lib.OracleModel(oracle, small_model, m.plan.attention_capacity_tokens)
+    p = prompt(plen, SMALL["vocab"], plen)
+    nxt = m.prefill(p, chunk)
+    # oracle: same chunking
+    for s in range(0, plen, chunk):
+        ch = p[s:s + chunk]
+        _, hn, lg = om.forward(ch, s)
+        om.mtp_process_chunk(ch, hn, s)
+    assert nxt == int(np.argmax(lg[-1]))
+    # one more forward: logits and normed rows within tolerance
+    am, glg, ghn = m.forward([nxt], advance=True, logits=True, normed=True)
+    _, hn1, lg1 = om.forward([nxt], plen)
+    assert rel(glg[0], lg1[0]) < LOGIT_RTOL and rel(ghn[0], hn1[0]) < LOGIT_RTOL
+    assert am[0] == int(np.argmax(lg1[0]))
+    om.close()
+    m.close()
+
+
+def test_greedy_decode_tokens_identical(ctx, oracle, small_model):
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=128)
+    om = oracle_lib.OracleModel(oracle, small_model, m.plan.attention_capacity_tokens)
+    p = prompt(24, SMALL["vocab"], 1)
+    nxt = m.prefill(p)
+    gtoks = m.decode_greedy(nxt, 48)
+    _, _, lg = om.forward(p, 0)
+    assert nxt == int(np.argmax(lg[-1]))
+    otoks, _ = om.generate_from(24, nxt, 49, mtp_draft_tokens=0)
+    assert otoks[0] == nxt
+    assert list(gtoks) == list(otoks[1:49])
+    om.close()
+    m.close()
+
+
+def test_decode_from_shared_state(ctx, oracle, small_model):
+    """Decode parity isolated from prefill numerics: the oracle imports the GPU's
+    prefilled KV/R/S state."""
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=64)
+    om = oracle_lib.OracleModel(oracle, small_model, m.plan.attention_capacity_tokens)
+    p = prompt(100, SMALL["vocab"], 2)
+    nxt = m.prefill(p, 32)
+    st = m.export_state()
+    om.state(st, into=True)
+    for i in range(6):
+        am, glg, _ = m.forward([nxt], advance=True, logits=True)
+        _, _, lg = om.forward([nxt], 100 + i)
+        assert rel(glg[0], lg[0]) < LOGIT_RTOL
+        assert am[0] == int(np.argmax(lg[0]))
+        nxt = am[0]
+    om.close()
+    m.close()
+
+
+@pytest.mark.parametrize("k", [1, 2, 3, 4])
+def test_verify_rows_match_oracle(ctx, oracle, small_model, k):
+    """Multi-token verify forward (k+1 rows, reference numerics bucket by rows)."""
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=64)
+    om = oracle_lib.OracleModel(oracle, small_model, m.plan.attention_capacity_tokens)
+    p = prompt(30, SMALL["vocab"], 3)
+    m.prefill(p)
+    om.state(m.export_state(), into=True)
+    toks = prompt(k + 1, SMALL["vocab"], 30 + k)
+    am, glg, _ = m.forward(toks, advance=False, logits=True)
+    _, _, lg = om.forward(toks, 30)
+    assert rel(glg, lg) < LOGIT_RTOL
+    assert list(am) == [int(np.argmax(r)) for r in lg]
+    om.close()
+    m.close()
+
+
+@pytest.mark.parametrize("draft,adaptive", [(1, False), (3, False), (3, True), (4, False)])
+def test_mtp_generate_matches_oracle(ctx, oracle, small_model, draft, adaptive):
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=96)
+    om = oracle_lib.OracleModel(oracle, small_model, m.plan.attention_capacity_tokens)
+    p = prompt(24, SMALL["vocab"], 5)
+    gt, res = m.generate(p, 40, enable_mtp=True, mtp_draft_tokens=draft, mtp_p_min=0.0, mtp_adaptive=adaptive,
+                         ignore_eos=True)
+    # oracle: prefill with MTP chunk processing, then the MTP loop
+    _, hn, lg = om.forward(p, 0)
+    om.mtp_process_chunk(p, hn, 0)
+    first = int(np.argmax(lg[-1]))
+    ot, st = om.generate_from(24, first, 40, mtp_draft_tokens=draft, adaptive=adaptive)
+    assert list(gt) == list(ot)
+    r = res.mtp
+    assert (r.drafted_tokens, r.accepted_tokens, r.verify_steps) == (st.drafted, st.accepted, st.verify_steps)
+    assert list(r.accepted_by_position) == list(st.accepted_by_position)
+    assert r.adaptive_budget == st.adaptive_budget and r.adaptive_changes == st.adaptive_changes
+    om.close()
+    m.close()
+
+
+def test_generate_greedy_matches_oracle(ctx, oracle, small_model):
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=96)
+    om = oracle_lib.OracleModel(oracle, small_model, m.plan.attention_capacity_tokens)
+    p = prompt(12, SMALL["vocab"], 6)
+    gt, res = m.generate(p, 50, enable_mtp=False, ignore_eos=True)
+    _, _, lg = om.forward(p, 0)
+    ot, _ = om.generate_from(12, int(np.argmax(lg[-1])), 50)
+    assert list(gt) == list(ot) and res.generated_tokens == 50
+    om.close()
+    m.close()
+
+
+def test_generate_stops_at_eos(ctx, small_model):
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=96)
+    p = prompt(12, SMALL["vocab"], 6)
+    gt, _ = m.generate(p, 20, ignore_eos=True)
+    eos = int(gt[5])
+    gt2, res = m.generate(p, 20, eos_token_id=eos)
+    assert list(gt2) == list(gt[:list(gt).index(eos)]) and res.finish_reason_stop == 1
+    m.close()
