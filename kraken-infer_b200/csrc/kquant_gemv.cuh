@@ -249,6 +249,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) kquant_gemv_kernel(const __gr
           unit_dequant_f16<QT>(b0, unit, wv);
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
+            if (t >= p.ntok) break;  // xs holds ntok rows only
             const float* xb = xs + t * p.cols + 256 * blk;
             float s = 0.0f;
 #pragma unroll
@@ -259,7 +260,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) kquant_gemv_kernel(const __gr
             unit_dequant_f16<QT>(b0 + p.stage_bytes / 2, unit, wv);
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
-              const float* xb = xs + t * p.cols + 256 * blk;
+              if (t >= p.ntok) break;  // xs holds ntok rows only
+            const float* xb = xs + t * p.cols + 256 * blk;
               float s = 0.0f;
 #pragma unroll
               for (int e = 0; e < 64; ++e) s = fmaf(wv[e], xb[unit_col<QT>(unit, e)], s);
