@@ -263,11 +263,13 @@ def main():
     with Clocks(local) as clk:
         h = m.h
         # same call kib_qwen35_decode_greedy makes, with events around it on the engine's stream
-        e0.record(stream)
         out = np.zeros(args.steps, np.int32)
+        torch.cuda.profiler.start()  # ncu --profile-from-start off captures the timed region only
+        e0.record(stream)
         rc = lib.kib_qwen35_decode_greedy(h, int(toks[-1]), args.steps, out.ctypes.data)
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     assert rc == 0
     barrier(world)
     ms = e0.elapsed_time(e1)
