@@ -116,64 +116,80 @@ def allmax(x, world):
     return float(t.item())
 
 
+MODEL_OVERRIDES = {}
+
+
 def model_path(rank, world):
     d = os.environ.get("KIB_BENCH_DIR", os.path.join(tempfile.gettempdir(), "kib_bench"))
     os.makedirs(d, exist_ok=True)
-    return os.path.join(d, "qwen35_0p8b_shape_q4_k_m_seed1234.gguf")
+    tag = "".join(f"_{k}{v}" for k, v in sorted(MODEL_OVERRIDES.items()))
+    return os.path.join(d, f"qwen35_0p8b_shape_q4_k_m_seed1234{tag}.gguf")
 
 
 def ensure_model(path, rank, world):
     import kib
     if rank == 0 and not os.path.exists(path):
         tmp = path + ".tmp"
-        kib.write_synthetic_qwen35(tmp, threads=min(os.cpu_count() or 8, 64), seed=1234)
+        kib.write_synthetic_qwen35(tmp, threads=min(os.cpu_count() or 8, 64), seed=1234, **MODEL_OVERRIDES)
         os.replace(tmp, path)
     barrier(world)
 
 
-def matvec_roofline(ctx, hbm_peak):
+def matvec_roofline(ctx, hbm_peak, reps=5, profile=False, qtype=None, rows=3584, cols=1024):
     """Config 1 (Q4_K 3584x1024, x ~ N(0,1)) over a rotating pool of distinct
-    weight copies > 4x L2, launched back to back; CUDA events on the stream the
-    kernels run on."""
+    weight copies > 4x L2, launched back to back from one CUDA graph; CUDA
+    events on the stream the kernels run on."""
     import numpy as np
     import torch
     import kib
-    rows, cols = 3584, 1024
-    w = kib.quantize(kib.Q4_K, (np.random.default_rng(1).standard_normal(rows * cols) * 0.02).astype(np.float32))
+    qtype = kib.Q4_K if qtype is None else qtype
+    w = kib.quantize(qtype, (np.random.default_rng(1).standard_normal(rows * cols) * 0.02).astype(np.float32))
     wbytes = w.size
     l2 = torch.cuda.get_device_properties(0).L2_cache_size
-    copies = max(8, (4 * l2) // wbytes + 1)
+    copies = int(max(8, (4 * l2) // wbytes + 1))
     pool = torch.from_numpy(np.tile(w, copies)).cuda()
     x = torch.randn(cols, device="cuda")
     y = torch.zeros(copies, rows, device="cuda")
     stream = torch.cuda.ExternalStream(ctx.lib.kib_stream(ctx.h))
-    ctx.begin_graph()
-    for i in range(copies):
-        ctx.matvec_kquant(kib.Q4_K, pool.data_ptr() + i * wbytes, rows, cols, x, y[i])
-    ctx.commit_graph()
-    reps = 3
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ctx.begin_graph()
-    e0.record(stream)
-    for _ in range(reps):
+    base = pool.data_ptr()
+
+    def launch_all():
         for i in range(copies):
-            ctx.matvec_kquant(kib.Q4_K, pool.data_ptr() + i * wbytes, rows, cols, x, y[i])
-    e1.record(stream)
+            ctx.matvec_kquant(qtype, base + i * wbytes, rows, cols, x, y[i])
+
+    ctx.begin_graph()
+    launch_all()  # warm-up, eager
     ctx.commit_graph()
+    if profile:  # ncu --profile-from-start off: three launches
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        ctx.begin_graph()
+        for i in range(3):
+            ctx.matvec_kquant(qtype, base + i * wbytes, rows, cols, x, y[i])
+        ctx.commit_graph()
+        torch.cuda.profiler.stop()
+    g = torch.cuda.CUDAGraph()
+    ctx.begin_graph()
+    with torch.cuda.graph(g, stream=stream):
+        launch_all()
+    ctx.commit_graph()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / (reps * copies)
     alg = wbytes + cols * 4 + rows * 4  # 2,082,816 B per call
     achieved = alg / (ms * 1e-3) / 1e9
-    # single-launch latency
-    torch.cuda.synchronize()
-    e0.record(stream)
-    ctx.matvec_kquant(kib.Q4_K, pool, rows, cols, x, y[0])
-    e1.record(stream)
-    torch.cuda.synchronize()
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "traffic": None,
-            "kernel": "kquant_gemv_kernel<Q4_K,1> (config 1: Q4_K 3584x1024 matvec)",
+            "kernel": f"kquant_gemv2_kernel<{qtype},1> ({rows}x{cols} matvec)",
             "bytes_per_launch": alg, "us_per_launch": round(ms * 1e3, 3), "launches": reps * copies,
-            "pool_copies": int(copies), "single_launch_us": round(e0.elapsed_time(e1) * 1e3, 2)}
+            "pool_copies": copies}
 
 
 def cpu_decode_sample(path, threads, budget_s=20.0, max_tokens=6):
@@ -234,8 +250,32 @@ def main():
     ap.add_argument("--impl", default="kib", choices=["kib", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--workload", default="decode", choices=["decode", "matvec"],
+                    help="matvec: BASELINE config 1 only (Q4_K 3584x1024 GEMV roofline)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling only: fewer layers than the BASELINE model (the JSON line says so)")
+    ap.add_argument("--vocab", type=int, default=None, help="profiling only: smaller vocabulary")
+    ap.add_argument("--mv-type", type=int, default=12, help="matvec workload: GGML type (12/13/14)")
+    ap.add_argument("--mv-rows", type=int, default=3584)
+    ap.add_argument("--mv-cols", type=int, default=1024)
     args = ap.parse_args()
     rank, world, local = dist_setup(args.gpus)
+    if args.layers:
+        MODEL_OVERRIDES["layers"] = args.layers
+    if args.vocab:
+        MODEL_OVERRIDES["vocab"] = args.vocab
+    if args.workload == "matvec":
+        import torch
+        import kib
+        torch.cuda.set_device(local)
+        ctx = kib.Context(local)
+        hbm, kind = peaks()
+        r = matvec_roofline(ctx, hbm, profile=True, qtype=args.mv_type, rows=args.mv_rows, cols=args.mv_cols)
+        r["peak_kind"] = kind
+        print(json.dumps({"metric": f"K-quant type {args.mv_type} {args.mv_rows}x{args.mv_cols} matvec GB/s", "value": r["achieved"], "unit": "GB/s",
+                          "roofline": r}), flush=True)
+        ctx.close()
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
@@ -306,7 +346,9 @@ def main():
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32 (K-quant weights, F16 KV)",
                 "data": "synthetic (random-init weights, seeded random token ids)",
                 "config": {"workload": WORKLOAD, "context": CONTEXT, "position_start": pos0,
-                           "quant_mix": "Q4_K projections, Q6_K ffn_down + tied head", "layers": 24,
+                           "quant_mix": "Q4_K projections, Q6_K ffn_down + tied head",
+                           "layers": int(m.plan.main_layers), "vocab": int(m.plan.vocab_size),
+                           "reduced_model_for_profiling": bool(MODEL_OVERRIDES),
                            "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (weights 513 MB)"},
                 "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
                         "api": "kib_qwen35_forward (token + position H2D, argmax D2H, per-token sync)"},

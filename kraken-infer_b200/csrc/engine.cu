@@ -19,6 +19,8 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -117,6 +119,11 @@ struct kib_qwen35 {
   cudaGraphExec_t decode_graph = nullptr;
   cudaGraphExec_t mtp_graph = nullptr;
   std::string err;
+  // KIB_TRACE=1: per-launch timeline of the decode graph (see trace_* in kib_common.cuh)
+  bool trace_on = false;
+  unsigned long long* d_trace = nullptr;
+  int trace_used = 0;
+  std::vector<std::string> trace_names;
 };
 
 namespace {
@@ -145,6 +152,12 @@ struct Enq {
   std::string why;
   cudaError_t e = cudaSuccess;
   bool ok() const { return e == cudaSuccess; }
+  bool tracing = false;
+  unsigned long long* slot(const char* name) {
+    if (!tracing || !m->d_trace || m->trace_used >= 4096) return nullptr;
+    m->trace_names.push_back(name);
+    return m->d_trace + 8 * (m->trace_used++);
+  }
   void run(cudaError_t r, const char* what) {
     if (e == cudaSuccess && r != cudaSuccess) {
       e = r;
@@ -190,6 +203,7 @@ void gemv_multi(Enq& q, GemvDesc tmpl, const std::vector<std::tuple<const DevT*,
   }
   for (auto& kv : by_type) {
     if (kv.second.nseg == 0) continue;
+    kv.second.trace = q.slot("gemv");
     std::string why;
     q.run(gemv_launch(kv.second, q.m->ctx->num_sms, q.st, &why), "gemv");
     if (!q.ok() && q.why == "gemv") q.why = why;
@@ -228,6 +242,7 @@ void linear_block_small(Enq& q, const LayerW& L, int T, const float* x_in, float
   g.key_heads = m->lkh;
   g.value_heads = m->lvh;
   g.eps = m->eps;
+  g.trace = q.slot("gdn_core");
   q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
   GemvDesc o = base_desc(m, L.ssm_out.type, m->VD, T);
   o.prologue = kProNormGate;
@@ -266,15 +281,16 @@ AttnParams attn_params(kib_qwen35* m, const LayerW& L, uint16_t* kc, uint16_t* v
   a.out = m->d_att;
   a.q_out = m->d_qout;
   a.round_q = T >= 64 ? 1 : 0;
+  a.trace = nullptr;
   return a;
 }
 
 template <int TM>
 cudaError_t launch_attn_decode(const AttnParams& a, int kvh, int nsplit, cudaStream_t st) {
-  const size_t smem = (static_cast<size_t>(a.T) * 4 * kHd + 8 * static_cast<size_t>(a.T) * (kHd + 2)) * sizeof(float);
+  const size_t smem = attn_decode_smem_bytes(a.T);
   static bool cfg = false;
   if (!cfg) {
-    cudaFuncSetAttribute(attn_decode_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(attn_decode_kernel<TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cfg = true;
   }
   return launch_pdl(attn_decode_kernel<TM>, dim3(nsplit, kvh), dim3(256), smem, st, a);
@@ -290,7 +306,8 @@ void attention_block_small(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc, 
   d.norm_w = L.attn_norm.f();
   gemv_multi(q, d,
              {{&L.q, m->d_qg, 2 * m->AD, kEpiStore}, {&L.k, m->d_kp, m->KD, kEpiStore}, {&L.v, m->d_vp, m->KD, kEpiStore}});
-  const AttnParams a = attn_params(m, L, kc, vc, pos, T);
+  AttnParams a = attn_params(m, L, kc, vc, pos, T);
+  a.trace = q.slot("attn_decode");
   q.run(T == 1 ? launch_attn_decode<1>(a, m->kvh, m->nsplit, q.st) : launch_attn_decode<8>(a, m->kvh, m->nsplit, q.st),
         "attn_decode");
   GemvDesc o = base_desc(m, L.o.type, m->AD, T);
@@ -311,6 +328,7 @@ void ffn_small(Enq& q, const LayerW& L, int T, const float* x_mid, float* x_out)
     d.norm_w = L.post_norm.f();
     d.nseg = 0;
     add_seg(d, L.ffn_gate, m->d_act, m->I, kEpiSiluMul, &L.ffn_up);
+    d.trace = q.slot("gemv_ffn_pair");
     std::string why;
     q.run(gemv_launch(d, m->ctx->num_sms, q.st, &why), "ffn_gate_up");
   } else {
@@ -353,6 +371,7 @@ void head_small(Enq& q, int T, const float* x, const DevT& norm_w, const DevT& h
   d.token_log = token_log;
   d.step_counter = step;
   d.pos_advance = pos_adv;
+  d.trace = q.slot("lm_head");
   std::string why;
   q.run(gemv_launch(d, m->ctx->num_sms, q.st, &why), "lm_head");
 }
@@ -401,6 +420,7 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
   g.key_heads = m->lkh;
   g.value_heads = m->lvh;
   g.eps = m->eps;
+  g.trace = nullptr;
   q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
   q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, T, m->lvh, m->lhd, m->eps, m->d_norm2, q.st), "norm_gate");
   gemm(q, L.ssm_out, m->d_norm2, m->VD, T, x_mid, m->H, x_in);
@@ -456,9 +476,10 @@ int bind(kib_qwen35* m, const std::map<std::string, DevT>& dev, const std::strin
   return KIB_OK;
 }
 
-int capture(kib_qwen35* m, cudaGraphExec_t* exec, const std::function<void(Enq&)>& body) {
+int capture(kib_qwen35* m, cudaGraphExec_t* exec, const std::function<void(Enq&)>& body, bool tracing = false) {
   cudaStream_t st = m->ctx->stream;
   Enq q{m, st};
+  q.tracing = tracing && m->trace_on;
   cudaGraph_t g = nullptr;
   ENG_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
   body(q);
@@ -767,6 +788,9 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
     return set_error(ctx, KIB_ERR_INTERNAL, "cache/activation allocation failed");
   }
   cudaMemset(m->d_attn_cnt, 0, 64 * sizeof(unsigned));
+  if (const char* tr = std::getenv("KIB_TRACE"); tr && tr[0] == '1') {
+    m->trace_on = cudaMalloc(&m->d_trace, 4096 * 8 * sizeof(unsigned long long)) == cudaSuccess;
+  }
   cudaMemset(m->d_head_cnt, 0, 4 * sizeof(unsigned));
   *out = mp.release();
   return kib_qwen35_reset(*out);
@@ -784,7 +808,7 @@ void kib_qwen35_free(kib_qwen35* m) {
                   m->d_act2, m->d_qg, m->d_kp, m->d_vp, m->d_att, m->d_qout, m->d_norm, m->d_norm2, m->d_hn,
                   m->d_logits, m->d_e, m->d_cat, m->d_hm, m->d_hm1, m->d_mtp_h, m->d_part, m->d_attn_cnt,
                   m->d_head_cnt, m->d_cand_max, m->d_cand_sum, m->d_cand_idx, m->d_pos, m->d_mtp_pos,
-                  m->d_tokens, m->d_argmax, m->d_prob, m->d_log, m->d_step, m->d_mtp_tok};
+                  m->d_tokens, m->d_argmax, m->d_prob, m->d_log, m->d_step, m->d_mtp_tok, m->d_trace};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (m->h_pin) cudaFreeHost(m->h_pin);
@@ -910,9 +934,10 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
       main_layers_small(q, 1, m->d_pos);
       head_small(q, 1, m->d_h, m->output_norm, head_weight(m), m->d_tokens, nullptr, nullptr, nullptr, m->d_log,
                  m->d_step, m->d_pos);
-    });
+    }, true);
     if (rc) return rc;
   }
+  if (m->trace_on && m->d_trace) ENG_CUDA(cudaMemsetAsync(m->d_trace, 0, 4096 * 8 * sizeof(unsigned long long), st));
   m->h_pin[0] = static_cast<int>(m->pos);
   m->h_pin[1] = first_token;
   m->h_pin[2] = 0;
@@ -924,6 +949,25 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   int rc = sync_check(m, "decode");
   if (rc) return rc;
   m->pos += steps;
+  if (m->trace_on && m->d_trace && m->trace_used > 0) {
+    // timeline of the last replayed step(s) merged: CSV to $KIB_TRACE_OUT
+    std::vector<unsigned long long> h(8 * static_cast<size_t>(m->trace_used));
+    cudaMemcpy(h.data(), m->d_trace, h.size() * 8, cudaMemcpyDeviceToHost);
+    const char* path = std::getenv("KIB_TRACE_OUT");
+    FILE* f = path ? std::fopen(path, "w") : nullptr;
+    if (f) {
+      unsigned long long t0 = ~0ull;
+      for (int i = 0; i < m->trace_used; ++i) t0 = std::min(t0, ~h[8 * i]);
+      auto rel = [&](unsigned long long v) { return v == 0 ? 0ull : v - t0; };
+      std::fprintf(f, "idx,kernel,first_entry_ns,first_past_wait_ns,last_past_wait_ns,last_exit_ns,last_entry_ns,"
+                      "last_tile_ready_ns,last_prologue_done_ns\n");
+      for (int i = 0; i < m->trace_used; ++i)
+        std::fprintf(f, "%d,%s,%llu,%llu,%llu,%llu,%llu,%llu,%llu\n", i, m->trace_names[i].c_str(), ~h[8 * i] - t0,
+                     ~h[8 * i + 3] - t0, rel(h[8 * i + 1]), rel(h[8 * i + 2]), rel(h[8 * i + 4]), rel(h[8 * i + 5]),
+                     rel(h[8 * i + 6]));
+      std::fclose(f);
+    }
+  }
   return KIB_OK;
 }
 

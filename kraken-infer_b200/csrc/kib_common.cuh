@@ -84,6 +84,39 @@ KIB_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 
 KIB_DEV void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
+// ------------------------------------------------------------------ trace
+// Per-launch timeline of one kernel (KIB_TRACE): slot[0] = ~first CTA entry,
+// slot[1] = last CTA past griddepcontrol.wait, slot[2] = last CTA exit,
+// slot[3] = ~first CTA past the wait (times from %globaltimer, ns; the
+// complemented fields turn atomicMax into a minimum).
+KIB_DEV unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+KIB_DEV void trace_entry(unsigned long long* s) {
+  if (s && threadIdx.x == 0) {
+    const unsigned long long t = gtimer();
+    atomicMax(&s[0], ~t);
+    atomicMax(&s[4], t);  // last CTA entry
+  }
+}
+// slot[5]: last CTA whose first staged tile has landed; slot[6]: last CTA
+// done with its compute (before the epilogue's final stores).
+KIB_DEV void trace_mark(unsigned long long* s, int field) {
+  if (s && threadIdx.x == 0) atomicMax(&s[field], gtimer());
+}
+KIB_DEV void trace_wait(unsigned long long* s) {
+  if (s && threadIdx.x == 0) {
+    const unsigned long long t = gtimer();
+    atomicMax(&s[1], t);
+    atomicMax(&s[3], ~t);
+  }
+}
+KIB_DEV void trace_exit(unsigned long long* s) {
+  if (s && threadIdx.x == 0) atomicMax(&s[2], gtimer());
+}
+
 // ------------------------------------------------------------- reductions
 KIB_DEV float warp_sum(float v) {
 #pragma unroll

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <string>
 
 #include "../../include/kib.h"
@@ -47,9 +48,31 @@ int finish_op(kib_ctx* ctx, const char* what);
 
 // Launch with programmatic stream serialization (PDL) so that the next
 // kernel's pre-wait prologue overlaps this one's tail.
+// KIB_PDL=0 turns programmatic dependent launch off (diagnostics).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("KIB_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// Every kernel of the decode chain asks for the same shared-memory carveout
+// (the maximum), so consecutive kernels never make an SM drain to
+// re-partition L1 / shared memory.
+template <typename... KArgs>
+void pin_carveout(void (*kernel)(KArgs...)) {
+  static bool done = false;  // one flag per kernel instantiation
+  if (!done) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    done = true;
+  }
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                        Args&&... args) {
+  pin_carveout(kernel);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -59,7 +82,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
@@ -103,6 +126,7 @@ struct GemvDesc {
   int* pos_advance = nullptr;
   float* x_out = nullptr;
   int* err = nullptr;
+  unsigned long long* trace = nullptr;
 };
 
 // Validates, plans the tile geometry and launches the GEMV.  Returns a cuda error.

@@ -71,13 +71,46 @@ KIB_DEV int unit_col(int u, int e) {
 
 // Codes of one unit as 16 words of 4 bytes each, ordered so that word w holds
 // elements 4w..4w+3 of the unit (element order as unit_col).
+// Raw bytes of one unit, as loaded from memory (shared or global):
+//   Q4_K: a,b = its 32 quant bytes, h = the 16-byte header (d, dmin, scales)
+//   Q5_K: as Q4_K plus qh0,qh1 = the block's 32 high-bit bytes
+//   Q6_K: a = ql[64c+16r..], b = ql[64c+32+16r..], h = qh[32c+16r..],
+//         s8 = scales[8c..8c+7], d = the fp16 super-block scale
 template <int QT>
-KIB_DEV void unit_codes(const uint8_t* blk, int u, uint32_t (&q)[16]) {
+struct RawUnit {
+  uint4 a, b, h;
+  uint4 qh0, qh1;
+  uint2 s8;
+  uint32_t d;
+};
+
+template <int QT>
+KIB_DEV RawUnit<QT> load_raw(const uint8_t* blk, int u) {
+  RawUnit<QT> r;
   if (QT == kTypeQ4K || QT == kTypeQ5K) {
     const uint8_t* qs = blk + (QT == kTypeQ4K ? 16 : 48) + 32 * u;
-    const uint4 a = *reinterpret_cast<const uint4*>(qs);
-    const uint4 b = *reinterpret_cast<const uint4*>(qs + 16);
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    r.a = *reinterpret_cast<const uint4*>(qs);
+    r.b = *reinterpret_cast<const uint4*>(qs + 16);
+    r.h = *reinterpret_cast<const uint4*>(blk);
+    if (QT == kTypeQ5K) {
+      r.qh0 = *reinterpret_cast<const uint4*>(blk + 16);
+      r.qh1 = *reinterpret_cast<const uint4*>(blk + 32);
+    }
+  } else {
+    const int c = u >> 1, rr = u & 1;
+    r.a = lds16_a2(blk + 64 * c + 16 * rr);
+    r.b = lds16_a2(blk + 64 * c + 32 + 16 * rr);
+    r.h = lds16_a2(blk + 128 + 32 * c + 16 * rr);
+    r.s8 = lds8_a2(blk + 192 + 8 * c);
+    r.d = lds_u16(blk + 208);
+  }
+  return r;
+}
+
+template <int QT>
+KIB_DEV void codes_from_raw(const RawUnit<QT>& r, int u, uint32_t (&q)[16]) {
+  if (QT == kTypeQ4K || QT == kTypeQ5K) {
+    const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
     if (QT == kTypeQ4K) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -85,9 +118,7 @@ KIB_DEV void unit_codes(const uint8_t* blk, int u, uint32_t (&q)[16]) {
         q[8 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
       }
     } else {
-      const uint4 ha = *reinterpret_cast<const uint4*>(blk + 16);
-      const uint4 hb = *reinterpret_cast<const uint4*>(blk + 32);
-      const uint32_t h[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+      const uint32_t h[8] = {r.qh0.x, r.qh0.y, r.qh0.z, r.qh0.w, r.qh1.x, r.qh1.y, r.qh1.z, r.qh1.w};
       const int sl = 2 * u, sh = 2 * u + 1;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -96,11 +127,8 @@ KIB_DEV void unit_codes(const uint8_t* blk, int u, uint32_t (&q)[16]) {
       }
     }
   } else {
-    const int c = u >> 1, r = u & 1;
-    const uint4 A = lds16_a2(blk + 64 * c + 16 * r);
-    const uint4 B = lds16_a2(blk + 64 * c + 32 + 16 * r);
-    const uint4 H = lds16_a2(blk + 128 + 32 * c + 16 * r);
-    const uint32_t a[4] = {A.x, A.y, A.z, A.w}, b[4] = {B.x, B.y, B.z, B.w}, h[4] = {H.x, H.y, H.z, H.w};
+    const uint32_t a[4] = {r.a.x, r.a.y, r.a.z, r.a.w}, b[4] = {r.b.x, r.b.y, r.b.z, r.b.w},
+                   h[4] = {r.h.x, r.h.y, r.h.z, r.h.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       q[i] = (a[i] & 0x0F0F0F0Fu) | ((h[i] << 4) & 0x30303030u);             // k=0
@@ -115,9 +143,9 @@ KIB_DEV void unit_codes(const uint8_t* blk, int u, uint32_t (&q)[16]) {
 //   Q4/Q5: A = d*sc, B = -dmin*m          (group 0 = sub-block 2u, 1 = 2u+1)
 //   Q6   : A = d*sc, B = -32*d*sc
 template <int QT>
-KIB_DEV void unit_coeffs(const uint8_t* blk, int u, float (&A)[4], float (&B)[4]) {
+KIB_DEV void coeffs_from_raw(const RawUnit<QT>& r, int u, float (&A)[4], float (&B)[4]) {
   if (QT == kTypeQ4K || QT == kTypeQ5K) {
-    const uint4 h = *reinterpret_cast<const uint4*>(blk);
+    const uint4 h = r.h;
     const float d = half_bits_to_float(static_cast<uint16_t>(h.x & 0xFFFFu));
     const float dmin = half_bits_to_float(static_cast<uint16_t>(h.x >> 16));
     uint32_t scw, mw;
@@ -141,18 +169,27 @@ KIB_DEV void unit_coeffs(const uint8_t* blk, int u, float (&A)[4], float (&B)[4]
     B[1] = -(dmin * m1);
     A[2] = A[3] = B[2] = B[3] = 0.0f;
   } else {
-    const int c = u >> 1, r = u & 1;
-    const float d = half_bits_to_float(static_cast<uint16_t>(lds_u16(blk + 208)));
-    const uint2 s8 = lds8_a2(blk + 192 + 8 * c);
-    const uint32_t sw[2] = {s8.x, s8.y};
+    const int rr = u & 1;
+    const float d = half_bits_to_float(static_cast<uint16_t>(r.d & 0xFFFFu));
+    const uint32_t sw[2] = {r.s8.x, r.s8.y};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int idx = r + 2 * k;  // 0..7
+      const int idx = rr + 2 * k;  // 0..7
       const int8_t sc = static_cast<int8_t>((sw[idx >> 2] >> (8 * (idx & 3))) & 0xFFu);
       A[k] = d * static_cast<float>(sc);
       B[k] = -32.0f * A[k];
     }
   }
+}
+
+template <int QT>
+KIB_DEV void unit_codes(const uint8_t* blk, int u, uint32_t (&q)[16]) {
+  codes_from_raw<QT>(load_raw<QT>(blk, u), u, q);
+}
+
+template <int QT>
+KIB_DEV void unit_coeffs(const uint8_t* blk, int u, float (&A)[4], float (&B)[4]) {
+  coeffs_from_raw<QT>(load_raw<QT>(blk, u), u, A, B);
 }
 
 KIB_DEV float2 code_pair_lo(uint32_t w) {
@@ -213,6 +250,44 @@ KIB_DEV void unit_dot(const uint8_t* blk, int u, const UnitX<QT> (&ux)[NT], floa
   unit_codes<QT>(blk, u, q);
   float A[4], B[4];
   unit_coeffs<QT>(blk, u, A, B);
+  float2 acc[NT][G];
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[t][g] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int w = 0; w < 16; ++w) {
+    const float2 lo = code_pair_lo(q[w]);
+    const float2 hi = code_pair_hi(q[w]);
+    const int g = w / WPG;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      acc[t][g] = ffma2(lo, ux[t].v[2 * w], acc[t][g]);
+      acc[t][g] = ffma2(hi, ux[t].v[2 * w + 1], acc[t][g]);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    float r = 0.0f;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      // sum(code * x) = 256*acc - 128*sum(x); value = A*code + B
+      const float cx = fmaf(256.0f, acc[t][g].x + acc[t][g].y, -128.0f * ux[t].s[g]);
+      r = fmaf(A[g], cx, fmaf(B[g], ux[t].s[g], r));
+    }
+    out[t] += r;
+  }
+}
+
+// Same dot product over a unit already loaded into registers.
+template <int QT, int NT>
+KIB_DEV void unit_dot_raw(const RawUnit<QT>& raw, int u, const UnitX<QT> (&ux)[NT], float (&out)[NT]) {
+  constexpr int G = KQ<QT>::kGroups;
+  constexpr int WPG = 16 / G;  // code words per group
+  uint32_t q[16];
+  codes_from_raw<QT>(raw, u, q);
+  float A[4], B[4];
+  coeffs_from_raw<QT>(raw, u, A, B);
   float2 acc[NT][G];
 #pragma unroll
   for (int t = 0; t < NT; ++t)

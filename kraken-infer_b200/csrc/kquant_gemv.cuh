@@ -72,6 +72,7 @@ struct GemvParams {
   float* conv_state;    // [rows][conv_k-1]
   const float* conv_w;  // [rows][conv_k]
   int conv_k;
+  int conv_off;         // compact kernel: byte offset of the staged conv state rows in a stage (0: none)
   // kEpiArgmax: per-CTA candidates, then the last CTA writes token/prob per token
   float* cand_max;      // [grid][tok]
   float* cand_sum;      // [grid][tok]
@@ -84,6 +85,7 @@ struct GemvParams {
   int* pos_advance;     // optional: *pos_advance += ntok once the head is done
   float* x_out;         // optional: CTA 0 stores the prologue's input vectors [tok][cols]
   int* err;
+  unsigned long long* trace;  // KIB_TRACE slot or null
 };
 
 KIB_DEV float silu_f(float v) { return v / (1.0f + expf(-v)); }

@@ -34,6 +34,7 @@ struct GdnParams {
   int key_heads;
   int value_heads;
   float eps;
+  unsigned long long* trace;
 };
 
 constexpr int kGdnRows = 16;  // state rows per CTA
@@ -50,12 +51,14 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
   const int key_dim = p.key_heads * D;
   float* S = p.state + static_cast<size_t>(h) * D * D;
   // warp w owns rows grp*16 + 4w .. +3; lane owns columns 4*lane .. +3
+  trace_entry(p.trace);
   float4 s[4];
 #pragma unroll
   for (int r = 0; r < 4; ++r)
     s[r] = *reinterpret_cast<const float4*>(S + static_cast<size_t>(grp * kGdnRows + 4 * warp + r) * D + 4 * lane);
 
   pdl_wait();
+  trace_wait(p.trace);
   pdl_launch_dependents();
   const float scale = 1.0f / sqrtf(static_cast<float>(D));
   for (int t = 0; t < p.T; ++t) {
@@ -107,6 +110,7 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
 #pragma unroll
   for (int r = 0; r < 4; ++r)
     *reinterpret_cast<float4*>(S + static_cast<size_t>(grp * kGdnRows + 4 * warp + r) * D + 4 * lane) = s[r];
+  trace_exit(p.trace);
 }
 
 // =============================================================== attention
@@ -132,6 +136,7 @@ struct AttnParams {
   float* out;             // [T][heads*hd]
   float* q_out;           // prefill: normed+roped q [T][heads][hd]
   int round_q;            // prefill T >= 64: Q rounded to half (flash256 numerics)
+  unsigned long long* trace;
 };
 
 constexpr int kHd = 256;
@@ -167,30 +172,77 @@ KIB_DEV void norm_rope_head(float* v, const float* in, const float* w, float eps
 }
 
 // Split-K decode attention for T <= 8 queries over an F16 KV cache.  Grid
-// (nsplit, kv_heads); 8 warps: warp w serves q head (w % 4) of the kv group and
-// key half (w / 4).  The CTA owning a new token's position normalises, rotates
-// and writes its K/V (single writer).  The last CTA of each kv head merges
-// all splits and applies sigmoid(gate) (attention_f32_batched_f16_kv,
-// mps_backend.mm:2943-3008, plus qwen35_runtime.cpp:3347-3351).
+// (nsplit, kv_heads); each CTA owns a contiguous key range of one kv head.
+// The range's cached keys (positions < pos) are staged into shared memory in
+// chunks of 32 keys by cp.async.bulk (K and V rows, 512 B each) -- the first
+// two chunks are issued before griddepcontrol.wait, since the cache was written
+// by earlier steps.  The CTA owning a new token's position normalises, rotates
+// and writes its K/V (single writer) and attends to it from shared memory.
+// 8 warps: warp w serves q head (w % 4) of the kv group and every other key
+// (w / 4).  The last CTA of each kv head merges all splits and applies
+// sigmoid(gate) (attention_f32_batched_f16_kv, mps_backend.mm:2943-3008, plus
+// qwen35_runtime.cpp:3347-3351).
+constexpr int kAttnChunk = 32;
+
+__host__ __device__ inline size_t attn_decode_smem_bytes(int T) {
+  return static_cast<size_t>(2) * kAttnChunk * 2 * kHd * sizeof(uint16_t) +
+         (static_cast<size_t>(T) * 4 * kHd + 2 * static_cast<size_t>(T) * kHd + 8 * static_cast<size_t>(T) * (kHd + 2)) *
+             sizeof(float);
+}
+
 template <int TM>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant__ AttnParams p) {
   constexpr int G = 4;  // q heads per kv head
-  extern __shared__ __align__(16) float sm[];
-  float* qs = sm;                        // [T][G][256]
-  float* merge = sm + p.T * G * kHd;     // [8 warps][T][256 + 2]
+  extern __shared__ __align__(128) uint8_t smraw[];
+  uint16_t* kvbuf = reinterpret_cast<uint16_t*>(smraw);  // [2][32 keys][K 256 | V 256] f16
+  float* qs = reinterpret_cast<float*>(smraw + 2 * kAttnChunk * 2 * kHd * sizeof(uint16_t));  // [T][G][256]
+  float* newk = qs + p.T * G * kHd;     // [T][256] new keys (f16-rounded)
+  float* newv = newk + p.T * kHd;       // [T][256]
+  float* merge = newv + p.T * kHd;      // [8 warps][T][256 + 2]
+  __shared__ uint64_t bar[2];
   __shared__ bool s_last;
   const int split = blockIdx.x, kvh = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kvd = p.kv_heads * kHd;
 
-  pdl_wait();
-  pdl_launch_dependents();
+  // the position was written at least two kernels earlier (host copy or the
+  // previous step's LM head), so it and the cached keys are readable now
+  trace_entry(p.trace);
   const int pos0 = *p.pos;
   const int nkeys = pos0 + p.T;
   int chunk = (nkeys + p.nsplit - 1) / p.nsplit;
   chunk = (chunk + 7) & ~7;
   const int kb = split * chunk, ke = min(kb + chunk, nkeys);
+  const int old_end = min(ke, pos0);
+  const int nold = max(0, old_end - kb);
+  const int nchunks = (nold + kAttnChunk - 1) / kAttnChunk;
+  auto issue = [&](int c) {  // warp 0 only
+    const int k0 = kb + c * kAttnChunk;
+    const int nk = min(kAttnChunk, old_end - k0);
+    const int st = c & 1;
+    if (lane == 0) mbar_arrive_expect_tx(&bar[st], static_cast<uint32_t>(nk) * 2u * kHd * 2u);
+    __syncwarp();
+    if (lane < nk) {
+      const size_t src = static_cast<size_t>(k0 + lane) * kvd + kvh * kHd;
+      uint16_t* dst = kvbuf + (static_cast<size_t>(st) * kAttnChunk + lane) * 2 * kHd;
+      bulk_g2s(dst, p.kcache + src, kHd * 2, &bar[st]);
+      bulk_g2s(dst + kHd, p.vcache + src, kHd * 2, &bar[st]);
+    }
+  };
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_init(&bar[0], 1);
+      mbar_init(&bar[1], 1);
+      fence_mbar_init();
+    }
+    __syncwarp();
+    for (int c = 0; c < min(2, nchunks); ++c) issue(c);
+  }
+  __syncthreads();
 
+  pdl_wait();
+  trace_wait(p.trace);
+  pdl_launch_dependents();
   // q prep: warp -> (head, token)
   for (int job = warp; job < G * p.T; job += 8) {
     const int j = job % G, t = job / G;
@@ -202,22 +254,22 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
   for (int t = warp; t < p.T; t += 8) {
     const int kpos = pos0 + t;
     if (kpos < kb || kpos >= ke) continue;
-    float* tmp = merge + warp * (kHd + 2);  // scratch row
-    norm_rope_head(tmp, p.kp + static_cast<size_t>(t) * kvd + kvh * kHd, p.k_norm, p.eps, kpos, p, lane);
+    float* kr = newk + t * kHd;
+    norm_rope_head(kr, p.kp + static_cast<size_t>(t) * kvd + kvh * kHd, p.k_norm, p.eps, kpos, p, lane);
     for (int i = lane; i < kHd; i += 32) {
-      p.kcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] = __half_as_ushort(__float2half_rn(tmp[i]));
-      p.vcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] =
-          __half_as_ushort(__float2half_rn(p.vp[static_cast<size_t>(t) * kvd + kvh * kHd + i]));
+      const __half kh = __float2half_rn(kr[i]);
+      const __half vh = __float2half_rn(p.vp[static_cast<size_t>(t) * kvd + kvh * kHd + i]);
+      p.kcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] = __half_as_ushort(kh);
+      p.vcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] = __half_as_ushort(vh);
+      kr[i] = __half2float(kh);
+      newv[t * kHd + i] = __half2float(vh);
     }
   }
-  __threadfence_block();
   __syncthreads();
 
-  // main loop: this warp's head j, keys kb + half, kb + half + 2, ...
   const int j = warp % G, kh2 = warp / G;
   const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
-  float m[TM], l[TM], acc[TM][8];
-  float qreg[TM][8];
+  float m[TM], l[TM], acc[TM][8], qreg[TM][8];
 #pragma unroll
   for (int t = 0; t < TM; ++t) {
     m[t] = -INFINITY;
@@ -228,23 +280,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
       qreg[t][i] = t < p.T ? qs[(t * G + j) * kHd + 8 * lane + i] : 0.0f;
     }
   }
-  for (int key = kb + kh2; key < ke; key += 2) {
-    const uint4 kr = __ldcg(reinterpret_cast<const uint4*>(p.kcache + static_cast<size_t>(key) * kvd + kvh * kHd + 8 * lane));
-    const uint4 vr = __ldcg(reinterpret_cast<const uint4*>(p.vcache + static_cast<size_t>(key) * kvd + kvh * kHd + 8 * lane));
-    float kf[8], vf[8];
-    {
-      const __half2* kh = reinterpret_cast<const __half2*>(&kr);
-      const __half2* vh = reinterpret_cast<const __half2*>(&vr);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 a = __half22float2(kh[i]);
-        const float2 b = __half22float2(vh[i]);
-        kf[2 * i] = a.x;
-        kf[2 * i + 1] = a.y;
-        vf[2 * i] = b.x;
-        vf[2 * i + 1] = b.y;
-      }
-    }
+  auto attend = [&](const float (&kf)[8], const float (&vf)[8], int key) {
 #pragma unroll
     for (int t = 0; t < TM; ++t) {
       if (t >= p.T) break;
@@ -260,6 +296,89 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[t][i] = acc[t][i] * ps + w * vf[i];
       m[t] = nm;
+    }
+  };
+  // 8 keys per step: the 8 scores reduce independently, then one
+  // online-softmax update per step
+  constexpr int KB = 8;
+#pragma unroll 1
+  for (int c = 0; c < nchunks; ++c) {
+    const int st = c & 1;
+    mbar_wait_bounded(&bar[st], static_cast<uint32_t>((c >> 1) & 1), nullptr);
+    const int k0 = kb + c * kAttnChunk;
+    const int nk = min(kAttnChunk, old_end - k0);
+#pragma unroll 1
+    for (int kk0 = kh2 * KB; kk0 < nk; kk0 += 2 * KB) {
+      float sc[TM][KB];
+      uint4 vraw[KB];
+#pragma unroll
+      for (int e = 0; e < KB; ++e) {
+        const int kk = min(kk0 + e, nk - 1);
+        const uint16_t* row = kvbuf + (static_cast<size_t>(st) * kAttnChunk + kk) * 2 * kHd;
+        const uint4 kr = *reinterpret_cast<const uint4*>(row + 8 * lane);
+        vraw[e] = *reinterpret_cast<const uint4*>(row + kHd + 8 * lane);
+        const __half2* kh = reinterpret_cast<const __half2*>(&kr);
+        float kf[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 a2 = __half22float2(kh[i]);
+          kf[2 * i] = a2.x;
+          kf[2 * i + 1] = a2.y;
+        }
+#pragma unroll
+        for (int t = 0; t < TM; ++t) {
+          float d = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) d = fmaf(qreg[t][i], kf[i], d);
+          sc[t][e] = d;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < TM; ++t)
+#pragma unroll
+        for (int e = 0; e < KB; ++e) sc[t][e] = warp_sum(sc[t][e]) * scale;
+#pragma unroll
+      for (int t = 0; t < TM; ++t) {
+        if (t >= p.T) break;
+        float mx = m[t];
+#pragma unroll
+        for (int e = 0; e < KB; ++e)
+          if (kk0 + e < nk) mx = fmaxf(mx, sc[t][e]);
+        const float ps = expf(m[t] - mx);
+        l[t] *= ps;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[t][i] *= ps;
+#pragma unroll
+        for (int e = 0; e < KB; ++e) {
+          if (kk0 + e >= nk) break;
+          const float w = expf(sc[t][e] - mx);
+          l[t] += w;
+          const __half2* vh = reinterpret_cast<const __half2*>(&vraw[e]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 b2 = __half22float2(vh[i]);
+            acc[t][2 * i] = fmaf(w, b2.x, acc[t][2 * i]);
+            acc[t][2 * i + 1] = fmaf(w, b2.y, acc[t][2 * i + 1]);
+          }
+        }
+        m[t] = mx;
+      }
+    }
+    __syncthreads();  // stage consumed
+    if (warp == 0 && c + 2 < nchunks) issue(c + 2);
+  }
+  // the new keys of this split (positions >= pos0), from shared memory
+  if (kh2 == 0) {
+    for (int t2 = 0; t2 < p.T; ++t2) {
+      const int kpos = pos0 + t2;
+      if (kpos < kb || kpos >= ke) continue;
+      float kf[8], vf[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        kf[i] = newk[t2 * kHd + 8 * lane + i];
+        vf[i] = newv[t2 * kHd + 8 * lane + i];
+      }
+      attend(kf, vf, kpos);
     }
   }
   // merge the two key halves of each head inside the CTA, then write the split partial
@@ -291,27 +410,61 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
   __syncthreads();
   if (tid == 0) s_last = atomicAdd(&p.counters[kvh], 1u) == static_cast<unsigned>(p.nsplit - 1);
   __syncthreads();
+  trace_exit(p.trace);
   if (!s_last) return;
   __threadfence();
-  for (int job = tid; job < G * p.T * kHd; job += 256) {
-    const int i = job % kHd, jt = job / kHd, jj = jt % G, t = jt / G;
-    const int head = kvh * G + jj;
-    float M = -INFINITY;
-    for (int sp = 0; sp < p.nsplit; ++sp)
-      M = fmaxf(M, __ldcg(p.part + ((static_cast<size_t>(sp) * p.T + t) * p.heads + head) * (kHd + 2) + kHd));
-    float num = 0.0f, den = 0.0f;
-    for (int sp = 0; sp < p.nsplit; ++sp) {
-      const float* src = p.part + ((static_cast<size_t>(sp) * p.T + t) * p.heads + head) * (kHd + 2);
-      const float ms = __ldcg(src + kHd);
-      if (ms == -INFINITY) continue;
-      const float e = expf(ms - M);
-      num += __ldcg(src + i) * e;
-      den += __ldcg(src + kHd + 1) * e;
-    }
-    const float o = den == 0.0f ? 0.0f : num / den;
-    const float g = p.qg[(static_cast<size_t>(t) * p.heads + head) * 2 * kHd + kHd + i];
-    p.out[static_cast<size_t>(t) * p.heads * kHd + head * kHd + i] = o * sigmoid_f(g);
+  // merge: per (head, token) pair the split weights exp(m_s - M) go to shared
+  // memory once; every output element then sums independent loads.
+  const int pairs = G * p.T;
+  const int nact = min(p.nsplit, (nkeys + chunk - 1) / chunk);  // splits that saw keys
+  float* wsm = merge;                          // [pairs][nsplit]  m, then the weights
+  float* lsm = merge + pairs * p.nsplit;       // [pairs][nsplit]  l
+  float* dsm = merge + 2 * pairs * p.nsplit;   // [pairs]
+  for (int idx = tid; idx < pairs * nact; idx += 256) {
+    const int pr = idx / nact, sp = idx % nact;
+    const int head = kvh * G + pr % G, t = pr / G;
+    const float* src = p.part + ((static_cast<size_t>(sp) * p.T + t) * p.heads + head) * (kHd + 2) + kHd;
+    wsm[pr * p.nsplit + sp] = __ldcg(src);
+    lsm[pr * p.nsplit + sp] = __ldcg(src + 1);
   }
+  __syncthreads();
+  for (int pr = tid; pr < pairs; pr += 256) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < nact; ++sp) M = fmaxf(M, wsm[pr * p.nsplit + sp]);
+    float den = 0.0f;
+    for (int sp = 0; sp < nact; ++sp) {
+      const float ms = wsm[pr * p.nsplit + sp];
+      const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
+      wsm[pr * p.nsplit + sp] = e;
+      den += lsm[pr * p.nsplit + sp] * e;
+    }
+    dsm[pr] = den;
+  }
+  __syncthreads();
+  // every thread owns 2 consecutive elements of one (head, token) pair and
+  // keeps 16 split loads in flight
+  for (int job = tid; job < pairs * (kHd / 2); job += 256) {
+    const int i = 2 * (job % (kHd / 2)), pr = job / (kHd / 2), jj = pr % G, t = pr / G;
+    const int head = kvh * G + jj;
+    const float* src = p.part + (static_cast<size_t>(t) * p.heads + head) * (kHd + 2) + i;
+    const size_t sstride = static_cast<size_t>(p.T) * p.heads * (kHd + 2);
+    float n0 = 0.0f, n1 = 0.0f;
+#pragma unroll 16
+    for (int sp = 0; sp < nact; ++sp) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(src + sp * sstride));
+      const float w = wsm[pr * p.nsplit + sp];
+      n0 = fmaf(v.x, w, n0);
+      n1 = fmaf(v.y, w, n1);
+    }
+    const float den = dsm[pr];
+    const float inv = den == 0.0f ? 0.0f : 1.0f / den;
+    const float* g = p.qg + (static_cast<size_t>(t) * p.heads + head) * 2 * kHd + kHd + i;
+    float* o = p.out + static_cast<size_t>(t) * p.heads * kHd + head * kHd + i;
+    o[0] = n0 * inv * sigmoid_f(g[0]);
+    o[1] = n1 * inv * sigmoid_f(g[1]);
+  }
+  __syncthreads();
+  trace_exit(p.trace);
   if (tid == 0) p.counters[kvh] = 0u;
 }
 

@@ -9,6 +9,7 @@
 #include <string>
 
 #include "kib_ctx.cuh"
+#include "kquant_gemv2.cuh"
 #include "layer_kernels.cuh"
 
 using namespace kib;
@@ -294,6 +295,36 @@ static cudaError_t gemv_dispatch(const GemvParams& p, int grid, size_t smem, cud
   }
 }
 
+template <int QT, int NT, int PRO>
+static cudaError_t gemv2_instance(const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kquant_gemv2_kernel<QT, NT, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  return launch_pdl(kquant_gemv2_kernel<QT, NT, PRO>, dim3(grid), dim3(kGemvThreads), smem, st, p);
+}
+
+template <int QT, int PRO>
+static cudaError_t gemv2_dispatch_pro(const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
+  switch (p.ntok) {
+    case 1: return gemv2_instance<QT, 1, PRO>(p, grid, smem, st);
+    case 2: return gemv2_instance<QT, 2, PRO>(p, grid, smem, st);
+    default: return gemv2_instance<QT, 3, PRO>(p, grid, smem, st);
+  }
+}
+
+template <int QT>
+static cudaError_t gemv2_dispatch(const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
+  switch (p.prologue) {
+    case kProRms: return gemv2_dispatch_pro<QT, kProRms>(p, grid, smem, st);
+    case kProNormGate: return gemv2_dispatch_pro<QT, kProNormGate>(p, grid, smem, st);
+    default: return gemv2_dispatch_pro<QT, kProPlain>(p, grid, smem, st);
+  }
+}
+
 cudaError_t gemv_launch(const GemvDesc& d, int num_sms, cudaStream_t st, std::string* why) {
   if (!kquant_type_ok(d.type) || d.cols <= 0 || d.cols % 256 || d.cols > 16384 || d.ntok < 1 ||
       d.ntok > kGemvMaxTok || d.nseg < 1 || d.nseg > kGemvMaxSegs) {
@@ -315,12 +346,30 @@ cudaError_t gemv_launch(const GemvDesc& d, int num_sms, cudaStream_t st, std::st
     paired = paired || d.seg[i].epilogue == kEpiSiluMul;
   }
   const int mult = paired ? 2 : 1;
+  bool has_conv = false;
+  for (int i = 0; i < d.nseg; ++i) has_conv = has_conv || d.seg[i].epilogue == kEpiConv;
+  const bool compact = d.ntok <= 3 && p.rg <= 128 &&
+                       (d.prologue != kProNormGate || (units == p.rg && d.head_dim == 128)) &&
+                       (!has_conv || d.conv_k == 4);
+  const int km1 = d.conv_k - 1;
+  auto count_tiles = [&](int tr) {
+    int n = 0;
+    for (int i = 0; i < d.nseg; ++i) n += (d.seg[i].rows + tr - 1) / tr;
+    return n;
+  };
   const int max_stage = 32 * 1024;
   int tr_max = (max_stage / (p.row_bytes * mult)) / m * m;
   if (tr_max < m) tr_max = m;
   int target = (total_rows + num_sms - 1) / num_sms;
   target = (target + m - 1) / m * m;
-  const int tr = target < tr_max ? target : tr_max;
+  int tr = target < tr_max ? target : tr_max;
+  if (compact) {
+    // one tile per CTA when the matrix fits a single wave of <= 64 KB tiles
+    const int cap = ((64 * 1024) / (p.row_bytes * mult)) / m * m;
+    int t2 = target;
+    while (count_tiles(t2) > num_sms && t2 + m <= cap) t2 += m;
+    if (count_tiles(t2) <= num_sms && t2 <= cap) tr = t2;
+  }
   p.tile_rows = tr;
   int tiles = 0;
   for (int i = 0; i < d.nseg; ++i) {
@@ -338,12 +387,18 @@ cudaError_t gemv_launch(const GemvDesc& d, int num_sms, cudaStream_t st, std::st
   const int grid = tiles < num_sms ? tiles : num_sms;
   const int half = ((tr * p.row_bytes) + 15) & ~15;
   p.stage_bytes = half * mult;
+  p.conv_off = 0;
+  if (compact && has_conv && !paired) {
+    p.conv_off = p.stage_bytes;
+    p.stage_bytes += ((tr * km1 * 4 + 15) & ~15) + ((tr * d.conv_k * 4 + 15) & ~15);
+  }
   const int per_cta = (tiles + grid - 1) / grid;
-  int S = (96 * 1024) / p.stage_bytes;
+  const bool small_tok = d.ntok <= 3;
+  int S = ((small_tok ? 160 : 96) * 1024) / p.stage_bytes;
   if (S < 1) S = 1;
   if (S > per_cta) S = per_cta;
   if (S > 8) S = 8;
-  const size_t xs_bytes = static_cast<size_t>(d.ntok) * d.cols * sizeof(float);
+  const size_t xs_bytes = compact ? 0 : static_cast<size_t>(d.ntok) * d.cols * sizeof(float);
   while (S > 1 && static_cast<size_t>(S) * p.stage_bytes + xs_bytes > 190 * 1024) --S;
   if (static_cast<size_t>(S) * p.stage_bytes + xs_bytes > 200 * 1024) {
     if (why) *why = "GEMV: shared memory plan exceeds 200 KB";
@@ -375,7 +430,15 @@ cudaError_t gemv_launch(const GemvDesc& d, int num_sms, cudaStream_t st, std::st
   p.pos_advance = d.pos_advance;
   p.x_out = d.x_out;
   p.err = d.err;
+  p.trace = d.trace;
   const size_t smem = static_cast<size_t>(S) * p.stage_bytes + xs_bytes;
+  if (compact) {
+    switch (d.type) {
+      case kTypeQ4K: return gemv2_dispatch<kTypeQ4K>(p, grid, smem, st);
+      case kTypeQ5K: return gemv2_dispatch<kTypeQ5K>(p, grid, smem, st);
+      default: return gemv2_dispatch<kTypeQ6K>(p, grid, smem, st);
+    }
+  }
   switch (d.type) {
     case kTypeQ4K: return gemv_dispatch<kTypeQ4K>(p, grid, smem, st);
     case kTypeQ5K: return gemv_dispatch<kTypeQ5K>(p, grid, smem, st);
