@@ -90,6 +90,21 @@ int kib_matmul_kquant_f32(kib_ctx* ctx, int type, const void* weight, uint64_t r
  * matvec_q{4,5,6}_k_f32_argmax / _top1 (mps_backend.hpp:141-146, 162-167, 183-188; 579-749, 1554-1688). */
 int kib_matvec_kquant_f32_argmax(kib_ctx* ctx, int type, const void* weight, uint64_t rows, uint64_t cols,
                                  const float* input, int32_t* token_out, float* prob_out);
+/* The same fused LM-head argmax for callers that must not allocate device
+ * memory (a host that owns all device memory through its own pool, or that
+ * forbids allocations after start-up).  No counterpart in the reference: it
+ * exists only in this backend.  Needs no kib_ctx; runs on the current device
+ * and on `stream` (a cudaStream_t, NULL for the legacy default stream) and
+ * returns once the kernel is queued: synchronise the stream before reading
+ * token_out / prob_out.  Its scratch is one fixed array per device inside the
+ * library (candidates of up to 1024 CTAs, i.e. devices of up to 1024 SMs;
+ * larger devices get KIB_ERR_INVALID_ARGUMENT, as do cols not a multiple of
+ * 256 or above 16384).  The first call on a device looks up that array's
+ * address; make it before any stream capture.  Every call shares the array:
+ * calls whose kernels may overlap on the GPU race and must be ordered by the
+ * caller. */
+int kib_matvec_kquant_f32_argmax_noalloc(int type, const void* weight, uint64_t rows, uint64_t cols,
+                                         const float* input, int32_t* token_out, float* prob_out, void* stream);
 /* dequantize_rows_q{4,5,6}_k_f32 / q*_k_get_rows (mps_backend.hpp:201-221;
  * mps_backend.mm:1693-1824): out[i] = row row_ids[i]; out-of-range ids give zeros. */
 int kib_dequantize_rows_kquant_f32(kib_ctx* ctx, int type, const void* weight, uint64_t rows,

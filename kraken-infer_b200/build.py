@@ -13,8 +13,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libkib.so")
-SOURCES = ["ops.cu", "engine.cu", "gguf.cpp"]
-HEADERS = ["kib_common.cuh", "kquant.cuh", "kquant_gemv.cuh", "layer_kernels.cuh", "kib_ctx.cuh", "gguf.hpp"]
+SOURCES = ["ops.cu", "engine.cu", "noalloc.cu", "gguf.cpp"]
+HEADERS = ["kib_common.cuh", "kquant.cuh", "kquant_gemv.cuh", "kquant_gemv2.cuh", "layer_kernels.cuh", "kib_ctx.cuh", "gguf.hpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-pthread",
