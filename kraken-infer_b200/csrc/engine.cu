@@ -31,6 +31,7 @@
 #include "gguf.hpp"
 #include "kib_ctx.cuh"
 #include "layer_kernels.cuh"
+#include "decode_persistent.cuh"
 
 namespace kib {
 cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const float* x, int x_ld, int T, float* y,
@@ -124,6 +125,19 @@ struct kib_qwen35 {
   unsigned long long* d_trace = nullptr;
   int trace_used = 0;
   std::vector<std::string> trace_names;
+  // persistent decode (one launch per token; KIB_PERSISTENT=0 turns it off)
+  bool pk_on = false;
+  std::string pk_why;
+  PkStage* d_pk = nullptr;
+  int pk_n = 0;
+  int pk_grid = 0;
+  unsigned* d_pk_ctr = nullptr;  // [0] grid barrier, [1] LM-head ticket
+  float* d_pk_part = nullptr;
+  float *d_pk_cmax = nullptr, *d_pk_csum = nullptr;
+  int* d_pk_cidx = nullptr;
+  unsigned long long* d_pk_trace = nullptr;
+  bool pk_coop = true;
+  cudaGraphExec_t pk_graph = nullptr;
 };
 
 namespace {
@@ -491,6 +505,7 @@ int capture(kib_qwen35* m, cudaGraphExec_t* exec, const std::function<void(Enq&)
   if (ce != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, std::string("graph capture: ") + cudaGetErrorString(ce));
   cudaError_t ie = cudaGraphInstantiate(exec, g, 0);
   cudaGraphDestroy(g);
+  if (ie != cudaSuccess) *exec = nullptr;
   if (ie != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, std::string("graph instantiate: ") + cudaGetErrorString(ie));
   return KIB_OK;
 }
@@ -582,6 +597,267 @@ void mtp_enqueue(Enq& q, int T, const int* ids, const float* h_rows, bool head, 
 
 // ====================================================================== C ABI
 extern "C" {
+
+// ---- persistent decode program ------------------------------------------------
+
+struct PkSegIn {
+  const DevT* w;
+  const DevT* w2;
+  float* out;
+  int epi;
+};
+
+// Fills the GEMV fields of a stage; false (with pk_why) when the shapes do
+// not meet the ring's copy rules.
+static bool pk_gemv_stage(kib_qwen35* m, PkStage& S, int kind, const std::vector<PkSegIn>& segs, int grid) {
+  const int type = segs[0].w->type;
+  const int cols = segs[0].w->cols();
+  if (type != kTypeQ4K && type != kTypeQ6K) {
+    m->pk_why = "matrix type other than Q4_K / Q6_K";
+    return false;
+  }
+  if (cols % 256 || cols > kPkMaxCols || static_cast<int>(segs.size()) > kPkMaxSegs) {
+    m->pk_why = "unsupported GEMV shape";
+    return false;
+  }
+  const int row_bytes = cols / 256 * kquant_block_bytes(type);
+  int g = 1;
+  while ((static_cast<long>(g) * row_bytes) % 16) ++g;  // rows per 16-byte aligned piece
+  S.kind = kind;
+  S.type = type;
+  S.cols = cols;
+  S.row_bytes = row_bytes;
+  S.nseg = 0;
+  S.paired = segs[0].w2 != nullptr;
+  int rows = 0;
+  for (const PkSegIn& in : segs) {
+    if (in.w->type != type || in.w->cols() != cols || (in.w2 != nullptr) != (S.paired != 0)) {
+      m->pk_why = "segments of one stage differ in type or shape";
+      return false;
+    }
+    const int r = in.w->rows();
+    if (r % g || reinterpret_cast<uintptr_t>(in.w->p) % 16 || (in.w2 && reinterpret_cast<uintptr_t>(in.w2->p) % 16)) {
+      m->pk_why = "segment rows/base not aligned for bulk copies";
+      return false;
+    }
+    PkSeg& sg = S.seg[S.nseg++];
+    sg.w = in.w->p;
+    sg.w2 = in.w2 ? in.w2->p : nullptr;
+    sg.out = in.out;
+    sg.row_begin = rows;
+    sg.rows = r;
+    sg.epi = in.epi;
+    rows += r;
+  }
+  S.rows = rows;
+  const int cap = (kPkSlotBytes / (S.paired ? 2 : 1)) / row_bytes / g * g;
+  int want = (rows + grid - 1) / grid;
+  want = (want + g - 1) / g * g;
+  S.tile_rows = std::max(g, std::min(cap, want));
+  S.ntiles = (rows + S.tile_rows - 1) / S.tile_rows;
+  const int units = cols / 64;
+  S.rg = units <= 16 ? 16 : units <= 32 ? 32 : 64;
+  S.eps = m->eps;
+  return cap >= g;
+}
+
+static int build_pk(kib_qwen35* m) {
+  m->pk_on = false;
+  if (const char* e = std::getenv("KIB_PERSISTENT"); e && e[0] == '0') {
+    m->pk_why = "disabled by KIB_PERSISTENT=0";
+    return KIB_OK;
+  }
+  const int grid = m->ctx->num_sms;
+  if (m->convk != 4 || m->hd != kHd || m->lhd != 128 || m->heads != 4 * m->kvh || m->kvh < 1 ||
+      grid / m->kvh > kPkMaxSplits || grid < m->lvh * (128 / kPkGdnRows) / 2) {
+    m->pk_why = "model shape outside the persistent kernel's limits";
+    return KIB_OK;
+  }
+  int coop = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->ctx->device);
+  const int nsplit = grid / m->kvh;
+  std::vector<PkStage> st;
+  auto add = [&](const PkStage& S) { st.push_back(S); };
+  bool first = true;
+  auto prologue_in = [&](PkStage& S, const DevT& norm) {
+    S.norm_w = norm.f();
+    if (first) {
+      S.prologue = kProEmbed;
+      S.emb = m->tok_embd.p;
+      S.emb_type = m->tok_embd.type;
+      S.emb_rows = m->V;
+      S.emb_out = m->d_h;
+      if (m->tok_embd.cols() != m->H) return false;
+      first = false;
+    } else {
+      S.prologue = kProRms;
+      S.in = m->d_h;
+    }
+    return true;
+  };
+  for (const LayerW& L : m->layers) {
+    const int li = L.cache_index;
+    if (L.kind == 0) {
+      PkStage a = {};
+      if (!pk_gemv_stage(m, a, kPkGemv,
+                         {{&L.qkv, nullptr, m->d_qkv, kEpiConv},
+                          {&L.zgate, nullptr, m->d_z, kEpiStore},
+                          {&L.beta, nullptr, m->d_beta, kEpiStore},
+                          {&L.alpha, nullptr, m->d_alpha, kEpiStore}},
+                         grid) ||
+          !prologue_in(a, L.attn_norm))
+        return KIB_OK;
+      a.conv_state = m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1);
+      a.conv_w = L.conv1d.f();
+      a.barrier_after = 1;
+      add(a);
+      PkStage g = {};
+      g.kind = kPkGdn;
+      g.conv_out = m->d_qkv;
+      g.C = m->C;
+      g.beta_raw = m->d_beta;
+      g.alpha_raw = m->d_alpha;
+      g.dt_bias = L.dt_bias.f();
+      g.ssm_a = L.ssm_a.f();
+      g.state = m->d_s + static_cast<size_t>(li) * m->lvh * m->lhd * m->lhd;
+      g.gdn_out = m->d_y;
+      g.key_heads = m->lkh;
+      g.value_heads = m->lvh;
+      g.eps = m->eps;
+      g.barrier_after = 1;
+      add(g);
+      PkStage o = {};
+      if (!pk_gemv_stage(m, o, kPkGemv, {{&L.ssm_out, nullptr, m->d_h1, kEpiResidual}}, grid)) return KIB_OK;
+      o.prologue = kProNormGate;
+      o.in = m->d_y;
+      o.gate = m->d_z;
+      o.norm_w = L.ssm_norm.f();
+      o.head_dim = m->lhd;
+      o.resid = m->d_h;
+      o.barrier_after = 1;
+      add(o);
+    } else {
+      const size_t off = static_cast<size_t>(li) * m->cap * m->KD;
+      PkStage a = {};
+      if (!pk_gemv_stage(m, a, kPkGemv,
+                         {{&L.q, nullptr, m->d_qg, kEpiStore},
+                          {&L.k, nullptr, m->d_kp, kEpiStore},
+                          {&L.v, nullptr, m->d_vp, kEpiStore}},
+                         grid) ||
+          !prologue_in(a, L.attn_norm))
+        return KIB_OK;
+      a.barrier_after = 1;
+      add(a);
+      PkStage t = {};
+      t.kind = kPkAttn;
+      t.qg = m->d_qg;
+      t.kp = m->d_kp;
+      t.vp = m->d_vp;
+      t.q_norm = L.q_norm.f();
+      t.k_norm = L.k_norm.f();
+      t.kcache = m->d_k + off;
+      t.vcache = m->d_v + off;
+      t.heads = m->heads;
+      t.kv_heads = m->kvh;
+      t.eps = m->eps;
+      t.theta = m->theta;
+      t.n_dims = 2 * (m->sections[0] + m->sections[1] + m->sections[2] + m->sections[3]);
+      t.nsplit = nsplit;
+      t.part = m->d_pk_part;
+      t.att_out = m->d_att;
+      t.barrier_after = 1;
+      add(t);
+      PkStage mg = t;
+      mg.kind = kPkMerge;
+      add(mg);
+      PkStage o = {};
+      if (!pk_gemv_stage(m, o, kPkGemv, {{&L.o, nullptr, m->d_h1, kEpiResidual}}, grid)) return KIB_OK;
+      o.prologue = kProPlain;
+      o.in = m->d_att;
+      o.resid = m->d_h;
+      o.barrier_after = 1;
+      add(o);
+    }
+    PkStage f = {};
+    if (L.ffn_gate.type != L.ffn_up.type ||
+        !pk_gemv_stage(m, f, kPkGemv, {{&L.ffn_gate, &L.ffn_up, m->d_act, kEpiSiluMul}}, grid)) {
+      if (m->pk_why.empty()) m->pk_why = "ffn gate/up types differ";
+      return KIB_OK;
+    }
+    f.prologue = kProRms;
+    f.in = m->d_h1;
+    f.norm_w = L.post_norm.f();
+    f.barrier_after = 1;
+    add(f);
+    PkStage d = {};
+    if (!pk_gemv_stage(m, d, kPkGemv, {{&L.ffn_down, nullptr, m->d_h, kEpiResidual}}, grid)) return KIB_OK;
+    d.prologue = kProPlain;
+    d.in = m->d_act;
+    d.resid = m->d_h1;
+    d.barrier_after = 1;
+    add(d);
+  }
+  PkStage h = {};
+  if (!pk_gemv_stage(m, h, kPkHead, {{&head_weight(m), nullptr, nullptr, kEpiArgmax}}, grid)) return KIB_OK;
+  h.prologue = kProRms;
+  h.in = m->d_h;
+  h.norm_w = m->output_norm.f();
+  add(h);
+  for (auto& S : st) S.eps = m->eps;
+  if (cudaMalloc(&m->d_pk, st.size() * sizeof(PkStage)) != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, "pk alloc");
+  ENG_CUDA(cudaMemcpy(m->d_pk, st.data(), st.size() * sizeof(PkStage), cudaMemcpyHostToDevice));
+  m->pk_n = static_cast<int>(st.size());
+  m->pk_grid = grid;
+  m->pk_coop = coop != 0;
+  ENG_CUDA(cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kPkSmemBytes)));
+  m->pk_on = true;
+  m->pk_why.clear();
+  return KIB_OK;
+}
+
+static PkProgram pk_program(kib_qwen35* m) {
+  PkProgram P = {};
+  P.stages = m->d_pk;
+  P.nstages = m->pk_n;
+  P.pos = m->d_pos;
+  P.token = m->d_tokens;
+  P.token_log = m->d_log;
+  P.step = m->d_step;
+  P.prob_out = nullptr;
+  P.bar_ctr = m->d_pk_ctr;
+  P.head_ctr = m->d_pk_ctr + 1;
+  P.cand_max = m->d_pk_cmax;
+  P.cand_sum = m->d_pk_csum;
+  P.cand_idx = m->d_pk_cidx;
+  P.err = m->ctx->d_err;
+  P.trace = m->trace_on ? m->d_pk_trace : nullptr;
+  return P;
+}
+
+static cudaError_t pk_launch(kib_qwen35* m, cudaStream_t st) {
+  PkProgram P = pk_program(m);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(m->pk_grid);
+  cfg.blockDim = dim3(kPkThreads);
+  cfg.dynamicSmemBytes = kPkSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (m->pk_coop) {
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, decode_persistent_kernel, P);
+}
 
 int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* opt, kib_qwen35** out) {
   if (!ctx || !path || !out) return KIB_ERR_INVALID_ARGUMENT;
@@ -792,6 +1068,19 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
     m->trace_on = cudaMalloc(&m->d_trace, 4096 * 8 * sizeof(unsigned long long)) == cudaSuccess;
   }
   cudaMemset(m->d_head_cnt, 0, 4 * sizeof(unsigned));
+  if (dalloc(&m->d_pk_ctr, 2) != cudaSuccess ||
+      dalloc(&m->d_pk_part, static_cast<size_t>(kPkMaxSplits) * m->heads * (kHd + 2)) != cudaSuccess ||
+      dalloc(&m->d_pk_cmax, 1024) != cudaSuccess || dalloc(&m->d_pk_csum, 1024) != cudaSuccess ||
+      dalloc(&m->d_pk_cidx, 1024) != cudaSuccess || dalloc(&m->d_pk_trace, 4096) != cudaSuccess) {
+    kib_qwen35_free(mp.release());
+    return set_error(ctx, KIB_ERR_INTERNAL, "persistent decode allocation failed");
+  }
+  cudaMemset(m->d_pk_ctr, 0, 2 * sizeof(unsigned));
+  if (build_pk(m) != KIB_OK) {
+    std::string why = m->err;
+    kib_qwen35_free(mp.release());
+    return set_error(ctx, KIB_ERR_INTERNAL, "persistent decode set-up failed: " + why);
+  }
   *out = mp.release();
   return kib_qwen35_reset(*out);
 }
@@ -803,6 +1092,10 @@ void kib_qwen35_free(kib_qwen35* m) {
     if (g) cudaGraphExecDestroy(g);
   if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
   if (m->mtp_graph) cudaGraphExecDestroy(m->mtp_graph);
+  if (m->pk_graph) cudaGraphExecDestroy(m->pk_graph);
+  void* pk_ptrs[] = {m->d_pk, m->d_pk_ctr, m->d_pk_part, m->d_pk_cmax, m->d_pk_csum, m->d_pk_cidx, m->d_pk_trace};
+  for (void* p : pk_ptrs)
+    if (p) cudaFree(p);
   void* ptrs[] = {m->d_weights, m->d_k, m->d_v, m->d_mk, m->d_mv, m->d_r, m->d_s, m->d_r_snap, m->d_s_snap,
                   m->d_pending_h, m->d_h, m->d_h1, m->d_qkv, m->d_z, m->d_beta, m->d_alpha, m->d_y, m->d_act,
                   m->d_act2, m->d_qg, m->d_kp, m->d_vp, m->d_att, m->d_qout, m->d_norm, m->d_norm2, m->d_hn,
@@ -928,7 +1221,17 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   if (m->pos + steps > static_cast<uint64_t>(m->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "decode exceeds cache capacity");
   if (steps > (1u << 20)) return KIB_ERR_INVALID_ARGUMENT;
   cudaStream_t st = m->ctx->stream;
-  if (!m->decode_graph) {
+  const bool use_pk = m->pk_on;
+  if (use_pk && !m->pk_graph) {
+    int rc = capture(m, &m->pk_graph, [&](Enq& q) { q.run(pk_launch(m, q.st), "decode_persistent"); });
+    if (rc && m->pk_coop) {  // the cooperative attribute is not accepted together with PDL on every driver
+      cudaGetLastError();
+      m->pk_coop = false;
+      rc = capture(m, &m->pk_graph, [&](Enq& q) { q.run(pk_launch(m, q.st), "decode_persistent"); });
+    }
+    if (rc) return rc;
+  }
+  if (!use_pk && !m->decode_graph) {
     int rc = capture(m, &m->decode_graph, [&](Enq& q) {
       q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, m->d_tokens, 1, m->d_h, m->H, q.st), "embed");
       main_layers_small(q, 1, m->d_pos);
@@ -944,12 +1247,33 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   ENG_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, st));
   ENG_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_pin + 1, sizeof(int), cudaMemcpyHostToDevice, st));
   ENG_CUDA(cudaMemcpyAsync(m->d_step, m->h_pin + 2, sizeof(int), cudaMemcpyHostToDevice, st));
-  for (uint64_t i = 0; i < steps; ++i) ENG_CUDA(cudaGraphLaunch(m->decode_graph, st));
+  cudaGraphExec_t g = use_pk ? m->pk_graph : m->decode_graph;
+  for (uint64_t i = 0; i < steps; ++i) ENG_CUDA(cudaGraphLaunch(g, st));
   if (tokens_out) ENG_CUDA(cudaMemcpyAsync(tokens_out, m->d_log, steps * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
   int rc = sync_check(m, "decode");
-  if (rc) return rc;
+  if (rc) {
+    if (use_pk) cudaMemset(m->d_pk_ctr, 0, 2 * sizeof(unsigned));  // an aborted step leaves its tickets behind
+    return rc;
+  }
   m->pos += steps;
-  if (m->trace_on && m->d_trace && m->trace_used > 0) {
+  if (use_pk && m->trace_on) {
+    // stage start times of CTA 0 in the last step: CSV to $KIB_TRACE_OUT
+    std::vector<unsigned long long> h(m->pk_n + 1);
+    std::vector<PkStage> stages(m->pk_n);
+    cudaMemcpy(h.data(), m->d_pk_trace, h.size() * 8, cudaMemcpyDeviceToHost);
+    cudaMemcpy(stages.data(), m->d_pk, stages.size() * sizeof(PkStage), cudaMemcpyDeviceToHost);
+    const char* path = std::getenv("KIB_TRACE_OUT");
+    FILE* f = path ? std::fopen(path, "w") : nullptr;
+    if (f) {
+      static const char* names[] = {"gemv", "gdn", "attn", "merge", "head"};
+      std::fprintf(f, "stage,kind,type,rows,cols,start_ns,dur_ns\n");
+      for (int i = 0; i < m->pk_n; ++i)
+        std::fprintf(f, "%d,%s,%d,%d,%d,%llu,%llu\n", i, names[stages[i].kind], stages[i].type, stages[i].rows,
+                     stages[i].cols, h[i] - h[0], h[i + 1] - h[i]);
+      std::fclose(f);
+    }
+  }
+  if (!use_pk && m->trace_on && m->d_trace && m->trace_used > 0) {
     // timeline of the last replayed step(s) merged: CSV to $KIB_TRACE_OUT
     std::vector<unsigned long long> h(8 * static_cast<size_t>(m->trace_used));
     cudaMemcpy(h.data(), m->d_trace, h.size() * 8, cudaMemcpyDeviceToHost);

@@ -82,6 +82,22 @@ KIB_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
       : "memory");
 }
 
+// Same copy for data streamed exactly once per step (weights): the lines are
+// marked evict-first in L2, so the stream does not push out what the step
+// re-reads (activations, KV cache, recurrent state).
+KIB_DEV uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+KIB_DEV void bulk_g2s_stream(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
 KIB_DEV void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 // ------------------------------------------------------------------ trace

@@ -142,3 +142,46 @@ def test_generate_stops_at_eos(ctx, small_model):
     gt2, res = m.generate(p, 20, eos_token_id=eos)
     assert list(gt2) == list(gt[:list(gt).index(eos)]) and res.finish_reason_stop == 1
     m.close()
+
+
+def _decode_tokens(ctx, path, prompt_ids, steps, persistent, monkeypatch, **kw):
+    monkeypatch.setenv("KIB_PERSISTENT", "1" if persistent else "0")
+    m = kib.Qwen35(ctx, path, **kw)
+    nxt = m.prefill(prompt_ids)
+    toks = m.decode_greedy(nxt, steps)
+    m.close()
+    return nxt, list(toks)
+
+
+def test_persistent_decode_matches_per_kernel_path(ctx, small_model, monkeypatch):
+    """The one-launch-per-token decode and the per-kernel graph give the same
+    greedy tokens."""
+    p = prompt(30, SMALL["vocab"], 7)
+    a = _decode_tokens(ctx, small_model, p, 40, True, monkeypatch, context_tokens=256, decode_tokens=64)
+    b = _decode_tokens(ctx, small_model, p, 40, False, monkeypatch, context_tokens=256, decode_tokens=64)
+    assert a == b
+
+
+FULL_WIDTH = dict(hidden=1024, layers=4, intermediate=3584, vocab=8192, heads=8, kv_heads=2, head_dim=256,
+                  ssm_heads=16, ssm_head_dim=128, nextn_layers=0, threads=16, seed=77)
+
+
+@pytest.fixture(scope="module")
+def full_width_model(tmp_path_factory):
+    path = str(tmp_path_factory.mktemp("fw") / "full_width.gguf")
+    kib.write_synthetic_qwen35(path, **FULL_WIDTH)
+    return path
+
+
+def test_persistent_decode_full_width_matches_oracle(ctx, oracle, full_width_model, monkeypatch):
+    """Decode at the benchmark's layer widths (hidden 1024, FFN 3584, 16 GDN
+    heads, 8/2 attention heads of 256): greedy tokens identical to the oracle."""
+    p = prompt(160, FULL_WIDTH["vocab"], 3)
+    nxt, toks = _decode_tokens(ctx, full_width_model, p, 24, True, monkeypatch, context_tokens=512,
+                               decode_tokens=64)
+    om = oracle_lib.OracleModel(oracle, full_width_model, 512)
+    _, _, lg = om.forward(p, 0)
+    assert nxt == int(np.argmax(lg[-1]))
+    otoks, _ = om.generate_from(160, nxt, 25, mtp_draft_tokens=0)
+    om.close()
+    assert toks == list(otoks[1:25])
