@@ -1,8 +1,8 @@
 // decode_persistent.cuh -- one launch per decode token (T = 1).
 //
-// The whole bs1 decode step of the hybrid decoder (embedding, 24 layers of
-// GDN or attention blocks with their FFNs, the fused LM-head argmax) runs as a
-// single persistent grid: one CTA per SM, eight consumer warps and one
+// The bs1 decode step of the hybrid decoder after the token embedding (24
+// layers of GDN or attention blocks with their FFNs, the fused LM-head argmax)
+// runs as a single persistent grid: one CTA per SM, eight consumer warps and one
 // producer warp.  The step is a host-built list of stages (PkStage); between
 // dependent stages the consumers meet at a grid barrier.  The producer warp
 // walks the same list independently and streams everything the consumers will
@@ -15,8 +15,8 @@
 //
 // Stage kinds and the reference ops they carry (the same fused groups as the
 // per-kernel path in kquant_gemv2.cuh / layer_kernels.cuh):
-//   kPkGemv / kPkHead  K-quant matvec with a prologue (input, RMSNorm, per-head
-//                      norm-gate, or the token embedding + RMSNorm) and
+//   kPkGemv / kPkHead  K-quant matvec with a prologue (input, RMSNorm or per-head
+//                      norm-gate) and
 //                      per-segment epilogues (store, residual add, conv+silu,
 //                      silu*up, argmax) -- q*_k_matvec, mps_backend.mm:295-463;
 //                      rms_norm 1891-1921; ssm_conv 2376-2457; argmax 2681-2779
@@ -55,7 +55,6 @@ constexpr int kPkMaxSplits = 128;
 constexpr int kPkGdnRows = 16;  // state rows per GDN item
 
 enum PkKind : int { kPkGemv = 0, kPkGdn = 1, kPkAttn = 2, kPkMerge = 3, kPkHead = 4 };
-constexpr int kProEmbed = 3;  // prologue: x = dequantised embedding row of the current token, then RMSNorm
 
 struct PkSeg {
   const uint8_t* w;   // this segment's rows (row_bytes each)
@@ -90,10 +89,6 @@ struct __align__(16) PkStage {
   const float* resid;  // kEpiResidual: resid[row]
   float* conv_state;   // kEpiConv: [rows][3]
   const float* conv_w; // kEpiConv: [rows][4]
-  const uint8_t* emb;  // kProEmbed: embedding matrix (emb_type rows of `cols`)
-  int emb_type;
-  int emb_rows;
-  float* emb_out;      // kProEmbed: CTA 0 stores the raw embedding row here
   // ---- GDN (one token)
   const float* conv_out;
   int C;
@@ -136,7 +131,7 @@ struct PkProgram {
   float* cand_sum;
   int* cand_idx;
   int* err;
-  unsigned long long* trace;  // optional: [nstages + 1] stage start times of CTA 0
+  unsigned long long* trace;  // optional: CTA 0's [stage][start, prologue done, first tile, done]
 };
 
 struct PkShared {
@@ -150,7 +145,7 @@ struct PkShared {
   int bidx[16];
   int abort;
   int last;
-  __align__(16) float xs[kPkMaxCols];  // stage input vector; attention/GDN scratch
+  __align__(16) float xs[kPkMaxCols + kPkMaxCols / 16];  // padded stage input; attention/GDN scratch
   float ws[kPkMaxSplits];
   float ls[kPkMaxSplits];
 };
@@ -195,6 +190,7 @@ struct PkProducer {
     int ok = 1;
     if (lane == 0) {
       ok = 0;
+      #pragma unroll 1
       for (uint32_t i = 0; i < (1u << 22); ++i) {
         if (mbar_try_wait(&sh->empty[slot], parity)) {
           ok = 1;
@@ -227,16 +223,22 @@ KIB_DEV void pk_produce(const PkProgram& P, PkProducer& pr) {
   const int lane = pr.lane;
   const int grid = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
   int pos = -1;
+  #pragma unroll 1
   for (int s = 0; s < P.nstages; ++s) {
     const PkStage& S = P.stages[s];
     const int kind = S.kind;
+    const uint32_t seq0 = pr.seq;
+    unsigned long long* tr = (P.trace && cta == 0 && lane == 0) ? P.trace + 16 * s : nullptr;
+    if (tr) tr[6] = gtimer();  // producer reached the stage
     if (kind == kPkGemv || kind == kPkHead) {
+      #pragma unroll 1
       for (int t = cta; t < S.ntiles; t += grid) {
         uint8_t* dst = pr.acquire();
         if (!dst) return;
         const int r0 = t * S.tile_rows;
         const int nr = min(S.tile_rows, S.rows - r0);
         pr.expect(pk_tile_bytes(S, r0, nr));
+        if (tr && pr.seq == seq0) tr[7] = gtimer();  // first tile issued
         if (lane < S.nseg) {
           const PkSeg& g = S.seg[lane];
           const int a = max(r0, g.row_begin), b = min(r0 + nr, g.row_begin + g.rows);
@@ -253,6 +255,7 @@ KIB_DEV void pk_produce(const PkProgram& P, PkProducer& pr) {
       }
     } else if (kind == kPkGdn) {
       const int items = S.value_heads * (128 / kPkGdnRows);
+      #pragma unroll 1
       for (int it = cta; it < items; it += grid) {
         pr.dep_wait();  // the state was written by the previous step
         uint8_t* dst = pr.acquire();
@@ -273,6 +276,7 @@ KIB_DEV void pk_produce(const PkProgram& P, PkProducer& pr) {
       chunk = (chunk + 7) & ~7;
       const int kb = split * chunk, old_end = min(kb + chunk, pos);
       const int kvd = S.kv_heads * kHd;
+      #pragma unroll 1
       for (int k0 = kb; k0 < old_end; k0 += kAttnChunk) {
         uint8_t* dst = pr.acquire();
         if (!dst) return;
@@ -297,6 +301,8 @@ struct PkCons {
   PkShared* sh;
   uint32_t seq = 0;
   int* err;
+  unsigned long long* tr = nullptr;  // trace of the current stage (CTA 0, thread 0) or null
+  bool first = true;
 
   // Waits for the next ring slot (all consumer threads); null on abort.
   KIB_DEV const uint8_t* take() {
@@ -304,6 +310,10 @@ struct PkCons {
     if (!mbar_wait_bounded(&sh->full[slot], (seq / kPkSlots) & 1u, err)) {
       sh->abort = 1;
       return nullptr;
+    }
+    if (tr && first) {
+      tr[2] = gtimer();
+      first = false;
     }
     return ring + static_cast<size_t>(slot) * kPkSlotBytes;
   }
@@ -317,10 +327,9 @@ struct PkCons {
 
 // Grid barrier of the consumer warps of all CTAs.  Returns false on abort.
 KIB_DEV bool pk_grid_sync(const PkProgram& P, PkShared* sh, unsigned target) {
-  pk_sync();
+  pk_sync();  // the CTA's writes happen before thread 0's release below
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(P.bar_ctr, 1u);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.bar_ctr) : "memory");
     uint32_t i = 0;
     while (ld_acquire_u32(P.bar_ctr) < target) {
       ++i;
@@ -334,7 +343,6 @@ KIB_DEV bool pk_grid_sync(const PkProgram& P, PkShared* sh, unsigned target) {
         break;
       }
     }
-    __threadfence();
   }
   pk_sync();
   return !*reinterpret_cast<volatile int*>(&sh->abort);
@@ -343,88 +351,124 @@ KIB_DEV bool pk_grid_sync(const PkProgram& P, PkShared* sh, unsigned target) {
 KIB_DEV void pk_copy_desc(PkStage* dst, const PkStage* src) {
   constexpr int n = static_cast<int>(sizeof(PkStage) / 16);
   static_assert(sizeof(PkStage) % 16 == 0, "PkStage must be a multiple of 16 bytes");
+  static_assert(n <= kPkConsumers, "one descriptor word per consumer thread");
+  #pragma unroll 1
   for (int i = threadIdx.x; i < n; i += kPkConsumers)
     reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
 }
 
 // ---- GEMV prologue: the stage's transformed input vector into sh->xs
-template <int ET>
-KIB_DEV void pk_embed_units(const PkStage& S, int token, float* xs) {
-  const int units = S.cols / 64;
-  for (int gu = threadIdx.x; gu < units; gu += kPkConsumers) {
-    const int blk = gu >> 2, u = gu & 3;
-    float v[64];
-    if (token < 0 || token >= S.emb_rows) {
-#pragma unroll
-      for (int e = 0; e < 64; ++e) v[e] = 0.0f;
-    } else {
-      const uint8_t* b =
-          S.emb + (static_cast<size_t>(token) * (S.cols / 256) + blk) * static_cast<size_t>(kquant_block_bytes(ET));
-      unit_dequant<ET>(b, u, v);
-    }
-#pragma unroll
-    for (int e = 0; e < 64; ++e) xs[256 * blk + unit_col<ET>(u, e)] = v[e];
-  }
-}
+// The stage input lives in shared memory with 4 floats of padding after every
+// 64: the 16 lanes of a row group read their units (64 consecutive inputs for
+// Q4_K) at a stride of 68 floats, which spreads them over the banks.
+KIB_DEV int xpad(int i) { return i + 4 * (i >> 6); }
 
-KIB_DEV void pk_prologue(const PkStage& S, PkShared* sh, int token) {
+// Prologue: every thread issues all of its loads (input, norm weights, gate)
+// before the first reduction, so the stage start costs one memory round trip.
+KIB_DEV void pk_prologue(const PkStage& S, PkShared* sh) {
   float* xs = sh->xs;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cols = S.cols;
   if (S.prologue == kProNormGate) {
-    // qk_norm over heads of head_dim (= 128: one warp covers one head per
-    // pass), silu(gate), mul (qwen35_runtime.cpp:2993-3003)
-    const int hd = S.head_dim;
+    // qk_norm over heads of 128 (one warp per head), silu(gate), mul
+    // (qwen35_runtime.cpp:2993-3003)
+    constexpr int hd = 128;
+    const float4 w = *reinterpret_cast<const float4*>(S.norm_w + 4 * lane);
+#pragma unroll 1
     for (int base = warp * hd; base < cols; base += kPkWarps * hd) {
-      float ss = 0.0f;
-      for (int i = lane; i < hd; i += 32) {
-        const float v = S.in[base + i];
-        ss += v * v;
-      }
-      ss = warp_sum(ss);
+      const float4 y = *reinterpret_cast<const float4*>(S.in + base + 4 * lane);
+      const float4 z = *reinterpret_cast<const float4*>(S.gate + base + 4 * lane);
+      const float ss = warp_sum((y.x * y.x + y.y * y.y) + (y.z * y.z + y.w * y.w));
       const float scale = 1.0f / sqrtf(ss / static_cast<float>(hd) + S.eps);
-      for (int i = lane; i < hd; i += 32) {
-        const float v = S.in[base + i] * (scale * S.norm_w[i]);
-        xs[base + i] = v * silu_f(S.gate[base + i]);
-      }
+      float4 o;
+      o.x = y.x * (scale * w.x) * silu_f(z.x);
+      o.y = y.y * (scale * w.y) * silu_f(z.y);
+      o.z = y.z * (scale * w.z) * silu_f(z.z);
+      o.w = y.w * (scale * w.w) * silu_f(z.w);
+      *reinterpret_cast<float4*>(xs + xpad(base + 4 * lane)) = o;
     }
     pk_sync();
     return;
   }
+  constexpr int kPer = kPkMaxCols / (4 * kPkConsumers);  // float4 per thread
+  float4 v[kPer], w[kPer];
   float ss = 0.0f;
-  if (S.prologue == kProEmbed) {
-    switch (S.emb_type) {
-      case kTypeQ4K: pk_embed_units<kTypeQ4K>(S, token, xs); break;
-      case kTypeQ5K: pk_embed_units<kTypeQ5K>(S, token, xs); break;
-      default: pk_embed_units<kTypeQ6K>(S, token, xs); break;
+  const bool rms = S.prologue == kProRms;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = 4 * tid + 4 * kPkConsumers * k;
+    if (i < cols) {
+      v[k] = *reinterpret_cast<const float4*>(S.in + i);
+      if (rms) w[k] = *reinterpret_cast<const float4*>(S.norm_w + i);
     }
+  }
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = 4 * tid + 4 * kPkConsumers * k;
+    if (i < cols) ss += (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
+  }
+  float scale = 1.0f;
+  if (rms) {
+    // rms_norm_f32_f32_batched (mps_backend.mm:1891-1921): x * rsqrt(mean(x^2)+eps) * w
+    ss = warp_sum(ss);
+    if (lane == 0) sh->red[warp][0] = ss;
     pk_sync();
-    for (int i = tid * 4; i < cols; i += kPkConsumers * 4) {
-      const float4 v = *reinterpret_cast<const float4*>(xs + i);
-      if (blockIdx.x == 0) *reinterpret_cast<float4*>(S.emb_out + i) = v;
-      ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+    float tot = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kPkWarps; ++q) tot += sh->red[q][0];
+    scale = 1.0f / sqrtf(tot / static_cast<float>(cols) + S.eps);
+  }
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = 4 * tid + 4 * kPkConsumers * k;
+    if (i < cols) {
+      float4 o = v[k];
+      if (rms) {
+        o.x = o.x * scale * w[k].x;
+        o.y = o.y * scale * w[k].y;
+        o.z = o.z * scale * w[k].z;
+        o.w = o.w * scale * w[k].w;
+      }
+      *reinterpret_cast<float4*>(xs + xpad(i)) = o;
+    }
+  }
+  pk_sync();
+}
+
+// x values of unit u of block blk from the padded stage input (element order
+// as unit_col, group sums as load_unit_x).
+template <int QT>
+KIB_DEV void pk_load_unit_x(const float* xs, int blk, int u, UnitX<QT>& ux) {
+  if (QT == kTypeQ6K) {
+    const int c = u >> 1, r = u & 1;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4* p = reinterpret_cast<const float4*>(xs + 68 * (4 * blk + 2 * c + (k >> 1)) + 32 * (k & 1) + 16 * r);
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 f = p[j];
+        ux.v[8 * k + 2 * j] = make_float2(f.x, f.y);
+        ux.v[8 * k + 2 * j + 1] = make_float2(f.z, f.w);
+        s += (f.x + f.y) + (f.z + f.w);
+      }
+      ux.s[k] = s;
     }
   } else {
-    for (int i = tid * 4; i < cols; i += kPkConsumers * 4) {
-      const float4 v = *reinterpret_cast<const float4*>(S.in + i);
-      *reinterpret_cast<float4*>(xs + i) = v;
-      ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+    const float4* p = reinterpret_cast<const float4*>(xs + 68 * (4 * blk + u));
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 f = p[8 * g + j];
+        ux.v[16 * g + 2 * j] = make_float2(f.x, f.y);
+        ux.v[16 * g + 2 * j + 1] = make_float2(f.z, f.w);
+        s += (f.x + f.y) + (f.z + f.w);
+      }
+      ux.s[g] = s;
     }
   }
-  if (S.prologue == kProPlain) {
-    pk_sync();
-    return;
-  }
-  // rms_norm_f32_f32_batched (mps_backend.mm:1891-1921): x * rsqrt(mean(x^2)+eps) * w
-  ss = warp_sum(ss);
-  if (lane == 0) sh->red[warp][0] = ss;
-  pk_sync();
-  float tot = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kPkWarps; ++w) tot += sh->red[w][0];
-  const float scale = 1.0f / sqrtf(tot / static_cast<float>(cols) + S.eps);
-  for (int i = tid; i < cols; i += kPkConsumers) xs[i] = xs[i] * scale * S.norm_w[i];
-  pk_sync();
 }
 
 struct PkArgmax {
@@ -459,8 +503,28 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, PkArgmax& am) {
   const bool active = gl < S.cols / 64;
   const int blk = gl >> 2, u = gl & 3;
   UnitX<QT> ux[1];
-  if (active) load_unit_x<QT>(cs.sh->xs + 256 * blk, u, ux[0]);
+  if (cs.tr) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "r"(blk));
+    cs.tr[8] = t;
+  }
+  if (active) pk_load_unit_x<QT>(cs.sh->xs, blk, u, ux[0]);
+  if (cs.tr) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(ux[0].v[31].y));
+    cs.tr[9] = t;
+    UnitX<QT> ux2;
+    pk_load_unit_x<QT>(cs.sh->xs, blk, u ^ 1, ux2);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(ux2.v[31].y));
+    cs.tr[10] = t;
+  }
+  if (cs.tr) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(ux[0].v[31].y));
+    cs.tr[4] = t;
+  }
   const int grid = static_cast<int>(gridDim.x);
+  #pragma unroll 1
   for (int t = static_cast<int>(blockIdx.x); t < S.ntiles; t += grid) {
     const uint8_t* tile = cs.take();
     if (!tile) return false;
@@ -493,8 +557,13 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, PkArgmax& am) {
       float acc[1] = {0.0f}, acc2[1] = {0.0f};
       if (ok && active) {
         const uint8_t* b0 = tile + static_cast<size_t>(rl) * S.row_bytes + blk * BB;
-        unit_dot<QT, 1>(b0, u, ux, acc);
-        if (S.paired) unit_dot<QT, 1>(b0 + kPkSlotBytes / 2, u, ux, acc2);
+        // gate and up rows of a pair run through one copy of the dot code
+#pragma unroll 1
+        for (int hh = 0; hh <= S.paired; ++hh) {
+          float a[1] = {0.0f};
+          unit_dot<QT, 1>(b0 + hh * (kPkSlotBytes / 2), u, ux, a);
+          if (hh == 0) acc[0] = a[0]; else acc2[0] = a[0];
+        }
       }
       const int lim = RG < 32 ? RG : 32;
       for (int o = lim / 2; o > 0; o >>= 1) {
@@ -508,6 +577,7 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, PkArgmax& am) {
         }
         pk_sync();
         if (gl == 0) {
+          #pragma unroll 1
           for (int w = 1; w < RG / 32; ++w) {
             acc[0] += cs.sh->red[warp + w][0];
             acc2[0] += cs.sh->red[warp + w][1];
@@ -556,6 +626,7 @@ KIB_DEV bool pk_gdn(const PkStage& S, PkCons& cs) {
   const int items = S.value_heads * (D / kPkGdnRows);
   const int key_dim = S.key_heads * D;
   const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  #pragma unroll 1
   for (int it = static_cast<int>(blockIdx.x); it < items; it += static_cast<int>(gridDim.x)) {
     const int h = it / (D / kPkGdnRows), grp = it % (D / kPkGdnRows);
     const int kh = h % S.key_heads;
@@ -618,18 +689,21 @@ KIB_DEV bool pk_gdn(const PkStage& S, PkCons& cs) {
 
 // qk_norm (mps_backend.mm:1991-2024) then mrope (2482-2527) of one 256-wide
 // head vector; text positions (all MRoPE streams equal); one warp.
-KIB_DEV void pk_norm_rope(float* v, const float* in, const float* w, float eps, float theta, int n_dims, int position,
+__device__ __noinline__ void pk_norm_rope(float* v, const float* in, const float* w, float eps, float theta, int n_dims, int position,
                           int lane) {
   float ss = 0.0f;
+  #pragma unroll 1
   for (int i = lane; i < kHd; i += 32) {
     const float x = in[i];
     ss += x * x;
   }
   ss = warp_sum(ss);
   const float scale = 1.0f / sqrtf(ss / static_cast<float>(kHd) + eps);
+  #pragma unroll 1
   for (int i = lane; i < kHd; i += 32) v[i] = in[i] * (scale * w[i]);
   __syncwarp();
   const int half = n_dims / 2;
+  #pragma unroll 1
   for (int pi = lane; pi < half; pi += 32) {
     const float exponent = static_cast<float>(2 * pi) / static_cast<float>(n_dims);
     const float freq = 1.0f / powf(theta, exponent);
@@ -668,6 +742,7 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
                  lane);
   } else if (warp == G && owner) {
     pk_norm_rope(newk, S.kp + kvh * kHd, S.k_norm, S.eps, S.theta, S.n_dims, pos, lane);
+    #pragma unroll 1
     for (int i = lane; i < kHd; i += 32) {
       const __half kh = __float2half_rn(newk[i]);
       const __half vh = __float2half_rn(S.vp[kvh * kHd + i]);
@@ -687,6 +762,7 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
     qreg[i] = qs[j * kHd + 8 * lane + i];
   }
   constexpr int KB = 8;
+  #pragma unroll 1
   for (int k0 = kb; k0 < old_end; k0 += kAttnChunk) {
     const uint8_t* tile = cs.take();
     if (!tile) return false;
@@ -761,6 +837,7 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
     mrow[kHd + 1] = l;
   }
   pk_sync();
+  #pragma unroll 1
   for (int job = tid; job < G * kHd; job += kPkConsumers) {
     const int i = job % kHd, jj = job / kHd;
     const float* a = merge + jj * (kHd + 2);
@@ -785,8 +862,10 @@ KIB_DEV void pk_merge(const PkStage& S, PkShared* sh) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int items = S.heads * (kHd / 16);
   const int ns = S.nsplit;
+  #pragma unroll 1
   for (int it = static_cast<int>(blockIdx.x); it < items; it += static_cast<int>(gridDim.x)) {
     const int h = it / (kHd / 16), d0 = (it % (kHd / 16)) * 16;
+    #pragma unroll 1
     for (int s = tid; s < ns; s += kPkConsumers) {
       const float* src = S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + kHd;
       sh->ws[s] = __ldcg(src);
@@ -795,9 +874,11 @@ KIB_DEV void pk_merge(const PkStage& S, PkShared* sh) {
     pk_sync();
     if (warp == 0) {
       float M = -INFINITY;
+      #pragma unroll 1
       for (int s = lane; s < ns; s += 32) M = fmaxf(M, sh->ws[s]);
       M = warp_max(M);
       float den = 0.0f;
+      #pragma unroll 1
       for (int s = lane; s < ns; s += 32) {
         const float ms = sh->ws[s];
         const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
@@ -810,6 +891,7 @@ KIB_DEV void pk_merge(const PkStage& S, PkShared* sh) {
     pk_sync();
     const int d = tid & 15, jl = tid >> 4;  // 16 split lanes
     float n = 0.0f;
+    #pragma unroll 1
     for (int s = jl; s < ns; s += kPkConsumers / 16)
       n = fmaf(__ldcg(S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + d0 + d), sh->ws[s], n);
     n += __shfl_xor_sync(0xffffffffu, n, 16);
@@ -843,6 +925,7 @@ KIB_DEV void pk_head_finish(const PkProgram& P, const PkStage& S, PkShared* sh, 
   if (tid == 0) {
     float m = -INFINITY, s = 0.0f;
     int idx = 0x7FFFFFFF;
+    #pragma unroll 1
     for (int g = 0; g < groups; ++g) {
       const int gi = sh->bidx[g];
       if (gi == 0x7FFFFFFF) continue;
@@ -866,6 +949,7 @@ KIB_DEV void pk_head_finish(const PkProgram& P, const PkStage& S, PkShared* sh, 
   __threadfence();
   float m = -INFINITY, s = 0.0f;
   int idx = 0x7FFFFFFF;
+  #pragma unroll 1
   for (unsigned c = lane; c < gridDim.x; c += 32) {
     const int gi = __ldcg(&P.cand_idx[c]);
     if (gi == 0x7FFFFFFF) continue;
@@ -934,6 +1018,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
     // leave only once the copies in flight have landed (bounded)
     if (pr.lane == 0) {
       const uint32_t n = min(pr.seq, static_cast<uint32_t>(kPkSlots));
+      #pragma unroll 1
       for (uint32_t q = pr.seq - n; q < pr.seq; ++q) {
         for (uint32_t i = 0; i < (1u << 22); ++i)
           if (mbar_try_wait(&sh->full[q % kPkSlots], (q / kPkSlots) & 1u)) break;
@@ -946,7 +1031,6 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
   pdl_wait();
   pdl_launch_dependents();
   const int pos = *P.pos;
-  const int token = *P.token;
   PkCons cs;
   cs.ring = ring;
   cs.sh = sh;
@@ -955,12 +1039,20 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
   unsigned barriers = 0;
   pk_copy_desc(&sh->desc[0], &P.stages[0]);
   pk_sync();
+  #pragma unroll 1
   for (int s = 0; s < P.nstages; ++s) {
     const PkStage& S = sh->desc[s & 1];
-    if (P.trace && blockIdx.x == 0 && tid == 0) P.trace[s] = gtimer();
+    // the next stage's descriptor: loaded now, stored after this stage's work
+    constexpr int kDescWords = static_cast<int>(sizeof(PkStage) / 16);
+    uint4 next_desc = make_uint4(0u, 0u, 0u, 0u);
+    if (tid < kDescWords && s + 1 < P.nstages) next_desc = __ldg(reinterpret_cast<const uint4*>(&P.stages[s + 1]) + tid);
+    cs.tr = (P.trace && blockIdx.x == 0 && tid == 0) ? P.trace + 16 * s : nullptr;
+    cs.first = true;
+    if (cs.tr) cs.tr[0] = gtimer();
     bool ok = true;
     if (S.kind == kPkGemv || S.kind == kPkHead) {
-      pk_prologue(S, sh, token);
+      pk_prologue(S, sh);
+      if (cs.tr) cs.tr[1] = gtimer();
       switch (S.type) {
         // Q5_K matrices are not instantiated here (both 4-bit paths in one
         // kernel push it into local memory); the host routes models that
@@ -977,9 +1069,11 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
       pk_merge(S, sh);
     }
     if (!ok) break;
+    if (cs.tr) cs.tr[3] = gtimer();
+    if (P.trace && tid == 0) atomicMax(P.trace + 16 * s + 5, gtimer());  // slowest CTA done
     if (s + 1 < P.nstages) {
       const bool need_barrier = S.barrier_after != 0;
-      pk_copy_desc(&sh->desc[(s + 1) & 1], &P.stages[s + 1]);
+      if (tid < kDescWords) reinterpret_cast<uint4*>(&sh->desc[(s + 1) & 1])[tid] = next_desc;
       if (need_barrier) {
         ++barriers;
         if (!pk_grid_sync(P, sh, barriers * gridDim.x)) break;
@@ -988,7 +1082,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
       }
     }
   }
-  if (P.trace && blockIdx.x == 0 && tid == 0) P.trace[P.nstages] = gtimer();
+  if (P.trace && blockIdx.x == 0 && tid == 0) P.trace[16 * P.nstages] = gtimer();
   if (*reinterpret_cast<volatile int*>(&sh->abort) && tid == 0) atomicCAS(P.err, 0, 6);
 }
 

@@ -678,21 +678,10 @@ static int build_pk(kib_qwen35* m) {
   const int nsplit = grid / m->kvh;
   std::vector<PkStage> st;
   auto add = [&](const PkStage& S) { st.push_back(S); };
-  bool first = true;
   auto prologue_in = [&](PkStage& S, const DevT& norm) {
     S.norm_w = norm.f();
-    if (first) {
-      S.prologue = kProEmbed;
-      S.emb = m->tok_embd.p;
-      S.emb_type = m->tok_embd.type;
-      S.emb_rows = m->V;
-      S.emb_out = m->d_h;
-      if (m->tok_embd.cols() != m->H) return false;
-      first = false;
-    } else {
-      S.prologue = kProRms;
-      S.in = m->d_h;
-    }
+    S.prologue = kProRms;
+    S.in = m->d_h;
     return true;
   };
   for (const LayerW& L : m->layers) {
@@ -796,6 +785,16 @@ static int build_pk(kib_qwen35* m) {
     d.resid = m->d_h1;
     d.barrier_after = 1;
     add(d);
+  }
+  if (const char* rep = std::getenv("KIB_PK_PROBE_REPEAT"); rep && std::atoi(rep) > 0) {
+    // timing probe only: the first layer's FFN gate/up stage repeated
+    std::vector<PkStage> probe;
+    for (const PkStage& S : st)
+      if (S.paired) {
+        for (int i = 0; i < std::atoi(rep); ++i) probe.push_back(S);
+        break;
+      }
+    st = probe;
   }
   PkStage h = {};
   if (!pk_gemv_stage(m, h, kPkHead, {{&head_weight(m), nullptr, nullptr, kEpiArgmax}}, grid)) return KIB_OK;
@@ -1071,7 +1070,7 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
   if (dalloc(&m->d_pk_ctr, 2) != cudaSuccess ||
       dalloc(&m->d_pk_part, static_cast<size_t>(kPkMaxSplits) * m->heads * (kHd + 2)) != cudaSuccess ||
       dalloc(&m->d_pk_cmax, 1024) != cudaSuccess || dalloc(&m->d_pk_csum, 1024) != cudaSuccess ||
-      dalloc(&m->d_pk_cidx, 1024) != cudaSuccess || dalloc(&m->d_pk_trace, 4096) != cudaSuccess) {
+      dalloc(&m->d_pk_cidx, 1024) != cudaSuccess || dalloc(&m->d_pk_trace, 16 * 4096) != cudaSuccess) {
     kib_qwen35_free(mp.release());
     return set_error(ctx, KIB_ERR_INTERNAL, "persistent decode allocation failed");
   }
@@ -1223,11 +1222,15 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   cudaStream_t st = m->ctx->stream;
   const bool use_pk = m->pk_on;
   if (use_pk && !m->pk_graph) {
-    int rc = capture(m, &m->pk_graph, [&](Enq& q) { q.run(pk_launch(m, q.st), "decode_persistent"); });
+    auto body = [&](Enq& q) {
+      q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, m->d_tokens, 1, m->d_h, m->H, q.st), "embed");
+      q.run(pk_launch(m, q.st), "decode_persistent");
+    };
+    int rc = capture(m, &m->pk_graph, body);
     if (rc && m->pk_coop) {  // the cooperative attribute is not accepted together with PDL on every driver
       cudaGetLastError();
       m->pk_coop = false;
-      rc = capture(m, &m->pk_graph, [&](Enq& q) { q.run(pk_launch(m, q.st), "decode_persistent"); });
+      rc = capture(m, &m->pk_graph, body);
     }
     if (rc) return rc;
   }
@@ -1241,6 +1244,7 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
     if (rc) return rc;
   }
   if (m->trace_on && m->d_trace) ENG_CUDA(cudaMemsetAsync(m->d_trace, 0, 4096 * 8 * sizeof(unsigned long long), st));
+  if (m->trace_on && m->d_pk_trace) ENG_CUDA(cudaMemsetAsync(m->d_pk_trace, 0, 16 * 4096 * sizeof(unsigned long long), st));
   m->h_pin[0] = static_cast<int>(m->pos);
   m->h_pin[1] = first_token;
   m->h_pin[2] = 0;
@@ -1258,7 +1262,7 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   m->pos += steps;
   if (use_pk && m->trace_on) {
     // stage start times of CTA 0 in the last step: CSV to $KIB_TRACE_OUT
-    std::vector<unsigned long long> h(m->pk_n + 1);
+    std::vector<unsigned long long> h(16 * m->pk_n + 16);
     std::vector<PkStage> stages(m->pk_n);
     cudaMemcpy(h.data(), m->d_pk_trace, h.size() * 8, cudaMemcpyDeviceToHost);
     cudaMemcpy(stages.data(), m->d_pk, stages.size() * sizeof(PkStage), cudaMemcpyDeviceToHost);
@@ -1266,10 +1270,16 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
     FILE* f = path ? std::fopen(path, "w") : nullptr;
     if (f) {
       static const char* names[] = {"gemv", "gdn", "attn", "merge", "head"};
-      std::fprintf(f, "stage,kind,type,rows,cols,start_ns,dur_ns\n");
-      for (int i = 0; i < m->pk_n; ++i)
-        std::fprintf(f, "%d,%s,%d,%d,%d,%llu,%llu\n", i, names[stages[i].kind], stages[i].type, stages[i].rows,
-                     stages[i].cols, h[i] - h[0], h[i + 1] - h[i]);
+      auto rel = [&](unsigned long long v) { return v ? static_cast<long long>(v - h[0]) : -1ll; };
+      std::fprintf(f, "stage,kind,type,rows,cols,start_ns,prologue_ns,first_tile_ns,done_ns,next_ns,max_done_ns,"
+                      "prod_stage_ns,prod_issue_ns,ux_ns,p8,p9,p10,p11\n");
+      for (int i = 0; i < m->pk_n; ++i) {
+        const unsigned long long* t = h.data() + 16 * i;
+        std::fprintf(f, "%d,%s,%d,%d,%d", i, names[stages[i].kind], stages[i].type, stages[i].rows, stages[i].cols);
+        const int order[] = {0, 1, 2, 3, 16, 5, 6, 7, 4, 8, 9, 10, 11};
+        for (int k : order) std::fprintf(f, ",%lld", rel(t[k]));
+        std::fprintf(f, "\n");
+      }
       std::fclose(f);
     }
   }
