@@ -47,13 +47,12 @@ constexpr int kPkConsumers = kPkWarps * 32;
 constexpr int kPkThreads = kPkConsumers + 128;
 constexpr int kPkProducerRegs = 40;
 constexpr int kPkConsumerRegs = 232;
-constexpr int kPkSlots = 5;
+constexpr int kPkSlots = 6;
 constexpr int kPkSlotBytes = 32 * 1024;
 constexpr int kPkMaxCols = 4096;
 constexpr int kPkMaxSegs = 4;
 constexpr int kPkMaxSplits = 128;
 constexpr int kPkGdnRows = 16;  // state rows per GDN item
-constexpr int kPkCoefs = 4096;
 
 enum PkKind : int { kPkGemv = 0, kPkGdn = 1, kPkAttn = 2, kPkMerge = 3, kPkHead = 4 };
 
@@ -141,39 +140,17 @@ struct PkShared {
   PkStage desc[2];
   float red[kPkWarps][2];
   float gb[2];
-  float best[kPkWarps];
-  float bsum[kPkWarps];
-  int bidx[kPkWarps];
+  float best[16];
+  float bsum[16];
+  int bidx[16];
   int abort;
   int last;
-  float xscale;         // GEMV stage: the dot products are scaled back by this power of two
-  float part[64][16];   // GEMV: per (row group, K slice) partial row sums
-  // GEMV: per (row, scale group) coefficients of the current tile.  Q4_K:
-  // [0, 2048) d*sc and [2048, 4096) -dmin*m per (row, 32-code sub-block);
-  // Q6_K: [0, 4096) d*sc per (row, 16-code group).
-  __align__(16) float coef[kPkCoefs];
-  // GEMV stage input (f16 hi | f16 lo | sums of 16); attention / GDN / merge scratch
-  __align__(16) float xs[kPkMaxCols + kPkMaxCols / 16];
+  __align__(16) float xs[kPkMaxCols + kPkMaxCols / 16];  // padded stage input; attention/GDN scratch
   float ws[kPkMaxSplits];
   float ls[kPkMaxSplits];
 };
 
 constexpr size_t kPkSmemBytes = static_cast<size_t>(kPkSlots) * kPkSlotBytes + sizeof(PkShared);
-
-// Alignment self-check of the vector loads (diagnostic): a misaligned
-// address is recorded (site code << 32 | low address bits) and the load is
-// skipped.
-static __device__ unsigned long long g_pk_diag;
-#define PK_LD(T, ptr, site)                                                                                     \
-  ([&]() -> T {                                                                                                 \
-    const void* pp_ = (ptr);                                                                                    \
-    if (reinterpret_cast<uintptr_t>(pp_) % sizeof(T)) {                                                         \
-      atomicCAS(&g_pk_diag, 0ull, (static_cast<unsigned long long>(site) << 32) |                              \
-                                      (reinterpret_cast<uintptr_t>(pp_) & 0xFFFFFFFFull));                    \
-      return T{};                                                                                               \
-    }                                                                                                           \
-    return *reinterpret_cast<const T*>(pp_);                                                                    \
-  }())
 
 // named barrier over the eight consumer warps (the producer never joins)
 KIB_DEV void pk_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kPkConsumers) : "memory"); }
@@ -381,148 +358,117 @@ KIB_DEV void pk_copy_desc(PkStage* dst, const PkStage* src) {
 }
 
 // ---- GEMV prologue: the stage's transformed input vector into sh->xs
-// GEMV stage input, as the integer tensor-core dot products take it: the
-// integers X = round(x * 2^p), with p chosen so that max|X| is in [2^26, 2^27),
-// written as four signed 8-bit limbs X = L0 2^21 + L1 2^14 + L2 2^7 + L3 (each
-// in [-64, 64]), and the sums of X over each 16 consecutive inputs (the
-// offset terms of the K-quant formulas).  x is carried to 2^-27 of its
-// maximum.
-struct PkX {
-  const int8_t* limb[4];
-  const float* sum16;
-};
-KIB_DEV PkX pk_x(const PkShared* sh) {
-  const int8_t* b = reinterpret_cast<const int8_t*>(sh->xs);
-  return {{b, b + kPkMaxCols, b + 2 * kPkMaxCols, b + 3 * kPkMaxCols}, sh->xs + kPkMaxCols};
-}
+// The stage input lives in shared memory with 4 floats of padding after every
+// 64: the 16 lanes of a row group read their units (64 consecutive inputs for
+// Q4_K) at a stride of 68 floats, which spreads them over the banks.
+KIB_DEV int xpad(int i) { return i + 4 * (i >> 6); }
 
 // Prologue: every thread issues all of its loads (input, norm weights, gate)
-// before the first reduction, so the stage start costs one memory round trip
-// and one block reduction.  Thread tid owns inputs 4*tid + 1024*k (k < 4).
+// before the first reduction, so the stage start costs one memory round trip.
 KIB_DEV void pk_prologue(const PkStage& S, PkShared* sh) {
+  float* xs = sh->xs;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cols = S.cols;
-  constexpr int kPer = kPkMaxCols / (4 * kPkConsumers);
-  float4 o[kPer];
-  float amax = 0.0f;
   if (S.prologue == kProNormGate) {
-    // qk_norm over heads of 128 (a warp covers one head per k), silu(gate),
-    // mul (qwen35_runtime.cpp:2993-3003)
+    // qk_norm over heads of 128 (one warp per head), silu(gate), mul
+    // (qwen35_runtime.cpp:2993-3003)
     constexpr int hd = 128;
-    const float4 w = PK_LD(float4, S.norm_w + 4 * lane, 15);
-    float4 y[kPer], z[kPer];
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int i = 4 * tid + 4 * kPkConsumers * k;
-      if (i < cols) {
-        y[k] = PK_LD(float4, S.in + i, 16);
-        z[k] = PK_LD(float4, S.gate + i, 17);
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int i = 4 * tid + 4 * kPkConsumers * k;
-      if (i < cols) {  // warp-uniform
-        const float ss = warp_sum((y[k].x * y[k].x + y[k].y * y[k].y) + (y[k].z * y[k].z + y[k].w * y[k].w));
-        const float scale = 1.0f / sqrtf(ss / static_cast<float>(hd) + S.eps);
-        o[k].x = y[k].x * (scale * w.x) * silu_f(z[k].x);
-        o[k].y = y[k].y * (scale * w.y) * silu_f(z[k].y);
-        o[k].z = y[k].z * (scale * w.z) * silu_f(z[k].z);
-        o[k].w = y[k].w * (scale * w.w) * silu_f(z[k].w);
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(o[k].x), fabsf(o[k].y)), fmaxf(fabsf(o[k].z), fabsf(o[k].w))));
-      }
-    }
-    amax = warp_max(amax);
-    if (lane == 0) sh->red[warp][1] = amax;
-    pk_sync();
-  } else {
-    const bool rms = S.prologue == kProRms;
-    float4 w[kPer];
-    float ss = 0.0f;
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int i = 4 * tid + 4 * kPkConsumers * k;
-      if (i < cols) {
-        o[k] = PK_LD(float4, S.in + i, 13);
-        w[k] = rms ? PK_LD(float4, S.norm_w + i, 14) : make_float4(1.f, 1.f, 1.f, 1.f);
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int i = 4 * tid + 4 * kPkConsumers * k;
-      if (i < cols) {
-        const float4 v = o[k];
-        ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x * w[k].x), fabsf(v.y * w[k].y)),
-                                 fmaxf(fabsf(v.z * w[k].z), fabsf(v.w * w[k].w))));
-      }
-    }
-    ss = warp_sum(ss);
-    amax = warp_max(amax);
-    if (lane == 0) {
-      sh->red[warp][0] = ss;
-      sh->red[warp][1] = amax;
+    const float4 w = *reinterpret_cast<const float4*>(S.norm_w + 4 * lane);
+#pragma unroll 1
+    for (int base = warp * hd; base < cols; base += kPkWarps * hd) {
+      const float4 y = *reinterpret_cast<const float4*>(S.in + base + 4 * lane);
+      const float4 z = *reinterpret_cast<const float4*>(S.gate + base + 4 * lane);
+      const float ss = warp_sum((y.x * y.x + y.y * y.y) + (y.z * y.z + y.w * y.w));
+      const float scale = 1.0f / sqrtf(ss / static_cast<float>(hd) + S.eps);
+      float4 o;
+      o.x = y.x * (scale * w.x) * silu_f(z.x);
+      o.y = y.y * (scale * w.y) * silu_f(z.y);
+      o.z = y.z * (scale * w.z) * silu_f(z.z);
+      o.w = y.w * (scale * w.w) * silu_f(z.w);
+      *reinterpret_cast<float4*>(xs + xpad(base + 4 * lane)) = o;
     }
     pk_sync();
-    if (rms) {
-      // rms_norm_f32_f32_batched (mps_backend.mm:1891-1921): x * rsqrt(mean(x^2)+eps) * w
-      float tot = 0.0f;
-#pragma unroll
-      for (int q = 0; q < kPkWarps; ++q) tot += sh->red[q][0];
-      const float scale = 1.0f / sqrtf(tot / static_cast<float>(cols) + S.eps);
-#pragma unroll
-      for (int k = 0; k < kPer; ++k) {
-        o[k].x = o[k].x * scale * w[k].x;
-        o[k].y = o[k].y * scale * w[k].y;
-        o[k].z = o[k].z * scale * w[k].z;
-        o[k].w = o[k].w * scale * w[k].w;
-      }
-      float m = 0.0f;
-#pragma unroll
-      for (int q = 0; q < kPkWarps; ++q) m = fmaxf(m, sh->red[q][1]);
-      amax = m * scale;
-    }
+    return;
   }
-  float m = amax;
-  if (S.prologue != kProRms) {
-    m = 0.0f;
-#pragma unroll
-    for (int q = 0; q < kPkWarps; ++q) m = fmaxf(m, sh->red[q][1]);
-  }
-  // 2^p with max|X| in [2^26, 2^27) (p = 0 for an all-zero or non-finite input)
-  int e = 0;
-  if (m > 0.0f && m < INFINITY) e = static_cast<int>((__float_as_uint(m) >> 23) & 0xFFu) - 127;
-  e = max(-90, min(90, e));
-  const float up = __uint_as_float(static_cast<uint32_t>(127 + 26 - e) << 23);
-  if (tid == 0) sh->xscale = __uint_as_float(static_cast<uint32_t>(127 - 26 + e) << 23);
-  int8_t* l0 = reinterpret_cast<int8_t*>(sh->xs);
-  float* sum16 = sh->xs + kPkMaxCols;
+  constexpr int kPer = kPkMaxCols / (4 * kPkConsumers);  // float4 per thread
+  float4 v[kPer], w[kPer];
+  float ss = 0.0f;
+  const bool rms = S.prologue == kProRms;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
     const int i = 4 * tid + 4 * kPkConsumers * k;
-    if (i < cols) {  // warp-uniform (cols is a multiple of 256)
-      const float xv[4] = {o[k].x, o[k].y, o[k].z, o[k].w};
-      uint32_t w[4] = {0u, 0u, 0u, 0u};
-      float s4 = 0.0f;
+    if (i < cols) {
+      v[k] = *reinterpret_cast<const float4*>(S.in + i);
+      if (rms) w[k] = *reinterpret_cast<const float4*>(S.norm_w + i);
+    }
+  }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        int X = __float2int_rn(xv[j] * up);
-        s4 += static_cast<float>(X);
+  for (int k = 0; k < kPer; ++k) {
+    const int i = 4 * tid + 4 * kPkConsumers * k;
+    if (i < cols) ss += (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
+  }
+  float scale = 1.0f;
+  if (rms) {
+    // rms_norm_f32_f32_batched (mps_backend.mm:1891-1921): x * rsqrt(mean(x^2)+eps) * w
+    ss = warp_sum(ss);
+    if (lane == 0) sh->red[warp][0] = ss;
+    pk_sync();
+    float tot = 0.0f;
 #pragma unroll
-        for (int q = 3; q >= 0; --q) {  // base-128 digits in [-64, 63], the top one in [-64, 64]
-          const int dgt = q == 0 ? X : ((X + 64) & 127) - 64;
-          w[q] |= (static_cast<uint32_t>(dgt) & 0xFFu) << (8 * j);
-          X = (X - dgt) >> 7;
-        }
+    for (int q = 0; q < kPkWarps; ++q) tot += sh->red[q][0];
+    scale = 1.0f / sqrtf(tot / static_cast<float>(cols) + S.eps);
+  }
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = 4 * tid + 4 * kPkConsumers * k;
+    if (i < cols) {
+      float4 o = v[k];
+      if (rms) {
+        o.x = o.x * scale * w[k].x;
+        o.y = o.y * scale * w[k].y;
+        o.z = o.z * scale * w[k].z;
+        o.w = o.w * scale * w[k].w;
       }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) *reinterpret_cast<uint32_t*>(l0 + q * kPkMaxCols + i) = w[q];
-      s4 += __shfl_xor_sync(0xffffffffu, s4, 1);
-      s4 += __shfl_xor_sync(0xffffffffu, s4, 2);
-      if ((lane & 3) == 0) sum16[i >> 4] = s4;
+      *reinterpret_cast<float4*>(xs + xpad(i)) = o;
     }
   }
   pk_sync();
+}
+
+// x values of unit u of block blk from the padded stage input (element order
+// as unit_col, group sums as load_unit_x).
+template <int QT>
+KIB_DEV void pk_load_unit_x(const float* xs, int blk, int u, UnitX<QT>& ux) {
+  if (QT == kTypeQ6K) {
+    const int c = u >> 1, r = u & 1;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4* p = reinterpret_cast<const float4*>(xs + 68 * (4 * blk + 2 * c + (k >> 1)) + 32 * (k & 1) + 16 * r);
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 f = p[j];
+        ux.v[8 * k + 2 * j] = make_float2(f.x, f.y);
+        ux.v[8 * k + 2 * j + 1] = make_float2(f.z, f.w);
+        s += (f.x + f.y) + (f.z + f.w);
+      }
+      ux.s[k] = s;
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(xs + 68 * (4 * blk + u));
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 f = p[8 * g + j];
+        ux.v[16 * g + 2 * j] = make_float2(f.x, f.y);
+        ux.v[16 * g + 2 * j + 1] = make_float2(f.z, f.w);
+        s += (f.x + f.y) + (f.z + f.w);
+      }
+      ux.s[g] = s;
+    }
+  }
 }
 
 struct PkArgmax {
@@ -547,252 +493,126 @@ KIB_DEV int pk_seg_of(const PkStage& S, int r) {
   return s;
 }
 
-// ---- K-quant GEMV on the integer tensor cores (mma.sync, s8 x s8 -> s32).
-// A = 16 rows of quant codes (Q4_K: 0..15; Q6_K: q - 32), B = the limbs of X,
-// so one mma gives, exactly, sum(code * limb) for
-// 16 rows and all four limbs (columns 0, 2, 4, 6); lane t of each quad
-// receives limb t's sums.  The k slots of a lane ({4t..4t+3} and, for k32, {4t+16..4t+19}) are
-// mapped to consecutive codes, so one 32- or 64-bit load of the packed bytes
-// yields A with a mask; B uses the same mapping.  Each lane then applies the
-// per-(sub)block scale to its own limb's sums (lane 3 also the Q4_K offset
-// term -dmin*m*sum(X)), and the quad's four partial sums combine with weights
-// 2^21, 2^14, 2^7, 1 at the end.  Q4_K unit c = sub-blocks 2c, 2c+1 (one k32 mma
-// each); Q6_K unit (half hc, i-range r) = four 16-code scale groups (k16).
-KIB_DEV void imma_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-KIB_DEV void imma_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a0), "r"(a1), "r"(b0));
-}
-
-KIB_DEV uint32_t lds_u32_a2(const uint8_t* p) { return lds_u16(p) | (lds_u16(p + 2) << 16); }
-
-// Exact int -> float for |i| < 2^22 without the conversion unit.
-KIB_DEV float pk_i2f(int i) { return __int_as_float(i + 0x4B400000) - 12582912.0f; }
-
-// Decodes the scale coefficients of every (row, block) of the tile into
-// sh->coef (Q4_K: get_scale_min_k4; Q6_K: int8 scales; both times the fp16
-// super-block scales, as unit_coeffs).  nmat = 2 for a gate/up pair.
-template <int QT>
-KIB_DEV void pk_tile_coeffs(const uint8_t* tile, int row_bytes, int nr, int nmat, int blocks, float* coef) {
-  const int pairs = nmat * nr * blocks;
-#pragma unroll 1
-  for (int i = threadIdx.x; i < pairs; i += kPkConsumers) {
-    const int b = i % blocks, rm = i / blocks;  // rm = mat * nr + row
-    const int mat = rm / nr, row = rm - mat * nr;
-    const uint8_t* blk = tile + mat * (kPkSlotBytes / 2) + static_cast<size_t>(row) * row_bytes + b * kquant_block_bytes(QT);
-    if (QT == kTypeQ4K) {
-      const uint4 h = PK_LD(uint4, blk, 1);
-      const float d = half_bits_to_float(static_cast<uint16_t>(h.x & 0xFFFFu));
-      const float dmin = half_bits_to_float(static_cast<uint16_t>(h.x >> 16));
-      const uint32_t sc_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
-      const uint32_t sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-      const uint32_t m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-      float* ca = coef + rm * blocks * 8 + b * 8;
-      float* cb = ca + kPkCoefs / 2;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t scw = j < 4 ? sc_lo : sc_hi, mw = j < 4 ? m_lo : m_hi;
-        const int sh = 8 * (j & 3);
-        ca[j] = d * pk_i2f(static_cast<int>((scw >> sh) & 0xFFu));
-        cb[j] = -(dmin * pk_i2f(static_cast<int>((mw >> sh) & 0xFFu)));
-      }
-    } else {
-      const float d = half_bits_to_float(static_cast<uint16_t>(lds_u16(blk + 208)));
-      const uint2 s0 = lds8_a2(blk + 192), s1 = lds8_a2(blk + 200);
-      const uint32_t sw[4] = {s0.x, s0.y, s1.x, s1.y};
-      float* ca = coef + rm * blocks * 16 + b * 16;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int sc = static_cast<int>(static_cast<int8_t>((sw[j >> 2] >> (8 * (j & 3))) & 0xFFu));
-        ca[j] = d * pk_i2f(sc);
-      }
-    }
-  }
-}
-
-// Adds this lane's share of sum(value * X) of unit U for tile rows ra, rb of
-// matrix mat (coefficient rows cra, crb).
-template <int QT>
-KIB_DEV void pk_unit_mma(const uint8_t* rp0, const uint8_t* rp1, const float* ca0, const float* ca1, int U,
-                         const PkX& X, int g, int t, float& acc0, float& acc1) {
-  const int blk = U >> 2, c = U & 3;
-  constexpr int BB = kquant_block_bytes(QT);
-  const uint8_t* b0p = rp0 + blk * BB;
-  const uint8_t* b1p = rp1 + blk * BB;
-  const bool bl = (g & 1) == 0;  // this lane carries a limb column of B (0, 2, 4, 6)
-  const int8_t* lp = X.limb[g >> 1];
-  if (QT == kTypeQ4K) {
-    const uint2 w0 = PK_LD(uint2, b0p + 16 + 32 * c + 8 * t, 2);
-    const uint2 w1 = PK_LD(uint2, b1p + 16 + 32 * c + 8 * t, 3);
-    const uint32_t al[4] = {w0.x & 0x0F0F0F0Fu, w1.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu};
-    const uint32_t ah[4] = {(w0.x >> 4) & 0x0F0F0F0Fu, (w1.x >> 4) & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu,
-                            (w1.y >> 4) & 0x0F0F0F0Fu};
-    uint2 bl0 = make_uint2(0u, 0u), bh0 = make_uint2(0u, 0u);
-    if (bl) {
-      bl0 = PK_LD(uint2, lp + 256 * blk + 64 * c + 8 * t, 4);  // sub-block 2c
-      bh0 = PK_LD(uint2, lp + 256 * blk + 64 * c + 32 + 8 * t, 5);  // sub-block 2c + 1
-    }
-    int cl[4] = {0, 0, 0, 0}, ch[4] = {0, 0, 0, 0};
-    imma_k32(cl, al, bl0.x, bl0.y);
-    imma_k32(ch, ah, bh0.x, bh0.y);
-    const int j = 8 * blk + 2 * c;  // sub-block index in the row
-    const float2 k0 = PK_LD(float2, ca0 + j, 6), k1 = PK_LD(float2, ca1 + j, 7);
-    acc0 += k0.x * pk_i2f(cl[0]) + k0.y * pk_i2f(ch[0]);
-    acc1 += k1.x * pk_i2f(cl[2]) + k1.y * pk_i2f(ch[2]);
-    if (t == 3) {  // the offset term -dmin*m*sum(X), at the weight of limb 3
-      const float2 m0 = PK_LD(float2, ca0 + kPkCoefs / 2 + j, 8);
-      const float2 m1 = PK_LD(float2, ca1 + kPkCoefs / 2 + j, 9);
-      const float4 xs = PK_LD(float4, X.sum16 + 16 * blk + 4 * c, 10);
-      const float xs0 = xs.x + xs.y, xs1 = xs.z + xs.w;
-      acc0 += m0.x * xs0 + m0.y * xs1;
-      acc1 += m1.x * xs0 + m1.y * xs1;
-    }
-  } else {
-    // group k = inputs 256 blk + 128 hc + 32 k + 16 r + [0, 16); code q - 32
-    const int hc = c >> 1, r = c & 1;
-    const uint32_t a0 = lds_u32_a2(b0p + 64 * hc + 16 * r + 4 * t);
-    const uint32_t a1 = lds_u32_a2(b1p + 64 * hc + 16 * r + 4 * t);
-    const uint32_t bb0 = lds_u32_a2(b0p + 64 * hc + 32 + 16 * r + 4 * t);
-    const uint32_t bb1 = lds_u32_a2(b1p + 64 * hc + 32 + 16 * r + 4 * t);
-    const uint32_t h0 = lds_u32_a2(b0p + 128 + 32 * hc + 16 * r + 4 * t);
-    const uint32_t h1 = lds_u32_a2(b1p + 128 + 32 * hc + 16 * r + 4 * t);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint32_t x0 = k & 1 ? bb0 : a0, x1 = k & 1 ? bb1 : a1;
-      const uint32_t v0 = __vsub4(((k >= 2 ? x0 >> 4 : x0) & 0x0F0F0F0Fu) | (((h0 >> (2 * k)) & 0x03030303u) << 4),
-                                  0x20202020u);
-      const uint32_t v1 = __vsub4(((k >= 2 ? x1 >> 4 : x1) & 0x0F0F0F0Fu) | (((h1 >> (2 * k)) & 0x03030303u) << 4),
-                                  0x20202020u);
-      const uint32_t b = bl ? PK_LD(uint32_t, lp + 256 * blk + 128 * hc + 32 * k + 16 * r + 4 * t, 11)
-                            : 0u;
-      int ck[4] = {0, 0, 0, 0};
-      imma_k16(ck, v0, v1, b);
-      const int j = 16 * blk + 8 * hc + 2 * k + r;  // scale group index in the row
-      acc0 += ca0[j] * pk_i2f(ck[0]);
-      acc1 += ca1[j] * pk_i2f(ck[2]);
-    }
-  }
-}
-
-// Combines the quad's limb partials (lanes t = 0..3 of group g).
-KIB_DEV float pk_quad_total(float acc, int t) {
-  const float w = t == 0 ? 2097152.0f : t == 1 ? 16384.0f : t == 2 ? 128.0f : 1.0f;
-  float v = acc * w;
-  v += __shfl_xor_sync(0xffffffffu, v, 1);
-  v += __shfl_xor_sync(0xffffffffu, v, 2);
-  return v;
-}
-
 template <int QT>
 KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, PkArgmax& am) {
+  constexpr int BB = kquant_block_bytes(QT);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, t = lane & 3;
-  const PkX X = pk_x(cs.sh);
-  const int units = S.cols / 64;
-  const float xscale = cs.sh->xscale;
+  const int RG = S.rg;
+  const int groups = kPkConsumers / RG;
+  const int group = tid / RG, gl = tid % RG;
+  const bool active = gl < S.cols / 64;
+  const int blk = gl >> 2, u = gl & 3;
+  UnitX<QT> ux[1];
+  if (cs.tr) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "r"(blk));
+    cs.tr[8] = t;
+  }
+  if (active) pk_load_unit_x<QT>(cs.sh->xs, blk, u, ux[0]);
+  if (cs.tr) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(ux[0].v[31].y));
+    cs.tr[9] = t;
+    UnitX<QT> ux2;
+    pk_load_unit_x<QT>(cs.sh->xs, blk, u ^ 1, ux2);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(ux2.v[31].y));
+    cs.tr[10] = t;
+  }
+  if (cs.tr) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(ux[0].v[31].y));
+    cs.tr[4] = t;
+  }
   const int grid = static_cast<int>(gridDim.x);
-#pragma unroll 1
-  for (int tile_i = static_cast<int>(blockIdx.x); tile_i < S.ntiles; tile_i += grid) {
-    const int r0 = tile_i * S.tile_rows;
-    const int nr = min(S.tile_rows, S.rows - r0);
-    // row owner (tid < nr): start the epilogue's loads before the dot products
-    int si = 0, row = 0, epi = kEpiStore;
-    float pre0 = 0.0f, pre1 = 0.0f, pre2 = 0.0f;
-    float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (tid < nr) {
-      si = pk_seg_of(S, r0 + tid);
-      row = r0 + tid - S.seg[si].row_begin;
-      epi = S.seg[si].epi;
-      if (epi == kEpiResidual) {
-        pre0 = S.resid[row];
-      } else if (epi == kEpiConv) {
-        const float* st = S.conv_state + static_cast<size_t>(row) * 3;
-        pre0 = st[0];
-        pre1 = st[1];
-        pre2 = st[2];
-        cw = PK_LD(float4, S.conv_w + static_cast<size_t>(row) * 4, 12);
-      }
-    }
+  #pragma unroll 1
+  for (int t = static_cast<int>(blockIdx.x); t < S.ntiles; t += grid) {
     const uint8_t* tile = cs.take();
     if (!tile) return false;
-    const bool trt = cs.tr && tile_i == static_cast<int>(blockIdx.x);
-    if (trt) cs.tr[8] = gtimer();
-    const int blocks = S.cols / 256;
-    pk_tile_coeffs<QT>(tile, S.row_bytes, nr, S.paired ? 2 : 1, blocks, cs.sh->coef);
-    pk_sync();
-    const int r16 = (nr + 15) >> 4;
-    const int mats = S.paired ? 2 : 1;
-    const int cstride = blocks * (QT == kTypeQ4K ? 8 : 16);  // coefficients per row
-    const int M = r16 * mats;
-    const int KS = M >= kPkWarps ? 1 : kPkWarps / M;
+    const int r0 = t * S.tile_rows;
+    const int nr = min(S.tile_rows, S.rows - r0);
+    const int passes = (nr + groups - 1) / groups;
 #pragma unroll 1
-    for (int item = warp; item < M * KS; item += kPkWarps) {
-      const int mg = item / KS, ks = item - mg * KS;
-      const int half = mg / r16, rg = mg - half * r16;
-      const int ra = min(16 * rg + g, nr - 1), rb = min(16 * rg + g + 8, nr - 1);
-      const uint8_t* base = tile + half * (kPkSlotBytes / 2);
-      const uint8_t* rp0 = base + static_cast<size_t>(ra) * S.row_bytes;
-      const uint8_t* rp1 = base + static_cast<size_t>(rb) * S.row_bytes;
-      const int u0 = (units * ks) / KS, u1 = (units * (ks + 1)) / KS;
-      float acc0 = 0.0f, acc1 = 0.0f;
-      const float* ca0 = cs.sh->coef + (half * nr + ra) * cstride;
-      const float* ca1 = cs.sh->coef + (half * nr + rb) * cstride;
-#pragma unroll 2
-      for (int U = u0; U < u1; ++U) pk_unit_mma<QT>(rp0, rp1, ca0, ca1, U, X, g, t, acc0, acc1);
-      acc0 = pk_quad_total(acc0, t);
-      acc1 = pk_quad_total(acc1, t);
-      if (t == 0) {
-        cs.sh->part[item][g] = acc0;
-        cs.sh->part[item][g + 8] = acc1;
+    for (int pass = 0; pass < passes; ++pass) {
+      const int rl = pass * groups + group;
+      const bool ok = rl < nr;
+      const int r = r0 + rl;
+      // the leader starts the epilogue's loads before the dot product
+      int si = 0, row = 0, epi = kEpiStore;
+      float pre0 = 0.0f, pre1 = 0.0f, pre2 = 0.0f;
+      float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gl == 0 && ok) {
+        si = pk_seg_of(S, r);
+        row = r - S.seg[si].row_begin;
+        epi = S.seg[si].epi;
+        if (epi == kEpiResidual) {
+          pre0 = S.resid[row];
+        } else if (epi == kEpiConv) {
+          const float* st = S.conv_state + static_cast<size_t>(row) * 3;
+          pre0 = st[0];
+          pre1 = st[1];
+          pre2 = st[2];
+          cw = *reinterpret_cast<const float4*>(S.conv_w + static_cast<size_t>(row) * 4);
+        }
       }
-      if (trt && item == 0) {
-        unsigned long long tt;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tt) : "f"(acc0));
-        cs.tr[9] = tt;
+      float acc[1] = {0.0f}, acc2[1] = {0.0f};
+      if (ok && active) {
+        const uint8_t* b0 = tile + static_cast<size_t>(rl) * S.row_bytes + blk * BB;
+        // gate and up rows of a pair run through one copy of the dot code
+#pragma unroll 1
+        for (int hh = 0; hh <= S.paired; ++hh) {
+          float a[1] = {0.0f};
+          unit_dot<QT, 1>(b0 + hh * (kPkSlotBytes / 2), u, ux, a);
+          if (hh == 0) acc[0] = a[0]; else acc2[0] = a[0];
+        }
+      }
+      const int lim = RG < 32 ? RG : 32;
+      for (int o = lim / 2; o > 0; o >>= 1) {
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
+        if (S.paired) acc2[0] += __shfl_xor_sync(0xffffffffu, acc2[0], o);
+      }
+      if (RG > 32) {
+        if (lane == 0) {
+          cs.sh->red[warp][0] = acc[0];
+          cs.sh->red[warp][1] = acc2[0];
+        }
+        pk_sync();
+        if (gl == 0) {
+          #pragma unroll 1
+          for (int w = 1; w < RG / 32; ++w) {
+            acc[0] += cs.sh->red[warp + w][0];
+            acc2[0] += cs.sh->red[warp + w][1];
+          }
+        }
+        pk_sync();
+      }
+      if (gl == 0 && ok) {
+        const PkSeg& g = S.seg[si];
+        const float v = acc[0];
+        if (epi == kEpiStore) {
+          g.out[row] = v;
+        } else if (epi == kEpiResidual) {
+          g.out[row] = v + pre0;
+        } else if (epi == kEpiSiluMul) {
+          g.out[row] = silu_f(v) * acc2[0];
+        } else if (epi == kEpiConv) {
+          // causal depthwise conv of kernel 4 over [state | new], then silu
+          float c = 0.0f;
+          c += pre0 * cw.x;
+          c += pre1 * cw.y;
+          c += pre2 * cw.z;
+          c += v * cw.w;
+          g.out[row] = silu_f(c);
+          float* st = S.conv_state + static_cast<size_t>(row) * 3;
+          st[0] = pre1;
+          st[1] = pre2;
+          st[2] = v;
+        } else {  // kEpiArgmax
+          am.push(v, row);
+          if (g.out) g.out[row] = v;
+        }
       }
     }
-    pk_sync();
-    if (trt) cs.tr[10] = gtimer();
-    if (tid < nr) {
-      const int rg = tid >> 4, rr = tid & 15;
-      float v = 0.0f, v2 = 0.0f;
-      for (int ks = 0; ks < KS; ++ks) v += cs.sh->part[rg * KS + ks][rr];
-      if (S.paired)
-        for (int ks = 0; ks < KS; ++ks) v2 += cs.sh->part[(r16 + rg) * KS + ks][rr];
-      v *= xscale;
-      v2 *= xscale;
-      const PkSeg& sg = S.seg[si];
-      if (epi == kEpiStore) {
-        sg.out[row] = v;
-      } else if (epi == kEpiResidual) {
-        sg.out[row] = v + pre0;
-      } else if (epi == kEpiSiluMul) {
-        sg.out[row] = silu_f(v) * v2;
-      } else if (epi == kEpiConv) {
-        // causal depthwise conv of kernel 4 over [state | new], then silu
-        float cacc = 0.0f;
-        cacc += pre0 * cw.x;
-        cacc += pre1 * cw.y;
-        cacc += pre2 * cw.z;
-        cacc += v * cw.w;
-        sg.out[row] = silu_f(cacc);
-        float* st = S.conv_state + static_cast<size_t>(row) * 3;
-        st[0] = pre1;
-        st[1] = pre2;
-        st[2] = v;
-      } else {  // kEpiArgmax
-        am.push(v, row);
-        if (sg.out) sg.out[row] = v;
-      }
-    }
-    if (trt) cs.tr[11] = gtimer();
-    cs.release();  // the pk_sync in it also protects part[] reuse
-    if (trt) cs.tr[12] = gtimer();
+    cs.release();
   }
   return true;
 }
@@ -846,7 +666,7 @@ KIB_DEV bool pk_gdn(const PkStage& S, PkCons& cs) {
     for (int rr = 0; rr < 2; ++rr) {
       const int lr = 2 * warp + rr;
       const int vrow = grp * kPkGdnRows + lr;
-      float4 st = PK_LD(float4, srows + lr * D + 4 * lane, 18);
+      float4 st = *reinterpret_cast<const float4*>(srows + lr * D + 4 * lane);
       st.x *= ge;
       st.y *= ge;
       st.z *= ge;
@@ -956,8 +776,8 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
       for (int e = 0; e < KB; ++e) {
         const int kk = min(kk0 + e, nk - 1);
         const uint16_t* row = kvbuf + static_cast<size_t>(kk) * 2 * kHd;
-        const uint4 kr = PK_LD(uint4, row + 8 * lane, 19);
-        vraw[e] = PK_LD(uint4, row + kHd + 8 * lane, 20);
+        const uint4 kr = *reinterpret_cast<const uint4*>(row + 8 * lane);
+        vraw[e] = *reinterpret_cast<const uint4*>(row + kHd + 8 * lane);
         const __half2* kh = reinterpret_cast<const __half2*>(&kr);
         float d = 0.0f;
 #pragma unroll
@@ -1092,40 +912,32 @@ KIB_DEV void pk_merge(const PkStage& S, PkShared* sh) {
 }
 
 // ---- LM head tail: CTA candidate, then the last CTA picks the token
-KIB_DEV void pk_argmax_merge(float& m, float& s, int& idx, float om, float os, int oi) {
-  if (oi == 0x7FFFFFFF) return;
-  if (idx == 0x7FFFFFFF || om > m || (om == m && oi < idx)) {
-    s = (idx == 0x7FFFFFFF ? 0.0f : s * expf(m - om)) + os;
-    m = om;
-    idx = oi;
-  } else {
-    s += os * expf(om - m);
-  }
-}
-
 KIB_DEV void pk_head_finish(const PkProgram& P, const PkStage& S, PkShared* sh, const PkArgmax& am) {
-  (void)S;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  {
-    float m = am.best, s = am.bsum;
-    int idx = am.bidx;
-    for (int o = 16; o > 0; o >>= 1) {
-      const float om = __shfl_xor_sync(0xffffffffu, m, o);
-      const float os = __shfl_xor_sync(0xffffffffu, s, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-      pk_argmax_merge(m, s, idx, om, os, oi);
-    }
-    if (lane == 0) {
-      sh->best[warp] = m;
-      sh->bsum[warp] = s;
-      sh->bidx[warp] = idx;
-    }
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int groups = kPkConsumers / S.rg;
+  const int group = tid / S.rg, gl = tid % S.rg;
+  if (gl == 0) {
+    sh->best[group] = am.best;
+    sh->bsum[group] = am.bsum;
+    sh->bidx[group] = am.bidx;
   }
   pk_sync();
   if (tid == 0) {
     float m = -INFINITY, s = 0.0f;
     int idx = 0x7FFFFFFF;
-    for (int w = 0; w < kPkWarps; ++w) pk_argmax_merge(m, s, idx, sh->best[w], sh->bsum[w], sh->bidx[w]);
+    #pragma unroll 1
+    for (int g = 0; g < groups; ++g) {
+      const int gi = sh->bidx[g];
+      if (gi == 0x7FFFFFFF) continue;
+      const float gm = sh->best[g], gs = sh->bsum[g];
+      if (gm > m || (gm == m && gi < idx)) {
+        s = s * expf(m - gm) + gs;
+        m = gm;
+        idx = gi;
+      } else {
+        s += gs * expf(gm - m);
+      }
+    }
     P.cand_max[blockIdx.x] = m;
     P.cand_sum[blockIdx.x] = s;
     P.cand_idx[blockIdx.x] = idx;
@@ -1137,14 +949,31 @@ KIB_DEV void pk_head_finish(const PkProgram& P, const PkStage& S, PkShared* sh, 
   __threadfence();
   float m = -INFINITY, s = 0.0f;
   int idx = 0x7FFFFFFF;
-#pragma unroll 1
-  for (unsigned c = lane; c < gridDim.x; c += 32)
-    pk_argmax_merge(m, s, idx, __ldcg(&P.cand_max[c]), __ldcg(&P.cand_sum[c]), __ldcg(&P.cand_idx[c]));
+  #pragma unroll 1
+  for (unsigned c = lane; c < gridDim.x; c += 32) {
+    const int gi = __ldcg(&P.cand_idx[c]);
+    if (gi == 0x7FFFFFFF) continue;
+    const float gm = __ldcg(&P.cand_max[c]), gs = __ldcg(&P.cand_sum[c]);
+    if (gm > m || (gm == m && gi < idx)) {
+      s = s * expf(m - gm) + gs;
+      m = gm;
+      idx = gi;
+    } else {
+      s += gs * expf(gm - m);
+    }
+  }
   for (int o = 16; o > 0; o >>= 1) {
     const float om = __shfl_xor_sync(0xffffffffu, m, o);
     const float os = __shfl_xor_sync(0xffffffffu, s, o);
     const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    pk_argmax_merge(m, s, idx, om, os, oi);
+    if (oi == 0x7FFFFFFF) continue;
+    if (idx == 0x7FFFFFFF || om > m || (om == m && oi < idx)) {
+      s = (idx == 0x7FFFFFFF ? 0.0f : s * expf(m - om)) + os;
+      m = om;
+      idx = oi;
+    } else {
+      s += os * expf(om - m);
+    }
   }
   if (lane == 0) {
     P.token[0] = idx;

@@ -650,11 +650,7 @@ static bool pk_gemv_stage(kib_qwen35* m, PkStage& S, int kind, const std::vector
     rows += r;
   }
   S.rows = rows;
-  int cap = (kPkSlotBytes / (S.paired ? 2 : 1)) / row_bytes / g * g;
-  // the tile's scale coefficients must fit the kernel's table
-  const int coef_per_row = (type == kTypeQ4K ? cols / 32 : cols / 16) * (S.paired ? 2 : 1);
-  const int coef_cap = (type == kTypeQ4K ? kPkCoefs / 2 : kPkCoefs) / coef_per_row;
-  cap = std::min(cap, coef_cap / g * g);
+  const int cap = (kPkSlotBytes / (S.paired ? 2 : 1)) / row_bytes / g * g;
   int want = (rows + grid - 1) / grid;
   want = (want + g - 1) / g * g;
   S.tile_rows = std::max(g, std::min(cap, want));
@@ -1259,12 +1255,6 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   for (uint64_t i = 0; i < steps; ++i) ENG_CUDA(cudaGraphLaunch(g, st));
   if (tokens_out) ENG_CUDA(cudaMemcpyAsync(tokens_out, m->d_log, steps * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
   int rc = sync_check(m, "decode");
-  if (use_pk) {
-    unsigned long long diag = 0;
-    cudaMemcpyFromSymbol(&diag, g_pk_diag, sizeof(diag));
-    if (diag) std::fprintf(stderr, "persistent decode: misaligned load at site %llu, address low bits 0x%llx\n",
-                           diag >> 32, diag & 0xFFFFFFFFull);
-  }
   if (rc) {
     if (use_pk) cudaMemset(m->d_pk_ctr, 0, 2 * sizeof(unsigned));  // an aborted step leaves its tickets behind
     return rc;
@@ -1282,11 +1272,11 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
       static const char* names[] = {"gemv", "gdn", "attn", "merge", "head"};
       auto rel = [&](unsigned long long v) { return v ? static_cast<long long>(v - h[0]) : -1ll; };
       std::fprintf(f, "stage,kind,type,rows,cols,start_ns,prologue_ns,first_tile_ns,done_ns,next_ns,max_done_ns,"
-                      "prod_stage_ns,prod_issue_ns,ux_ns,p8,p9,p10,p11,p12\n");
+                      "prod_stage_ns,prod_issue_ns,ux_ns,p8,p9,p10,p11\n");
       for (int i = 0; i < m->pk_n; ++i) {
         const unsigned long long* t = h.data() + 16 * i;
         std::fprintf(f, "%d,%s,%d,%d,%d", i, names[stages[i].kind], stages[i].type, stages[i].rows, stages[i].cols);
-        const int order[] = {0, 1, 2, 3, 16, 5, 6, 7, 4, 8, 9, 10, 11, 12};
+        const int order[] = {0, 1, 2, 3, 16, 5, 6, 7, 4, 8, 9, 10, 11};
         for (int k : order) std::fprintf(f, ",%lld", rel(t[k]));
         std::fprintf(f, "\n");
       }
