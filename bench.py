@@ -11,8 +11,11 @@ argmax).  Weights (513 MB) exceed L2 (126 MB), so no flush is needed.
   e2e    the same metric through the public C ABI with host buffers: per step
          kib_qwen35_forward() copies the token and position host->device and
          reads the argmax back (the reference's per-token loop)
-  roofline  the dominant kernel family (K-quant GEMV) on BASELINE config 1,
-         Q4_K 3584x1024, over a rotating pool of weight copies > 4x L2
+  roofline  the dominant kernel, decode_persistent_kernel (one launch per
+         token, with the embedding row gather before it): algorithmic bytes
+         per token / device time per token, against the measured HBM copy peak
+  matvec_config1  BASELINE config 1 on its own: the Q4_K 3584x1024 GEMV kernel
+         over a rotating pool of weight copies > 4x L2
   cpu_baseline  the CPU oracle's decode step on the host cores (bounded sample)
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kib|reference]
@@ -38,6 +41,11 @@ WORKLOAD = "qwen35-0.8b-shape-q4_k_m-bs1-greedy-decode-ctx4096"
 # (24 layers 304.7 + Q6_K LM head 208.6), GDN S r+w 37.7, conv R r+w 2.7,
 # KV read 50.3 (6 layers x 4096 x 2 heads x 256 x 2 B x K,V).
 TOKEN_BYTES = 604.0e6
+# DRAM bytes per token of decode_persistent_kernel from ncu (dram__bytes_read.sum
+# + dram__bytes_write.sum), the capture summarised in
+# profiles/decode_persistent_small_full.md (a 4-layer capture scaled to the full
+# model by algorithmic bytes: traffic/algorithmic = 1.005).
+PK_TRAFFIC = 607.0e6  # 1.005 x 604 MB: the 4-layer capture scaled by its algorithmic bytes
 
 
 def peaks():
@@ -330,9 +338,15 @@ def main():
     hbm_peak, peak_kind = peaks()
     line = None
     if rank == 0:
-        roof = matvec_roofline(ctx, hbm_peak)
-        roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"
+        mv = matvec_roofline(ctx, hbm_peak)
+        mv["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"
         step_achieved = TOKEN_BYTES / (ms / args.steps * 1e-3) / 1e9
+        persistent = os.environ.get("KIB_PERSISTENT", "1") != "0"
+        roof = {"bound": "hbm", "achieved": round(step_achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(step_achieved / hbm_peak, 4), "traffic": PK_TRAFFIC,
+                "kernel": "decode_persistent_kernel" if persistent else "per-kernel decode graph",
+                "bytes_per_launch": TOKEN_BYTES, "us_per_launch": round(ms / args.steps * 1e3, 2),
+                "peak_kind": mv["peak_kind"]}
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             threads = os.cpu_count() or 1
@@ -340,7 +354,9 @@ def main():
             cpu = {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port",
                    "sample": f"{n} oracle decode steps at position {CONTEXT} in {dt:.1f} s "
                              f"(oracle/kib_oracle.cpp, {threads} threads)"}
-        launches_per_step = 2 + 5 * int(m.plan.main_layers)
+        # persistent path: embedding gather + the persistent kernel; otherwise
+        # the per-kernel graph (embedding, 5 per layer... plus the head)
+        launches_per_step = 2 if persistent else 2 + 5 * int(m.plan.main_layers)
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32 (K-quant weights, F16 KV)",
@@ -353,8 +369,7 @@ def main():
                 "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
                         "api": "kib_qwen35_forward (token + position H2D, argmax D2H, per-token sync)"},
                 "roofline": roof,
-                "step_roofline": {"bound": "hbm", "bytes_per_token": TOKEN_BYTES, "achieved": round(step_achieved, 1),
-                                  "peak": hbm_peak, "unit": "GB/s", "frac": round(step_achieved / hbm_peak, 4)},
+                "matvec_config1": mv,
                 "cpu_baseline": cpu, "gpu_launches": launches_per_step * args.steps,
                 "clocks": clk.summary(),
                 "tokens_head": [int(x) for x in out[:8]]}

@@ -858,6 +858,23 @@ static cudaError_t pk_launch(kib_qwen35* m, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, decode_persistent_kernel, P);
 }
 
+// The per-token graph of the persistent path: the embedding row gather, then
+// the persistent decode kernel (programmatic dependent launch between them).
+static int ensure_pk_graph(kib_qwen35* m) {
+  if (m->pk_graph) return KIB_OK;
+  auto body = [&](Enq& q) {
+    q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, m->d_tokens, 1, m->d_h, m->H, q.st), "embed");
+    q.run(pk_launch(m, q.st), "decode_persistent");
+  };
+  int rc = capture(m, &m->pk_graph, body);
+  if (rc && m->pk_coop) {  // the cooperative attribute is not accepted together with PDL on every driver
+    cudaGetLastError();
+    m->pk_coop = false;
+    rc = capture(m, &m->pk_graph, body);
+  }
+  return rc;
+}
+
 int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* opt, kib_qwen35** out) {
   if (!ctx || !path || !out) return KIB_ERR_INVALID_ARGUMENT;
   *out = nullptr;
@@ -1144,6 +1161,28 @@ int kib_qwen35_forward(kib_qwen35* m, const int32_t* tokens, uint64_t n, int adv
   if (!m || !tokens || n < 1 || n > kMaxSmallT) return KIB_ERR_INVALID_ARGUMENT;
   if (m->pos + n > static_cast<uint64_t>(m->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "forward exceeds cache capacity");
   cudaStream_t st = m->ctx->stream;
+  if (n == 1 && !logits && !normed_hidden && m->pk_on) {
+    // one token, argmax only: the persistent decode path (its head writes the
+    // argmax to the token log and advances the device position)
+    int rc = ensure_pk_graph(m);
+    if (rc) return rc;
+    m->h_pin[0] = static_cast<int>(m->pos);
+    m->h_pin[1] = tokens[0];
+    m->h_pin[2] = 0;
+    ENG_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, st));
+    ENG_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_pin + 1, sizeof(int), cudaMemcpyHostToDevice, st));
+    ENG_CUDA(cudaMemcpyAsync(m->d_step, m->h_pin + 2, sizeof(int), cudaMemcpyHostToDevice, st));
+    ENG_CUDA(cudaGraphLaunch(m->pk_graph, st));
+    ENG_CUDA(cudaMemcpyAsync(m->h_pin + 32, m->d_log, sizeof(int), cudaMemcpyDeviceToHost, st));
+    rc = sync_check(m, "forward");
+    if (rc) {
+      cudaMemset(m->d_pk_ctr, 0, 2 * sizeof(unsigned));
+      return rc;
+    }
+    if (argmax_out) argmax_out[0] = m->h_pin[32];
+    if (advance) m->pos += 1;
+    return KIB_OK;
+  }
   std::memcpy(m->h_pin + 16, tokens, n * sizeof(int32_t));
   m->h_pin[0] = static_cast<int>(m->pos);
   ENG_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, st));
@@ -1221,17 +1260,8 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   if (steps > (1u << 20)) return KIB_ERR_INVALID_ARGUMENT;
   cudaStream_t st = m->ctx->stream;
   const bool use_pk = m->pk_on;
-  if (use_pk && !m->pk_graph) {
-    auto body = [&](Enq& q) {
-      q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, m->d_tokens, 1, m->d_h, m->H, q.st), "embed");
-      q.run(pk_launch(m, q.st), "decode_persistent");
-    };
-    int rc = capture(m, &m->pk_graph, body);
-    if (rc && m->pk_coop) {  // the cooperative attribute is not accepted together with PDL on every driver
-      cudaGetLastError();
-      m->pk_coop = false;
-      rc = capture(m, &m->pk_graph, body);
-    }
+  if (use_pk) {
+    int rc = ensure_pk_graph(m);
     if (rc) return rc;
   }
   if (!use_pk && !m->decode_graph) {

@@ -185,3 +185,23 @@ def test_persistent_decode_full_width_matches_oracle(ctx, oracle, full_width_mod
     otoks, _ = om.generate_from(160, nxt, 25, mtp_draft_tokens=0)
     om.close()
     assert toks == list(otoks[1:25])
+
+
+def test_forward_one_token_argmax_matches_decode(ctx, small_model):
+    """kib_qwen35_forward with one token and only the argmax requested (the
+    per-token host loop) gives the same tokens as the device-side greedy loop."""
+    p = prompt(20, SMALL["vocab"], 9)
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=64)
+    nxt = m.prefill(p)
+    toks = list(m.decode_greedy(nxt, 16))
+    m.close()
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=64)
+    tok = m.prefill(p)
+    got = []
+    for _ in range(16):
+        am, _, _ = m.forward([tok], advance=True)
+        tok = int(am[0])
+        got.append(tok)
+    assert m.position == 20 + 16
+    m.close()
+    assert got == toks
