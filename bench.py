@@ -242,7 +242,8 @@ def run_reference(args, rank, world):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * secs / max(toks, 1), 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "context": CONTEXT, "quant_mix": "Q4_K + Q6_K ffn_down/head",
-                       "l2": "weights 513 MB > L2"},
+                       "l2": "weights 513 MB > L2", "reduced_model_for_profiling": bool(MODEL_OVERRIDES),
+                       "parallelism": f"rank 0 of {world} (CPU arm)"},
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": f"{toks} decode steps at position {CONTEXT} (oracle/kib_oracle.cpp, "
                                        f"{threads} threads)"},
