@@ -14,7 +14,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libkib.so")
 SOURCES = ["ops.cu", "engine.cu", "noalloc.cu", "gguf.cpp"]
-HEADERS = ["kib_common.cuh", "kquant.cuh", "kquant_gemv.cuh", "kquant_gemv2.cuh", "layer_kernels.cuh", "kib_ctx.cuh", "gguf.hpp"]
+HEADERS = ["kib_common.cuh", "kquant.cuh", "kquant_gemv.cuh", "kquant_gemv2.cuh", "decode_persistent.cuh", "layer_kernels.cuh", "kib_ctx.cuh", "gguf.hpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-pthread",

@@ -53,6 +53,7 @@ constexpr int kPkMaxCols = 4096;
 constexpr int kPkMaxSegs = 4;
 constexpr int kPkMaxSplits = 128;
 constexpr int kPkGdnRows = 16;  // state rows per GDN item
+constexpr int kPkMaxTileRows = 256;  // rows of a GEMV tile
 
 enum PkKind : int { kPkGemv = 0, kPkGdn = 1, kPkAttn = 2, kPkMerge = 3, kPkHead = 4 };
 
@@ -145,6 +146,8 @@ struct PkShared {
   int bidx[16];
   int abort;
   int last;
+  float4 ep[kPkMaxTileRows];   // GEMV: per-row epilogue inputs of the tile
+  float4 epw[kPkMaxTileRows];
   __align__(16) float xs[kPkMaxCols + kPkMaxCols / 16];  // padded stage input; attention/GDN scratch
   float ws[kPkMaxSplits];
   float ls[kPkMaxSplits];
@@ -197,6 +200,7 @@ struct PkProducer {
           break;
         }
         if ((i & 255u) == 255u && *reinterpret_cast<volatile int*>(&sh->abort)) break;
+        __nanosleep(200);  // the ring is full: leave the issue slots to the consumer warps
       }
       if (!ok) {
         if (!*reinterpret_cast<volatile int*>(&sh->abort)) atomicExch(err, 4);
@@ -526,17 +530,33 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, PkArgmax& am) {
   const int grid = static_cast<int>(gridDim.x);
   #pragma unroll 1
   for (int t = static_cast<int>(blockIdx.x); t < S.ntiles; t += grid) {
-    const uint8_t* tile = cs.take();
-    if (!tile) return false;
     const int r0 = t * S.tile_rows;
     const int nr = min(S.tile_rows, S.rows - r0);
+    // the epilogue inputs of every row of the tile (residual, conv state and
+    // weights) are loaded at once, before the tile is waited for
+    if (tid < nr) {
+      const int si = pk_seg_of(S, r0 + tid);
+      const int row = r0 + tid - S.seg[si].row_begin;
+      const int epi = S.seg[si].epi;
+      if (epi == kEpiResidual) {
+        cs.sh->ep[tid] = make_float4(S.resid[row], 0.f, 0.f, 0.f);
+      } else if (epi == kEpiConv) {
+        const float* st = S.conv_state + static_cast<size_t>(row) * 3;
+        cs.sh->ep[tid] = make_float4(st[0], st[1], st[2], 0.f);
+        cs.sh->epw[tid] = *reinterpret_cast<const float4*>(S.conv_w + static_cast<size_t>(row) * 4);
+      }
+    }
+    const uint8_t* tile = cs.take();
+    if (!tile) return false;
+    pk_sync();  // ep / epw
+    const bool trt = cs.tr && t == static_cast<int>(blockIdx.x);
+    if (trt) cs.tr[8] = gtimer();
     const int passes = (nr + groups - 1) / groups;
 #pragma unroll 1
     for (int pass = 0; pass < passes; ++pass) {
       const int rl = pass * groups + group;
       const bool ok = rl < nr;
       const int r = r0 + rl;
-      // the leader starts the epilogue's loads before the dot product
       int si = 0, row = 0, epi = kEpiStore;
       float pre0 = 0.0f, pre1 = 0.0f, pre2 = 0.0f;
       float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -544,15 +564,11 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, PkArgmax& am) {
         si = pk_seg_of(S, r);
         row = r - S.seg[si].row_begin;
         epi = S.seg[si].epi;
-        if (epi == kEpiResidual) {
-          pre0 = S.resid[row];
-        } else if (epi == kEpiConv) {
-          const float* st = S.conv_state + static_cast<size_t>(row) * 3;
-          pre0 = st[0];
-          pre1 = st[1];
-          pre2 = st[2];
-          cw = *reinterpret_cast<const float4*>(S.conv_w + static_cast<size_t>(row) * 4);
-        }
+        const float4 e = cs.sh->ep[rl];
+        pre0 = e.x;
+        pre1 = e.y;
+        pre2 = e.z;
+        if (epi == kEpiConv) cw = cs.sh->epw[rl];
       }
       float acc[1] = {0.0f}, acc2[1] = {0.0f};
       if (ok && active) {
@@ -564,6 +580,11 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, PkArgmax& am) {
           unit_dot<QT, 1>(b0 + hh * (kPkSlotBytes / 2), u, ux, a);
           if (hh == 0) acc[0] = a[0]; else acc2[0] = a[0];
         }
+      }
+      if (trt && pass == 0) {
+        unsigned long long tt;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tt) : "f"(acc[0]));
+        cs.tr[9] = tt;
       }
       const int lim = RG < 32 ? RG : 32;
       for (int o = lim / 2; o > 0; o >>= 1) {
@@ -611,8 +632,11 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, PkArgmax& am) {
           if (g.out) g.out[row] = v;
         }
       }
+      if (trt && pass == 0) cs.tr[10] = gtimer();
     }
+    if (trt) cs.tr[11] = gtimer();
     cs.release();
+    if (trt) cs.tr[12] = gtimer();
   }
   return true;
 }
@@ -685,6 +709,30 @@ KIB_DEV bool pk_gdn(const PkStage& S, PkCons& cs) {
     cs.release();  // also orders qn/kn reuse
   }
   return true;
+}
+
+// Sums 8 values over the warp; every lane ends with the 8 totals.  Three
+// halving exchanges leave each lane one value summed over 8 lanes, two more
+// finish it, and 8 broadcasts return the totals (17 shuffles instead of 40).
+KIB_DEV void pk_warp_sum8(float (&v)[8], int lane) {
+  float a[4], b[2];
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = h16 ? v[i] : v[i + 4], keep = h16 ? v[i + 4] : v[i];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = h8 ? a[i] : a[i + 2], keep = h8 ? a[i + 2] : a[i];
+    b[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float c = (h4 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h4 ? b[0] : b[1], 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  // lane L holds the total of value ((L >> 4) & 1) * 4 + ((L >> 3) & 1) * 2 + ((L >> 2) & 1)
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = __shfl_sync(0xffffffffu, c, ((e >> 2) & 1) << 4 | ((e >> 1) & 1) << 3 | (e & 1) << 2);
 }
 
 // qk_norm (mps_backend.mm:1991-2024) then mrope (2482-2527) of one 256-wide
@@ -788,8 +836,9 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
         }
         sc[e] = d;
       }
+      pk_warp_sum8(sc, lane);
 #pragma unroll
-      for (int e = 0; e < KB; ++e) sc[e] = warp_sum(sc[e]) * scale;
+      for (int e = 0; e < KB; ++e) sc[e] *= scale;
       float mx = m;
 #pragma unroll
       for (int e = 0; e < KB; ++e)

@@ -650,13 +650,21 @@ static bool pk_gemv_stage(kib_qwen35* m, PkStage& S, int kind, const std::vector
     rows += r;
   }
   S.rows = rows;
-  const int cap = (kPkSlotBytes / (S.paired ? 2 : 1)) / row_bytes / g * g;
+  const int cap = std::min((kPkSlotBytes / (S.paired ? 2 : 1)) / row_bytes, kPkMaxTileRows) / g * g;
   int want = (rows + grid - 1) / grid;
   want = (want + g - 1) / g * g;
-  S.tile_rows = std::max(g, std::min(cap, want));
-  S.ntiles = (rows + S.tile_rows - 1) / S.tile_rows;
   const int units = cols / 64;
   S.rg = units <= 16 ? 16 : units <= 32 ? 32 : 64;
+  S.tile_rows = std::max(g, std::min(cap, want));
+  if (want > cap) {
+    // several tiles per CTA: make a tile a whole number of passes of the
+    // CTA's row groups, so no pass runs part-empty
+    const int groups = kPkConsumers / S.rg;
+    int l = groups;
+    while (l % g) l += groups;  // lcm(groups, g)
+    if (cap >= l) S.tile_rows = cap / l * l;
+  }
+  S.ntiles = (rows + S.tile_rows - 1) / S.tile_rows;
   S.eps = m->eps;
   return cap >= g;
 }
@@ -1302,11 +1310,11 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
       static const char* names[] = {"gemv", "gdn", "attn", "merge", "head"};
       auto rel = [&](unsigned long long v) { return v ? static_cast<long long>(v - h[0]) : -1ll; };
       std::fprintf(f, "stage,kind,type,rows,cols,start_ns,prologue_ns,first_tile_ns,done_ns,next_ns,max_done_ns,"
-                      "prod_stage_ns,prod_issue_ns,ux_ns,p8,p9,p10,p11\n");
+                      "prod_stage_ns,prod_issue_ns,ux_ns,p8,p9,p10,p11,p12\n");
       for (int i = 0; i < m->pk_n; ++i) {
         const unsigned long long* t = h.data() + 16 * i;
         std::fprintf(f, "%d,%s,%d,%d,%d", i, names[stages[i].kind], stages[i].type, stages[i].rows, stages[i].cols);
-        const int order[] = {0, 1, 2, 3, 16, 5, 6, 7, 4, 8, 9, 10, 11};
+        const int order[] = {0, 1, 2, 3, 16, 5, 6, 7, 4, 8, 9, 10, 11, 12};
         for (int k : order) std::fprintf(f, ",%lld", rel(t[k]));
         std::fprintf(f, "\n");
       }
