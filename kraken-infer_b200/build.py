@@ -34,7 +34,7 @@ def build(force=False, verbose=False, ptxas_info=False):
     if not force and not _stale():
         return LIB
     os.makedirs(LIB_DIR, exist_ok=True)
-    objs = []
+    objs, cmds = [], []
     for src in SOURCES:
         obj = os.path.join(LIB_DIR, src + ".o")
         cmd = [NVCC] + ARCH + FLAGS + ["-c", os.path.join(CSRC, src), "-o", obj]
@@ -42,8 +42,14 @@ def build(force=False, verbose=False, ptxas_info=False):
             cmd += ["-Xptxas", "-v"]
         if verbose:
             print(" ".join(cmd))
-        subprocess.check_call(cmd)
+        cmds.append(cmd)
         objs.append(obj)
+    # the translation units are independent: compile them side by side
+    procs = [subprocess.Popen(c) for c in cmds]
+    codes = [p.wait() for p in procs]
+    for c, rc in zip(cmds, codes):
+        if rc:
+            raise subprocess.CalledProcessError(rc, c)
     cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs
     if verbose:
         print(" ".join(cmd))

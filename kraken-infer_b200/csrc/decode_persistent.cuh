@@ -3,23 +3,41 @@
 // The bs1 decode step of the hybrid decoder after the token embedding (24
 // layers of GDN or attention blocks with their FFNs, the fused LM-head argmax)
 // runs as a single persistent grid: one CTA per SM, eight consumer warps and one
-// producer warp.  The step is a host-built list of stages (PkStage); between
-// dependent stages the consumers meet at a grid barrier.  The producer warp
-// walks the same list independently and streams everything the consumers will
-// read from HBM -- weight row tiles, the GDN state rows, the cached K/V rows --
-// into a ring of shared-memory slots with cp.async.bulk, so the weight stream
-// runs ahead across the barriers instead of restarting after every kernel
-// boundary.  Weights are constant, so the producer starts them before
-// griddepcontrol.wait (overlapping the previous token's tail); everything
-// written by the previous step is read only after it.
+// producer warp.  The step is a host-built list of stages (PkStage).  The
+// producer warp walks the same list independently and streams everything the
+// consumers will read from HBM -- weight row tiles, the GDN state rows, the
+// cached K/V rows -- into a ring of shared-memory slots with cp.async.bulk, so
+// the weight stream runs ahead of the arithmetic instead of restarting after
+// every kernel boundary.  Weights are constant, so the producer starts them
+// before griddepcontrol.wait (overlapping the previous token's tail);
+// everything written by the previous step is read only after it.
+//
+// Stages do not meet at grid barriers.  Every activation one CTA hands to
+// another inside the step is a *cell*: 8 bytes holding the fp32 value and a
+// 32-bit tag (step epoch << 8 | writing stage + 1), written with one 64-bit
+// store.  A reader loads the cells it needs and re-loads them until every tag
+// is the expected one.  The value and its tag travel in one single-copy-atomic
+// access, so no fence is needed on either side, a stage starts as soon as the
+// rows it reads exist (a GDN head waits only for its own q/k/v rows), and the
+// barrier's fence + ticket + poll round trips disappear from the critical path.
+// Every stage writes its own cell array, so no cell is rewritten within a step;
+// the epoch advances once per step (by the LM head's last CTA).
+//
+// Code size is a first-order cost here: every stage runs a different part of
+// the kernel once, so instructions come from the instruction cache only if the
+// whole step's code fits in it (on B200 a working set above ~64 KB runs at
+// several cycles per instruction, fetched from L2).  The kernel therefore keeps
+// one copy of each routine: one GEMV for both K-quant types, the slow paths
+// (cell polls, transcendental helpers) out of line, and little unrolling
+// outside the dot-product core.
 //
 // Stage kinds and the reference ops they carry (the same fused groups as the
 // per-kernel path in kquant_gemv2.cuh / layer_kernels.cuh):
 //   kPkGemv / kPkHead  K-quant matvec with a prologue (input, RMSNorm or per-head
-//                      norm-gate) and
-//                      per-segment epilogues (store, residual add, conv+silu,
-//                      silu*up, argmax) -- q*_k_matvec, mps_backend.mm:295-463;
-//                      rms_norm 1891-1921; ssm_conv 2376-2457; argmax 2681-2779
+//                      norm-gate) and per-segment epilogues (store, residual
+//                      add, conv+silu, silu*up, argmax) -- q*_k_matvec,
+//                      mps_backend.mm:295-463; rms_norm 1891-1921; ssm_conv
+//                      2376-2457; argmax 2681-2779
 //   kPkGdn             split_qkv_l2_norm + gate/beta prepare + delta-rule
 //                      update of 16 state rows (mps_backend.mm:2097-2153,
 //                      2588-2605, 2307-2374)
@@ -28,7 +46,7 @@
 //   kPkMerge           combine of the splits + sigmoid(gate)
 //                      (qwen35_runtime.cpp:3347-3351)
 //
-// Every wait is bounded: a barrier or mbarrier wait that runs out raises the
+// Every wait is bounded: a cell poll or mbarrier wait that runs out raises the
 // error flag, and all warps then leave the step (the producer first waits,
 // again bounded, for the copies it has in flight).
 #pragma once
@@ -42,34 +60,102 @@ constexpr int kPkWarps = 8;                    // consumer warps
 constexpr int kPkConsumers = kPkWarps * 32;
 // + one producer warpgroup (warps 8-11; warp 8 issues the copies).  The block
 // launches at 168 registers a thread (384 x 168 = 64512); the producer
-// warpgroup then gives back down to 40 and the consumers take 232:
-// 256 x 232 + 128 x 40 = 64512, the launch total.
+// warpgroup then gives back down to kPkProducerRegs and the consumers take
+// kPkConsumerRegs: 256 x 232 + 128 x 40 = 64512, the launch total.
 constexpr int kPkThreads = kPkConsumers + 128;
-constexpr int kPkProducerRegs = 40;
 constexpr int kPkConsumerRegs = 232;
+constexpr int kPkProducerRegs = (kPkThreads * 168 - kPkConsumers * kPkConsumerRegs) / 128;
+static_assert(kPkProducerRegs >= 24 && kPkProducerRegs % 8 == 0, "register split");
 constexpr int kPkSlots = 6;
 constexpr int kPkSlotBytes = 32 * 1024;
 constexpr int kPkMaxCols = 4096;
 constexpr int kPkMaxSegs = 4;
 constexpr int kPkMaxSplits = 128;
-constexpr int kPkGdnRows = 16;  // state rows per GDN item
+constexpr int kPkGdnRows = 16;       // state rows per GDN item
 constexpr int kPkMaxTileRows = 256;  // rows of a GEMV tile
+constexpr int kPkRows = 2;           // rows a lane dots per pass (independent chains, half the passes)
+constexpr int kPkMaxStages = 254;    // stage tags are 1..254 in the low byte
+constexpr int kPkRopePairs = 128;    // rotary pairs with a precomputed frequency
+constexpr uint32_t kPkPollLimit = 1u << 21;
 
 enum PkKind : int { kPkGemv = 0, kPkGdn = 1, kPkAttn = 2, kPkMerge = 3, kPkHead = 4 };
+
+// ------------------------------------------------------------------ cells
+// A cell is {fp32 value, 32-bit tag} in one aligned 64-bit word.
+KIB_DEV void cell_st(uint64_t* p, float v, uint32_t tag) {
+  const uint64_t c = (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(c) : "memory");
+}
+KIB_DEV ulonglong2 cell_ld2(const uint64_t* p) {
+  ulonglong2 r;
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(r.x), "=l"(r.y) : "l"(p) : "memory");
+  return r;
+}
+KIB_DEV uint64_t cell_ld1(const uint64_t* p) {
+  uint64_t r;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
+  return r;
+}
+KIB_DEV bool cell_ok(uint64_t c, uint32_t tag) { return static_cast<uint32_t>(c >> 32) == tag; }
+KIB_DEV float cell_val(uint64_t c) { return __uint_as_float(static_cast<uint32_t>(c)); }
+
+// Asynchronous global -> shared copies (no register destination, so an
+// out-of-line call made while they are in flight does not wait for them).
+KIB_DEV void cp_async_ca4(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+KIB_DEV void cp_async_ca16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+// L2 only: for data other CTAs rewrite every step (cells)
+KIB_DEV void cp_async_cg16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+KIB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+KIB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Out-of-line poll of one cell: re-loads until it carries `tag`.  Returns the
+// cell, or 0 (tag 0 is never a stage tag) when the poll limit runs out or
+// another CTA raised the error flag.
+__device__ __noinline__ uint64_t pk_poll1(const uint64_t* p, uint32_t tag, const int* err) {
+  #pragma unroll 1
+  for (uint32_t i = 0; i < kPkPollLimit; ++i) {
+    const uint64_t c = cell_ld1(p);
+    if (cell_ok(c, tag)) return c;
+    if ((i & 255u) == 255u && *reinterpret_cast<const volatile int*>(err) != 0) break;
+  }
+  return 0;
+}
+// Loads one cell and waits for it; ok becomes false on a failed wait.
+KIB_DEV float pk_cell(const uint64_t* p, uint32_t tag, const int* err, bool& ok) {
+  uint64_t c = cell_ld1(p);
+  if (!cell_ok(c, tag)) {
+    c = pk_poll1(p, tag, err);
+    ok = ok && cell_ok(c, tag);
+  }
+  return cell_val(c);
+}
+
+// Out-of-line copies of the transcendental helpers: each exists once in the kernel.
+__device__ __noinline__ float pk_expf(float v) { return expf(v); }
+__device__ __noinline__ float pk_silu(float v) { return v / (1.0f + expf(-v)); }
+__device__ __noinline__ float pk_sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
 
 struct PkSeg {
   const uint8_t* w;   // this segment's rows (row_bytes each)
   const uint8_t* w2;  // gate/up pair: the up matrix (same rows)
-  float* out;         // indexed by the row within the segment
+  uint64_t* out;      // cells, indexed by the row within the segment
   int row_begin;      // first stage row of the segment
   int rows;
   int epi;            // GemvEpilogue
   int pad;
 };
 
+// Input tags: 0 = plain floats written before this launch (the embedding
+// row), else the low byte of the writing stage's tag.
 struct __align__(16) PkStage {
   int kind;
-  int barrier_after;  // grid barrier between this stage and the next
+  int tag;            // low byte of the tags this stage writes (index + 1)
   // ---- GEMV / head
   int type;
   int cols;
@@ -83,39 +169,48 @@ struct __align__(16) PkStage {
   int rg;             // lanes per row (16, 32 or 64)
   int head_dim;       // norm-gate head size
   float eps;
+  int in_tag;
+  int gate_tag;
+  int resid_tag;
+  int src_tag;        // GDN / attention / merge: the stage that wrote their inputs
+  int src2_tag;       // merge: the q|gate projection
+  int pad0;
   PkSeg seg[kPkMaxSegs];
-  const float* in;
+  const void* in;      // cells (in_tag) or floats
   const float* norm_w;
-  const float* gate;
-  const float* resid;  // kEpiResidual: resid[row]
+  const uint64_t* gate;  // cells
+  const void* resid;   // kEpiResidual: resid[row], cells (resid_tag) or floats
   float* conv_state;   // kEpiConv: [rows][3]
   const float* conv_w; // kEpiConv: [rows][4]
   // ---- GDN (one token)
-  const float* conv_out;
-  int C;
-  const float* beta_raw;
-  const float* alpha_raw;
+  const uint64_t* conv_out;  // cells: q | k | v after conv + silu
+  const uint64_t* beta_raw;  // cells
+  const uint64_t* alpha_raw; // cells
   const float* dt_bias;
   const float* ssm_a;
   float* state;       // [Hv][128][128]
-  float* gdn_out;     // [Hv*128]
+  uint64_t* gdn_out;  // cells [Hv*128]
+  int C;
   int key_heads;
   int value_heads;
+  int pad1;
   // ---- attention (one token)
-  const float* qg;    // [heads][2*256] q | gate
-  const float* kp;
-  const float* vp;
+  const uint64_t* qg;  // cells [heads][2*256] q | gate
+  const uint64_t* kp;  // cells
+  const uint64_t* vp;  // cells
   const float* q_norm;
   const float* k_norm;
+  const float* rope_freq;  // [n_dims/2] 1/theta^(2p/n_dims), computed on the host
   uint16_t* kcache;   // [cap][kv_heads*256]
   uint16_t* vcache;
+  uint64_t* part;     // cells [nsplit][heads][256 + 2]
+  uint64_t* att_out;  // cells [heads*256]
   int heads;
   int kv_heads;
   float theta;
   int n_dims;
   int nsplit;         // splits per kv head (kv_heads * nsplit <= grid)
-  float* part;        // [nsplit][heads][256 + 2]
-  float* att_out;     // [heads*256]
+  int pad2;
 };
 
 struct PkProgram {
@@ -126,57 +221,62 @@ struct PkProgram {
   int* token_log;     // token_log[*step] = argmax, then ++*step
   int* step;
   float* prob_out;    // optional p(top1)
-  unsigned* bar_ctr;  // grid barrier ticket (0 at launch; reset by the last CTA)
   unsigned* head_ctr; // LM-head last-CTA ticket
+  unsigned* epoch;    // tag epoch, advanced once per step by the head's last CTA
   float* cand_max;    // [grid]
   float* cand_sum;
   int* cand_idx;
   int* err;
-  unsigned long long* trace;  // optional: CTA 0's [stage][start, prologue done, first tile, done]
+  unsigned long long* trace;  // optional: CTA 0's [stage][start, input ready, first tile, end, ...]
+  int probe;                  // timing experiments only (bit 0: skip the GEMV dot products)
+  int nslots;                 // ring slots in use (0 = all)
 };
 
 struct PkShared {
   uint64_t full[kPkSlots];
   uint64_t empty[kPkSlots];
   PkStage desc[2];
-  float red[kPkWarps][2];
+  float red[kPkWarps][4 * kPkRows];
   float gb[2];
-  float best[16];
-  float bsum[16];
-  int bidx[16];
+  float best[kPkWarps];
+  float bsum[kPkWarps];
+  int bidx[kPkWarps];
   int abort;
   int last;
-  float4 ep[kPkMaxTileRows];   // GEMV: per-row epilogue inputs of the tile
-  float4 epw[kPkMaxTileRows];
   __align__(16) float xs[kPkMaxCols + kPkMaxCols / 16];  // padded stage input; attention/GDN scratch
+  __align__(16) uint64_t epi[kPkConsumers][4];  // GEMV: a row owner's epilogue inputs (cp.async)
   float ws[kPkMaxSplits];
   float ls[kPkMaxSplits];
 };
 
 constexpr size_t kPkSmemBytes = static_cast<size_t>(kPkSlots) * kPkSlotBytes + sizeof(PkShared);
+static_assert(kPkSmemBytes <= 227 * 1024, "persistent kernel shared memory above the per-CTA limit");
 
 // named barrier over the eight consumer warps (the producer never joins)
 KIB_DEV void pk_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kPkConsumers) : "memory"); }
 
-KIB_DEV unsigned ld_acquire_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// Records a failed wait: the first error code wins, the CTA leaves the step.
+__device__ __noinline__ void pk_fail(PkShared* sh, int* err, int code) {
+  atomicCAS(err, 0, code);
+  *reinterpret_cast<volatile int*>(&sh->abort) = 1;
 }
 
-// ------------------------------------------------------------------ tiles
-// Row granule of a stage: rows per aligned bulk copy (row_bytes * granule is
-// a multiple of 16), computed on the host; tiles and segments are multiples.
+KIB_DEV void pk_mark(unsigned long long* tr, int i) {
+  if (tr) tr[i] = gtimer();
+}
 
-// Stage rows [r0, r0 + nr) of `stage` copied to dst (paired: the up rows to
-// dst + kPkSlotBytes / 2).  Called by one lane per piece.
-KIB_DEV uint32_t pk_tile_bytes(const PkStage& S, int r0, int nr) {
-  (void)r0;
-  const uint32_t b = static_cast<uint32_t>(nr) * static_cast<uint32_t>(S.row_bytes);
-  return S.paired ? 2u * b : b;
+// Key range of attention split `split` for nkeys keys (shared by producer and
+// consumers).
+KIB_DEV void pk_split_range(int nkeys, int nsplit, int split, int& kb, int& ke) {
+  int chunk = (nkeys + nsplit - 1) / nsplit;
+  chunk = (chunk + 7) & ~7;
+  kb = split * chunk;
+  ke = min(kb + chunk, nkeys);
 }
 
 // ------------------------------------------------------------------ producer
+// The producer warp's ring position; the empty barriers count one arrival per
+// consumer warp.
 struct PkProducer {
   uint8_t* ring;
   PkShared* sh;
@@ -185,17 +285,27 @@ struct PkProducer {
   int lane;
   int* err;
   uint64_t pol;
+  int nslots = kPkSlots;  // ring slots in use (timing experiments may use fewer)
+  int slot = 0;
+  uint32_t phase = 0;
 
-  // Waits for slot `seq` to be free (bounded); returns its address or null.
-  KIB_DEV uint8_t* acquire() {
-    const int slot = static_cast<int>(seq % kPkSlots);
-    const uint32_t parity = ((seq / kPkSlots) & 1u) ^ 1u;
+  KIB_DEV void advance() {
+    __syncwarp();
+    ++seq;
+    if (++slot == nslots) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+  // Waits for the current slot to be free (bounded) and arms it for `bytes`;
+  // returns its address or null.
+  KIB_DEV uint8_t* acquire(uint32_t bytes) {
     int ok = 1;
     if (lane == 0) {
       ok = 0;
       #pragma unroll 1
       for (uint32_t i = 0; i < (1u << 22); ++i) {
-        if (mbar_try_wait(&sh->empty[slot], parity)) {
+        if (mbar_try_wait(&sh->empty[slot], phase ^ 1u)) {
           ok = 1;
           break;
         }
@@ -203,18 +313,16 @@ struct PkProducer {
         __nanosleep(200);  // the ring is full: leave the issue slots to the consumer warps
       }
       if (!ok) {
-        if (!*reinterpret_cast<volatile int*>(&sh->abort)) atomicExch(err, 4);
+        if (!*reinterpret_cast<volatile int*>(&sh->abort)) atomicCAS(err, 0, 4);
         *reinterpret_cast<volatile int*>(&sh->abort) = 1;
+      } else {
+        mbar_arrive_expect_tx(&sh->full[slot], bytes);
       }
     }
     ok = __shfl_sync(0xffffffffu, ok, 0);
     return ok ? ring + static_cast<size_t>(slot) * kPkSlotBytes : nullptr;
   }
-  KIB_DEV void expect(uint32_t bytes) {
-    if (lane == 0) mbar_arrive_expect_tx(&sh->full[seq % kPkSlots], bytes);
-    __syncwarp();
-  }
-  KIB_DEV uint64_t* bar() { return &sh->full[seq % kPkSlots]; }
+  KIB_DEV uint64_t* bar() { return &sh->full[slot]; }
   KIB_DEV void dep_wait() {
     if (!waited) {
       pdl_wait();
@@ -223,7 +331,7 @@ struct PkProducer {
   }
 };
 
-KIB_DEV void pk_produce(const PkProgram& P, PkProducer& pr) {
+__device__ __noinline__ void pk_produce(const PkProgram& P, PkProducer& pr) {
   const int lane = pr.lane;
   const int grid = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
   int pos = -1;
@@ -231,69 +339,64 @@ KIB_DEV void pk_produce(const PkProgram& P, PkProducer& pr) {
   for (int s = 0; s < P.nstages; ++s) {
     const PkStage& S = P.stages[s];
     const int kind = S.kind;
-    const uint32_t seq0 = pr.seq;
     unsigned long long* tr = (P.trace && cta == 0 && lane == 0) ? P.trace + 16 * s : nullptr;
-    if (tr) tr[6] = gtimer();  // producer reached the stage
+    pk_mark(tr, 6);  // producer reached the stage
     if (kind == kPkGemv || kind == kPkHead) {
+      const int tile_rows = S.tile_rows, rows = S.rows, row_bytes = S.row_bytes, paired = S.paired;
       #pragma unroll 1
       for (int t = cta; t < S.ntiles; t += grid) {
-        uint8_t* dst = pr.acquire();
+        const int r0 = t * tile_rows;
+        const int nr = min(tile_rows, rows - r0);
+        const uint32_t b = static_cast<uint32_t>(nr) * static_cast<uint32_t>(row_bytes);
+        // probe bit 3 (timing only): no weight traffic, the tile is left as it is
+        const bool skip = P.probe & 8;
+        uint8_t* dst = pr.acquire(skip ? 0u : paired ? 2u * b : b);
         if (!dst) return;
-        const int r0 = t * S.tile_rows;
-        const int nr = min(S.tile_rows, S.rows - r0);
-        pr.expect(pk_tile_bytes(S, r0, nr));
-        if (tr && pr.seq == seq0) tr[7] = gtimer();  // first tile issued
-        if (lane < S.nseg) {
+        if (lane < S.nseg && !skip) {
           const PkSeg& g = S.seg[lane];
-          const int a = max(r0, g.row_begin), b = min(r0 + nr, g.row_begin + g.rows);
-          if (a < b) {
-            const size_t src = static_cast<size_t>(a - g.row_begin) * S.row_bytes;
-            const uint32_t bytes = static_cast<uint32_t>(b - a) * static_cast<uint32_t>(S.row_bytes);
-            uint8_t* d = dst + static_cast<size_t>(a - r0) * S.row_bytes;
+          const int a = max(r0, g.row_begin), e = min(r0 + nr, g.row_begin + g.rows);
+          if (a < e) {
+            const size_t src = static_cast<size_t>(a - g.row_begin) * row_bytes;
+            const uint32_t bytes = static_cast<uint32_t>(e - a) * static_cast<uint32_t>(row_bytes);
+            uint8_t* d = dst + static_cast<size_t>(a - r0) * row_bytes;
             bulk_g2s_stream(d, g.w + src, bytes, pr.bar(), pr.pol);
-            if (S.paired) bulk_g2s_stream(d + kPkSlotBytes / 2, g.w2 + src, bytes, pr.bar(), pr.pol);
+            if (paired) bulk_g2s_stream(d + kPkSlotBytes / 2, g.w2 + src, bytes, pr.bar(), pr.pol);
           }
         }
-        __syncwarp();
-        ++pr.seq;
+        pr.advance();
       }
     } else if (kind == kPkGdn) {
       const int items = S.value_heads * (128 / kPkGdnRows);
       #pragma unroll 1
       for (int it = cta; it < items; it += grid) {
         pr.dep_wait();  // the state was written by the previous step
-        uint8_t* dst = pr.acquire();
-        if (!dst) return;
         constexpr uint32_t bytes = kPkGdnRows * 128 * sizeof(float);
-        pr.expect(bytes);
+        uint8_t* dst = pr.acquire(bytes);
+        if (!dst) return;
         if (lane == 0) bulk_g2s(dst, S.state + static_cast<size_t>(it) * kPkGdnRows * 128, bytes, pr.bar());
-        __syncwarp();
-        ++pr.seq;
+        pr.advance();
       }
     } else if (kind == kPkAttn) {
       if (cta >= S.kv_heads * S.nsplit) continue;
       pr.dep_wait();
       if (pos < 0) pos = *P.pos;
       const int kvh = cta / S.nsplit, split = cta % S.nsplit;
-      const int nkeys = pos + 1;
-      int chunk = (nkeys + S.nsplit - 1) / S.nsplit;
-      chunk = (chunk + 7) & ~7;
-      const int kb = split * chunk, old_end = min(kb + chunk, pos);
+      int kb, ke;
+      pk_split_range(pos + 1, S.nsplit, split, kb, ke);
+      const int old_end = min(ke, pos);
       const int kvd = S.kv_heads * kHd;
       #pragma unroll 1
       for (int k0 = kb; k0 < old_end; k0 += kAttnChunk) {
-        uint8_t* dst = pr.acquire();
-        if (!dst) return;
         const int nk = min(kAttnChunk, old_end - k0);
-        pr.expect(static_cast<uint32_t>(nk) * 2u * kHd * 2u);
+        uint8_t* dst = pr.acquire(static_cast<uint32_t>(nk) * 2u * kHd * 2u);
+        if (!dst) return;
         if (lane < nk) {
           const size_t src = static_cast<size_t>(k0 + lane) * kvd + kvh * kHd;
           uint8_t* d = dst + static_cast<size_t>(lane) * 2 * kHd * 2;
           bulk_g2s(d, S.kcache + src, kHd * 2, pr.bar());
           bulk_g2s(d + kHd * 2, S.vcache + src, kHd * 2, pr.bar());
         }
-        __syncwarp();
-        ++pr.seq;
+        pr.advance();
       }
     }
   }
@@ -303,63 +406,44 @@ KIB_DEV void pk_produce(const PkProgram& P, PkProducer& pr) {
 struct PkCons {
   uint8_t* ring;
   PkShared* sh;
-  uint32_t seq = 0;
+  uint32_t tagbase = 0;  // epoch << 8
   int* err;
   unsigned long long* tr = nullptr;  // trace of the current stage (CTA 0, thread 0) or null
-  bool first = true;
+  int probe = 0;
+  int nslots = kPkSlots;
+  int slot = 0;
+  uint32_t phase = 0;
 
-  // Waits for the next ring slot (all consumer threads); null on abort.
-  KIB_DEV const uint8_t* take() {
-    const int slot = static_cast<int>(seq % kPkSlots);
-    if (!mbar_wait_bounded(&sh->full[slot], (seq / kPkSlots) & 1u, err)) {
-      sh->abort = 1;
-      return nullptr;
+  KIB_DEV uint32_t tag(int low) const { return tagbase | static_cast<uint32_t>(low); }
+  KIB_DEV void advance() {
+    if (++slot == nslots) {
+      slot = 0;
+      phase ^= 1u;
     }
-    if (tr && first) {
-      tr[2] = gtimer();
-      first = false;
+  }
+  // Waits for the next ring slot (every consumer thread); null on abort.
+  KIB_DEV const uint8_t* take() {
+    if (!mbar_wait_bounded(&sh->full[slot], phase, nullptr)) {
+      pk_fail(sh, err, 2);
+      return nullptr;
     }
     return ring + static_cast<size_t>(slot) * kPkSlotBytes;
   }
-  // Every consumer thread is done with the slot.
+  // Every consumer thread is done with the slot (CTA barrier, then one arrival
+  // per warp).
   KIB_DEV void release() {
     pk_sync();
-    if (threadIdx.x == 0) mbar_arrive(&sh->empty[seq % kPkSlots]);
-    ++seq;
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&sh->empty[slot]);
+    advance();
   }
+  // This warp is done with the slot.
+  KIB_DEV void release_warp() {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&sh->empty[slot]);
+    advance();
+  }
+  KIB_DEV bool aborted() const { return *reinterpret_cast<volatile int*>(&sh->abort) != 0; }
 };
-
-// Grid barrier of the consumer warps of all CTAs.  Returns false on abort.
-KIB_DEV bool pk_grid_sync(const PkProgram& P, PkShared* sh, unsigned target) {
-  pk_sync();  // the CTA's writes happen before thread 0's release below
-  if (threadIdx.x == 0) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.bar_ctr) : "memory");
-    uint32_t i = 0;
-    while (ld_acquire_u32(P.bar_ctr) < target) {
-      ++i;
-      if ((i & 63u) == 0u && *reinterpret_cast<volatile int*>(P.err) != 0) {
-        sh->abort = 1;
-        break;
-      }
-      if (i > (1u << 22)) {
-        atomicExch(P.err, 5);
-        sh->abort = 1;
-        break;
-      }
-    }
-  }
-  pk_sync();
-  return !*reinterpret_cast<volatile int*>(&sh->abort);
-}
-
-KIB_DEV void pk_copy_desc(PkStage* dst, const PkStage* src) {
-  constexpr int n = static_cast<int>(sizeof(PkStage) / 16);
-  static_assert(sizeof(PkStage) % 16 == 0, "PkStage must be a multiple of 16 bytes");
-  static_assert(n <= kPkConsumers, "one descriptor word per consumer thread");
-  #pragma unroll 1
-  for (int i = threadIdx.x; i < n; i += kPkConsumers)
-    reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
-}
 
 // ---- GEMV prologue: the stage's transformed input vector into sh->xs
 // The stage input lives in shared memory with 4 floats of padding after every
@@ -367,117 +451,243 @@ KIB_DEV void pk_copy_desc(PkStage* dst, const PkStage* src) {
 // Q4_K) at a stride of 68 floats, which spreads them over the banks.
 KIB_DEV int xpad(int i) { return i + 4 * (i >> 6); }
 
-// Prologue: every thread issues all of its loads (input, norm weights, gate)
-// before the first reduction, so the stage start costs one memory round trip.
-KIB_DEV void pk_prologue(const PkStage& S, PkShared* sh) {
-  float* xs = sh->xs;
+// Norm-gate prologue: qk_norm over heads of 128 (one warp per head), silu(gate),
+// mul (qwen35_runtime.cpp:2993-3003).
+__device__ __noinline__ void pk_prologue_norm_gate(const PkStage& S, PkCons& cs) {
+  float* xs = cs.sh->xs;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cols = S.cols;
-  if (S.prologue == kProNormGate) {
-    // qk_norm over heads of 128 (one warp per head), silu(gate), mul
-    // (qwen35_runtime.cpp:2993-3003)
-    constexpr int hd = 128;
-    const float4 w = *reinterpret_cast<const float4*>(S.norm_w + 4 * lane);
-#pragma unroll 1
-    for (int base = warp * hd; base < cols; base += kPkWarps * hd) {
-      const float4 y = *reinterpret_cast<const float4*>(S.in + base + 4 * lane);
-      const float4 z = *reinterpret_cast<const float4*>(S.gate + base + 4 * lane);
-      const float ss = warp_sum((y.x * y.x + y.y * y.y) + (y.z * y.z + y.w * y.w));
-      const float scale = 1.0f / sqrtf(ss / static_cast<float>(hd) + S.eps);
-      float4 o;
-      o.x = y.x * (scale * w.x) * silu_f(z.x);
-      o.y = y.y * (scale * w.y) * silu_f(z.y);
-      o.z = y.z * (scale * w.z) * silu_f(z.z);
-      o.w = y.w * (scale * w.w) * silu_f(z.w);
-      *reinterpret_cast<float4*>(xs + xpad(base + 4 * lane)) = o;
+  const uint32_t it = cs.tag(S.in_tag), gt = cs.tag(S.gate_tag);
+  constexpr int hd = 128;
+  const float4 w = *reinterpret_cast<const float4*>(S.norm_w + 4 * lane);
+  const float eps = S.eps;
+  bool ok = true;
+  #pragma unroll 1
+  for (int base = warp * hd; base < cols; base += kPkWarps * hd) {
+    // the eight cells of this lane are loaded together (one round trip)
+    const uint64_t* yc = reinterpret_cast<const uint64_t*>(S.in) + base + 4 * lane;
+    const uint64_t* zc = S.gate + base + 4 * lane;
+    ulonglong2 ya = cell_ld2(yc), yb = cell_ld2(yc + 2), za = cell_ld2(zc), zb = cell_ld2(zc + 2);
+    if (!(cell_ok(ya.x, it) & cell_ok(ya.y, it) & cell_ok(yb.x, it) & cell_ok(yb.y, it) & cell_ok(za.x, gt) &
+          cell_ok(za.y, gt) & cell_ok(zb.x, gt) & cell_ok(zb.y, gt))) {
+      bool r = true;
+      ya.x = cell_ok(ya.x, it) ? ya.x : pk_poll1(yc, it, cs.err);
+      ya.y = cell_ok(ya.y, it) ? ya.y : pk_poll1(yc + 1, it, cs.err);
+      yb.x = cell_ok(yb.x, it) ? yb.x : pk_poll1(yc + 2, it, cs.err);
+      yb.y = cell_ok(yb.y, it) ? yb.y : pk_poll1(yc + 3, it, cs.err);
+      za.x = cell_ok(za.x, gt) ? za.x : pk_poll1(zc, gt, cs.err);
+      za.y = cell_ok(za.y, gt) ? za.y : pk_poll1(zc + 1, gt, cs.err);
+      zb.x = cell_ok(zb.x, gt) ? zb.x : pk_poll1(zc + 2, gt, cs.err);
+      zb.y = cell_ok(zb.y, gt) ? zb.y : pk_poll1(zc + 3, gt, cs.err);
+      r = cell_ok(ya.x, it) & cell_ok(ya.y, it) & cell_ok(yb.x, it) & cell_ok(yb.y, it) & cell_ok(za.x, gt) &
+          cell_ok(za.y, gt) & cell_ok(zb.x, gt) & cell_ok(zb.y, gt);
+      ok = ok && r;
     }
-    pk_sync();
-    return;
+    const float y[4] = {cell_val(ya.x), cell_val(ya.y), cell_val(yb.x), cell_val(yb.y)};
+    const float z[4] = {cell_val(za.x), cell_val(za.y), cell_val(zb.x), cell_val(zb.y)};
+    const float ss = warp_sum((y[0] * y[0] + y[1] * y[1]) + (y[2] * y[2] + y[3] * y[3]));
+    const float scale = 1.0f / sqrtf(ss / static_cast<float>(hd) + eps);
+    float4 o;
+    o.x = y[0] * (scale * w.x) * pk_silu(z[0]);
+    o.y = y[1] * (scale * w.y) * pk_silu(z[1]);
+    o.z = y[2] * (scale * w.z) * pk_silu(z[2]);
+    o.w = y[3] * (scale * w.w) * pk_silu(z[3]);
+    *reinterpret_cast<float4*>(xs + xpad(base + 4 * lane)) = o;
   }
-  constexpr int kPer = kPkMaxCols / (4 * kPkConsumers);  // float4 per thread
-  float4 v[kPer], w[kPer];
-  float ss = 0.0f;
-  const bool rms = S.prologue == kProRms;
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int i = 4 * tid + 4 * kPkConsumers * k;
-    if (i < cols) {
-      v[k] = *reinterpret_cast<const float4*>(S.in + i);
-      if (rms) w[k] = *reinterpret_cast<const float4*>(S.norm_w + i);
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int i = 4 * tid + 4 * kPkConsumers * k;
-    if (i < cols) ss += (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
-  }
-  float scale = 1.0f;
-  if (rms) {
-    // rms_norm_f32_f32_batched (mps_backend.mm:1891-1921): x * rsqrt(mean(x^2)+eps) * w
-    ss = warp_sum(ss);
-    if (lane == 0) sh->red[warp][0] = ss;
-    pk_sync();
-    float tot = 0.0f;
-#pragma unroll
-    for (int q = 0; q < kPkWarps; ++q) tot += sh->red[q][0];
-    scale = 1.0f / sqrtf(tot / static_cast<float>(cols) + S.eps);
-  }
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int i = 4 * tid + 4 * kPkConsumers * k;
-    if (i < cols) {
-      float4 o = v[k];
-      if (rms) {
-        o.x = o.x * scale * w[k].x;
-        o.y = o.y * scale * w[k].y;
-        o.z = o.z * scale * w[k].z;
-        o.w = o.w * scale * w[k].w;
-      }
-      *reinterpret_cast<float4*>(xs + xpad(i)) = o;
-    }
-  }
+  if (!ok) pk_fail(cs.sh, cs.err, 7);
   pk_sync();
 }
 
-// x values of unit u of block blk from the padded stage input (element order
-// as unit_col, group sums as load_unit_x).
-template <int QT>
-KIB_DEV void pk_load_unit_x(const float* xs, int blk, int u, UnitX<QT>& ux) {
-  if (QT == kTypeQ6K) {
-    const int c = u >> 1, r = u & 1;
+// Waits for this thread's input cells (up to four groups of four at
+// i = 4*tid + 1024*k) and writes their values (times the norm weights) to xs;
+// returns the thread's sum of squares.  Every pass loads all of the thread's
+// groups at once, so a pass costs one memory round trip; each cell is loaded
+// by exactly one thread of the CTA (148 CTAs read every input line, so
+// duplicate loads would turn the line into a hot spot), and a pass that finds
+// a cell missing backs off briefly before the next.
+__device__ __noinline__ float pk_poll_input(const uint64_t* c, uint32_t t, int cols, const float* norm_w, float* xs,
+                                            const int* err, bool& ok, unsigned long long* tr) {
+  constexpr int kPer = kPkMaxCols / (4 * kPkConsumers);  // float4 per thread
+  const int tid = threadIdx.x;
+  const int n = (cols - 4 * tid + 4 * kPkConsumers - 1) / (4 * kPkConsumers);  // groups of this thread
+  float4 w[kPer];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float4* p = reinterpret_cast<const float4*>(xs + 68 * (4 * blk + 2 * c + (k >> 1)) + 32 * (k & 1) + 16 * r);
-      float s = 0.0f;
+  for (int k = 0; k < kPer; ++k) {
+    const int i = 4 * tid + 4 * kPkConsumers * k;
+    w[k] = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (norm_w && k < n) w[k] = *reinterpret_cast<const float4*>(norm_w + i);
+  }
+  float ss = 0.0f;
+  uint32_t iter = 0;
+  #pragma unroll 1
+  while (true) {
+    bool ready = true;
+    ss = 0.0f;
+    ulonglong2 a[kPer], b[kPer];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float4 f = p[j];
-        ux.v[8 * k + 2 * j] = make_float2(f.x, f.y);
-        ux.v[8 * k + 2 * j + 1] = make_float2(f.z, f.w);
-        s += (f.x + f.y) + (f.z + f.w);
+    for (int k = 0; k < kPer; ++k) {
+      const int i = 4 * tid + 4 * kPkConsumers * k;
+      if (k < n) {
+        a[k] = cell_ld2(c + i);
+        b[k] = cell_ld2(c + i + 2);
       }
-      ux.s[k] = s;
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = 4 * tid + 4 * kPkConsumers * k;
+      if (k < n) {
+        ready = ready & cell_ok(a[k].x, t) & cell_ok(a[k].y, t) & cell_ok(b[k].x, t) & cell_ok(b[k].y, t);
+        const float4 o = make_float4(cell_val(a[k].x), cell_val(a[k].y), cell_val(b[k].x), cell_val(b[k].y));
+        ss += (o.x * o.x + o.y * o.y) + (o.z * o.z + o.w * o.w);
+        *reinterpret_cast<float4*>(xs + xpad(i)) = make_float4(o.x * w[k].x, o.y * w[k].y, o.z * w[k].z, o.w * w[k].w);
+      }
+    }
+    if (ready) break;
+    if (++iter > kPkPollLimit || ((iter & 255u) == 0u && *reinterpret_cast<const volatile int*>(err) != 0)) {
+      ok = false;
+      break;
+    }
+    __nanosleep(32);
+  }
+  if (tr) tr[12] = iter;
+  return ss;
+}
+
+// Plain / RMS prologue.  The RMS norm's scalar is not applied here: xs holds
+// x * w and every thread folds 1/rms into its own unit registers, so the
+// prologue needs a single CTA barrier.  Returns the scale (1
+// for the other prologues); on a failed wait the CTA's abort flag is set
+// (checked after the barrier).
+__device__ __noinline__ float pk_prologue(const PkStage& S, PkCons& cs) {
+  if (S.prologue == kProNormGate) {
+    pk_prologue_norm_gate(S, cs);
+    return 1.0f;
+  }
+  PkShared* sh = cs.sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cols = S.cols;
+  const bool rms = S.prologue == kProRms;
+  bool ok = true;
+  float ss = 0.0f;
+  if (S.in_tag == 0) {
+    #pragma unroll 1
+    for (int i = 4 * tid; i < cols; i += 4 * kPkConsumers) {
+      const float4 o = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(S.in) + i);
+      const float4 w = rms ? *reinterpret_cast<const float4*>(S.norm_w + i) : make_float4(1.f, 1.f, 1.f, 1.f);
+      ss += (o.x * o.x + o.y * o.y) + (o.z * o.z + o.w * o.w);
+      *reinterpret_cast<float4*>(sh->xs + xpad(i)) = make_float4(o.x * w.x, o.y * w.y, o.z * w.z, o.w * w.w);
     }
   } else {
-    const float4* p = reinterpret_cast<const float4*>(xs + 68 * (4 * blk + u));
+    pk_mark(cs.tr, 13);
+    ss = pk_poll_input(reinterpret_cast<const uint64_t*>(S.in), cs.tag(S.in_tag), cols, rms ? S.norm_w : nullptr, sh->xs,
+                       cs.err, ok, cs.tr);
+  }
+  pk_mark(cs.tr, 4);
+  // rms_norm_f32_f32_batched (mps_backend.mm:1891-1921): x * rsqrt(mean(x^2)+eps) * w;
+  // the weights are applied when the units are loaded
+  ss = warp_sum(ss);
+  if (lane == 0) sh->red[warp][0] = ss;
+  if (!ok) pk_fail(sh, cs.err, 7);
+  pk_sync();
+  if (!rms) return 1.0f;
+  float tot = 0.0f;
+  #pragma unroll 1
+  for (int q = 0; q < kPkWarps; ++q) tot += sh->red[q][0];
+  return 1.0f / sqrtf(tot / static_cast<float>(cols) + S.eps);
+}
+
+// x values of one lane's unit in registers: 64 floats as 32 float2 (element
+// order as unit_col) and the sums of its four quarters (16 elements each).
+struct PkX {
+  float2 v[32];
+  float s[4];
+};
+
+// x values of unit u of block blk: the padded stage input times `scale`.  Q4_K: quarter q = elements
+// 16q..16q+15 of the 64 contiguous columns; Q6_K: quarter k = the 16-column
+// run of group k.
+KIB_DEV void pk_load_x(int type, const float* xs, int blk, int u, float scale, PkX& x) {
+  // first column of each quarter's 16-column run
+  int col0, cstep;
+  if (type == kTypeQ6K) {
+    col0 = 256 * blk + 128 * (u >> 1) + 16 * (u & 1);
+    cstep = 32;
+  } else {
+    col0 = 256 * blk + 64 * u;
+    cstep = 16;
+  }
+  #pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int col = col0 + cstep * q;
+    const float4* p = reinterpret_cast<const float4*>(xs + xpad(col));
+    float sum = 0.0f;
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      float s = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 f = p[8 * g + j];
-        ux.v[16 * g + 2 * j] = make_float2(f.x, f.y);
-        ux.v[16 * g + 2 * j + 1] = make_float2(f.z, f.w);
-        s += (f.x + f.y) + (f.z + f.w);
-      }
-      ux.s[g] = s;
+    for (int j = 0; j < 4; ++j) {
+      const float4 f = p[j];
+      const float2 a = make_float2(f.x * scale, f.y * scale), b = make_float2(f.z * scale, f.w * scale);
+      x.v[8 * q + 2 * j] = a;
+      x.v[8 * q + 2 * j + 1] = b;
+      sum += (a.x + a.y) + (b.x + b.y);
     }
+    x.s[q] = sum;
+  }
+}
+
+// Codes (16 words of 4 byte-codes, element order as unit_col) and per-quarter
+// affine coefficients (value = A*code + B) of unit u of one row's block.
+KIB_DEV void pk_decode(int type, const uint8_t* blk, int u, uint32_t (&q)[16], float (&A)[4], float (&B)[4]) {
+  if (type == kTypeQ6K) {
+    const RawUnit<kTypeQ6K> raw = load_raw<kTypeQ6K>(blk, u);
+    codes_from_raw<kTypeQ6K>(raw, u, q);
+    coeffs_from_raw<kTypeQ6K>(raw, u, A, B);
+  } else {
+    const RawUnit<kTypeQ4K> raw = load_raw<kTypeQ4K>(blk, u);
+    codes_from_raw<kTypeQ4K>(raw, u, q);
+    float a2[4], b2[4];
+    coeffs_from_raw<kTypeQ4K>(raw, u, a2, b2);
+    A[0] = A[1] = a2[0];
+    A[2] = A[3] = a2[1];
+    B[0] = B[1] = b2[0];
+    B[2] = B[3] = b2[1];
+  }
+}
+
+// Dot products of one unit of R rows with the same x: the R rows' codes are
+// decoded first and their FMA chains are independent, so loads and arithmetic
+// of different rows overlap.  Codes are the floats 0.5 + b/256 (one PRMT);
+// sum(b*x) over a quarter is 256*acc - 128*sum(x), exact up to fp32 rounding.
+template <int R>
+KIB_DEV void pk_dot_rows(int type, const uint8_t* const (&blk)[R], int u, const PkX& x, float (&out)[R]) {
+  uint32_t q[R][16];
+  float A[R][4], B[R][4];
+#pragma unroll
+  for (int k = 0; k < R; ++k) pk_decode(type, blk[k], u, q[k], A[k], B[k]);
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    float2 acc[4][2];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) acc[g][0] = acc[g][1] = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int w = 0; w < 16; ++w) {
+      const int g = w >> 2, c = w & 1;
+      acc[g][c] = ffma2(code_pair_lo(q[k][w]), x.v[2 * w], acc[g][c]);
+      acc[g][c] = ffma2(code_pair_hi(q[k][w]), x.v[2 * w + 1], acc[g][c]);
+    }
+    float r = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const float a = (acc[g][0].x + acc[g][0].y) + (acc[g][1].x + acc[g][1].y);
+      const float cx = fmaf(256.0f, a, -128.0f * x.s[g]);
+      r = fmaf(A[k][g], cx, fmaf(B[k][g], x.s[g], r));
+    }
+    out[k] = r;
   }
 }
 
 struct PkArgmax {
   float best = -INFINITY, bsum = 0.0f;
   int bidx = 0x7FFFFFFF;
+  // one row; ties -> lowest index (inline: it runs inside the GEMV pass loop)
   KIB_DEV void push(float v, int row) {
     if (v > best || (v == best && row < bidx)) {
       bsum = bsum * expf(best - v) + 1.0f;
@@ -487,198 +697,335 @@ struct PkArgmax {
       bsum += expf(v - best);
     }
   }
+  // merges another candidate (max, sum of exp(v - max), index)
+  KIB_DEV void merge(float om, float os, int oi) {
+    if (oi == 0x7FFFFFFF) return;
+    if (bidx == 0x7FFFFFFF || om > best || (om == best && oi < bidx)) {
+      bsum = (bidx == 0x7FFFFFFF ? 0.0f : bsum * pk_expf(best - om)) + os;
+      best = om;
+      bidx = oi;
+    } else {
+      bsum += os * pk_expf(om - best);
+    }
+  }
 };
 
-KIB_DEV int pk_seg_of(const PkStage& S, int r) {
-  int s = 0;
-  if (S.nseg > 1 && r >= S.seg[1].row_begin) s = 1;
-  if (S.nseg > 2 && r >= S.seg[2].row_begin) s = 2;
-  if (S.nseg > 3 && r >= S.seg[3].row_begin) s = 3;
-  return s;
+// Epilogue inputs of one output row, loaded by its owner lane before the dot
+// products so that their latency hides behind them.
+struct PkEpi {
+  int epi = kEpiStore;
+  int row = 0;
+  uint64_t* out = nullptr;
+};
+
+// Starts the copies of one output row's epilogue inputs into the owner
+// thread's shared-memory slot: the residual cell pair (or plain float pair)
+// around the row, or the conv state (3 floats) and conv weights (4 floats).
+KIB_DEV void pk_epi_issue(const PkStage& S, PkShared* sh, int r, PkEpi& e) {
+  int si = 0;
+  if (S.nseg > 1 && r >= S.seg[1].row_begin) si = 1;
+  if (S.nseg > 2 && r >= S.seg[2].row_begin) si = 2;
+  if (S.nseg > 3 && r >= S.seg[3].row_begin) si = 3;
+  const PkSeg& g = S.seg[si];
+  e.row = r - g.row_begin;
+  e.epi = g.epi;
+  e.out = g.out;
+  uint64_t* slot = sh->epi[threadIdx.x];
+  if (e.epi == kEpiResidual) {
+    if (S.resid_tag) cp_async_cg16(slot, reinterpret_cast<const uint64_t*>(S.resid) + (e.row & ~1));
+    else cp_async_ca16(slot, reinterpret_cast<const float*>(S.resid) + (e.row & ~3));
+  } else if (e.epi == kEpiConv) {
+    const float* st = S.conv_state + static_cast<size_t>(e.row) * 3;
+    float* d = reinterpret_cast<float*>(slot);
+    cp_async_ca4(d, st);
+    cp_async_ca4(d + 1, st + 1);
+    cp_async_ca4(d + 2, st + 2);
+    cp_async_ca16(d + 4, S.conv_w + static_cast<size_t>(e.row) * 4);
+  }
+  cp_async_commit();
 }
 
-template <int QT>
-KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, PkArgmax& am) {
-  constexpr int BB = kquant_block_bytes(QT);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int RG = S.rg;
-  const int groups = kPkConsumers / RG;
-  const int group = tid / RG, gl = tid % RG;
-  const bool active = gl < S.cols / 64;
-  const int blk = gl >> 2, u = gl & 3;
-  UnitX<QT> ux[1];
-  if (cs.tr) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "r"(blk));
-    cs.tr[8] = t;
-  }
-  if (active) pk_load_unit_x<QT>(cs.sh->xs, blk, u, ux[0]);
-  if (cs.tr) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(ux[0].v[31].y));
-    cs.tr[9] = t;
-    UnitX<QT> ux2;
-    pk_load_unit_x<QT>(cs.sh->xs, blk, u ^ 1, ux2);
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(ux2.v[31].y));
-    cs.tr[10] = t;
-  }
-  if (cs.tr) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(ux[0].v[31].y));
-    cs.tr[4] = t;
-  }
-  const int grid = static_cast<int>(gridDim.x);
-  #pragma unroll 1
-  for (int t = static_cast<int>(blockIdx.x); t < S.ntiles; t += grid) {
-    const int r0 = t * S.tile_rows;
-    const int nr = min(S.tile_rows, S.rows - r0);
-    // the epilogue inputs of every row of the tile (residual, conv state and
-    // weights) are loaded at once, before the tile is waited for
-    if (tid < nr) {
-      const int si = pk_seg_of(S, r0 + tid);
-      const int row = r0 + tid - S.seg[si].row_begin;
-      const int epi = S.seg[si].epi;
-      if (epi == kEpiResidual) {
-        cs.sh->ep[tid] = make_float4(S.resid[row], 0.f, 0.f, 0.f);
-      } else if (epi == kEpiConv) {
-        const float* st = S.conv_state + static_cast<size_t>(row) * 3;
-        cs.sh->ep[tid] = make_float4(st[0], st[1], st[2], 0.f);
-        cs.sh->epw[tid] = *reinterpret_cast<const float4*>(S.conv_w + static_cast<size_t>(row) * 4);
+// Epilogue of one output row (its owner lane).  Inline: an out-of-line call
+// here would save and restore the caller's unit registers on every pass.
+KIB_DEV void pk_epi_run(const PkStage& S, PkCons& cs, PkEpi& e, float v, float v2, PkArgmax& am) {
+  cp_async_wait_all();
+  const uint64_t* slot = cs.sh->epi[threadIdx.x];
+  float o;
+  if (e.epi == kEpiResidual) {
+    float res;
+    if (S.resid_tag) {
+      const uint32_t rt = cs.tag(S.resid_tag);
+      uint64_t c = slot[e.row & 1];
+      if (!cell_ok(c, rt)) {
+        c = pk_poll1(reinterpret_cast<const uint64_t*>(S.resid) + e.row, rt, cs.err);
+        if (!cell_ok(c, rt)) pk_fail(cs.sh, cs.err, 8);
       }
+      res = cell_val(c);
+    } else {
+      res = reinterpret_cast<const float*>(slot)[e.row & 3];
     }
+    o = v + res;
+  } else if (e.epi == kEpiSiluMul) {
+    o = silu_f(v) * v2;
+  } else if (e.epi == kEpiConv) {
+    // causal depthwise conv of kernel 4 over [state | new], then silu
+    const float* f = reinterpret_cast<const float*>(slot);
+    const float4 st3 = make_float4(f[0], f[1], f[2], 0.f);
+    const float4 cw = *reinterpret_cast<const float4*>(f + 4);
+    float c = 0.0f;
+    c += st3.x * cw.x;
+    c += st3.y * cw.y;
+    c += st3.z * cw.z;
+    c += v * cw.w;
+    o = silu_f(c);
+    float* st = S.conv_state + static_cast<size_t>(e.row) * 3;
+    st[0] = st3.y;
+    st[1] = st3.z;
+    st[2] = v;
+  } else if (e.epi == kEpiArgmax) {
+    am.push(v, e.row);
+    return;
+  } else {
+    o = v;
+  }
+  cell_st(e.out + e.row, o, cs.tag(S.tag));
+}
+
+// Merges the argmax candidates of a warp (butterfly); every lane ends with the total.
+__device__ __noinline__ void pk_argmax_warp(PkArgmax& a) {
+  #pragma unroll 1
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, a.best, o);
+    const float os = __shfl_xor_sync(0xffffffffu, a.bsum, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, a.bidx, o);
+    a.merge(om, os, oi);
+  }
+}
+
+// ---- LM head tail: CTA candidate, then the last CTA picks the token and
+// closes the step (token log, position, epoch)
+__device__ __noinline__ void pk_head_finish(const PkProgram& P, PkShared* sh, PkArgmax am, uint32_t epoch) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pk_argmax_warp(am);
+  if (lane == 0) {
+    sh->best[warp] = am.best;
+    sh->bsum[warp] = am.bsum;
+    sh->bidx[warp] = am.bidx;
+  }
+  pk_sync();
+  if (tid == 0) {
+    PkArgmax c;
+    #pragma unroll 1
+    for (int w = 0; w < kPkWarps; ++w) c.merge(sh->best[w], sh->bsum[w], sh->bidx[w]);
+    P.cand_max[blockIdx.x] = c.best;
+    P.cand_sum[blockIdx.x] = c.bsum;
+    P.cand_idx[blockIdx.x] = c.bidx;
+    __threadfence();
+    sh->last = atomicAdd(P.head_ctr, 1u) == gridDim.x - 1;
+  }
+  pk_sync();
+  if (!sh->last || tid >= 32) return;
+  __threadfence();
+  PkArgmax c;
+  #pragma unroll 1
+  for (unsigned i = lane; i < gridDim.x; i += 32)
+    c.merge(__ldcg(&P.cand_max[i]), __ldcg(&P.cand_sum[i]), __ldcg(&P.cand_idx[i]));
+  pk_argmax_warp(c);
+  if (lane == 0) {
+    P.token[0] = c.bidx;
+    if (P.prob_out) P.prob_out[0] = 1.0f / c.bsum;
+    if (P.token_log) {
+      const int st = *P.step;
+      P.token_log[st] = c.bidx;
+      *P.step = st + 1;
+    }
+    *P.pos = *P.pos + 1;
+    *P.head_ctr = 0u;
+    *P.epoch = epoch + 1u;
+    __threadfence();
+  }
+}
+
+// The stage's GEMV: row groups of RG lanes; each lane dots its 64-column unit
+// of kPkRows rows per pass, the partial sums are reduced across the group so
+// that lane (k * RG/kPkRows) ends with row k's total and runs its epilogue.
+// Warps go through the tiles independently: each waits for a tile itself and
+// releases it with one arrival per warp (no CTA barrier per tile).
+KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t epoch) {
+  constexpr int R = kPkRows;
+  constexpr int R_LOG2 = R == 1 ? 0 : R == 2 ? 1 : 2;
+  const int tid = threadIdx.x;
+  // per-stage constants, in registers
+  const int rg_log2 = S.rg == 16 ? 4 : S.rg == 32 ? 5 : 6;
+  const int groups = kPkConsumers >> rg_log2;
+  const int group = tid >> rg_log2, gl = tid & (S.rg - 1);
+  const int lim_log2 = rg_log2 < 5 ? rg_log2 : 5;
+  const int lim = 1 << lim_log2;
+  const int own_shift = lim_log2 - R_LOG2;
+  const int k_own = (gl & (lim - 1)) >> own_shift;
+  const bool owner2 = (gl & ((1 << own_shift) - 1)) == 0;  // holds a row total in its warp
+  const bool owner = owner2 && gl < 32;                   // writes the row
+  const int my_off = k_own * groups + group;
+  const int per_pass = groups * R;
+  const bool active = gl < (S.cols >> 6);
+  const int blk = gl >> 2, u = gl & 3;
+  const int type = S.type;
+  const int blk_off = blk * kquant_block_bytes(type);
+  const int rows = S.rows, tile_rows = S.tile_rows, ntiles = S.ntiles, row_bytes = S.row_bytes;
+  const bool paired = S.paired != 0;
+  const bool two_warps = rg_log2 > 5;
+  const int grid = static_cast<int>(gridDim.x);
+  const int cta = static_cast<int>(blockIdx.x);
+  PkArgmax am;  // LM head: this thread's rows
+  // the first pass's epilogue inputs go out before the prologue's wait
+  PkEpi e;
+  if (owner && my_off < min(tile_rows, rows - cta * tile_rows)) pk_epi_issue(S, cs.sh, cta * tile_rows + my_off, e);
+  const float scale = pk_prologue(S, cs);
+  pk_mark(cs.tr, 1);
+  if (cs.aborted()) return false;
+  PkX ux;
+  if (active) pk_load_x(type, cs.sh->xs, blk, u, scale, ux);
+  bool first = true;
+  #pragma unroll 1
+  for (int t = cta; t < ntiles; t += grid) {
+    const int r0 = t * tile_rows;
+    const int nr = min(tile_rows, rows - r0);
     const uint8_t* tile = cs.take();
     if (!tile) return false;
-    pk_sync();  // ep / epw
-    const bool trt = cs.tr && t == static_cast<int>(blockIdx.x);
-    if (trt) cs.tr[8] = gtimer();
-    const int passes = (nr + groups - 1) / groups;
-#pragma unroll 1
-    for (int pass = 0; pass < passes; ++pass) {
-      const int rl = pass * groups + group;
-      const bool ok = rl < nr;
-      const int r = r0 + rl;
-      int si = 0, row = 0, epi = kEpiStore;
-      float pre0 = 0.0f, pre1 = 0.0f, pre2 = 0.0f;
-      float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (gl == 0 && ok) {
-        si = pk_seg_of(S, r);
-        row = r - S.seg[si].row_begin;
-        epi = S.seg[si].epi;
-        const float4 e = cs.sh->ep[rl];
-        pre0 = e.x;
-        pre1 = e.y;
-        pre2 = e.z;
-        if (epi == kEpiConv) cw = cs.sh->epw[rl];
+    if (first) pk_mark(cs.tr, 2);
+    // probe bit 2 (timing only): the first tile's passes run twice, the first
+    // time without epilogues, to compare a cold and a warm run of the code
+    const int reps = (cs.probe & 4) && t == cta ? 2 : 1;
+    #pragma unroll 1
+    for (int rep = 0; rep < reps; ++rep) {
+    const bool dry = rep + 1 < reps;
+    #pragma unroll 1
+    for (int p0 = 0; p0 < nr; p0 += per_pass) {
+      const int rl = p0 + my_off;
+      if (!first && !dry && owner && rl < nr) pk_epi_issue(S, cs.sh, r0 + rl, e);
+      if (!dry) first = false;
+      float acc[R], acc2[R];
+      const uint8_t* b[R];
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        const int rk = min(p0 + k * groups + group, nr - 1);  // clamped: never past the tile
+        b[k] = tile + static_cast<size_t>(rk) * row_bytes + blk_off;
+        acc[k] = acc2[k] = 0.0f;
       }
-      float acc[1] = {0.0f}, acc2[1] = {0.0f};
-      if (ok && active) {
-        const uint8_t* b0 = tile + static_cast<size_t>(rl) * S.row_bytes + blk * BB;
-        // gate and up rows of a pair run through one copy of the dot code
-#pragma unroll 1
-        for (int hh = 0; hh <= S.paired; ++hh) {
-          float a[1] = {0.0f};
-          unit_dot<QT, 1>(b0 + hh * (kPkSlotBytes / 2), u, ux, a);
-          if (hh == 0) acc[0] = a[0]; else acc2[0] = a[0];
-        }
-      }
-      if (trt && pass == 0) {
-        unsigned long long tt;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tt) : "f"(acc[0]));
-        cs.tr[9] = tt;
-      }
-      const int lim = RG < 32 ? RG : 32;
-      for (int o = lim / 2; o > 0; o >>= 1) {
-        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
-        if (S.paired) acc2[0] += __shfl_xor_sync(0xffffffffu, acc2[0], o);
-      }
-      if (RG > 32) {
-        if (lane == 0) {
-          cs.sh->red[warp][0] = acc[0];
-          cs.sh->red[warp][1] = acc2[0];
-        }
-        pk_sync();
-        if (gl == 0) {
-          #pragma unroll 1
-          for (int w = 1; w < RG / 32; ++w) {
-            acc[0] += cs.sh->red[warp + w][0];
-            acc2[0] += cs.sh->red[warp + w][1];
+      if (active && !(cs.probe & 1)) {
+        // a gate/up pair runs both halves through one copy of the dot code
+        #pragma unroll 1
+        for (int h = 0; h <= static_cast<int>(paired); ++h) {
+          float d[R];
+          pk_dot_rows<R>(type, b, u, ux, d);
+#pragma unroll
+          for (int k = 0; k < R; ++k) {
+            if (h == 0) acc[k] = d[k];
+            else acc2[k] = d[k];
+            b[k] += kPkSlotBytes / 2;
           }
         }
-        pk_sync();
       }
-      if (gl == 0 && ok) {
-        const PkSeg& g = S.seg[si];
-        const float v = acc[0];
-        if (epi == kEpiStore) {
-          g.out[row] = v;
-        } else if (epi == kEpiResidual) {
-          g.out[row] = v + pre0;
-        } else if (epi == kEpiSiluMul) {
-          g.out[row] = silu_f(v) * acc2[0];
-        } else if (epi == kEpiConv) {
-          // causal depthwise conv of kernel 4 over [state | new], then silu
-          float c = 0.0f;
-          c += pre0 * cw.x;
-          c += pre1 * cw.y;
-          c += pre2 * cw.z;
-          c += v * cw.w;
-          g.out[row] = silu_f(c);
-          float* st = S.conv_state + static_cast<size_t>(row) * 3;
-          st[0] = pre1;
-          st[1] = pre2;
-          st[2] = v;
-        } else {  // kEpiArgmax
-          am.push(v, row);
-          if (g.out) g.out[row] = v;
+      // transposed reduction: each halving exchange keeps half of the rows on
+      // each side (lane bit lim/2 keeps rows {R/2..R-1}, ...); then a plain
+      // butterfly over the remaining lane bits
+      float v, v2;
+      if (R == 4) {
+        const bool h1 = gl & (lim >> 1), h2 = gl & (lim >> 2);
+        const float a0 = (h1 ? acc[2] : acc[0]) + __shfl_xor_sync(0xffffffffu, h1 ? acc[0] : acc[2], lim >> 1);
+        const float a1 = (h1 ? acc[3] : acc[1]) + __shfl_xor_sync(0xffffffffu, h1 ? acc[1] : acc[3], lim >> 1);
+        const float c0 = (h1 ? acc2[2] : acc2[0]) + __shfl_xor_sync(0xffffffffu, h1 ? acc2[0] : acc2[2], lim >> 1);
+        const float c1 = (h1 ? acc2[3] : acc2[1]) + __shfl_xor_sync(0xffffffffu, h1 ? acc2[1] : acc2[3], lim >> 1);
+        v = (h2 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h2 ? a0 : a1, lim >> 2);
+        v2 = (h2 ? c1 : c0) + __shfl_xor_sync(0xffffffffu, h2 ? c0 : c1, lim >> 2);
+      } else if (R == 2) {
+        const bool hi = gl & (lim >> 1);
+        v = (hi ? acc[1] : acc[0]) + __shfl_xor_sync(0xffffffffu, hi ? acc[0] : acc[1], lim >> 1);
+        v2 = (hi ? acc2[1] : acc2[0]) + __shfl_xor_sync(0xffffffffu, hi ? acc2[0] : acc2[1], lim >> 1);
+      } else {
+        v = acc[0];
+        v2 = acc2[0];
+      }
+      #pragma unroll 1
+      for (int o = lim >> (1 + R_LOG2); o > 0; o >>= 1) {
+        v += __shfl_xor_sync(0xffffffffu, v, o);
+        v2 += __shfl_xor_sync(0xffffffffu, v2, o);
+      }
+      if (two_warps) {
+        // two warps per row group: the second warp's totals through shared
+        // memory, under a barrier of the pair only
+        const int wp = (tid >> 5) & ~1;
+        if (owner2 && gl >= 32) {
+          cs.sh->red[wp + 1][2 * k_own] = v;
+          cs.sh->red[wp + 1][2 * k_own + 1] = v2;
         }
+        asm volatile("bar.sync %0, 64;" ::"r"(2 + (wp >> 1)) : "memory");
+        if (owner) {
+          v += cs.sh->red[wp + 1][2 * k_own];
+          v2 += cs.sh->red[wp + 1][2 * k_own + 1];
+        }
+        asm volatile("bar.sync %0, 64;" ::"r"(2 + (wp >> 1)) : "memory");
       }
-      if (trt && pass == 0) cs.tr[10] = gtimer();
+      if (owner && rl < nr && !dry) pk_epi_run(S, cs, e, v, v2, am);
+      if (dry && owner && rl < nr && v == 1.2345f) cell_st(e.out, v, 0);  // keeps the dry run's result live
     }
-    if (trt) cs.tr[11] = gtimer();
-    cs.release();
-    if (trt) cs.tr[12] = gtimer();
+    pk_mark(cs.tr, dry ? 10 : 11);
+    }
+    cs.release_warp();
   }
+  if (S.kind == kPkHead) pk_head_finish(P, cs.sh, am, epoch);
   return true;
 }
 
 // ---- GDN: items of (value head, 16 state rows); warp w updates rows 2w, 2w+1
-KIB_DEV bool pk_gdn(const PkStage& S, PkCons& cs) {
+__device__ __noinline__ bool pk_gdn(const PkStage& S, PkCons& cs) {
   constexpr int D = 128;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* qn = cs.sh->xs;
   float* kn = cs.sh->xs + D;
+  float* vv = cs.sh->xs + 2 * D;
   const int items = S.value_heads * (D / kPkGdnRows);
   const int key_dim = S.key_heads * D;
   const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  const uint32_t in_tag = cs.tag(S.src_tag), otag = cs.tag(S.tag);
   #pragma unroll 1
   for (int it = static_cast<int>(blockIdx.x); it < items; it += static_cast<int>(gridDim.x)) {
     const int h = it / (D / kPkGdnRows), grp = it % (D / kPkGdnRows);
     const int kh = h % S.key_heads;
+    bool ok = true;
     float qv = 0.0f, kv = 0.0f;
     if (tid < D) {
-      qv = S.conv_out[kh * D + tid];
-      kv = S.conv_out[key_dim + kh * D + tid];
+      // this head's q and k rows (and nothing else) must exist
+      qv = pk_cell(S.conv_out + kh * D + tid, in_tag, cs.err, ok);
+      kv = pk_cell(S.conv_out + key_dim + kh * D + tid, in_tag, cs.err, ok);
       const float q2 = warp_sum(qv * qv), k2 = warp_sum(kv * kv);
       if (lane == 0) {
         cs.sh->red[warp][0] = q2;
         cs.sh->red[warp][1] = k2;
       }
-    }
-    if (tid == 0) {
-      const float a = S.alpha_raw[h];
-      const float b = S.beta_raw[h];
+    } else if (tid < D + kPkGdnRows) {
+      const int r = tid - D;
+      vv[r] = pk_cell(S.conv_out + 2 * key_dim + h * D + grp * kPkGdnRows + r, in_tag, cs.err, ok);
+    } else if (tid == D + kPkGdnRows) {
+      const float a = pk_cell(S.alpha_raw + h, in_tag, cs.err, ok);
+      const float b = pk_cell(S.beta_raw + h, in_tag, cs.err, ok);
       cs.sh->gb[0] = softplus20_f(a + S.dt_bias[h]) * S.ssm_a[h];
-      cs.sh->gb[1] = sigmoid_f(b);
+      cs.sh->gb[1] = pk_sigmoid(b);
     }
+    if (!ok) pk_fail(cs.sh, cs.err, 9);
     pk_sync();
+    if (cs.aborted()) return false;
     if (tid < D) {
-      const float* r0 = &cs.sh->red[0][0];
-      const float qsum = (r0[0] + r0[2]) + (r0[4] + r0[6]);
-      const float ksum = (r0[1] + r0[3]) + (r0[5] + r0[7]);
+      float qsum = 0.0f, ksum = 0.0f;
+      #pragma unroll 1
+      for (int w = 0; w < D / 32; ++w) {
+        qsum += cs.sh->red[w][0];
+        ksum += cs.sh->red[w][1];
+      }
       qn[tid] = qv * (1.0f / fmaxf(sqrtf(qsum), S.eps));
       kn[tid] = kv * (1.0f / fmaxf(sqrtf(ksum), S.eps));
     }
-    const float ge = expf(cs.sh->gb[0]);
+    const float ge = pk_expf(cs.sh->gb[0]);
     const float beta = cs.sh->gb[1];
     const uint8_t* tile = cs.take();
     if (!tile) return false;
@@ -686,7 +1033,7 @@ KIB_DEV bool pk_gdn(const PkStage& S, PkCons& cs) {
     const float4 k4 = *reinterpret_cast<const float4*>(kn + 4 * lane);
     const float4 q4 = *reinterpret_cast<const float4*>(qn + 4 * lane);
     const float* srows = reinterpret_cast<const float*>(tile);
-#pragma unroll
+    #pragma unroll 1
     for (int rr = 0; rr < 2; ++rr) {
       const int lr = 2 * warp + rr;
       const int vrow = grp * kPkGdnRows + lr;
@@ -696,17 +1043,16 @@ KIB_DEV bool pk_gdn(const PkStage& S, PkCons& cs) {
       st.z *= ge;
       st.w *= ge;
       const float sk = warp_sum(st.x * k4.x + st.y * k4.y + st.z * k4.z + st.w * k4.w);
-      const float v = S.conv_out[2 * key_dim + h * D + vrow];
-      const float delta = (v - sk) * beta;
+      const float delta = (vv[lr] - sk) * beta;
       st.x += k4.x * delta;
       st.y += k4.y * delta;
       st.z += k4.z * delta;
       st.w += k4.w * delta;
       const float y = warp_sum(st.x * q4.x + st.y * q4.y + st.z * q4.z + st.w * q4.w);
-      if (lane == 0) S.gdn_out[h * D + vrow] = y * scale;
+      if (lane == 0) cell_st(S.gdn_out + h * D + vrow, y * scale, otag);
       *reinterpret_cast<float4*>(S.state + (static_cast<size_t>(h) * D + vrow) * D + 4 * lane) = st;
     }
-    cs.release();  // also orders qn/kn reuse
+    cs.release();  // also orders qn/kn/vv reuse
   }
   return true;
 }
@@ -736,9 +1082,10 @@ KIB_DEV void pk_warp_sum8(float (&v)[8], int lane) {
 }
 
 // qk_norm (mps_backend.mm:1991-2024) then mrope (2482-2527) of one 256-wide
-// head vector; text positions (all MRoPE streams equal); one warp.
-__device__ __noinline__ void pk_norm_rope(float* v, const float* in, const float* w, float eps, float theta, int n_dims, int position,
-                          int lane) {
+// head vector staged in shared memory; text positions (all MRoPE streams
+// equal), frequencies from the host's table; one warp.
+__device__ __noinline__ void pk_norm_rope(float* v, const float* in, const float* w, const float* freq, float eps,
+                                          int n_dims, int position, int lane) {
   float ss = 0.0f;
   #pragma unroll 1
   for (int i = lane; i < kHd; i += 32) {
@@ -753,9 +1100,7 @@ __device__ __noinline__ void pk_norm_rope(float* v, const float* in, const float
   const int half = n_dims / 2;
   #pragma unroll 1
   for (int pi = lane; pi < half; pi += 32) {
-    const float exponent = static_cast<float>(2 * pi) / static_cast<float>(n_dims);
-    const float freq = 1.0f / powf(theta, exponent);
-    const float angle = static_cast<float>(position) * freq;
+    const float angle = static_cast<float>(position) * freq[pi];
     float sn, csn;
     sincosf(angle, &sn, &csn);
     const float x0 = v[pi], x1 = v[half + pi];
@@ -767,7 +1112,7 @@ __device__ __noinline__ void pk_norm_rope(float* v, const float* in, const float
 
 // ---- attention: item = (kv head, split); warp w serves q head (w % 4) of the
 // group and every other block of 8 keys (w / 4)
-KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
+__device__ __noinline__ bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
   constexpr int G = 4;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cta = static_cast<int>(blockIdx.x);
@@ -775,25 +1120,46 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
   float* qs = cs.sh->xs;               // [4][256]
   float* newk = qs + G * kHd;          // [256]
   float* newv = newk + kHd;            // [256]
-  float* merge = newv + kHd;           // [8][258]
+  float* merge = newv + kHd;           // [8][258]; first the raw q (4 x 256) and k (256)
+  float* qraw = merge;
   const int kvh = cta / S.nsplit, split = cta % S.nsplit;
   const int kvd = S.kv_heads * kHd;
-  const int nkeys = pos + 1;
-  int chunk = (nkeys + S.nsplit - 1) / S.nsplit;
-  chunk = (chunk + 7) & ~7;
-  const int kb = split * chunk, ke = min(kb + chunk, nkeys);
+  int kb, ke;
+  pk_split_range(pos + 1, S.nsplit, split, kb, ke);
   const int old_end = min(ke, pos);
   const bool owner = pos >= kb && pos < ke;
+  const uint32_t in_tag = cs.tag(S.src_tag), otag = cs.tag(S.tag);
+  {
+    // stage the group's q rows (and, for the owner of the new key, k and v)
+    bool ok = true;
+    const int n = owner ? G * kHd + 2 * kHd : G * kHd;
+    #pragma unroll 1
+    for (int i = 2 * tid; i < n; i += 2 * kPkConsumers) {
+      const uint64_t* c;
+      if (i < G * kHd) {
+        c = S.qg + static_cast<size_t>(kvh * G + i / kHd) * 2 * kHd + i % kHd;
+      } else if (i < G * kHd + kHd) {
+        c = S.kp + kvh * kHd + (i - G * kHd);
+      } else {
+        c = S.vp + kvh * kHd + (i - G * kHd - kHd);
+      }
+      const float a = pk_cell(c, in_tag, cs.err, ok), b = pk_cell(c + 1, in_tag, cs.err, ok);
+      float* dst = i < G * kHd + kHd ? qraw + i : newv + (i - G * kHd - kHd);
+      dst[0] = a;
+      dst[1] = b;
+    }
+    if (!ok) pk_fail(cs.sh, cs.err, 10);
+    pk_sync();
+    if (cs.aborted()) return false;
+  }
   if (warp < G) {
-    const int head = kvh * G + warp;
-    pk_norm_rope(qs + warp * kHd, S.qg + static_cast<size_t>(head) * 2 * kHd, S.q_norm, S.eps, S.theta, S.n_dims, pos,
-                 lane);
+    pk_norm_rope(qs + warp * kHd, qraw + warp * kHd, S.q_norm, S.rope_freq, S.eps, S.n_dims, pos, lane);
   } else if (warp == G && owner) {
-    pk_norm_rope(newk, S.kp + kvh * kHd, S.k_norm, S.eps, S.theta, S.n_dims, pos, lane);
+    pk_norm_rope(newk, qraw + G * kHd, S.k_norm, S.rope_freq, S.eps, S.n_dims, pos, lane);
     #pragma unroll 1
     for (int i = lane; i < kHd; i += 32) {
       const __half kh = __float2half_rn(newk[i]);
-      const __half vh = __float2half_rn(S.vp[kvh * kHd + i]);
+      const __half vh = __float2half_rn(newv[i]);
       S.kcache[static_cast<size_t>(pos) * kvd + kvh * kHd + i] = __half_as_ushort(kh);
       S.vcache[static_cast<size_t>(pos) * kvd + kvh * kHd + i] = __half_as_ushort(vh);
       newk[i] = __half2float(kh);
@@ -816,16 +1182,13 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
     if (!tile) return false;
     const uint16_t* kvbuf = reinterpret_cast<const uint16_t*>(tile);
     const int nk = min(kAttnChunk, old_end - k0);
-#pragma unroll 1
+    #pragma unroll 1
     for (int kk0 = kh2 * KB; kk0 < nk; kk0 += 2 * KB) {
       float sc[KB];
-      uint4 vraw[KB];
 #pragma unroll
       for (int e = 0; e < KB; ++e) {
         const int kk = min(kk0 + e, nk - 1);
-        const uint16_t* row = kvbuf + static_cast<size_t>(kk) * 2 * kHd;
-        const uint4 kr = *reinterpret_cast<const uint4*>(row + 8 * lane);
-        vraw[e] = *reinterpret_cast<const uint4*>(row + kHd + 8 * lane);
+        const uint4 kr = *reinterpret_cast<const uint4*>(kvbuf + static_cast<size_t>(kk) * 2 * kHd + 8 * lane);
         const __half2* kh = reinterpret_cast<const __half2*>(&kr);
         float d = 0.0f;
 #pragma unroll
@@ -837,22 +1200,27 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
         sc[e] = d;
       }
       pk_warp_sum8(sc, lane);
-#pragma unroll
-      for (int e = 0; e < KB; ++e) sc[e] *= scale;
       float mx = m;
 #pragma unroll
-      for (int e = 0; e < KB; ++e)
+      for (int e = 0; e < KB; ++e) {
+        sc[e] *= scale;
         if (kk0 + e < nk) mx = fmaxf(mx, sc[e]);
+      }
       const float ps = expf(m - mx);
       l *= ps;
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] *= ps;
-#pragma unroll
+      #pragma unroll 1
       for (int e = 0; e < KB; ++e) {
         if (kk0 + e >= nk) break;
-        const float w = expf(sc[e] - mx);
+        float s = sc[0];
+        #pragma unroll
+        for (int q = 1; q < KB; ++q)
+          if (q == e) s = sc[q];
+        const float w = expf(s - mx);
         l += w;
-        const __half2* vh = reinterpret_cast<const __half2*>(&vraw[e]);
+        const uint4 vr = *reinterpret_cast<const uint4*>(kvbuf + static_cast<size_t>(kk0 + e) * 2 * kHd + kHd + 8 * lane);
+        const __half2* vh = reinterpret_cast<const __half2*>(&vr);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 b2 = __half22float2(vh[i]);
@@ -895,11 +1263,11 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
     const float M = fmaxf(ma, mb);
     const float ea = ma == -INFINITY ? 0.0f : expf(ma - M);
     const float eb = mb == -INFINITY ? 0.0f : expf(mb - M);
-    float* dst = S.part + (static_cast<size_t>(split) * S.heads + kvh * G + jj) * (kHd + 2);
-    dst[i] = a[i] * ea + b[i] * eb;
+    uint64_t* dst = S.part + (static_cast<size_t>(split) * S.heads + kvh * G + jj) * (kHd + 2);
+    cell_st(dst + i, a[i] * ea + b[i] * eb, otag);
     if (i == 0) {
-      dst[kHd] = M;
-      dst[kHd + 1] = a[kHd + 1] * ea + b[kHd + 1] * eb;
+      cell_st(dst + kHd, M, otag);
+      cell_st(dst + kHd + 1, a[kHd + 1] * ea + b[kHd + 1] * eb, otag);
     }
   }
   pk_sync();
@@ -907,20 +1275,25 @@ KIB_DEV bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
 }
 
 // ---- merge: item = (head, 16 output dims); thread = (dim, split lane)
-KIB_DEV void pk_merge(const PkStage& S, PkShared* sh) {
+__device__ __noinline__ bool pk_merge(const PkStage& S, PkCons& cs) {
+  PkShared* sh = cs.sh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int items = S.heads * (kHd / 16);
   const int ns = S.nsplit;
+  const uint32_t ptag = cs.tag(S.src_tag), gtag = cs.tag(S.src2_tag), otag = cs.tag(S.tag);
   #pragma unroll 1
   for (int it = static_cast<int>(blockIdx.x); it < items; it += static_cast<int>(gridDim.x)) {
     const int h = it / (kHd / 16), d0 = (it % (kHd / 16)) * 16;
+    bool ok = true;
     #pragma unroll 1
     for (int s = tid; s < ns; s += kPkConsumers) {
-      const float* src = S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + kHd;
-      sh->ws[s] = __ldcg(src);
-      sh->ls[s] = __ldcg(src + 1);
+      const uint64_t* src = S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + kHd;
+      sh->ws[s] = pk_cell(src, ptag, cs.err, ok);
+      sh->ls[s] = pk_cell(src + 1, ptag, cs.err, ok);
     }
+    if (!ok) pk_fail(sh, cs.err, 11);
     pk_sync();
+    if (cs.aborted()) return false;
     if (warp == 0) {
       float M = -INFINITY;
       #pragma unroll 1
@@ -930,7 +1303,7 @@ KIB_DEV void pk_merge(const PkStage& S, PkShared* sh) {
       #pragma unroll 1
       for (int s = lane; s < ns; s += 32) {
         const float ms = sh->ws[s];
-        const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
+        const float e = ms == -INFINITY ? 0.0f : pk_expf(ms - M);
         sh->ws[s] = e;
         den += sh->ls[s] * e;
       }
@@ -941,101 +1314,63 @@ KIB_DEV void pk_merge(const PkStage& S, PkShared* sh) {
     const int d = tid & 15, jl = tid >> 4;  // 16 split lanes
     float n = 0.0f;
     #pragma unroll 1
-    for (int s = jl; s < ns; s += kPkConsumers / 16)
-      n = fmaf(__ldcg(S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + d0 + d), sh->ws[s], n);
+    for (int s = jl; s < ns; s += kPkConsumers / 16) {
+      // each value is waited for on its own tag (a split's threads write
+      // values, m and l independently)
+      const uint64_t* src = S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + d0 + d;
+      n = fmaf(pk_cell(src, ptag, cs.err, ok), sh->ws[s], n);
+    }
     n += __shfl_xor_sync(0xffffffffu, n, 16);
     float* part = sh->xs;                     // [8 warps][16]
     if (lane < 16) part[warp * 16 + d] = n;
+    float g = 0.0f;
+    if (tid < 16) g = pk_cell(S.qg + static_cast<size_t>(h) * 2 * kHd + kHd + d0 + tid, gtag, cs.err, ok);
+    if (!ok) pk_fail(sh, cs.err, 11);
     pk_sync();
+    if (cs.aborted()) return false;
     if (tid < 16) {
       float tot = 0.0f;
-#pragma unroll
+      #pragma unroll 1
       for (int w = 0; w < kPkWarps; ++w) tot += part[w * 16 + tid];
       const float den = sh->gb[0];
       const float inv = den == 0.0f ? 0.0f : 1.0f / den;
-      const float g = S.qg[static_cast<size_t>(h) * 2 * kHd + kHd + d0 + tid];
-      S.att_out[h * kHd + d0 + tid] = tot * inv * sigmoid_f(g);
+      cell_st(S.att_out + h * kHd + d0 + tid, tot * inv * pk_sigmoid(g), otag);
     }
     pk_sync();
   }
+  return true;
 }
 
-// ---- LM head tail: CTA candidate, then the last CTA picks the token
-KIB_DEV void pk_head_finish(const PkProgram& P, const PkStage& S, PkShared* sh, const PkArgmax& am) {
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int groups = kPkConsumers / S.rg;
-  const int group = tid / S.rg, gl = tid % S.rg;
-  if (gl == 0) {
-    sh->best[group] = am.best;
-    sh->bsum[group] = am.bsum;
-    sh->bidx[group] = am.bidx;
-  }
-  pk_sync();
-  if (tid == 0) {
-    float m = -INFINITY, s = 0.0f;
-    int idx = 0x7FFFFFFF;
+// Timing experiment only (probe bit 1): a GDN / attention / merge stage that
+// keeps the ring in step and writes its output cells (zeros) without running
+// the stage's code, to measure what the other stages cost.
+__device__ __noinline__ void pk_probe_stub(const PkStage& S, PkCons& cs, int pos) {
+  const int tid = threadIdx.x, cta = static_cast<int>(blockIdx.x), grid = static_cast<int>(gridDim.x);
+  const uint32_t otag = cs.tag(S.tag);
+  if (S.kind == kPkGdn) {
     #pragma unroll 1
-    for (int g = 0; g < groups; ++g) {
-      const int gi = sh->bidx[g];
-      if (gi == 0x7FFFFFFF) continue;
-      const float gm = sh->best[g], gs = sh->bsum[g];
-      if (gm > m || (gm == m && gi < idx)) {
-        s = s * expf(m - gm) + gs;
-        m = gm;
-        idx = gi;
-      } else {
-        s += gs * expf(gm - m);
-      }
+    for (int it = cta; it < S.value_heads * (128 / kPkGdnRows); it += grid) {
+      if (!cs.take()) return;
+      if (tid < kPkGdnRows) cell_st(S.gdn_out + it * kPkGdnRows + tid, 0.0f, otag);
+      cs.release();
     }
-    P.cand_max[blockIdx.x] = m;
-    P.cand_sum[blockIdx.x] = s;
-    P.cand_idx[blockIdx.x] = idx;
-    __threadfence();
-    sh->last = atomicAdd(P.head_ctr, 1u) == gridDim.x - 1;
-  }
-  pk_sync();
-  if (!sh->last || tid >= 32) return;
-  __threadfence();
-  float m = -INFINITY, s = 0.0f;
-  int idx = 0x7FFFFFFF;
-  #pragma unroll 1
-  for (unsigned c = lane; c < gridDim.x; c += 32) {
-    const int gi = __ldcg(&P.cand_idx[c]);
-    if (gi == 0x7FFFFFFF) continue;
-    const float gm = __ldcg(&P.cand_max[c]), gs = __ldcg(&P.cand_sum[c]);
-    if (gm > m || (gm == m && gi < idx)) {
-      s = s * expf(m - gm) + gs;
-      m = gm;
-      idx = gi;
-    } else {
-      s += gs * expf(gm - m);
+  } else if (S.kind == kPkAttn) {
+    if (cta >= S.kv_heads * S.nsplit) return;
+    const int kvh = cta / S.nsplit, split = cta % S.nsplit;
+    int kb, ke;
+    pk_split_range(pos + 1, S.nsplit, split, kb, ke);
+    #pragma unroll 1
+    for (int k0 = kb; k0 < min(ke, pos); k0 += kAttnChunk) {
+      if (!cs.take()) return;
+      cs.release();
     }
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    const float om = __shfl_xor_sync(0xffffffffu, m, o);
-    const float os = __shfl_xor_sync(0xffffffffu, s, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (oi == 0x7FFFFFFF) continue;
-    if (idx == 0x7FFFFFFF || om > m || (om == m && oi < idx)) {
-      s = (idx == 0x7FFFFFFF ? 0.0f : s * expf(m - om)) + os;
-      m = om;
-      idx = oi;
-    } else {
-      s += os * expf(om - m);
-    }
-  }
-  if (lane == 0) {
-    P.token[0] = idx;
-    if (P.prob_out) P.prob_out[0] = 1.0f / s;
-    if (P.token_log) {
-      const int st = *P.step;
-      P.token_log[st] = idx;
-      *P.step = st + 1;
-    }
-    *P.pos = *P.pos + 1;
-    *P.head_ctr = 0u;
-    *P.bar_ctr = 0u;  // every CTA has passed its last barrier
-    __threadfence();
+    #pragma unroll 1
+    for (int i = tid; i < 4 * (kHd + 2); i += kPkConsumers)
+      cell_st(S.part + (static_cast<size_t>(split) * S.heads + kvh * 4) * (kHd + 2) + i, i % (kHd + 2) == kHd ? -1e30f : 1.0f, otag);
+  } else {
+    #pragma unroll 1
+    for (int it = cta; it < S.heads * (kHd / 16); it += grid)
+      if (tid < 16) cell_st(S.att_out + (it / 16) * kHd + (it % 16) * 16 + tid, 0.0f, otag);
   }
 }
 
@@ -1047,12 +1382,13 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
   if (tid == 0) {
     for (int i = 0; i < kPkSlots; ++i) {
       mbar_init(&sh->full[i], 1);
-      mbar_init(&sh->empty[i], 1);
+      mbar_init(&sh->empty[i], kPkWarps);
     }
     sh->abort = 0;
     fence_mbar_init();
   }
   __syncthreads();
+  const int nslots = P.nslots >= 1 && P.nslots <= kPkSlots ? P.nslots : kPkSlots;
   if (warp >= kPkWarps) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPkProducerRegs));
     pdl_launch_dependents();
@@ -1063,14 +1399,18 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
     pr.lane = tid & 31;
     pr.err = P.err;
     pr.pol = l2_evict_first_policy();
+    pr.nslots = nslots;
     pk_produce(P, pr);
     // leave only once the copies in flight have landed (bounded)
     if (pr.lane == 0) {
-      const uint32_t n = min(pr.seq, static_cast<uint32_t>(kPkSlots));
+      const uint32_t n = min(pr.seq, static_cast<uint32_t>(nslots));
       #pragma unroll 1
       for (uint32_t q = pr.seq - n; q < pr.seq; ++q) {
+        const int sl = static_cast<int>(q % static_cast<uint32_t>(nslots));
+        const uint32_t ph = (q / static_cast<uint32_t>(nslots)) & 1u;
+        #pragma unroll 1
         for (uint32_t i = 0; i < (1u << 22); ++i)
-          if (mbar_try_wait(&sh->full[q % kPkSlots], (q / kPkSlots) & 1u)) break;
+          if (mbar_try_wait(&sh->full[sl], ph)) break;
       }
     }
     return;
@@ -1080,55 +1420,58 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
   pdl_wait();
   pdl_launch_dependents();
   const int pos = *P.pos;
+  const uint32_t epoch = *reinterpret_cast<volatile unsigned*>(P.epoch);
   PkCons cs;
   cs.ring = ring;
   cs.sh = sh;
   cs.err = P.err;
-  PkArgmax am;
-  unsigned barriers = 0;
-  pk_copy_desc(&sh->desc[0], &P.stages[0]);
+  cs.tagbase = epoch << 8;
+  cs.probe = P.probe;
+  cs.nslots = nslots;
+  constexpr int kDescWords = static_cast<int>(sizeof(PkStage) / 16);
+  static_assert(sizeof(PkStage) % 16 == 0, "PkStage must be a multiple of 16 bytes");
+  static_assert(kDescWords <= kPkConsumers, "one descriptor word per consumer thread");
+  if (tid < kDescWords) reinterpret_cast<uint4*>(&sh->desc[0])[tid] = __ldg(reinterpret_cast<const uint4*>(P.stages) + tid);
   pk_sync();
   #pragma unroll 1
   for (int s = 0; s < P.nstages; ++s) {
     const PkStage& S = sh->desc[s & 1];
-    // the next stage's descriptor: loaded now, stored after this stage's work
-    constexpr int kDescWords = static_cast<int>(sizeof(PkStage) / 16);
-    uint4 next_desc = make_uint4(0u, 0u, 0u, 0u);
-    if (tid < kDescWords && s + 1 < P.nstages) next_desc = __ldg(reinterpret_cast<const uint4*>(&P.stages[s + 1]) + tid);
+    // the next stage's descriptor goes into the other buffer asynchronously
+    // (that buffer's stage ended at the last barrier)
+    if (tid < kDescWords && s + 1 < P.nstages) {
+      cp_async_cg16(reinterpret_cast<uint4*>(&sh->desc[(s + 1) & 1]) + tid, reinterpret_cast<const uint4*>(&P.stages[s + 1]) + tid);
+      cp_async_commit();
+    }
     cs.tr = (P.trace && blockIdx.x == 0 && tid == 0) ? P.trace + 16 * s : nullptr;
-    cs.first = true;
-    if (cs.tr) cs.tr[0] = gtimer();
+    pk_mark(cs.tr, 0);
+    const int kind = S.kind;
     bool ok = true;
-    if (S.kind == kPkGemv || S.kind == kPkHead) {
-      pk_prologue(S, sh);
-      if (cs.tr) cs.tr[1] = gtimer();
-      switch (S.type) {
-        // Q5_K matrices are not instantiated here (both 4-bit paths in one
-        // kernel push it into local memory); the host routes models that
-        // have them to the per-kernel path
-        case kTypeQ4K: ok = pk_gemv<kTypeQ4K>(S, cs, am); break;
-        default: ok = pk_gemv<kTypeQ6K>(S, cs, am); break;
-      }
-      if (ok && S.kind == kPkHead) pk_head_finish(P, S, sh, am);
-    } else if (S.kind == kPkGdn) {
+    if (kind == kPkGemv || kind == kPkHead) {
+      // CTAs without a tile of this stage skip its input entirely.  Q4_K and
+      // Q6_K only: the host routes models with Q5_K projections to the
+      // per-kernel path.
+      // (the LM head's finish runs inside pk_gemv; a CTA without a head tile
+      // still takes part in the last-CTA ticket)
+      if (static_cast<int>(blockIdx.x) < S.ntiles) ok = pk_gemv(S, cs, P, epoch);
+      else if (kind == kPkHead) pk_head_finish(P, sh, PkArgmax(), epoch);
+    } else if (cs.probe & 2) {
+      pk_probe_stub(S, cs, pos);
+    } else if (kind == kPkGdn) {
       ok = pk_gdn(S, cs);
-    } else if (S.kind == kPkAttn) {
+    } else if (kind == kPkAttn) {
       ok = pk_attn(S, cs, pos);
     } else {
-      pk_merge(S, sh);
+      ok = pk_merge(S, cs);
     }
     if (!ok) break;
-    if (cs.tr) cs.tr[3] = gtimer();
-    if (P.trace && tid == 0) atomicMax(P.trace + 16 * s + 5, gtimer());  // slowest CTA done
     if (s + 1 < P.nstages) {
-      const bool need_barrier = S.barrier_after != 0;
-      if (tid < kDescWords) reinterpret_cast<uint4*>(&sh->desc[(s + 1) & 1])[tid] = next_desc;
-      if (need_barrier) {
-        ++barriers;
-        if (!pk_grid_sync(P, sh, barriers * gridDim.x)) break;
-      } else {
-        pk_sync();
-      }
+      cp_async_wait_all();
+      pk_sync();
+    }
+    if (cs.tr) {
+      pk_mark(cs.tr, 3);
+      // slowest CTA done (no return value: a reduction, not a round trip)
+      asm volatile("red.relaxed.gpu.global.max.u64 [%0], %1;" ::"l"(P.trace + 16 * s + 5), "l"(gtimer()) : "memory");
     }
   }
   if (P.trace && blockIdx.x == 0 && tid == 0) P.trace[16 * P.nstages] = gtimer();

@@ -131,8 +131,9 @@ struct kib_qwen35 {
   PkStage* d_pk = nullptr;
   int pk_n = 0;
   int pk_grid = 0;
-  unsigned* d_pk_ctr = nullptr;  // [0] grid barrier, [1] LM-head ticket
-  float* d_pk_part = nullptr;
+  unsigned* d_pk_ctr = nullptr;  // [1] LM-head ticket, [2] cell tag epoch
+  uint64_t* d_pk_cells = nullptr;
+  float* d_pk_rope = nullptr;  // [kPkRopePairs] rotary inverse frequencies
   float *d_pk_cmax = nullptr, *d_pk_csum = nullptr;
   int* d_pk_cidx = nullptr;
   unsigned long long* d_pk_trace = nullptr;
@@ -603,7 +604,7 @@ extern "C" {
 struct PkSegIn {
   const DevT* w;
   const DevT* w2;
-  float* out;
+  uint64_t* out;  // cells
   int epi;
 };
 
@@ -659,14 +660,40 @@ static bool pk_gemv_stage(kib_qwen35* m, PkStage& S, int kind, const std::vector
   if (want > cap) {
     // several tiles per CTA: make a tile a whole number of passes of the
     // CTA's row groups, so no pass runs part-empty
-    const int groups = kPkConsumers / S.rg;
-    int l = groups;
-    while (l % g) l += groups;  // lcm(groups, g)
+    const int per_pass = kPkConsumers / S.rg * kPkRows;
+    int l = per_pass;
+    while (l % g) l += per_pass;  // lcm(per_pass, g)
     if (cap >= l) S.tile_rows = cap / l * l;
   }
   S.ntiles = (rows + S.tile_rows - 1) / S.tile_rows;
   S.eps = m->eps;
   return cap >= g;
+}
+
+// Cells of the persistent step: every stage output gets its own array (an
+// even number of cells, so pair loads stay 16-byte aligned).
+static size_t pk_cells_needed(const kib_qwen35* m, int nsplit) {
+  size_t n = 0;
+  auto need = [&](size_t c) { n += (c + 1) & ~size_t(1); };
+  for (const LayerW& L : m->layers) {
+    if (L.kind == 0) {
+      need(L.qkv.rows());
+      need(L.zgate.rows());
+      need(L.beta.rows());
+      need(L.alpha.rows());
+      need(static_cast<size_t>(m->lvh) * m->lhd);
+    } else {
+      need(L.q.rows());
+      need(L.k.rows());
+      need(L.v.rows());
+      need(static_cast<size_t>(nsplit) * m->heads * (kHd + 2));
+      need(static_cast<size_t>(m->heads) * kHd);
+    }
+    need(m->H);
+    need(L.ffn_gate.rows());
+    need(m->H);
+  }
+  return n;
 }
 
 static int build_pk(kib_qwen35* m) {
@@ -684,72 +711,117 @@ static int build_pk(kib_qwen35* m) {
   int coop = 0;
   cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->ctx->device);
   const int nsplit = grid / m->kvh;
-  std::vector<PkStage> st;
-  auto add = [&](const PkStage& S) { st.push_back(S); };
-  auto prologue_in = [&](PkStage& S, const DevT& norm) {
-    S.norm_w = norm.f();
-    S.prologue = kProRms;
-    S.in = m->d_h;
-    return true;
+  const int n_dims = 2 * (m->sections[0] + m->sections[1] + m->sections[2] + m->sections[3]);
+  if (n_dims / 2 > kPkRopePairs) {
+    m->pk_why = "rotary dimensions beyond the persistent kernel's table";
+    return KIB_OK;
+  }
+  if (!m->d_pk_rope) {
+    // 1 / theta^(2p / n_dims) in float, the reference's expression (mrope_f32_in_place)
+    std::vector<float> fr(kPkRopePairs, 0.0f);
+    for (int p = 0; p < n_dims / 2; ++p) {
+      const float exponent = static_cast<float>(2 * p) / static_cast<float>(n_dims);
+      fr[p] = 1.0f / std::pow(m->theta, exponent);
+    }
+    if (dalloc(&m->d_pk_rope, kPkRopePairs) != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, "pk rope alloc");
+    ENG_CUDA(cudaMemcpy(m->d_pk_rope, fr.data(), fr.size() * sizeof(float), cudaMemcpyHostToDevice));
+  }
+  const size_t ncells = pk_cells_needed(m, nsplit);
+  if (!m->d_pk_cells) {
+    if (dalloc(&m->d_pk_cells, ncells) != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, "pk cell alloc");
+    ENG_CUDA(cudaMemset(m->d_pk_cells, 0, ncells * sizeof(uint64_t)));
+  }
+  uint64_t* next_cell = m->d_pk_cells;
+  auto cells = [&](size_t c) {
+    uint64_t* p = next_cell;
+    next_cell += (c + 1) & ~size_t(1);
+    return p;
   };
+  std::vector<PkStage> st;
+  // a stage's tag is its index + 1; readers name the tag of the stage that wrote their input
+  auto add = [&](PkStage& S) {
+    S.tag = static_cast<int>(st.size()) + 1;
+    st.push_back(S);
+    return S.tag;
+  };
+  const void* h_in = m->d_h;  // the residual stream entering the layer (layer 0: the embedding row)
+  int h_tag = 0;
   for (const LayerW& L : m->layers) {
     const int li = L.cache_index;
+    const void* mid = nullptr;  // the stream after the mixer (attention or GDN) block
+    int mid_tag = 0;
     if (L.kind == 0) {
+      uint64_t* c_qkv = cells(L.qkv.rows());
+      uint64_t* c_z = cells(L.zgate.rows());
+      uint64_t* c_beta = cells(L.beta.rows());
+      uint64_t* c_alpha = cells(L.alpha.rows());
       PkStage a = {};
       if (!pk_gemv_stage(m, a, kPkGemv,
-                         {{&L.qkv, nullptr, m->d_qkv, kEpiConv},
-                          {&L.zgate, nullptr, m->d_z, kEpiStore},
-                          {&L.beta, nullptr, m->d_beta, kEpiStore},
-                          {&L.alpha, nullptr, m->d_alpha, kEpiStore}},
-                         grid) ||
-          !prologue_in(a, L.attn_norm))
+                         {{&L.qkv, nullptr, c_qkv, kEpiConv},
+                          {&L.zgate, nullptr, c_z, kEpiStore},
+                          {&L.beta, nullptr, c_beta, kEpiStore},
+                          {&L.alpha, nullptr, c_alpha, kEpiStore}},
+                         grid))
         return KIB_OK;
+      a.prologue = kProRms;
+      a.in = h_in;
+      a.in_tag = h_tag;
+      a.norm_w = L.attn_norm.f();
       a.conv_state = m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1);
       a.conv_w = L.conv1d.f();
-      a.barrier_after = 1;
-      add(a);
+      const int a_tag = add(a);
       PkStage g = {};
       g.kind = kPkGdn;
-      g.conv_out = m->d_qkv;
+      g.conv_out = c_qkv;
       g.C = m->C;
-      g.beta_raw = m->d_beta;
-      g.alpha_raw = m->d_alpha;
+      g.beta_raw = c_beta;
+      g.alpha_raw = c_alpha;
+      g.src_tag = a_tag;
       g.dt_bias = L.dt_bias.f();
       g.ssm_a = L.ssm_a.f();
       g.state = m->d_s + static_cast<size_t>(li) * m->lvh * m->lhd * m->lhd;
-      g.gdn_out = m->d_y;
+      g.gdn_out = cells(static_cast<size_t>(m->lvh) * m->lhd);
       g.key_heads = m->lkh;
       g.value_heads = m->lvh;
       g.eps = m->eps;
-      g.barrier_after = 1;
-      add(g);
+      const int g_tag = add(g);
+      uint64_t* c_h1 = cells(m->H);
       PkStage o = {};
-      if (!pk_gemv_stage(m, o, kPkGemv, {{&L.ssm_out, nullptr, m->d_h1, kEpiResidual}}, grid)) return KIB_OK;
+      if (!pk_gemv_stage(m, o, kPkGemv, {{&L.ssm_out, nullptr, c_h1, kEpiResidual}}, grid)) return KIB_OK;
       o.prologue = kProNormGate;
-      o.in = m->d_y;
-      o.gate = m->d_z;
+      o.in = g.gdn_out;
+      o.in_tag = g_tag;
+      o.gate = c_z;
+      o.gate_tag = a_tag;
       o.norm_w = L.ssm_norm.f();
       o.head_dim = m->lhd;
-      o.resid = m->d_h;
-      o.barrier_after = 1;
-      add(o);
+      o.resid = h_in;
+      o.resid_tag = h_tag;
+      mid_tag = add(o);
+      mid = c_h1;
     } else {
       const size_t off = static_cast<size_t>(li) * m->cap * m->KD;
+      uint64_t* c_qg = cells(L.q.rows());
+      uint64_t* c_k = cells(L.k.rows());
+      uint64_t* c_v = cells(L.v.rows());
       PkStage a = {};
       if (!pk_gemv_stage(m, a, kPkGemv,
-                         {{&L.q, nullptr, m->d_qg, kEpiStore},
-                          {&L.k, nullptr, m->d_kp, kEpiStore},
-                          {&L.v, nullptr, m->d_vp, kEpiStore}},
-                         grid) ||
-          !prologue_in(a, L.attn_norm))
+                         {{&L.q, nullptr, c_qg, kEpiStore},
+                          {&L.k, nullptr, c_k, kEpiStore},
+                          {&L.v, nullptr, c_v, kEpiStore}},
+                         grid))
         return KIB_OK;
-      a.barrier_after = 1;
-      add(a);
+      a.prologue = kProRms;
+      a.in = h_in;
+      a.in_tag = h_tag;
+      a.norm_w = L.attn_norm.f();
+      const int a_tag = add(a);
       PkStage t = {};
       t.kind = kPkAttn;
-      t.qg = m->d_qg;
-      t.kp = m->d_kp;
-      t.vp = m->d_vp;
+      t.qg = c_qg;
+      t.kp = c_k;
+      t.vp = c_v;
+      t.src_tag = a_tag;
       t.q_norm = L.q_norm.f();
       t.k_norm = L.k_norm.f();
       t.kcache = m->d_k + off;
@@ -758,58 +830,63 @@ static int build_pk(kib_qwen35* m) {
       t.kv_heads = m->kvh;
       t.eps = m->eps;
       t.theta = m->theta;
-      t.n_dims = 2 * (m->sections[0] + m->sections[1] + m->sections[2] + m->sections[3]);
+      t.n_dims = n_dims;
+      t.rope_freq = m->d_pk_rope;
       t.nsplit = nsplit;
-      t.part = m->d_pk_part;
-      t.att_out = m->d_att;
-      t.barrier_after = 1;
-      add(t);
+      t.part = cells(static_cast<size_t>(nsplit) * m->heads * (kHd + 2));
+      const int t_tag = add(t);
       PkStage mg = t;
       mg.kind = kPkMerge;
-      add(mg);
+      mg.src_tag = t_tag;
+      mg.src2_tag = a_tag;
+      mg.att_out = cells(static_cast<size_t>(m->heads) * kHd);
+      const int mg_tag = add(mg);
+      uint64_t* c_h1 = cells(m->H);
       PkStage o = {};
-      if (!pk_gemv_stage(m, o, kPkGemv, {{&L.o, nullptr, m->d_h1, kEpiResidual}}, grid)) return KIB_OK;
+      if (!pk_gemv_stage(m, o, kPkGemv, {{&L.o, nullptr, c_h1, kEpiResidual}}, grid)) return KIB_OK;
       o.prologue = kProPlain;
-      o.in = m->d_att;
-      o.resid = m->d_h;
-      o.barrier_after = 1;
-      add(o);
+      o.in = mg.att_out;
+      o.in_tag = mg_tag;
+      o.resid = h_in;
+      o.resid_tag = h_tag;
+      mid_tag = add(o);
+      mid = c_h1;
     }
+    uint64_t* c_act = cells(L.ffn_gate.rows());
     PkStage f = {};
     if (L.ffn_gate.type != L.ffn_up.type ||
-        !pk_gemv_stage(m, f, kPkGemv, {{&L.ffn_gate, &L.ffn_up, m->d_act, kEpiSiluMul}}, grid)) {
+        !pk_gemv_stage(m, f, kPkGemv, {{&L.ffn_gate, &L.ffn_up, c_act, kEpiSiluMul}}, grid)) {
       if (m->pk_why.empty()) m->pk_why = "ffn gate/up types differ";
       return KIB_OK;
     }
     f.prologue = kProRms;
-    f.in = m->d_h1;
+    f.in = mid;
+    f.in_tag = mid_tag;
     f.norm_w = L.post_norm.f();
-    f.barrier_after = 1;
-    add(f);
+    const int f_tag = add(f);
+    uint64_t* c_h = cells(m->H);
     PkStage d = {};
-    if (!pk_gemv_stage(m, d, kPkGemv, {{&L.ffn_down, nullptr, m->d_h, kEpiResidual}}, grid)) return KIB_OK;
+    if (!pk_gemv_stage(m, d, kPkGemv, {{&L.ffn_down, nullptr, c_h, kEpiResidual}}, grid)) return KIB_OK;
     d.prologue = kProPlain;
-    d.in = m->d_act;
-    d.resid = m->d_h1;
-    d.barrier_after = 1;
-    add(d);
-  }
-  if (const char* rep = std::getenv("KIB_PK_PROBE_REPEAT"); rep && std::atoi(rep) > 0) {
-    // timing probe only: the first layer's FFN gate/up stage repeated
-    std::vector<PkStage> probe;
-    for (const PkStage& S : st)
-      if (S.paired) {
-        for (int i = 0; i < std::atoi(rep); ++i) probe.push_back(S);
-        break;
-      }
-    st = probe;
+    d.in = c_act;
+    d.in_tag = f_tag;
+    d.resid = mid;
+    d.resid_tag = mid_tag;
+    h_tag = add(d);
+    h_in = c_h;
   }
   PkStage h = {};
   if (!pk_gemv_stage(m, h, kPkHead, {{&head_weight(m), nullptr, nullptr, kEpiArgmax}}, grid)) return KIB_OK;
   h.prologue = kProRms;
-  h.in = m->d_h;
+  h.in = h_in;
+  h.in_tag = h_tag;
   h.norm_w = m->output_norm.f();
   add(h);
+  if (st.size() > static_cast<size_t>(kPkMaxStages)) {
+    m->pk_why = "more stages than the cell tags can name";
+    return KIB_OK;
+  }
+  if (static_cast<size_t>(next_cell - m->d_pk_cells) > ncells) return fail(m, KIB_ERR_INTERNAL, "pk cell arena overrun");
   for (auto& S : st) S.eps = m->eps;
   if (cudaMalloc(&m->d_pk, st.size() * sizeof(PkStage)) != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, "pk alloc");
   ENG_CUDA(cudaMemcpy(m->d_pk, st.data(), st.size() * sizeof(PkStage), cudaMemcpyHostToDevice));
@@ -823,6 +900,17 @@ static int build_pk(kib_qwen35* m) {
   return KIB_OK;
 }
 
+// After an aborted step: clear the LM-head ticket and move the cell epoch on,
+// so cells the aborted step wrote can never pass for the next step's.
+static void pk_reset_after_error(kib_qwen35* m) {
+  unsigned c[3] = {0u, 0u, 0u};
+  cudaMemcpy(c, m->d_pk_ctr, sizeof(c), cudaMemcpyDeviceToHost);
+  c[0] = 0u;
+  c[1] = 0u;
+  c[2] += 1u;
+  cudaMemcpy(m->d_pk_ctr, c, sizeof(c), cudaMemcpyHostToDevice);
+}
+
 static PkProgram pk_program(kib_qwen35* m) {
   PkProgram P = {};
   P.stages = m->d_pk;
@@ -832,13 +920,15 @@ static PkProgram pk_program(kib_qwen35* m) {
   P.token_log = m->d_log;
   P.step = m->d_step;
   P.prob_out = nullptr;
-  P.bar_ctr = m->d_pk_ctr;
   P.head_ctr = m->d_pk_ctr + 1;
+  P.epoch = m->d_pk_ctr + 2;
   P.cand_max = m->d_pk_cmax;
   P.cand_sum = m->d_pk_csum;
   P.cand_idx = m->d_pk_cidx;
   P.err = m->ctx->d_err;
   P.trace = m->trace_on ? m->d_pk_trace : nullptr;
+  if (const char* pr = std::getenv("KIB_PK_PROBE")) P.probe = std::atoi(pr);
+  if (const char* ns = std::getenv("KIB_PK_SLOTS")) P.nslots = std::atoi(ns);
   return P;
 }
 
@@ -1092,14 +1182,13 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
     m->trace_on = cudaMalloc(&m->d_trace, 4096 * 8 * sizeof(unsigned long long)) == cudaSuccess;
   }
   cudaMemset(m->d_head_cnt, 0, 4 * sizeof(unsigned));
-  if (dalloc(&m->d_pk_ctr, 2) != cudaSuccess ||
-      dalloc(&m->d_pk_part, static_cast<size_t>(kPkMaxSplits) * m->heads * (kHd + 2)) != cudaSuccess ||
+  if (dalloc(&m->d_pk_ctr, 4) != cudaSuccess ||
       dalloc(&m->d_pk_cmax, 1024) != cudaSuccess || dalloc(&m->d_pk_csum, 1024) != cudaSuccess ||
       dalloc(&m->d_pk_cidx, 1024) != cudaSuccess || dalloc(&m->d_pk_trace, 16 * 4096) != cudaSuccess) {
     kib_qwen35_free(mp.release());
     return set_error(ctx, KIB_ERR_INTERNAL, "persistent decode allocation failed");
   }
-  cudaMemset(m->d_pk_ctr, 0, 2 * sizeof(unsigned));
+  cudaMemset(m->d_pk_ctr, 0, 4 * sizeof(unsigned));
   if (build_pk(m) != KIB_OK) {
     std::string why = m->err;
     kib_qwen35_free(mp.release());
@@ -1117,7 +1206,7 @@ void kib_qwen35_free(kib_qwen35* m) {
   if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
   if (m->mtp_graph) cudaGraphExecDestroy(m->mtp_graph);
   if (m->pk_graph) cudaGraphExecDestroy(m->pk_graph);
-  void* pk_ptrs[] = {m->d_pk, m->d_pk_ctr, m->d_pk_part, m->d_pk_cmax, m->d_pk_csum, m->d_pk_cidx, m->d_pk_trace};
+  void* pk_ptrs[] = {m->d_pk, m->d_pk_ctr, m->d_pk_cells, m->d_pk_rope, m->d_pk_cmax, m->d_pk_csum, m->d_pk_cidx, m->d_pk_trace};
   for (void* p : pk_ptrs)
     if (p) cudaFree(p);
   void* ptrs[] = {m->d_weights, m->d_k, m->d_v, m->d_mk, m->d_mv, m->d_r, m->d_s, m->d_r_snap, m->d_s_snap,
@@ -1184,7 +1273,7 @@ int kib_qwen35_forward(kib_qwen35* m, const int32_t* tokens, uint64_t n, int adv
     ENG_CUDA(cudaMemcpyAsync(m->h_pin + 32, m->d_log, sizeof(int), cudaMemcpyDeviceToHost, st));
     rc = sync_check(m, "forward");
     if (rc) {
-      cudaMemset(m->d_pk_ctr, 0, 2 * sizeof(unsigned));
+      pk_reset_after_error(m);
       return rc;
     }
     if (argmax_out) argmax_out[0] = m->h_pin[32];
@@ -1294,7 +1383,7 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   if (tokens_out) ENG_CUDA(cudaMemcpyAsync(tokens_out, m->d_log, steps * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
   int rc = sync_check(m, "decode");
   if (rc) {
-    if (use_pk) cudaMemset(m->d_pk_ctr, 0, 2 * sizeof(unsigned));  // an aborted step leaves its tickets behind
+    if (use_pk) pk_reset_after_error(m);  // an aborted step leaves its ticket and epoch behind
     return rc;
   }
   m->pos += steps;
@@ -1310,15 +1399,28 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
       static const char* names[] = {"gemv", "gdn", "attn", "merge", "head"};
       auto rel = [&](unsigned long long v) { return v ? static_cast<long long>(v - h[0]) : -1ll; };
       std::fprintf(f, "stage,kind,type,rows,cols,start_ns,prologue_ns,first_tile_ns,done_ns,next_ns,max_done_ns,"
-                      "prod_stage_ns,prod_issue_ns,ux_ns,p8,p9,p10,p11,p12\n");
+                      "prod_stage_ns,prod_issue_ns,ux_ns,p8,p9,p10,p11,p12,p13\n");
       for (int i = 0; i < m->pk_n; ++i) {
         const unsigned long long* t = h.data() + 16 * i;
         std::fprintf(f, "%d,%s,%d,%d,%d", i, names[stages[i].kind], stages[i].type, stages[i].rows, stages[i].cols);
-        const int order[] = {0, 1, 2, 3, 16, 5, 6, 7, 4, 8, 9, 10, 11, 12};
+        const int order[] = {0, 1, 2, 3, 16, 5, 6, 7, 4, 8, 9, 10, 11, 12, 13};
         for (int k : order) std::fprintf(f, ",%lld", rel(t[k]));
         std::fprintf(f, "\n");
       }
       std::fclose(f);
+    }
+    if (const char* p2 = std::getenv("KIB_TRACE_OUT2")) {
+      // per-tile times of the LM head on CTA 0: wait start, taken, dots done, released
+      std::vector<unsigned long long> t(8 * 500);
+      cudaMemcpy(t.data(), m->d_pk_trace + 8192, t.size() * 8, cudaMemcpyDeviceToHost);
+      if (FILE* f2 = std::fopen(p2, "w")) {
+        for (int j = 0; j < 500 && t[8 * j]; ++j) {
+          std::fprintf(f2, "%d", j);
+          for (int q = 0; q < 7; ++q) std::fprintf(f2, ",%lld", t[8 * j + q] ? (long long)(t[8 * j + q] - h[0]) : -1ll);
+          std::fprintf(f2, "\n");
+        }
+        std::fclose(f2);
+      }
     }
   }
   if (!use_pk && m->trace_on && m->d_trace && m->trace_used > 0) {
