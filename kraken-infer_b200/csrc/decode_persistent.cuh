@@ -228,8 +228,6 @@ struct PkProgram {
   int* cand_idx;
   int* err;
   unsigned long long* trace;  // optional: CTA 0's [stage][start, input ready, first tile, end, ...]
-  int probe;                  // timing experiments only (bit 0: skip the GEMV dot products)
-  int nslots;                 // ring slots in use (0 = all)
 };
 
 struct PkShared {
@@ -348,11 +346,9 @@ __device__ __noinline__ void pk_produce(const PkProgram& P, PkProducer& pr) {
         const int r0 = t * tile_rows;
         const int nr = min(tile_rows, rows - r0);
         const uint32_t b = static_cast<uint32_t>(nr) * static_cast<uint32_t>(row_bytes);
-        // probe bit 3 (timing only): no weight traffic, the tile is left as it is
-        const bool skip = P.probe & 8;
-        uint8_t* dst = pr.acquire(skip ? 0u : paired ? 2u * b : b);
+        uint8_t* dst = pr.acquire(paired ? 2u * b : b);
         if (!dst) return;
-        if (lane < S.nseg && !skip) {
+        if (lane < S.nseg) {
           const PkSeg& g = S.seg[lane];
           const int a = max(r0, g.row_begin), e = min(r0 + nr, g.row_begin + g.rows);
           if (a < e) {
@@ -409,7 +405,6 @@ struct PkCons {
   uint32_t tagbase = 0;  // epoch << 8
   int* err;
   unsigned long long* tr = nullptr;  // trace of the current stage (CTA 0, thread 0) or null
-  int probe = 0;
   int nslots = kPkSlots;
   int slot = 0;
   uint32_t phase = 0;
@@ -603,10 +598,10 @@ struct PkX {
   float s[4];
 };
 
-// x values of unit u of block blk: the padded stage input times `scale`.  Q4_K: quarter q = elements
+// x values of unit u of block blk from the padded stage input.  Q4_K: quarter q = elements
 // 16q..16q+15 of the 64 contiguous columns; Q6_K: quarter k = the 16-column
 // run of group k.
-KIB_DEV void pk_load_x(int type, const float* xs, int blk, int u, float scale, PkX& x) {
+KIB_DEV void pk_load_x(int type, const float* xs, int blk, int u, PkX& x) {
   // first column of each quarter's 16-column run
   int col0, cstep;
   if (type == kTypeQ6K) {
@@ -618,16 +613,14 @@ KIB_DEV void pk_load_x(int type, const float* xs, int blk, int u, float scale, P
   }
   #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const int col = col0 + cstep * q;
-    const float4* p = reinterpret_cast<const float4*>(xs + xpad(col));
+    const float4* p = reinterpret_cast<const float4*>(xs + xpad(col0 + cstep * q));
     float sum = 0.0f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 f = p[j];
-      const float2 a = make_float2(f.x * scale, f.y * scale), b = make_float2(f.z * scale, f.w * scale);
-      x.v[8 * q + 2 * j] = a;
-      x.v[8 * q + 2 * j + 1] = b;
-      sum += (a.x + a.y) + (b.x + b.y);
+      x.v[8 * q + 2 * j] = make_float2(f.x, f.y);
+      x.v[8 * q + 2 * j + 1] = make_float2(f.z, f.w);
+      sum += (f.x + f.y) + (f.z + f.w);
     }
     x.s[q] = sum;
   }
@@ -883,8 +876,8 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
   const float scale = pk_prologue(S, cs);
   pk_mark(cs.tr, 1);
   if (cs.aborted()) return false;
-  PkX ux;
-  if (active) pk_load_x(type, cs.sh->xs, blk, u, scale, ux);
+  PkX ux;  // unscaled: the RMS scale multiplies each row's result instead
+  if (active) pk_load_x(type, cs.sh->xs, blk, u, ux);
   bool first = true;
   #pragma unroll 1
   for (int t = cta; t < ntiles; t += grid) {
@@ -893,17 +886,11 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
     const uint8_t* tile = cs.take();
     if (!tile) return false;
     if (first) pk_mark(cs.tr, 2);
-    // probe bit 2 (timing only): the first tile's passes run twice, the first
-    // time without epilogues, to compare a cold and a warm run of the code
-    const int reps = (cs.probe & 4) && t == cta ? 2 : 1;
-    #pragma unroll 1
-    for (int rep = 0; rep < reps; ++rep) {
-    const bool dry = rep + 1 < reps;
     #pragma unroll 1
     for (int p0 = 0; p0 < nr; p0 += per_pass) {
       const int rl = p0 + my_off;
-      if (!first && !dry && owner && rl < nr) pk_epi_issue(S, cs.sh, r0 + rl, e);
-      if (!dry) first = false;
+      if (!first && owner && rl < nr) pk_epi_issue(S, cs.sh, r0 + rl, e);
+      first = false;
       float acc[R], acc2[R];
       const uint8_t* b[R];
 #pragma unroll
@@ -912,7 +899,7 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
         b[k] = tile + static_cast<size_t>(rk) * row_bytes + blk_off;
         acc[k] = acc2[k] = 0.0f;
       }
-      if (active && !(cs.probe & 1)) {
+      if (active) {
         // a gate/up pair runs both halves through one copy of the dot code
         #pragma unroll 1
         for (int h = 0; h <= static_cast<int>(paired); ++h) {
@@ -966,10 +953,7 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
         }
         asm volatile("bar.sync %0, 64;" ::"r"(2 + (wp >> 1)) : "memory");
       }
-      if (owner && rl < nr && !dry) pk_epi_run(S, cs, e, v, v2, am);
-      if (dry && owner && rl < nr && v == 1.2345f) cell_st(e.out, v, 0);  // keeps the dry run's result live
-    }
-    pk_mark(cs.tr, dry ? 10 : 11);
+      if (owner && rl < nr) pk_epi_run(S, cs, e, v * scale, v2 * scale, am);
     }
     cs.release_warp();
   }
@@ -1341,39 +1325,6 @@ __device__ __noinline__ bool pk_merge(const PkStage& S, PkCons& cs) {
   return true;
 }
 
-// Timing experiment only (probe bit 1): a GDN / attention / merge stage that
-// keeps the ring in step and writes its output cells (zeros) without running
-// the stage's code, to measure what the other stages cost.
-__device__ __noinline__ void pk_probe_stub(const PkStage& S, PkCons& cs, int pos) {
-  const int tid = threadIdx.x, cta = static_cast<int>(blockIdx.x), grid = static_cast<int>(gridDim.x);
-  const uint32_t otag = cs.tag(S.tag);
-  if (S.kind == kPkGdn) {
-    #pragma unroll 1
-    for (int it = cta; it < S.value_heads * (128 / kPkGdnRows); it += grid) {
-      if (!cs.take()) return;
-      if (tid < kPkGdnRows) cell_st(S.gdn_out + it * kPkGdnRows + tid, 0.0f, otag);
-      cs.release();
-    }
-  } else if (S.kind == kPkAttn) {
-    if (cta >= S.kv_heads * S.nsplit) return;
-    const int kvh = cta / S.nsplit, split = cta % S.nsplit;
-    int kb, ke;
-    pk_split_range(pos + 1, S.nsplit, split, kb, ke);
-    #pragma unroll 1
-    for (int k0 = kb; k0 < min(ke, pos); k0 += kAttnChunk) {
-      if (!cs.take()) return;
-      cs.release();
-    }
-    #pragma unroll 1
-    for (int i = tid; i < 4 * (kHd + 2); i += kPkConsumers)
-      cell_st(S.part + (static_cast<size_t>(split) * S.heads + kvh * 4) * (kHd + 2) + i, i % (kHd + 2) == kHd ? -1e30f : 1.0f, otag);
-  } else {
-    #pragma unroll 1
-    for (int it = cta; it < S.heads * (kHd / 16); it += grid)
-      if (tid < 16) cell_st(S.att_out + (it / 16) * kHd + (it % 16) * 16 + tid, 0.0f, otag);
-  }
-}
-
 __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const __grid_constant__ PkProgram P) {
   extern __shared__ __align__(1024) uint8_t pk_smem[];
   uint8_t* ring = pk_smem;
@@ -1388,7 +1339,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
     fence_mbar_init();
   }
   __syncthreads();
-  const int nslots = P.nslots >= 1 && P.nslots <= kPkSlots ? P.nslots : kPkSlots;
+  constexpr int nslots = kPkSlots;
   if (warp >= kPkWarps) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPkProducerRegs));
     pdl_launch_dependents();
@@ -1426,7 +1377,6 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
   cs.sh = sh;
   cs.err = P.err;
   cs.tagbase = epoch << 8;
-  cs.probe = P.probe;
   cs.nslots = nslots;
   constexpr int kDescWords = static_cast<int>(sizeof(PkStage) / 16);
   static_assert(sizeof(PkStage) % 16 == 0, "PkStage must be a multiple of 16 bytes");
@@ -1454,8 +1404,6 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
       // still takes part in the last-CTA ticket)
       if (static_cast<int>(blockIdx.x) < S.ntiles) ok = pk_gemv(S, cs, P, epoch);
       else if (kind == kPkHead) pk_head_finish(P, sh, PkArgmax(), epoch);
-    } else if (cs.probe & 2) {
-      pk_probe_stub(S, cs, pos);
     } else if (kind == kPkGdn) {
       ok = pk_gdn(S, cs);
     } else if (kind == kPkAttn) {

@@ -927,8 +927,6 @@ static PkProgram pk_program(kib_qwen35* m) {
   P.cand_idx = m->d_pk_cidx;
   P.err = m->ctx->d_err;
   P.trace = m->trace_on ? m->d_pk_trace : nullptr;
-  if (const char* pr = std::getenv("KIB_PK_PROBE")) P.probe = std::atoi(pr);
-  if (const char* ns = std::getenv("KIB_PK_SLOTS")) P.nslots = std::atoi(ns);
   return P;
 }
 
