@@ -136,6 +136,16 @@ KIB_DEV float pk_cell(const uint64_t* p, uint32_t tag, const int* err, bool& ok)
   return cell_val(c);
 }
 
+// Waits for a cell whose first load is already in `c` (loads are issued in a
+// batch first, then checked: one round trip for the batch instead of one each).
+KIB_DEV float pk_cell_chk(const uint64_t* p, uint64_t c, uint32_t tag, const int* err, bool& ok) {
+  if (!cell_ok(c, tag)) {
+    c = pk_poll1(p, tag, err);
+    ok = ok && cell_ok(c, tag);
+  }
+  return cell_val(c);
+}
+
 // Out-of-line copies of the transcendental helpers: each exists once in the kernel.
 __device__ __noinline__ float pk_expf(float v) { return expf(v); }
 __device__ __noinline__ float pk_silu(float v) { return v / (1.0f + expf(-v)); }
@@ -980,8 +990,11 @@ __device__ __noinline__ bool pk_gdn(const PkStage& S, PkCons& cs) {
     float qv = 0.0f, kv = 0.0f;
     if (tid < D) {
       // this head's q and k rows (and nothing else) must exist
-      qv = pk_cell(S.conv_out + kh * D + tid, in_tag, cs.err, ok);
-      kv = pk_cell(S.conv_out + key_dim + kh * D + tid, in_tag, cs.err, ok);
+      const uint64_t* qp = S.conv_out + kh * D + tid;
+      const uint64_t* kp = S.conv_out + key_dim + kh * D + tid;
+      const uint64_t qc = cell_ld1(qp), kc = cell_ld1(kp);
+      qv = pk_cell_chk(qp, qc, in_tag, cs.err, ok);
+      kv = pk_cell_chk(kp, kc, in_tag, cs.err, ok);
       const float q2 = warp_sum(qv * qv), k2 = warp_sum(kv * kv);
       if (lane == 0) {
         cs.sh->red[warp][0] = q2;
@@ -991,8 +1004,9 @@ __device__ __noinline__ bool pk_gdn(const PkStage& S, PkCons& cs) {
       const int r = tid - D;
       vv[r] = pk_cell(S.conv_out + 2 * key_dim + h * D + grp * kPkGdnRows + r, in_tag, cs.err, ok);
     } else if (tid == D + kPkGdnRows) {
-      const float a = pk_cell(S.alpha_raw + h, in_tag, cs.err, ok);
-      const float b = pk_cell(S.beta_raw + h, in_tag, cs.err, ok);
+      const uint64_t ac = cell_ld1(S.alpha_raw + h), bc = cell_ld1(S.beta_raw + h);
+      const float a = pk_cell_chk(S.alpha_raw + h, ac, in_tag, cs.err, ok);
+      const float b = pk_cell_chk(S.beta_raw + h, bc, in_tag, cs.err, ok);
       cs.sh->gb[0] = softplus20_f(a + S.dt_bias[h]) * S.ssm_a[h];
       cs.sh->gb[1] = pk_sigmoid(b);
     }
@@ -1067,24 +1081,30 @@ KIB_DEV void pk_warp_sum8(float (&v)[8], int lane) {
 
 // qk_norm (mps_backend.mm:1991-2024) then mrope (2482-2527) of one 256-wide
 // head vector staged in shared memory; text positions (all MRoPE streams
-// equal), frequencies from the host's table; one warp.
+// equal), frequencies from the host's table; one warp.  Lane l owns elements
+// l + 32i; its norm weights and rotary frequency are loaded in one batch.
 __device__ __noinline__ void pk_norm_rope(float* v, const float* in, const float* w, const float* freq, float eps,
                                           int n_dims, int position, int lane) {
-  float ss = 0.0f;
-  #pragma unroll 1
-  for (int i = lane; i < kHd; i += 32) {
-    const float x = in[i];
-    ss += x * x;
+  constexpr int E = kHd / 32;
+  float x[E], wv[E];
+  const int half = n_dims / 2;
+  const float fr = lane < half ? freq[lane] : 0.0f;  // n_dims/2 <= 32 pairs handled per lane below
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    wv[i] = w[lane + 32 * i];
+    x[i] = in[lane + 32 * i];
   }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < E; ++i) ss += x[i] * x[i];
   ss = warp_sum(ss);
   const float scale = 1.0f / sqrtf(ss / static_cast<float>(kHd) + eps);
-  #pragma unroll 1
-  for (int i = lane; i < kHd; i += 32) v[i] = in[i] * (scale * w[i]);
+#pragma unroll
+  for (int i = 0; i < E; ++i) v[lane + 32 * i] = x[i] * (scale * wv[i]);
   __syncwarp();
-  const int half = n_dims / 2;
   #pragma unroll 1
   for (int pi = lane; pi < half; pi += 32) {
-    const float angle = static_cast<float>(position) * freq[pi];
+    const float angle = static_cast<float>(position) * (pi == lane ? fr : freq[pi]);
     float sn, csn;
     sincosf(angle, &sn, &csn);
     const float x0 = v[pi], x1 = v[half + pi];
@@ -1114,28 +1134,40 @@ __device__ __noinline__ bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
   const bool owner = pos >= kb && pos < ke;
   const uint32_t in_tag = cs.tag(S.src_tag), otag = cs.tag(S.tag);
   {
-    // stage the group's q rows (and, for the owner of the new key, k and v)
+    // stage the group's q rows (and, for the owner of the new key, k and v):
+    // a thread's (up to three) cell pairs are loaded together, then checked
     bool ok = true;
     const int n = owner ? G * kHd + 2 * kHd : G * kHd;
-    #pragma unroll 1
-    for (int i = 2 * tid; i < n; i += 2 * kPkConsumers) {
-      const uint64_t* c;
+    const uint64_t* src[3];
+    ulonglong2 c[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int i = min(2 * tid + 2 * kPkConsumers * j, n - 2);
       if (i < G * kHd) {
-        c = S.qg + static_cast<size_t>(kvh * G + i / kHd) * 2 * kHd + i % kHd;
+        src[j] = S.qg + static_cast<size_t>(kvh * G + i / kHd) * 2 * kHd + i % kHd;
       } else if (i < G * kHd + kHd) {
-        c = S.kp + kvh * kHd + (i - G * kHd);
+        src[j] = S.kp + kvh * kHd + (i - G * kHd);
       } else {
-        c = S.vp + kvh * kHd + (i - G * kHd - kHd);
+        src[j] = S.vp + kvh * kHd + (i - G * kHd - kHd);
       }
-      const float a = pk_cell(c, in_tag, cs.err, ok), b = pk_cell(c + 1, in_tag, cs.err, ok);
-      float* dst = i < G * kHd + kHd ? qraw + i : newv + (i - G * kHd - kHd);
-      dst[0] = a;
-      dst[1] = b;
+      if (2 * tid + 2 * kPkConsumers * j < n) c[j] = cell_ld2(src[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int i = 2 * tid + 2 * kPkConsumers * j;
+      if (i < n) {
+        const float a = pk_cell_chk(src[j], c[j].x, in_tag, cs.err, ok);
+        const float b = pk_cell_chk(src[j] + 1, c[j].y, in_tag, cs.err, ok);
+        float* dst = i < G * kHd + kHd ? qraw + i : newv + (i - G * kHd - kHd);
+        dst[0] = a;
+        dst[1] = b;
+      }
     }
     if (!ok) pk_fail(cs.sh, cs.err, 10);
     pk_sync();
     if (cs.aborted()) return false;
   }
+  pk_mark(cs.tr, 4);
   if (warp < G) {
     pk_norm_rope(qs + warp * kHd, qraw + warp * kHd, S.q_norm, S.rope_freq, S.eps, S.n_dims, pos, lane);
   } else if (warp == G && owner) {
@@ -1151,6 +1183,7 @@ __device__ __noinline__ bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
     }
   }
   pk_sync();
+  pk_mark(cs.tr, 9);
   const int j = warp % G, kh2 = warp / G;
   const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
   float m = -INFINITY, l = 0.0f, acc[8], qreg[8];
@@ -1194,17 +1227,16 @@ __device__ __noinline__ bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
       l *= ps;
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] *= ps;
-      #pragma unroll 1
+      // the block's V rows are loaded together; keys past the chunk get weight 0
+      uint4 vr[KB];
+#pragma unroll
+      for (int e = 0; e < KB; ++e)
+        vr[e] = *reinterpret_cast<const uint4*>(kvbuf + static_cast<size_t>(min(kk0 + e, nk - 1)) * 2 * kHd + kHd + 8 * lane);
+#pragma unroll
       for (int e = 0; e < KB; ++e) {
-        if (kk0 + e >= nk) break;
-        float s = sc[0];
-        #pragma unroll
-        for (int q = 1; q < KB; ++q)
-          if (q == e) s = sc[q];
-        const float w = expf(s - mx);
+        const float w = kk0 + e < nk ? expf(sc[e] - mx) : 0.0f;
         l += w;
-        const uint4 vr = *reinterpret_cast<const uint4*>(kvbuf + static_cast<size_t>(kk0 + e) * 2 * kHd + kHd + 8 * lane);
-        const __half2* vh = reinterpret_cast<const __half2*>(&vr);
+        const __half2* vh = reinterpret_cast<const __half2*>(&vr[e]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 b2 = __half22float2(vh[i]);
@@ -1214,7 +1246,7 @@ __device__ __noinline__ bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
       }
       m = mx;
     }
-    cs.release();
+    cs.release_warp();
   }
   if (owner && kh2 == 0) {  // the new key, from shared memory
     float d = 0.0f;
@@ -1229,6 +1261,7 @@ __device__ __noinline__ bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
     for (int i = 0; i < 8; ++i) acc[i] = acc[i] * ps + w * newv[8 * lane + i];
     m = nm;
   }
+  pk_mark(cs.tr, 10);
   // merge the two key halves of each head, then write the split's partial
   float* mrow = merge + warp * (kHd + 2);
 #pragma unroll
@@ -1272,9 +1305,21 @@ __device__ __noinline__ bool pk_merge(const PkStage& S, PkCons& cs) {
     #pragma unroll 1
     for (int s = tid; s < ns; s += kPkConsumers) {
       const uint64_t* src = S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + kHd;
-      sh->ws[s] = pk_cell(src, ptag, cs.err, ok);
-      sh->ls[s] = pk_cell(src + 1, ptag, cs.err, ok);
+      const ulonglong2 c = cell_ld2(src);  // m, l (kHd is even: a 16-byte pair)
+      sh->ws[s] = pk_cell_chk(src, c.x, ptag, cs.err, ok);
+      sh->ls[s] = pk_cell_chk(src + 1, c.y, ptag, cs.err, ok);
     }
+    // the value cells this thread will need, loaded while the weights are formed
+    const int d = tid & 15, jl = tid >> 4;  // 16 split lanes
+    constexpr int kMaxPer = (kPkMaxSplits + kPkConsumers / 16 - 1) / (kPkConsumers / 16);
+    uint64_t vc[kMaxPer];
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+      const int s = jl + j * (kPkConsumers / 16);
+      if (s < ns) vc[j] = cell_ld1(S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + d0 + d);
+    }
+    uint64_t gcell = 0;
+    if (tid < 16) gcell = cell_ld1(S.qg + static_cast<size_t>(h) * 2 * kHd + kHd + d0 + tid);
     if (!ok) pk_fail(sh, cs.err, 11);
     pk_sync();
     if (cs.aborted()) return false;
@@ -1295,20 +1340,22 @@ __device__ __noinline__ bool pk_merge(const PkStage& S, PkCons& cs) {
       if (lane == 0) sh->gb[0] = den;
     }
     pk_sync();
-    const int d = tid & 15, jl = tid >> 4;  // 16 split lanes
     float n = 0.0f;
-    #pragma unroll 1
-    for (int s = jl; s < ns; s += kPkConsumers / 16) {
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
       // each value is waited for on its own tag (a split's threads write
       // values, m and l independently)
-      const uint64_t* src = S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + d0 + d;
-      n = fmaf(pk_cell(src, ptag, cs.err, ok), sh->ws[s], n);
+      const int s = jl + j * (kPkConsumers / 16);
+      if (s < ns) {
+        const uint64_t* src = S.part + (static_cast<size_t>(s) * S.heads + h) * (kHd + 2) + d0 + d;
+        n = fmaf(pk_cell_chk(src, vc[j], ptag, cs.err, ok), sh->ws[s], n);
+      }
     }
     n += __shfl_xor_sync(0xffffffffu, n, 16);
     float* part = sh->xs;                     // [8 warps][16]
     if (lane < 16) part[warp * 16 + d] = n;
     float g = 0.0f;
-    if (tid < 16) g = pk_cell(S.qg + static_cast<size_t>(h) * 2 * kHd + kHd + d0 + tid, gtag, cs.err, ok);
+    if (tid < 16) g = pk_cell_chk(S.qg + static_cast<size_t>(h) * 2 * kHd + kHd + d0 + tid, gcell, gtag, cs.err, ok);
     if (!ok) pk_fail(sh, cs.err, 11);
     pk_sync();
     if (cs.aborted()) return false;
