@@ -230,11 +230,9 @@ struct PkProgram {
   int* token;         // in: the token; out: the argmax
   int* token_log;     // token_log[*step] = argmax, then ++*step
   int* step;
-  float* prob_out;    // optional p(top1)
   unsigned* head_ctr; // LM-head last-CTA ticket
   unsigned* epoch;    // tag epoch, advanced once per step by the head's last CTA
   float* cand_max;    // [grid]
-  float* cand_sum;
   int* cand_idx;
   int* err;
   unsigned long long* trace;  // optional: CTA 0's [stage][start, input ready, first tile, end, ...]
@@ -247,7 +245,6 @@ struct PkShared {
   float red[kPkWarps][4 * kPkRows];
   float gb[2];
   float best[kPkWarps];
-  float bsum[kPkWarps];
   int bidx[kPkWarps];
   int abort;
   int last;
@@ -433,6 +430,16 @@ struct PkCons {
       return nullptr;
     }
     return ring + static_cast<size_t>(slot) * kPkSlotBytes;
+  }
+  // The slot after the current one (taken before the current one is released).
+  KIB_DEV const uint8_t* take_next() {
+    const int s1 = slot + 1 == nslots ? 0 : slot + 1;
+    const uint32_t p1 = slot + 1 == nslots ? phase ^ 1u : phase;
+    if (!mbar_wait_bounded(&sh->full[s1], p1, nullptr)) {
+      pk_fail(sh, err, 2);
+      return nullptr;
+    }
+    return ring + static_cast<size_t>(s1) * kPkSlotBytes;
   }
   // Every consumer thread is done with the slot (CTA barrier, then one arrival
   // per warp).
@@ -687,28 +694,23 @@ KIB_DEV void pk_dot_rows(int type, const uint8_t* const (&blk)[R], int u, const 
   }
 }
 
+// Argmax candidate (max, lowest index at ties).  The persistent path decodes
+// greedily and reports only the token; p(top1) (used by the MTP loop's
+// adaptive budget) comes from the per-kernel path.
 struct PkArgmax {
-  float best = -INFINITY, bsum = 0.0f;
+  float best = -INFINITY;
   int bidx = 0x7FFFFFFF;
-  // one row; ties -> lowest index (inline: it runs inside the GEMV pass loop)
   KIB_DEV void push(float v, int row) {
     if (v > best || (v == best && row < bidx)) {
-      bsum = bsum * expf(best - v) + 1.0f;
       best = v;
       bidx = row;
-    } else {
-      bsum += expf(v - best);
     }
   }
-  // merges another candidate (max, sum of exp(v - max), index)
-  KIB_DEV void merge(float om, float os, int oi) {
+  KIB_DEV void merge(float om, int oi) {
     if (oi == 0x7FFFFFFF) return;
     if (bidx == 0x7FFFFFFF || om > best || (om == best && oi < bidx)) {
-      bsum = (bidx == 0x7FFFFFFF ? 0.0f : bsum * pk_expf(best - om)) + os;
       best = om;
       bidx = oi;
-    } else {
-      bsum += os * pk_expf(om - best);
     }
   }
 };
@@ -795,13 +797,12 @@ KIB_DEV void pk_epi_run(const PkStage& S, PkCons& cs, PkEpi& e, float v, float v
 }
 
 // Merges the argmax candidates of a warp (butterfly); every lane ends with the total.
-__device__ __noinline__ void pk_argmax_warp(PkArgmax& a) {
+KIB_DEV void pk_argmax_warp(PkArgmax& a) {
   #pragma unroll 1
   for (int o = 16; o > 0; o >>= 1) {
     const float om = __shfl_xor_sync(0xffffffffu, a.best, o);
-    const float os = __shfl_xor_sync(0xffffffffu, a.bsum, o);
     const int oi = __shfl_xor_sync(0xffffffffu, a.bidx, o);
-    a.merge(om, os, oi);
+    a.merge(om, oi);
   }
 }
 
@@ -812,16 +813,14 @@ __device__ __noinline__ void pk_head_finish(const PkProgram& P, PkShared* sh, Pk
   pk_argmax_warp(am);
   if (lane == 0) {
     sh->best[warp] = am.best;
-    sh->bsum[warp] = am.bsum;
     sh->bidx[warp] = am.bidx;
   }
   pk_sync();
   if (tid == 0) {
     PkArgmax c;
     #pragma unroll 1
-    for (int w = 0; w < kPkWarps; ++w) c.merge(sh->best[w], sh->bsum[w], sh->bidx[w]);
+    for (int w = 0; w < kPkWarps; ++w) c.merge(sh->best[w], sh->bidx[w]);
     P.cand_max[blockIdx.x] = c.best;
-    P.cand_sum[blockIdx.x] = c.bsum;
     P.cand_idx[blockIdx.x] = c.bidx;
     __threadfence();
     sh->last = atomicAdd(P.head_ctr, 1u) == gridDim.x - 1;
@@ -831,12 +830,10 @@ __device__ __noinline__ void pk_head_finish(const PkProgram& P, PkShared* sh, Pk
   __threadfence();
   PkArgmax c;
   #pragma unroll 1
-  for (unsigned i = lane; i < gridDim.x; i += 32)
-    c.merge(__ldcg(&P.cand_max[i]), __ldcg(&P.cand_sum[i]), __ldcg(&P.cand_idx[i]));
+  for (unsigned i = lane; i < gridDim.x; i += 32) c.merge(__ldcg(&P.cand_max[i]), __ldcg(&P.cand_idx[i]));
   pk_argmax_warp(c);
   if (lane == 0) {
     P.token[0] = c.bidx;
-    if (P.prob_out) P.prob_out[0] = 1.0f / c.bsum;
     if (P.token_log) {
       const int st = *P.step;
       P.token_log[st] = c.bidx;
@@ -888,13 +885,56 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
   if (cs.aborted()) return false;
   PkX ux;  // unscaled: the RMS scale multiplies each row's result instead
   if (active) pk_load_x(type, cs.sh->xs, blk, u, ux);
+  if (S.kind == kPkHead && rg_log2 == 4 && tile_rows == groups * R) {
+    // LM head: two tiles per pass (a lane dots rows of both), so each pass has
+    // twice the independent work between its waits
+    PkArgmax am2;
+    const int own2 = (gl & 15) >> 2;  // 0,1: tile A rows group, group+16; 2,3: tile B
+    #pragma unroll 1
+    for (int t = cta; t < ntiles; t += 2 * grid) {
+      const bool two = t + grid < ntiles;
+      const uint8_t* ta = cs.take();
+      if (!ta) return false;
+      const uint8_t* tb = two ? cs.take_next() : ta;
+      if (!tb) return false;
+      const int na = min(tile_rows, rows - t * tile_rows);
+      const int nb = two ? min(tile_rows, rows - (t + grid) * tile_rows) : 0;
+      const uint8_t* b[4];
+      b[0] = ta + static_cast<size_t>(min(group, na - 1)) * row_bytes + blk_off;
+      b[1] = ta + static_cast<size_t>(min(group + groups, na - 1)) * row_bytes + blk_off;
+      b[2] = tb + static_cast<size_t>(min(group, max(nb, 1) - 1)) * row_bytes + blk_off;
+      b[3] = tb + static_cast<size_t>(min(group + groups, max(nb, 1) - 1)) * row_bytes + blk_off;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (active) pk_dot_rows<4>(type, b, u, ux, acc);
+      // lanes 0-3 / 4-7 / 8-11 / 12-15 of the group end with rows 0..3
+      const bool h1 = gl & 8, h2 = gl & 4;
+      const float a0 = (h1 ? acc[2] : acc[0]) + __shfl_xor_sync(0xffffffffu, h1 ? acc[0] : acc[2], 8);
+      const float a1 = (h1 ? acc[3] : acc[1]) + __shfl_xor_sync(0xffffffffu, h1 ? acc[1] : acc[3], 8);
+      float v = (h2 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h2 ? a0 : a1, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      if ((gl & 3) == 0) {
+        const int tt = own2 < 2 ? t : t + grid;
+        const int rl = group + (own2 & 1) * groups;
+        if (rl < (own2 < 2 ? na : nb)) am2.push(v * scale, tt * tile_rows + rl);
+      }
+      cs.release_warp();
+      if (two) cs.release_warp();
+    }
+    pk_head_finish(P, cs.sh, am2, epoch);
+    return true;
+  }
   bool first = true;
   #pragma unroll 1
   for (int t = cta; t < ntiles; t += grid) {
     const int r0 = t * tile_rows;
     const int nr = min(tile_rows, rows - r0);
+    unsigned long long* ttr = nullptr;  // LM head: per-tile times of CTA 0, thread 0 (trace only)
+    if (cs.tr && S.kind == kPkHead && (t - cta) / grid < 500) ttr = cs.tr - 16 * (P.nstages - 1) + 8192 + 4 * ((t - cta) / grid);
+    pk_mark(ttr, 0);
     const uint8_t* tile = cs.take();
     if (!tile) return false;
+    pk_mark(ttr, 1);
     if (first) pk_mark(cs.tr, 2);
     #pragma unroll 1
     for (int p0 = 0; p0 < nr; p0 += per_pass) {
@@ -965,7 +1005,9 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
       }
       if (owner && rl < nr) pk_epi_run(S, cs, e, v * scale, v2 * scale, am);
     }
+    pk_mark(ttr, 2);
     cs.release_warp();
+    pk_mark(ttr, 3);
   }
   if (S.kind == kPkHead) pk_head_finish(P, cs.sh, am, epoch);
   return true;

@@ -134,7 +134,7 @@ struct kib_qwen35 {
   unsigned* d_pk_ctr = nullptr;  // [1] LM-head ticket, [2] cell tag epoch
   uint64_t* d_pk_cells = nullptr;
   float* d_pk_rope = nullptr;  // [kPkRopePairs] rotary inverse frequencies
-  float *d_pk_cmax = nullptr, *d_pk_csum = nullptr;
+  float* d_pk_cmax = nullptr;
   int* d_pk_cidx = nullptr;
   unsigned long long* d_pk_trace = nullptr;
   bool pk_coop = true;
@@ -919,11 +919,9 @@ static PkProgram pk_program(kib_qwen35* m) {
   P.token = m->d_tokens;
   P.token_log = m->d_log;
   P.step = m->d_step;
-  P.prob_out = nullptr;
   P.head_ctr = m->d_pk_ctr + 1;
   P.epoch = m->d_pk_ctr + 2;
   P.cand_max = m->d_pk_cmax;
-  P.cand_sum = m->d_pk_csum;
   P.cand_idx = m->d_pk_cidx;
   P.err = m->ctx->d_err;
   P.trace = m->trace_on ? m->d_pk_trace : nullptr;
@@ -1181,7 +1179,7 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
   }
   cudaMemset(m->d_head_cnt, 0, 4 * sizeof(unsigned));
   if (dalloc(&m->d_pk_ctr, 4) != cudaSuccess ||
-      dalloc(&m->d_pk_cmax, 1024) != cudaSuccess || dalloc(&m->d_pk_csum, 1024) != cudaSuccess ||
+      dalloc(&m->d_pk_cmax, 1024) != cudaSuccess ||
       dalloc(&m->d_pk_cidx, 1024) != cudaSuccess || dalloc(&m->d_pk_trace, 16 * 4096) != cudaSuccess) {
     kib_qwen35_free(mp.release());
     return set_error(ctx, KIB_ERR_INTERNAL, "persistent decode allocation failed");
@@ -1204,7 +1202,7 @@ void kib_qwen35_free(kib_qwen35* m) {
   if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
   if (m->mtp_graph) cudaGraphExecDestroy(m->mtp_graph);
   if (m->pk_graph) cudaGraphExecDestroy(m->pk_graph);
-  void* pk_ptrs[] = {m->d_pk, m->d_pk_ctr, m->d_pk_cells, m->d_pk_rope, m->d_pk_cmax, m->d_pk_csum, m->d_pk_cidx, m->d_pk_trace};
+  void* pk_ptrs[] = {m->d_pk, m->d_pk_ctr, m->d_pk_cells, m->d_pk_rope, m->d_pk_cmax, m->d_pk_cidx, m->d_pk_trace};
   for (void* p : pk_ptrs)
     if (p) cudaFree(p);
   void* ptrs[] = {m->d_weights, m->d_k, m->d_v, m->d_mk, m->d_mv, m->d_r, m->d_s, m->d_r_snap, m->d_s_snap,
@@ -1409,12 +1407,12 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
     }
     if (const char* p2 = std::getenv("KIB_TRACE_OUT2")) {
       // per-tile times of the LM head on CTA 0: wait start, taken, dots done, released
-      std::vector<unsigned long long> t(8 * 500);
+      std::vector<unsigned long long> t(4 * 500);
       cudaMemcpy(t.data(), m->d_pk_trace + 8192, t.size() * 8, cudaMemcpyDeviceToHost);
       if (FILE* f2 = std::fopen(p2, "w")) {
-        for (int j = 0; j < 500 && t[8 * j]; ++j) {
+        for (int j = 0; j < 500 && t[4 * j]; ++j) {
           std::fprintf(f2, "%d", j);
-          for (int q = 0; q < 7; ++q) std::fprintf(f2, ",%lld", t[8 * j + q] ? (long long)(t[8 * j + q] - h[0]) : -1ll);
+          for (int q = 0; q < 4; ++q) std::fprintf(f2, ",%lld", t[4 * j + q] ? (long long)(t[4 * j + q] - h[0]) : -1ll);
           std::fprintf(f2, "\n");
         }
         std::fclose(f2);
