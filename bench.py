@@ -43,9 +43,10 @@ WORKLOAD = "qwen35-0.8b-shape-q4_k_m-bs1-greedy-decode-ctx4096"
 TOKEN_BYTES = 604.0e6
 # DRAM bytes per token of decode_persistent_kernel from ncu (dram__bytes_read.sum
 # + dram__bytes_write.sum), the capture summarised in
-# profiles/decode_persistent_small_full.md (a 4-layer capture scaled to the full
-# model by algorithmic bytes: traffic/algorithmic = 1.005).
-PK_TRAFFIC = 607.0e6  # 1.005 x 604 MB: the 4-layer capture scaled by its algorithmic bytes
+# profiles/decode_persistent_small_full.md: a 4-layer capture (70.51 MB read +
+# 0.46 MB written against 72.44 MB algorithmic) scaled to the full model by
+# algorithmic bytes, traffic/algorithmic = 0.980.
+PK_TRAFFIC = 591.7e6  # 0.980 x 604 MB
 
 
 def peaks():
@@ -351,7 +352,7 @@ def main():
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             threads = os.cpu_count() or 1
-            v, n, dt = cpu_decode_sample(path, threads, budget_s=20.0, max_tokens=6)
+            v, n, dt = cpu_decode_sample(path, threads, budget_s=12.0, max_tokens=256)
             cpu = {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port",
                    "sample": f"{n} oracle decode steps at position {CONTEXT} in {dt:.1f} s "
                              f"(oracle/kib_oracle.cpp, {threads} threads)"}
