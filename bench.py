@@ -201,13 +201,75 @@ def matvec_roofline(ctx, hbm_peak, reps=5, profile=False, qtype=None, rows=3584,
             "pool_copies": copies}
 
 
+MTP_CONTEXT = 2048
+# HBM bytes of one (k+1)-token verify forward at ctx 2048 (algorithmic, nearly
+# independent of k): weights 513.3 MB + GDN S/R read+write 40.4 MB + K/V read
+# once for all k+1 queries 25.2 MB.
+VERIFY_BYTES = 578.8e6
+
+
+def mtp_verify_bench(ctx, hbm_peak, reps=20):
+    """the config-1 model plus one NextN layer, prompt of
+    2048 seeded tokens.  For draft budgets k = 1..4: the latency of one verify
+    forward over k+1 tokens through kib_qwen35_forward (argmax per row on the
+    device, no state advance; device time by CUDA events on the engine's
+    stream and the call's wall time), and tokens per verify step of greedy MTP
+    generation with the budget fixed at k."""
+    import numpy as np
+    import torch
+    import kib
+    d = os.environ.get("KIB_BENCH_DIR", os.path.join(tempfile.gettempdir(), "kib_bench"))
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, "qwen35_0p8b_shape_q4_k_m_nextn1_seed1234.gguf")
+    if not os.path.exists(path):
+        tmp = path + ".tmp"
+        kib.write_synthetic_qwen35(tmp, threads=min(os.cpu_count() or 8, 64), seed=1234, nextn_layers=1)
+        os.replace(tmp, path)
+    m = kib.Qwen35(ctx, path, context_tokens=MTP_CONTEXT + 256, decode_tokens=64, prefill_chunk=1024, enable_mtp=True)
+    rng = np.random.default_rng(2048)
+    prompt = rng.integers(0, m.plan.vocab_size, MTP_CONTEXT).astype(np.int32)
+    m.prefill(prompt, 1024)
+    stream = torch.cuda.ExternalStream(ctx.lib.kib_stream(ctx.h))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    res = {}
+    for k in (1, 2, 3, 4):
+        toks = rng.integers(0, m.plan.vocab_size, k + 1).astype(np.int32)
+        for _ in range(3):
+            m.forward(toks, advance=False)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(reps):
+            m.forward(toks, advance=False)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        wall_ms = (time.perf_counter() - t0) * 1e3 / reps
+        dev_ms = e0.elapsed_time(e1) / reps
+        res[f"k{k}"] = {"verify_tokens": k + 1, "verify_ms_device": round(dev_ms, 4),
+                        "verify_ms_call": round(wall_ms, 4),
+                        "verify_hbm_gbs": round(VERIFY_BYTES / (dev_ms * 1e-3) / 1e9, 1)}
+    for k in (1, 2, 3, 4):
+        m.reset()
+        out, r = m.generate(prompt, 48, enable_mtp=True, mtp_draft_tokens=k, mtp_adaptive=False, ignore_eos=True)
+        steps = max(int(r.mtp.verify_steps), 1)
+        res[f"k{k}"].update({"generated": int(r.generated_tokens), "verify_steps": int(r.mtp.verify_steps),
+                             "drafted": int(r.mtp.drafted_tokens), "accepted": int(r.mtp.accepted_tokens),
+                             "tokens_per_step": round(int(r.generated_tokens) / steps, 3),
+                             "decode_ms": round(float(r.decode_ms), 2)})
+    m.close()
+    return {"workload": "BASELINE config 3: MTP verify at ctx 2048, fixed draft budget k (random-init weights: "
+                        "drafts rarely match, so tokens/step sits near 1)",
+            "bytes_per_verify": VERIFY_BYTES, "peak": hbm_peak, "by_k": res}
+
+
+
 def cpu_decode_sample(path, threads, budget_s=20.0, max_tokens=6):
     """The oracle's bs1 decode step at position 4096 on the host cores (state
     content does not change the work)."""
     import numpy as np
     import oracle_lib
     o = oracle_lib.Oracle(threads=threads)
-    om = oracle_lib.OracleModel(o, path, CONTEXT + 16)
+    om = oracle_lib.OracleModel(o, path, CONTEXT + max_tokens + 16)
     tok = 1
     t0 = time.perf_counter()
     n = 0
@@ -260,6 +322,7 @@ def main():
     ap.add_argument("--impl", default="kib", choices=["kib", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--no-mtp", action="store_true", help="skip the config-3 MTP verify measurement")
     ap.add_argument("--workload", default="decode", choices=["decode", "matvec"],
                     help="matvec: BASELINE config 1 only (Q4_K 3584x1024 GEMV roofline)")
     ap.add_argument("--layers", type=int, default=None,
@@ -349,6 +412,9 @@ def main():
                 "kernel": "decode_persistent_kernel" if persistent else "per-kernel decode graph",
                 "bytes_per_launch": TOKEN_BYTES, "us_per_launch": round(ms / args.steps * 1e3, 2),
                 "peak_kind": mv["peak_kind"]}
+        mtp = None
+        if not args.no_mtp and world == 1:
+            mtp = mtp_verify_bench(ctx, hbm_peak)
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             threads = os.cpu_count() or 1
@@ -372,6 +438,7 @@ def main():
                         "api": "kib_qwen35_forward (token + position H2D, argmax D2H, per-token sync)"},
                 "roofline": roof,
                 "matvec_config1": mv,
+                "mtp_verify_config3": mtp,
                 "cpu_baseline": cpu, "gpu_launches": launches_per_step * args.steps,
                 "clocks": clk.summary(),
                 "tokens_head": [int(x) for x in out[:8]]}
