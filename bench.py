@@ -263,6 +263,44 @@ def mtp_verify_bench(ctx, hbm_peak, reps=20):
 
 
 
+PREFILL_TOKENS = 8192
+# FLOPs of the 8192-token prefill (algorithmic): linear projections 8.15 TFLOP,
+# causal attention 1.65 TFLOP, delta-rule GDN 0.23 TFLOP.
+PREFILL_FLOP = 10.03e12
+
+
+def prefill_bench(ctx, path):
+    """an 8192-token prompt of seeded uniform token ids
+    through kib_qwen35_prefill in 1024-token chunks (device time by CUDA events
+    on the engine's stream), against the measured dense bf16 tensor peak."""
+    import numpy as np
+    import torch
+    import kib
+    m = kib.Qwen35(ctx, path, context_tokens=PREFILL_TOKENS + 16, decode_tokens=8, prefill_chunk=1024, enable_mtp=False)
+    prompt = np.random.default_rng(8192).integers(0, m.plan.vocab_size, PREFILL_TOKENS).astype(np.int32)
+    stream = torch.cuda.ExternalStream(ctx.lib.kib_stream(ctx.h))
+    m.prefill(prompt[:1024], 1024)  # warm-up: graphs and kernels
+    m.reset()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    nxt = m.prefill(prompt, 1024)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    m.close()
+    tflops = PREFILL_FLOP / (ms * 1e-3) / 1e12
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, kind = (float(json.load(open(pk))["bf16_tflops_sustained"]), "measured sustained bf16") if os.path.exists(pk) \
+        else (1400.0, "fallback")
+    return {"workload": "BASELINE config 4: 8192-token prefill in 1024-token chunks (fp16 mma.sync GEMMs, "
+                        "not yet tcgen05)", "tokens": PREFILL_TOKENS, "ms": round(ms, 2),
+            "tok_per_s": round(PREFILL_TOKENS / (ms * 1e-3), 1), "bound": "tensor", "achieved": round(tflops, 2),
+            "peak": peak, "unit": "TFLOP/s", "frac": round(tflops / peak, 4), "peak_kind": kind,
+            "flop": PREFILL_FLOP, "next_token": int(nxt)}
+
+
+
 def cpu_decode_sample(path, threads, budget_s=20.0, max_tokens=6):
     """The oracle's bs1 decode step at position 4096 on the host cores (state
     content does not change the work)."""
@@ -323,6 +361,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--no-mtp", action="store_true", help="skip the config-3 MTP verify measurement")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
     ap.add_argument("--workload", default="decode", choices=["decode", "matvec"],
                     help="matvec: BASELINE config 1 only (Q4_K 3584x1024 GEMV roofline)")
     ap.add_argument("--layers", type=int, default=None,
@@ -415,6 +454,9 @@ def main():
         mtp = None
         if not args.no_mtp and world == 1:
             mtp = mtp_verify_bench(ctx, hbm_peak)
+        pre = None
+        if not args.no_prefill and world == 1:
+            pre = prefill_bench(ctx, path)
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             threads = os.cpu_count() or 1
@@ -439,6 +481,7 @@ def main():
                 "roofline": roof,
                 "matvec_config1": mv,
                 "mtp_verify_config3": mtp,
+                "prefill_config4": pre,
                 "cpu_baseline": cpu, "gpu_launches": launches_per_step * args.steps,
                 "clocks": clk.summary(),
                 "tokens_head": [int(x) for x in out[:8]]}
