@@ -253,9 +253,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) kquant_gemv_kernel(const __gr
           for (int t = 0; t < NT; ++t) {
             if (t >= p.ntok) break;  // xs holds ntok rows only
             const float* xb = xs + t * p.cols + 256 * blk;
+            // x in runs of four contiguous columns (unit_col is contiguous
+            // within every aligned group of four elements): one LDS.128 each
             float s = 0.0f;
 #pragma unroll
-            for (int e = 0; e < 64; ++e) s = fmaf(wv[e], xb[unit_col<QT>(unit, e)], s);
+            for (int e = 0; e < 64; e += 4) {
+              const float4 x4 = *reinterpret_cast<const float4*>(xb + unit_col<QT>(unit, e));
+              s = fmaf(wv[e], x4.x, s);
+              s = fmaf(wv[e + 1], x4.y, s);
+              s = fmaf(wv[e + 2], x4.z, s);
+              s = fmaf(wv[e + 3], x4.w, s);
+            }
             acc[t] = s;
           }
           if (paired) {
@@ -266,7 +274,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) kquant_gemv_kernel(const __gr
             const float* xb = xs + t * p.cols + 256 * blk;
               float s = 0.0f;
 #pragma unroll
-              for (int e = 0; e < 64; ++e) s = fmaf(wv[e], xb[unit_col<QT>(unit, e)], s);
+              for (int e = 0; e < 64; e += 4) {
+                const float4 x4 = *reinterpret_cast<const float4*>(xb + unit_col<QT>(unit, e));
+                s = fmaf(wv[e], x4.x, s);
+                s = fmaf(wv[e + 1], x4.y, s);
+                s = fmaf(wv[e + 2], x4.z, s);
+                s = fmaf(wv[e + 3], x4.w, s);
+              }
               acc2[t] = s;
             }
           }

@@ -61,18 +61,31 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
   trace_wait(p.trace);
   pdl_launch_dependents();
   const float scale = 1.0f / sqrtf(static_cast<float>(D));
-  for (int t = 0; t < p.T; ++t) {
+  // the next token's inputs are loaded while the current one is processed
+  // (one global round trip per token would otherwise sit on the sequential path)
+  auto load_tok = [&](int t, float& qv, float& kv, float (&vv)[4], float& a, float& b) {
     const float* row = p.conv_out + static_cast<size_t>(t) * p.C;
-    const float qv = row[kh * D + tid];
-    const float kv = row[key_dim + kh * D + tid];
+    qv = row[kh * D + tid];
+    kv = row[key_dim + kh * D + tid];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) vv[r] = row[2 * key_dim + h * D + grp * kGdnRows + 4 * warp + r];
+    a = p.alpha_raw[static_cast<size_t>(t) * p.ld_ba + h];
+    b = p.beta_raw[static_cast<size_t>(t) * p.ld_ba + h];
+  };
+  float nq = 0.f, nk = 0.f, nv[4] = {0.f, 0.f, 0.f, 0.f}, na = 0.f, nb = 0.f;
+  if (p.T > 0) load_tok(0, nq, nk, nv, na, nb);
+  for (int t = 0; t < p.T; ++t) {
+    const float qv = nq, kv = nk, a = na, b = nb;
+    float vcur[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) vcur[r] = nv[r];
+    if (t + 1 < p.T) load_tok(t + 1, nq, nk, nv, na, nb);
     float q2 = warp_sum(qv * qv), k2 = warp_sum(kv * kv);
     if (lane == 0) {
       red[0][warp] = q2;
       red[1][warp] = k2;
     }
     if (tid == 0) {
-      const float a = p.alpha_raw[static_cast<size_t>(t) * p.ld_ba + h];
-      const float b = p.beta_raw[static_cast<size_t>(t) * p.ld_ba + h];
       s_gb[0] = softplus20_f(a + p.dt_bias[h]) * p.ssm_a[h];
       s_gb[1] = sigmoid_f(b);
     }
@@ -95,8 +108,7 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
       st.z *= ge;
       st.w *= ge;
       const float sk = warp_sum(st.x * k4.x + st.y * k4.y + st.z * k4.z + st.w * k4.w);
-      const float v = row[2 * key_dim + h * D + vrow];
-      const float delta = (v - sk) * beta;
+      const float delta = (vcur[r] - sk) * beta;
       st.x += k4.x * delta;
       st.y += k4.y * delta;
       st.z += k4.z * delta;

@@ -74,24 +74,41 @@ __global__ void split_qkv_l2_kernel(const float* src, float* q, float* k, float*
   for (int i = lane; i < d; i += 32) dst[(static_cast<size_t>(t) * key_heads + h) * d + i] = s[i] * scale;
 }
 
-// build_ssm_conv_state_f32 + ssm_conv_f32 (+ optional silu): one thread per
-// channel, sequential over tokens, state updated in place.
+// build_ssm_conv_state_f32 + ssm_conv_f32 (+ optional silu), in place or not.
+// A CTA owns 32 channels and all T tokens; thread (channel, tile) convolves one
+// tile of tokens.  Every thread first reads the K-1 inputs before its tile (the
+// carried state for the first tile), then the CTA barrier, then each thread
+// reads and overwrites only its own tokens, so tiles run in parallel even when
+// out aliases in.  The last tile leaves with the new state in its window.  The
+// sum order per output is the reference's (j = 0..K-1).
 __global__ void conv_stateful_kernel(float* state, const float* in, int in_ld, const float* w, int K, int C, int T,
                                      float* out, int out_ld, int apply_silu) {
   pdl_wait();
   pdl_launch_dependents();
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  const int ntiles = blockDim.y, tile = threadIdx.y;
+  const int len = (T + ntiles - 1) / ntiles;
+  const int t0 = min(tile * len, T), t1 = min(t0 + len, T);
+  float win[16], wc[16];
+  if (c < C) {
+    for (int j = 0; j < K; ++j) wc[j] = w[static_cast<size_t>(c) * K + j];
+    for (int j = 0; j < K - 1; ++j) {
+      const int t = t0 - (K - 1) + j;
+      win[j] = t >= 0 ? in[static_cast<size_t>(t) * in_ld + c] : state[static_cast<size_t>(c) * (K - 1) + (t + K - 1)];
+    }
+  }
+  __syncthreads();
   if (c >= C) return;
-  float win[16];
-  for (int j = 0; j < K - 1; ++j) win[j] = state[static_cast<size_t>(c) * (K - 1) + j];
-  for (int t = 0; t < T; ++t) {
+  for (int t = t0; t < t1; ++t) {
     win[K - 1] = in[static_cast<size_t>(t) * in_ld + c];
     float s = 0.0f;
-    for (int j = 0; j < K; ++j) s += win[j] * w[static_cast<size_t>(c) * K + j];
+    for (int j = 0; j < K; ++j) s += win[j] * wc[j];
     out[static_cast<size_t>(t) * out_ld + c] = apply_silu ? silu_k(s) : s;
     for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
   }
-  for (int j = 0; j < K - 1; ++j) state[static_cast<size_t>(c) * (K - 1) + j] = win[j];
+  // the tile holding token T-1 ends with the window [.., T-1]; with T < K-1 that
+  // is tile 0, whose window also carries the older state entries
+  if (t1 == T && t0 < T) for (int j = 0; j < K - 1; ++j) state[static_cast<size_t>(c) * (K - 1) + j] = win[j];
 }
 
 __global__ void prepare_gate_beta_kernel(float* gate, float* beta, const float* bias, const float* scale, int total,
@@ -496,8 +513,10 @@ cudaError_t norm_gate_launch(float* v, const float* w, const float* gate, int T,
 
 cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w, int K, int C, int T, float* out,
                         int out_ld, int silu, cudaStream_t st) {
-  return launch_pdl(conv_stateful_kernel, dim3(blocks_for(C, 128)), dim3(128), 0, st, state, in, in_ld, w, K, C, T,
-                    out, out_ld, silu);
+  // tiles of >= 16 tokens, at most 32 per CTA (32 x 32 threads)
+  const int ntiles = T >= 512 ? 32 : (T + 15) / 16;
+  return launch_pdl(conv_stateful_kernel, dim3((C + 31) / 32), dim3(32, ntiles), 0, st, state, in, in_ld, w, K, C, T, out,
+                    out_ld, silu);
 }
 
 cudaError_t silu_mul_launch(float* g, const float* u, size_t n, cudaStream_t st) {
