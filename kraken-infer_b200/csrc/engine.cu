@@ -436,7 +436,15 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
   g.value_heads = m->lvh;
   g.eps = m->eps;
   g.trace = nullptr;
-  q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
+  if (m->lhd == 128 && m->lkh <= m->lvh) {
+    // token-parallel norms and gate/beta first, then the sequential scan alone
+    q.run(launch_pdl(gdn_prep_kernel, dim3(T, m->lkh), dim3(128), 0, q.st, m->d_qkv, m->C, m->d_alpha, m->d_beta, m->lvh,
+                     L.dt_bias.f(), L.ssm_a.f(), m->lkh, m->lvh, m->eps),
+          "gdn_prep");
+    q.run(launch_pdl(gdn_scan_kernel, dim3(m->lvh, m->lhd / (4 * kGdnScanRows)), dim3(128), 0, q.st, g), "gdn_scan");
+  } else {
+    q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
+  }
   q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, T, m->lvh, m->lhd, m->eps, m->d_norm2, q.st), "norm_gate");
   gemm(q, L.ssm_out, m->d_norm2, m->VD, T, x_mid, m->H, x_in);
 }

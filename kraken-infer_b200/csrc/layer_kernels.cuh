@@ -125,6 +125,100 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
   trace_exit(p.trace);
 }
 
+// Multi-token GDN in two steps.  gdn_prep_kernel does the token-parallel part:
+// the L2 norms of each token's q and k head rows (in place in the conv output,
+// same reduction order as gdn_core_kernel) and g = softplus(alpha + dt_bias) *
+// ssm_a, beta = sigmoid(beta) (in place).  gdn_scan_kernel then runs only the
+// sequential delta rule: a warp owns kGdnScanRows state rows, lane l columns
+// 4l..4l+3, the next token's inputs are loaded while the current one is
+// processed, and no CTA barrier sits in the per-token chain.
+constexpr int kGdnScanRows = 2;
+
+static __global__ void __launch_bounds__(128) gdn_prep_kernel(float* conv_out, int C, float* alpha, float* beta,
+                                                               int ld_ba, const float* dt_bias, const float* ssm_a,
+                                                               int key_heads, int value_heads, float eps) {
+  constexpr int D = 128;
+  __shared__ float red[2][4];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = blockIdx.x, kh = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* row = conv_out + static_cast<size_t>(t) * C;
+  const int key_dim = key_heads * D;
+  const float qv = row[kh * D + tid], kv = row[key_dim + kh * D + tid];
+  const float q2 = warp_sum(qv * qv), k2 = warp_sum(kv * kv);
+  if (lane == 0) {
+    red[0][warp] = q2;
+    red[1][warp] = k2;
+  }
+  __syncthreads();
+  const float qs = 1.0f / fmaxf(sqrtf((red[0][0] + red[0][1]) + (red[0][2] + red[0][3])), eps);
+  const float ks = 1.0f / fmaxf(sqrtf((red[1][0] + red[1][1]) + (red[1][2] + red[1][3])), eps);
+  row[kh * D + tid] = qv * qs;
+  row[key_dim + kh * D + tid] = kv * ks;
+  // gate/beta of the value heads this key head serves (h % key_heads == kh)
+  for (int h = kh + key_heads * tid; h < value_heads; h += key_heads * 128) {
+    const size_t o = static_cast<size_t>(t) * ld_ba + h;
+    alpha[o] = softplus20_f(alpha[o] + dt_bias[h]) * ssm_a[h];
+    beta[o] = sigmoid_f(beta[o]);
+  }
+}
+
+static __global__ void __launch_bounds__(128) gdn_scan_kernel(const __grid_constant__ GdnParams p) {
+  constexpr int D = 128;
+  const int h = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r0 = (blockIdx.y * 4 + warp) * kGdnScanRows;
+  const int kh = h % p.key_heads;
+  const int key_dim = p.key_heads * D;
+  float* S = p.state + static_cast<size_t>(h) * D * D;
+  float4 s[kGdnScanRows];
+#pragma unroll
+  for (int r = 0; r < kGdnScanRows; ++r) s[r] = *reinterpret_cast<const float4*>(S + static_cast<size_t>(r0 + r) * D + 4 * lane);
+  pdl_wait();
+  pdl_launch_dependents();
+  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  auto load_tok = [&](int t, float4& q4, float4& k4, float (&vv)[kGdnScanRows], float& g, float& b) {
+    const float* row = p.conv_out + static_cast<size_t>(t) * p.C;
+    q4 = *reinterpret_cast<const float4*>(row + kh * D + 4 * lane);
+    k4 = *reinterpret_cast<const float4*>(row + key_dim + kh * D + 4 * lane);
+#pragma unroll
+    for (int r = 0; r < kGdnScanRows; ++r) vv[r] = row[2 * key_dim + h * D + r0 + r];
+    g = p.alpha_raw[static_cast<size_t>(t) * p.ld_ba + h];
+    b = p.beta_raw[static_cast<size_t>(t) * p.ld_ba + h];
+  };
+  float4 nq = make_float4(0.f, 0.f, 0.f, 0.f), nk = nq;
+  float nv[kGdnScanRows], ng = 0.f, nb = 0.f;
+  if (p.T > 0) load_tok(0, nq, nk, nv, ng, nb);
+  for (int t = 0; t < p.T; ++t) {
+    const float4 q4 = nq, k4 = nk;
+    float v[kGdnScanRows];
+#pragma unroll
+    for (int r = 0; r < kGdnScanRows; ++r) v[r] = nv[r];
+    const float ge = expf(ng), beta = nb;
+    if (t + 1 < p.T) load_tok(t + 1, nq, nk, nv, ng, nb);
+#pragma unroll
+    for (int r = 0; r < kGdnScanRows; ++r) {
+      float4 st = s[r];
+      st.x *= ge;
+      st.y *= ge;
+      st.z *= ge;
+      st.w *= ge;
+      const float sk = warp_sum(st.x * k4.x + st.y * k4.y + st.z * k4.z + st.w * k4.w);
+      const float delta = (v[r] - sk) * beta;
+      st.x += k4.x * delta;
+      st.y += k4.y * delta;
+      st.z += k4.z * delta;
+      st.w += k4.w * delta;
+      const float y = warp_sum(st.x * q4.x + st.y * q4.y + st.z * q4.z + st.w * q4.w);
+      if (lane == 0) p.out[static_cast<size_t>(t) * p.value_heads * D + h * D + r0 + r] = y * scale;
+      s[r] = st;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kGdnScanRows; ++r) *reinterpret_cast<float4*>(S + static_cast<size_t>(r0 + r) * D + 4 * lane) = s[r];
+}
+
 // =============================================================== attention
 struct AttnParams {
   const float* qg;        // [T][heads][2*hd]: q | gate per head (joint projection)
