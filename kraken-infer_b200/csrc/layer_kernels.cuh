@@ -736,25 +736,55 @@ struct GemmParams {
   const float* resid;  // optional [T][y_ld]
 };
 
+// Multi-token (T > 8) K-quant GEMM on the tensor cores: the reference's M > 8
+// numerics (mul_mm_simd: weights and x rounded to fp16, fp32 accumulation).
+// CTA tile 128 weight rows x 128 tokens, one 256-column super-block per
+// k-step: the 256 threads dequantize the tile's weights into shared memory as
+// fp16 (each weight value exactly as unit_dequant_f16 rounds it) and round the
+// x tile to fp16; 8 warps (4 along rows x 2 along tokens) each own a 32 x 64
+// output tile of mma.sync m16n8k16 f16 x f16 -> f32, fragments by ldmatrix.
+// Shared rows are padded to 264 halves so the ldmatrix rows spread over banks.
+constexpr int kGemmTileM = 128, kGemmTileN = 128, kGemmLd = 256 + 8;
+constexpr size_t kGemmSmem = static_cast<size_t>(kGemmTileM + kGemmTileN) * kGemmLd * 2;
+
+KIB_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+KIB_DEV void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 template <int QT>
-__global__ void __launch_bounds__(256) kquant_gemm_f16_kernel(const __grid_constant__ GemmParams p) {
-  extern __shared__ __align__(16) float gsm[];
-  float* Ws = gsm;              // [256 k][64 rows]
-  float* Xs = gsm + 256 * 64;   // [256 k][64 tokens]
-  const int tid = threadIdx.x;
-  const int r0 = blockIdx.x * 64, t0 = blockIdx.y * 64;
+__global__ void __launch_bounds__(256, 1) kquant_gemm_f16_kernel(const __grid_constant__ GemmParams p) {
+  extern __shared__ __align__(16) uint8_t gsm_raw[];
+  __half* As = reinterpret_cast<__half*>(gsm_raw);        // [128 rows][kGemmLd]
+  __half* Bs = As + kGemmTileM * kGemmLd;                 // [128 tokens][kGemmLd]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r0 = blockIdx.x * kGemmTileM, t0 = blockIdx.y * kGemmTileN;
   const int bpr = p.cols / 256;
-  const int tr = tid / 16, tt = tid % 16;  // thread computes rows tr*4..+3, tokens tt*4..+3
-  float acc[4][4];
+  const int wm = (warp & 3) * 32, wn = (warp >> 2) * 64;  // warp tile origin
+  float acc[2][8][4];
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int i = 0; i < 2; ++i)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.0f;
   pdl_wait();
   pdl_launch_dependents();
+  const uint32_t as_base = smem_u32(As), bs_base = smem_u32(Bs);
   for (int kb = 0; kb < bpr; ++kb) {
-    {  // weights: 64 rows x 4 units = 256 units, one per thread
-      const int rl = tid >> 2, unit = tid & 3;
+    // weights: 128 rows x 4 units of 64 = 512 units, two per thread
+#pragma unroll 1
+    for (int job = tid; job < kGemmTileM * 4; job += 256) {
+      const int rl = job >> 2, unit = job & 3;
       const int row = r0 + rl;
       float v[64];
       if (row < p.rows) {
@@ -763,38 +793,63 @@ __global__ void __launch_bounds__(256) kquant_gemm_f16_kernel(const __grid_const
 #pragma unroll
         for (int e = 0; e < 64; ++e) v[e] = 0.0f;
       }
+      __half* dst = As + rl * kGemmLd;
 #pragma unroll
-      for (int e = 0; e < 64; ++e) Ws[unit_col<QT>(unit, e) * 64 + rl] = v[e];
+      for (int e = 0; e < 64; e += 2) {
+        // unit_col is contiguous within aligned pairs
+        *reinterpret_cast<__half2*>(dst + unit_col<QT>(unit, e)) = __floats2half2_rn(v[e], v[e + 1]);
+      }
     }
-    for (int i = tid; i < 64 * 256; i += 256) {
-      const int tl = i / 256, k = i % 256;
+    // x: 128 tokens x 256 k, rounded to half
+#pragma unroll 4
+    for (int i = tid; i < kGemmTileN * 64; i += 256) {
+      const int tl = i >> 6, k4 = (i & 63) * 4;
       const int t = t0 + tl;
-      Xs[k * 64 + tl] = t < p.T ? round_to_half(p.x[static_cast<size_t>(t) * p.x_ld + kb * 256 + k]) : 0.0f;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t < p.T) x = *reinterpret_cast<const float4*>(p.x + static_cast<size_t>(t) * p.x_ld + kb * 256 + k4);
+      __half2* dst = reinterpret_cast<__half2*>(Bs + tl * kGemmLd + k4);
+      dst[0] = __floats2half2_rn(x.x, x.y);
+      dst[1] = __floats2half2_rn(x.z, x.w);
     }
     __syncthreads();
-#pragma unroll 4
-    for (int k = 0; k < 256; ++k) {
-      const float4 wv = *reinterpret_cast<const float4*>(Ws + k * 64 + tr * 4);
-      const float4 xv = *reinterpret_cast<const float4*>(Xs + k * 64 + tt * 4);
-      const float w4[4] = {wv.x, wv.y, wv.z, wv.w}, x4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll 2
+    for (int k0 = 0; k0 < 256; k0 += 16) {
+      uint32_t a[2][4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+      for (int i = 0; i < 2; ++i) {
+        const int row = wm + 16 * i + (lane & 15), col = k0 + (lane >> 4) * 8;
+        ldsm_x4(as_base + static_cast<uint32_t>(row * kGemmLd + col) * 2, a[i][0], a[i][1], a[i][2], a[i][3]);
+      }
 #pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(w4[a], x4[b], acc[a][b]);
+      for (int j = 0; j < 8; j += 2) {
+        const int n = wn + 8 * j + (lane & 7) + ((lane >> 4) << 3), col = k0 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(bs_base + static_cast<uint32_t>(n * kGemmLd + col) * 2, b0, b1, b2, b3);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          mma_f16_16816(acc[i][j], a[i], b0, b1);
+          mma_f16_16816(acc[i][j + 1], a[i], b2, b3);
+        }
+      }
     }
     __syncthreads();
   }
+  // D fragment: c0,c1 at (row g, tokens 2q, 2q+1), c2,c3 at row g+8
+  const int g = lane >> 2, q = lane & 3;
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int i = 0; i < 2; ++i)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int row = r0 + tr * 4 + a, t = t0 + tt * 4 + b;
-      if (row < p.rows && t < p.T) {
-        float v = acc[a][b];
-        if (p.resid) v += p.resid[static_cast<size_t>(t) * p.y_ld + row];
-        p.y[static_cast<size_t>(t) * p.y_ld + row] = v;
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int row = r0 + wm + 16 * i + g + (c >> 1) * 8;
+        const int t = t0 + wn + 8 * j + 2 * q + (c & 1);
+        if (row < p.rows && t < p.T) {
+          float v = acc[i][j][c];
+          if (p.resid) v += p.resid[static_cast<size_t>(t) * p.y_ld + row];
+          p.y[static_cast<size_t>(t) * p.y_ld + row] = v;
+        }
       }
-    }
 }
 
 }  // namespace kib

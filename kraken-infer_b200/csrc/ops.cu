@@ -476,8 +476,8 @@ cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const f
   p.y = y;
   p.y_ld = y_ld;
   p.resid = resid;
-  const size_t smem = 2 * 256 * 64 * sizeof(float);
-  dim3 grid((rows + 63) / 64, (T + 63) / 64);
+  const size_t smem = kGemmSmem;
+  dim3 grid((rows + kGemmTileM - 1) / kGemmTileM, (T + kGemmTileN - 1) / kGemmTileN);
   static bool cfg[3] = {false, false, false};
   switch (type) {
     case kTypeQ4K:
