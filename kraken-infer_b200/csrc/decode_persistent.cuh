@@ -1097,29 +1097,7 @@ __device__ __noinline__ bool pk_gdn(const PkStage& S, PkCons& cs) {
   return true;
 }
 
-// Sums 8 values over the warp; every lane ends with the 8 totals.  Three
-// halving exchanges leave each lane one value summed over 8 lanes, two more
-// finish it, and 8 broadcasts return the totals (17 shuffles instead of 40).
-KIB_DEV void pk_warp_sum8(float (&v)[8], int lane) {
-  float a[4], b[2];
-  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float send = h16 ? v[i] : v[i + 4], keep = h16 ? v[i + 4] : v[i];
-    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float send = h8 ? a[i] : a[i + 2], keep = h8 ? a[i + 2] : a[i];
-    b[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-  float c = (h4 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h4 ? b[0] : b[1], 4);
-  c += __shfl_xor_sync(0xffffffffu, c, 2);
-  c += __shfl_xor_sync(0xffffffffu, c, 1);
-  // lane L holds the total of value ((L >> 4) & 1) * 4 + ((L >> 3) & 1) * 2 + ((L >> 2) & 1)
-#pragma unroll
-  for (int e = 0; e < 8; ++e) v[e] = __shfl_sync(0xffffffffu, c, ((e >> 2) & 1) << 4 | ((e >> 1) & 1) << 3 | (e & 1) << 2);
-}
+KIB_DEV void pk_warp_sum8(float (&v)[8], int lane) { warp_sum8(v, lane); }
 
 // qk_norm (mps_backend.mm:1991-2024) then mrope (2482-2527) of one 256-wide
 // head vector staged in shared memory; text positions (all MRoPE streams

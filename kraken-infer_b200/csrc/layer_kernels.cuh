@@ -132,7 +132,7 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
 // sequential delta rule: a warp owns kGdnScanRows state rows, lane l columns
 // 4l..4l+3, the next token's inputs are loaded while the current one is
 // processed, and no CTA barrier sits in the per-token chain.
-constexpr int kGdnScanRows = 2;
+constexpr int kGdnScanRows = 1;
 
 static __global__ void __launch_bounds__(128) gdn_prep_kernel(float* conv_out, int C, float* alpha, float* beta,
                                                                int ld_ba, const float* dt_bias, const float* ssm_a,
@@ -601,8 +601,33 @@ static __global__ void __launch_bounds__(256) attn_prep_kernel(const __grid_cons
   }
 }
 
-// Prefill step 2: one warp per (query, head), sequential online softmax over
-// keys <= query position (attention_f32_batched_f16_kv order); Q rounded to
+// Sums 8 values over the warp; every lane ends with the 8 totals.  Three
+// halving exchanges leave each lane one value summed over 8 lanes, two more
+// finish it, and 8 broadcasts return the totals (17 shuffles instead of 40).
+KIB_DEV void warp_sum8(float (&v)[8], int lane) {
+  float a[4], b[2];
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = h16 ? v[i] : v[i + 4], keep = h16 ? v[i + 4] : v[i];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = h8 ? a[i] : a[i + 2], keep = h8 ? a[i + 2] : a[i];
+    b[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float c = (h4 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h4 ? b[0] : b[1], 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  // lane L holds the total of value ((L >> 4) & 1) * 4 + ((L >> 3) & 1) * 2 + ((L >> 2) & 1)
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = __shfl_sync(0xffffffffu, c, ((e >> 2) & 1) << 4 | ((e >> 1) & 1) << 3 | (e & 1) << 2);
+}
+
+// Prefill step 2: one warp per (query, head), online softmax over keys <= query
+// position in blocks of 8 (attention_f32_batched_f16_kv, with the running max
+// updated once per block); Q rounded to
 // half when round_q (flash256 numerics, mps_backend.mm:3450-3460); output
 // multiplied by sigmoid(gate).  grid (ceil(T/8), heads).
 static __global__ void __launch_bounds__(256) attn_prefill_kernel(const __grid_constant__ AttnParams p) {
@@ -624,27 +649,52 @@ static __global__ void __launch_bounds__(256) attn_prefill_kernel(const __grid_c
   }
   const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
   float m = -INFINITY, l = 0.0f;
-  for (int key = 0; key <= qpos; ++key) {
-    const uint4 kr = __ldcg(reinterpret_cast<const uint4*>(p.kcache + static_cast<size_t>(key) * kvd + kvh * kHd + 8 * lane));
-    const uint4 vr = __ldcg(reinterpret_cast<const uint4*>(p.vcache + static_cast<size_t>(key) * kvd + kvh * kHd + 8 * lane));
-    const __half2* kh = reinterpret_cast<const __half2*>(&kr);
-    const __half2* vh = reinterpret_cast<const __half2*>(&vr);
-    float d = 0.0f;
+  // blocks of 8 keys: the 8 partial dot products share one butterfly, and the
+  // block's K and V rows are loaded together
+  const size_t kbase = static_cast<size_t>(kvh) * kHd + 8 * lane;
+  for (int k0 = 0; k0 <= qpos; k0 += 8) {
+    uint4 kr[8], vr[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 a = __half22float2(kh[i]);
-      d = fmaf(q[2 * i], a.x, d);
-      d = fmaf(q[2 * i + 1], a.y, d);
+    for (int e = 0; e < 8; ++e) {
+      const int key = min(k0 + e, qpos);
+      kr[e] = __ldcg(reinterpret_cast<const uint4*>(p.kcache + static_cast<size_t>(key) * kvd + kbase));
+      vr[e] = __ldcg(reinterpret_cast<const uint4*>(p.vcache + static_cast<size_t>(key) * kvd + kbase));
     }
-    const float sc = warp_sum(d) * scale;
-    const float nm = fmaxf(m, sc);
-    const float ps = expf(m - nm), w = expf(sc - nm);
-    l = l * ps + w;
+    float sc[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 b = __half22float2(vh[i]);
-      acc[2 * i] = acc[2 * i] * ps + w * b.x;
-      acc[2 * i + 1] = acc[2 * i + 1] * ps + w * b.y;
+    for (int e = 0; e < 8; ++e) {
+      const __half2* kh = reinterpret_cast<const __half2*>(&kr[e]);
+      float d = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __half22float2(kh[i]);
+        d = fmaf(q[2 * i], a.x, d);
+        d = fmaf(q[2 * i + 1], a.y, d);
+      }
+      sc[e] = d;
+    }
+    warp_sum8(sc, lane);
+    float nm = m;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      sc[e] *= scale;
+      if (k0 + e <= qpos) nm = fmaxf(nm, sc[e]);
+    }
+    const float ps = expf(m - nm);
+    l *= ps;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= ps;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float w = k0 + e <= qpos ? expf(sc[e] - nm) : 0.0f;
+      l += w;
+      const __half2* vh = reinterpret_cast<const __half2*>(&vr[e]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 b = __half22float2(vh[i]);
+        acc[2 * i] = fmaf(w, b.x, acc[2 * i]);
+        acc[2 * i + 1] = fmaf(w, b.y, acc[2 * i + 1]);
+      }
     }
     m = nm;
   }
