@@ -130,7 +130,7 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
 // same reduction order as gdn_core_kernel) and g = softplus(alpha + dt_bias) *
 // ssm_a, beta = sigmoid(beta) (in place).  gdn_scan_kernel then runs only the
 // sequential delta rule: a warp owns kGdnScanRows state rows, lane l columns
-// 4l..4l+3, the next token's inputs are loaded while the current one is
+// 4l..4l+3, the inputs of the next tokens are loaded while the current one is
 // processed, and no CTA barrier sits in the per-token chain.
 constexpr int kGdnScanRows = 1;
 
@@ -187,32 +187,42 @@ static __global__ void __launch_bounds__(128) gdn_scan_kernel(const __grid_const
     g = p.alpha_raw[static_cast<size_t>(t) * p.ld_ba + h];
     b = p.beta_raw[static_cast<size_t>(t) * p.ld_ba + h];
   };
-  float4 nq = make_float4(0.f, 0.f, 0.f, 0.f), nk = nq;
-  float nv[kGdnScanRows], ng = 0.f, nb = 0.f;
-  if (p.T > 0) load_tok(0, nq, nk, nv, ng, nb);
-  for (int t = 0; t < p.T; ++t) {
-    const float4 q4 = nq, k4 = nk;
-    float v[kGdnScanRows];
+  // inputs of the next kPf tokens stay in flight (a global round trip is
+  // several times one token's arithmetic)
+  constexpr int kPf = 4;
+  float4 bq[kPf], bk[kPf];
+  float bv[kPf][kGdnScanRows], bg[kPf], bb[kPf];
 #pragma unroll
-    for (int r = 0; r < kGdnScanRows; ++r) v[r] = nv[r];
-    const float ge = expf(ng), beta = nb;
-    if (t + 1 < p.T) load_tok(t + 1, nq, nk, nv, ng, nb);
+  for (int u = 0; u < kPf; ++u)
+    if (u < p.T) load_tok(u, bq[u], bk[u], bv[u], bg[u], bb[u]);
+  for (int t0 = 0; t0 < p.T; t0 += kPf) {
 #pragma unroll
-    for (int r = 0; r < kGdnScanRows; ++r) {
-      float4 st = s[r];
-      st.x *= ge;
-      st.y *= ge;
-      st.z *= ge;
-      st.w *= ge;
-      const float sk = warp_sum(st.x * k4.x + st.y * k4.y + st.z * k4.z + st.w * k4.w);
-      const float delta = (v[r] - sk) * beta;
-      st.x += k4.x * delta;
-      st.y += k4.y * delta;
-      st.z += k4.z * delta;
-      st.w += k4.w * delta;
-      const float y = warp_sum(st.x * q4.x + st.y * q4.y + st.z * q4.z + st.w * q4.w);
-      if (lane == 0) p.out[static_cast<size_t>(t) * p.value_heads * D + h * D + r0 + r] = y * scale;
-      s[r] = st;
+    for (int u = 0; u < kPf; ++u) {
+      const int t = t0 + u;
+      if (t >= p.T) break;
+      const float4 q4 = bq[u], k4 = bk[u];
+      float v[kGdnScanRows];
+#pragma unroll
+      for (int r = 0; r < kGdnScanRows; ++r) v[r] = bv[u][r];
+      const float ge = expf(bg[u]), beta = bb[u];
+      if (t + kPf < p.T) load_tok(t + kPf, bq[u], bk[u], bv[u], bg[u], bb[u]);
+#pragma unroll
+      for (int r = 0; r < kGdnScanRows; ++r) {
+        float4 st = s[r];
+        st.x *= ge;
+        st.y *= ge;
+        st.z *= ge;
+        st.w *= ge;
+        const float sk = warp_sum(st.x * k4.x + st.y * k4.y + st.z * k4.z + st.w * k4.w);
+        const float delta = (v[r] - sk) * beta;
+        st.x += k4.x * delta;
+        st.y += k4.y * delta;
+        st.z += k4.z * delta;
+        st.w += k4.w * delta;
+        const float y = warp_sum(st.x * q4.x + st.y * q4.y + st.z * q4.z + st.w * q4.w);
+        if (lane == 0) p.out[static_cast<size_t>(t) * p.value_heads * D + h * D + r0 + r] = y * scale;
+        s[r] = st;
+      }
     }
   }
 #pragma unroll
