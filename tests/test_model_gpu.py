@@ -29,9 +29,9 @@ def prompt(n, vocab, seed=0):
     return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int32)
 
 
-@pytest.mark.parametrize("plen,chunk", [(5, 1024), (40, 16), (70, 1024)])
+@pytest.mark.parametrize("plen,chunk", [(5, 1024), (40, 16), (70, 1024), (300, 160)])
 def test_prefill_logits_match_oracle(ctx, oracle, small_model, plen, chunk):
-    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=64, prefill_chunk=1024)
+    m = kib.Qwen35(ctx, small_model, context_tokens=max(256, plen + 16), decode_tokens=64, prefill_chunk=1024)
     om = oracle_lib.OracleModel(oracle, small_model, m.plan.attention_capacity_tokens)
     p = prompt(plen, SMALL["vocab"], plen)
     nxt = m.prefill(p, chunk)
