@@ -283,10 +283,12 @@ def prefill_bench(ctx, path):
     m.reset()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()  # ncu --profile-from-start off captures the timed prefill only
     e0.record(stream)
     nxt = m.prefill(prompt, 1024)
     e1.record(stream)
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     ms = e0.elapsed_time(e1)
     m.close()
     tflops = PREFILL_FLOP / (ms * 1e-3) / 1e12
@@ -362,7 +364,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--no-mtp", action="store_true", help="skip the config-3 MTP verify measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
-    ap.add_argument("--workload", default="decode", choices=["decode", "matvec"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "prefill"],
                     help="matvec: BASELINE config 1 only (Q4_K 3584x1024 GEMV roofline)")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: fewer layers than the BASELINE model (the JSON line says so)")
@@ -386,6 +388,18 @@ def main():
         r["peak_kind"] = kind
         print(json.dumps({"metric": f"K-quant type {args.mv_type} {args.mv_rows}x{args.mv_cols} matvec GB/s", "value": r["achieved"], "unit": "GB/s",
                           "roofline": r}), flush=True)
+        ctx.close()
+        return
+    if args.workload == "prefill":
+        import torch
+        import kib
+        torch.cuda.set_device(local)
+        path = model_path(rank, world)
+        ensure_model(path, rank, world)
+        ctx = kib.Context(local)
+        r = prefill_bench(ctx, path)
+        print(json.dumps({"metric": "Qwen3.5-0.8B-shape 8192-token chunked prefill tok/s", "value": r["tok_per_s"],
+                          "unit": "tok/s", "prefill_config4": r}), flush=True)
         ctx.close()
         return
     if args.impl == "reference":
