@@ -877,14 +877,46 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
   const int grid = static_cast<int>(gridDim.x);
   const int cta = static_cast<int>(blockIdx.x);
   PkArgmax am;  // LM head: this thread's rows
+  // quad mode: a stage whose single tile per CTA holds 33..64 rows of 1024
+  // columns runs as one pass of four rows per lane (the LM head's dot code)
+  // instead of two passes of two
+  const int nr0 = min(tile_rows, rows - cta * tile_rows);
+  const bool quad = S.kind == kPkGemv && rg_log2 == 4 && !paired && ntiles <= grid && nr0 > groups * R &&
+                    nr0 <= 4 * groups;
+  const bool q_owner = (gl & 3) == 0;
+  const int q_off = ((gl & 15) >> 2) * groups + group;
   // the first pass's epilogue inputs go out before the prologue's wait
   PkEpi e;
-  if (owner && my_off < min(tile_rows, rows - cta * tile_rows)) pk_epi_issue(S, cs.sh, cta * tile_rows + my_off, e);
+  if (quad) {
+    if (q_owner && q_off < nr0) pk_epi_issue(S, cs.sh, cta * tile_rows + q_off, e);
+  } else if (owner && my_off < nr0) {
+    pk_epi_issue(S, cs.sh, cta * tile_rows + my_off, e);
+  }
   const float scale = pk_prologue(S, cs);
   pk_mark(cs.tr, 1);
   if (cs.aborted()) return false;
   PkX ux;  // unscaled: the RMS scale multiplies each row's result instead
   if (active) pk_load_x(type, cs.sh->xs, blk, u, ux);
+  if (quad) {
+    const uint8_t* tile = cs.take();
+    if (!tile) return false;
+    pk_mark(cs.tr, 2);
+    const uint8_t* b[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) b[k] = tile + static_cast<size_t>(min(k * groups + group, nr0 - 1)) * row_bytes + blk_off;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (active) pk_dot_rows<4>(type, b, u, ux, acc);
+    // lanes 0-3 / 4-7 / 8-11 / 12-15 of the group end with rows 0..3
+    const bool h1 = gl & 8, h2 = gl & 4;
+    const float a0 = (h1 ? acc[2] : acc[0]) + __shfl_xor_sync(0xffffffffu, h1 ? acc[0] : acc[2], 8);
+    const float a1 = (h1 ? acc[3] : acc[1]) + __shfl_xor_sync(0xffffffffu, h1 ? acc[1] : acc[3], 8);
+    float v = (h2 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h2 ? a0 : a1, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    if (q_owner && q_off < nr0) pk_epi_run(S, cs, e, v * scale, 0.0f, am);
+    cs.release_warp();
+    return true;
+  }
   if (S.kind == kPkHead && rg_log2 == 4 && tile_rows == groups * R) {
     // LM head: two tiles per pass (a lane dots rows of both), so each pass has
     // twice the independent work between its waits
