@@ -897,6 +897,11 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
   if (cs.aborted()) return false;
   PkX ux;  // unscaled: the RMS scale multiplies each row's result instead
   if (active) pk_load_x(type, cs.sh->xs, blk, u, ux);
+  if (cs.tr) {
+    unsigned long long tt;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tt) : "f"(ux.v[31].y), "f"(ux.s[3]));
+    cs.tr[9] = tt;
+  }
   if (quad) {
     const uint8_t* tile = cs.take();
     if (!tile) return false;
