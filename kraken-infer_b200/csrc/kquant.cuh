@@ -344,8 +344,11 @@ KIB_DEV void unit_dequant(const uint8_t* blk, int u, float (&out)[64]) {
 // Per-weight fp16 value used by the reference's multi-token buckets
 // (dequantize_q{4,5,6}_k_mm, mps_backend.mm:780-864): the fp32 value
 // dl*q - ml rounded to half.  Q6_K rounds dl0*q' and then subtracts 32*dl0.
+// Returned as 32 half2 pairs (element order as unit_col): codes become floats
+// by exponent insertion (2^23 + b, exact), each pair is rounded with one packed
+// conversion.
 template <int QT>
-KIB_DEV void unit_dequant_f16(const uint8_t* blk, int u, float (&out)[64]) {
+KIB_DEV void unit_dequant_h2(const uint8_t* blk, int u, __half2 (&out)[32]) {
   uint32_t q[16];
   unit_codes<QT>(blk, u, q);
   float A[4], B[4];
@@ -353,18 +356,19 @@ KIB_DEV void unit_dequant_f16(const uint8_t* blk, int u, float (&out)[64]) {
   constexpr int WPG = 16 / KQ<QT>::kGroups;
 #pragma unroll
   for (int w = 0; w < 16; ++w) {
+    const int g = w / WPG;
+    float v[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float code = static_cast<float>((q[w] >> (8 * k)) & 0xFFu);
-      const int g = w / WPG;
-      float v;
+      const float code = __uint_as_float(0x4B000000u | ((q[w] >> (8 * k)) & 0xFFu)) - 8388608.0f;
       if (QT == kTypeQ6K) {
-        v = __fsub_rn(__fmul_rn(A[g], code), __fmul_rn(A[g], 32.0f));
+        v[k] = __fsub_rn(__fmul_rn(A[g], code), __fmul_rn(A[g], 32.0f));
       } else {
-        v = fmaf(A[g], code, B[g]);
+        v[k] = fmaf(A[g], code, B[g]);
       }
-      out[4 * w + k] = round_to_half(v);
     }
+    out[2 * w] = __floats2half2_rn(v[0], v[1]);
+    out[2 * w + 1] = __floats2half2_rn(v[2], v[3]);
   }
 }
 

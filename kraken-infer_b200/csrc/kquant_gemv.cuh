@@ -247,41 +247,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) kquant_gemv_kernel(const __gr
       if (row_ok && active) {
         const uint8_t* b0 = tile + static_cast<size_t>(rl) * p.row_bytes + blk * BB;
         if constexpr (F16W) {
-          float wv[64];
-          unit_dequant_f16<QT>(b0, unit, wv);
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            if (t >= p.ntok) break;  // xs holds ntok rows only
-            const float* xb = xs + t * p.cols + 256 * blk;
-            // x in runs of four contiguous columns (unit_col is contiguous
-            // within every aligned group of four elements): one LDS.128 each
-            float s = 0.0f;
-#pragma unroll
-            for (int e = 0; e < 64; e += 4) {
-              const float4 x4 = *reinterpret_cast<const float4*>(xb + unit_col<QT>(unit, e));
-              s = fmaf(wv[e], x4.x, s);
-              s = fmaf(wv[e + 1], x4.y, s);
-              s = fmaf(wv[e + 2], x4.z, s);
-              s = fmaf(wv[e + 3], x4.w, s);
-            }
-            acc[t] = s;
-          }
-          if (paired) {
-            unit_dequant_f16<QT>(b0 + p.stage_bytes / 2, unit, wv);
+          // weights rounded to half (two per register), x read as float4 runs
+          // of unit_col, products accumulated in two fp32 lanes (FFMA2)
+          __half2 wh[32];
+#pragma unroll 1
+          for (int hh = 0; hh <= static_cast<int>(paired); ++hh) {
+            unit_dequant_h2<QT>(b0 + hh * (p.stage_bytes / 2), unit, wh);
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
               if (t >= p.ntok) break;  // xs holds ntok rows only
-            const float* xb = xs + t * p.cols + 256 * blk;
-              float s = 0.0f;
+              const float* xb = xs + t * p.cols + 256 * blk;
+              float2 s2 = make_float2(0.0f, 0.0f);
 #pragma unroll
               for (int e = 0; e < 64; e += 4) {
                 const float4 x4 = *reinterpret_cast<const float4*>(xb + unit_col<QT>(unit, e));
-                s = fmaf(wv[e], x4.x, s);
-                s = fmaf(wv[e + 1], x4.y, s);
-                s = fmaf(wv[e + 2], x4.z, s);
-                s = fmaf(wv[e + 3], x4.w, s);
+                s2 = ffma2(__half22float2(wh[e / 2]), make_float2(x4.x, x4.y), s2);
+                s2 = ffma2(__half22float2(wh[e / 2 + 1]), make_float2(x4.z, x4.w), s2);
               }
-              acc2[t] = s;
+              if (hh == 0) acc[t] = s2.x + s2.y;
+              else acc2[t] = s2.x + s2.y;
             }
           }
         } else {

@@ -800,7 +800,7 @@ struct GemmParams {
 // numerics (mul_mm_simd: weights and x rounded to fp16, fp32 accumulation).
 // CTA tile 128 weight rows x 128 tokens, one 256-column super-block per
 // k-step: the 256 threads dequantize the tile's weights into shared memory as
-// fp16 (each weight value exactly as unit_dequant_f16 rounds it) and round the
+// fp16 (each weight value exactly as unit_dequant_h2 rounds it) and round the
 // x tile to fp16; 8 warps (4 along rows x 2 along tokens) each own a 32 x 64
 // output tile of mma.sync m16n8k16 f16 x f16 -> f32, fragments by ldmatrix.
 // Shared rows are padded to 264 halves so the ldmatrix rows spread over banks.
@@ -846,18 +846,18 @@ __global__ void __launch_bounds__(256, 1) kquant_gemm_f16_kernel(const __grid_co
     for (int job = tid; job < kGemmTileM * 4; job += 256) {
       const int rl = job >> 2, unit = job & 3;
       const int row = r0 + rl;
-      float v[64];
+      __half2 v[32];
       if (row < p.rows) {
-        unit_dequant_f16<QT>(p.w + (static_cast<size_t>(row) * bpr + kb) * kquant_block_bytes(QT), unit, v);
+        unit_dequant_h2<QT>(p.w + (static_cast<size_t>(row) * bpr + kb) * kquant_block_bytes(QT), unit, v);
       } else {
 #pragma unroll
-        for (int e = 0; e < 64; ++e) v[e] = 0.0f;
+        for (int e = 0; e < 32; ++e) v[e] = __floats2half2_rn(0.0f, 0.0f);
       }
       __half* dst = As + rl * kGemmLd;
 #pragma unroll
       for (int e = 0; e < 64; e += 2) {
         // unit_col is contiguous within aligned pairs
-        *reinterpret_cast<__half2*>(dst + unit_col<QT>(unit, e)) = __floats2half2_rn(v[e], v[e + 1]);
+        *reinterpret_cast<__half2*>(dst + unit_col<QT>(unit, e)) = v[e / 2];
       }
     }
     // x: 128 tokens x 256 k, rounded to half

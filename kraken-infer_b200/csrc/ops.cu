@@ -308,6 +308,7 @@ static cudaError_t gemv_dispatch(const GemvParams& p, int grid, size_t smem, cud
     case 1: return gemv_instance<QT, 1, false>(p, grid, smem, st);
     case 2: return gemv_instance<QT, 2, false>(p, grid, smem, st);
     case 3: return gemv_instance<QT, 3, false>(p, grid, smem, st);
+    case 4: return gemv_instance<QT, 4, true>(p, grid, smem, st);  // reductions and epilogues sized to 4
     default: return gemv_instance<QT, 8, true>(p, grid, smem, st);
   }
 }
