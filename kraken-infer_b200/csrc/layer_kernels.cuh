@@ -798,13 +798,15 @@ struct GemmParams {
 
 // Multi-token (T > 8) K-quant GEMM on the tensor cores: the reference's M > 8
 // numerics (mul_mm_simd: weights and x rounded to fp16, fp32 accumulation).
-// CTA tile 128 weight rows x 128 tokens, one 256-column super-block per
+// CTA tile 128 weight rows x 64 tokens (two CTAs per SM, so one CTA's
+// dequantization overlaps the other's MMAs), one 256-column super-block per
 // k-step: the 256 threads dequantize the tile's weights into shared memory as
 // fp16 (each weight value exactly as unit_dequant_h2 rounds it) and round the
-// x tile to fp16; 8 warps (4 along rows x 2 along tokens) each own a 32 x 64
+// x tile to fp16; 8 warps (4 along rows x 2 along tokens) each own a 32 x 32
 // output tile of mma.sync m16n8k16 f16 x f16 -> f32, fragments by ldmatrix.
 // Shared rows are padded to 264 halves so the ldmatrix rows spread over banks.
-constexpr int kGemmTileM = 128, kGemmTileN = 128, kGemmLd = 256 + 8;
+constexpr int kGemmTileM = 128, kGemmTileN = 64, kGemmLd = 256 + 8;
+constexpr int kGemmWarpN = kGemmTileN / 2, kGemmNT = kGemmWarpN / 8;  // warp tile: 32 rows x kGemmWarpN tokens
 constexpr size_t kGemmSmem = static_cast<size_t>(kGemmTileM + kGemmTileN) * kGemmLd * 2;
 
 KIB_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -822,19 +824,19 @@ KIB_DEV void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, u
 }
 
 template <int QT>
-__global__ void __launch_bounds__(256, 1) kquant_gemm_f16_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(256, 2) kquant_gemm_f16_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(16) uint8_t gsm_raw[];
   __half* As = reinterpret_cast<__half*>(gsm_raw);        // [128 rows][kGemmLd]
   __half* Bs = As + kGemmTileM * kGemmLd;                 // [128 tokens][kGemmLd]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r0 = blockIdx.x * kGemmTileM, t0 = blockIdx.y * kGemmTileN;
   const int bpr = p.cols / 256;
-  const int wm = (warp & 3) * 32, wn = (warp >> 2) * 64;  // warp tile origin
-  float acc[2][8][4];
+  const int wm = (warp & 3) * 32, wn = (warp >> 2) * kGemmWarpN;  // warp tile origin
+  float acc[2][kGemmNT][4];
 #pragma unroll
   for (int i = 0; i < 2; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < kGemmNT; ++j)
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.0f;
   pdl_wait();
@@ -881,7 +883,7 @@ __global__ void __launch_bounds__(256, 1) kquant_gemm_f16_kernel(const __grid_co
         ldsm_x4(as_base + static_cast<uint32_t>(row * kGemmLd + col) * 2, a[i][0], a[i][1], a[i][2], a[i][3]);
       }
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
+      for (int j = 0; j < kGemmNT; j += 2) {
         const int n = wn + 8 * j + (lane & 7) + ((lane >> 4) << 3), col = k0 + ((lane >> 3) & 1) * 8;
         uint32_t b0, b1, b2, b3;
         ldsm_x4(bs_base + static_cast<uint32_t>(n * kGemmLd + col) * 2, b0, b1, b2, b3);
@@ -899,7 +901,7 @@ __global__ void __launch_bounds__(256, 1) kquant_gemm_f16_kernel(const __grid_co
 #pragma unroll
   for (int i = 0; i < 2; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < kGemmNT; ++j)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int row = r0 + wm + 16 * i + g + (c >> 1) * 8;
