@@ -660,15 +660,16 @@ static __global__ void __launch_bounds__(256) attn_prefill_kernel(const __grid_c
   const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
   float m = -INFINITY, l = 0.0f;
   // blocks of 8 keys: the 8 partial dot products share one butterfly, and the
-  // block's K and V rows are loaded together
+  // block's K and V rows are loaded together, through L1 (the CTA's eight
+  // warps are eight consecutive queries of one head and read the same rows)
   const size_t kbase = static_cast<size_t>(kvh) * kHd + 8 * lane;
   for (int k0 = 0; k0 <= qpos; k0 += 8) {
     uint4 kr[8], vr[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int key = min(k0 + e, qpos);
-      kr[e] = __ldcg(reinterpret_cast<const uint4*>(p.kcache + static_cast<size_t>(key) * kvd + kbase));
-      vr[e] = __ldcg(reinterpret_cast<const uint4*>(p.vcache + static_cast<size_t>(key) * kvd + kbase));
+      kr[e] = __ldg(reinterpret_cast<const uint4*>(p.kcache + static_cast<size_t>(key) * kvd + kbase));
+      vr[e] = __ldg(reinterpret_cast<const uint4*>(p.vcache + static_cast<size_t>(key) * kvd + kbase));
     }
     float sc[8];
 #pragma unroll
