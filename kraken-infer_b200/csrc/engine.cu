@@ -436,12 +436,19 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
   g.value_heads = m->lvh;
   g.eps = m->eps;
   g.trace = nullptr;
-  if (m->lhd == 128 && m->lkh <= m->lvh) {
+  if (m->lhd == 128 && m->lkh <= m->lvh && m->C % 4 == 0) {
     // token-parallel norms and gate/beta first, then the sequential scan alone
     q.run(launch_pdl(gdn_prep_kernel, dim3(T, m->lkh), dim3(128), 0, q.st, m->d_qkv, m->C, m->d_alpha, m->d_beta, m->lvh,
                      L.dt_bias.f(), L.ssm_a.f(), m->lkh, m->lvh, m->eps),
           "gdn_prep");
-    q.run(launch_pdl(gdn_scan_kernel, dim3(m->lvh, m->lhd / (4 * kGdnScanRows)), dim3(128), 0, q.st, g), "gdn_scan");
+    static bool scan_cfg = false;
+    if (!scan_cfg) {
+      q.run(cudaFuncSetAttribute(gdn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGdnScanSmem),
+            "gdn_scan_attr");
+      scan_cfg = true;
+    }
+    q.run(launch_pdl(gdn_scan_kernel, dim3(m->lvh, m->lhd / kGdnScanRowsPerCta), dim3(128), kGdnScanSmem, q.st, g),
+          "gdn_scan");
   } else {
     q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
   }

@@ -129,10 +129,20 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
 // the L2 norms of each token's q and k head rows (in place in the conv output,
 // same reduction order as gdn_core_kernel) and g = softplus(alpha + dt_bias) *
 // ssm_a, beta = sigmoid(beta) (in place).  gdn_scan_kernel then runs only the
-// sequential delta rule: a warp owns kGdnScanRows state rows, lane l columns
-// 4l..4l+3, the inputs of the next tokens are loaded while the current one is
-// processed, and no CTA barrier sits in the per-token chain.
-constexpr int kGdnScanRows = 1;
+// sequential delta rule (the recurrence of ggml_gated_delta_net, one value row
+// of the state at a time; rows are independent of each other):
+//   S_v *= exp(g);  delta = (v_v - S_v . k) * beta;  S_v += delta * k;
+//   y_v = (S_v . q) / sqrt(128)
+// Eight lanes own one value row (sixteen key columns each, as four float4 at
+// columns 32j + 4c, so eight lanes read 128 contiguous bytes of k or q), so
+// each dot product ends in three shuffles.  A CTA owns sixteen rows of one
+// head; the q, k, v, g and beta of kGdnScanChunk tokens are staged in shared
+// memory by cp.async one chunk ahead, so the per-token chain never waits on
+// global memory, and the only CTA barrier sits between chunks.
+constexpr int kGdnScanRowsPerCta = 16;
+constexpr int kGdnScanChunk = 32;
+constexpr int kGdnScanStage = kGdnScanChunk * (2 * 128 + kGdnScanRowsPerCta + 2);  // floats per buffer
+constexpr int kGdnScanSmem = 2 * kGdnScanStage * 4;
 
 static __global__ void __launch_bounds__(128) gdn_prep_kernel(float* conv_out, int C, float* alpha, float* beta,
                                                                int ld_ba, const float* dt_bias, const float* ssm_a,
@@ -164,69 +174,110 @@ static __global__ void __launch_bounds__(128) gdn_prep_kernel(float* conv_out, i
   }
 }
 
+__device__ __forceinline__ void gs_cp16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void gs_cp4(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+
+// Requires C % 4 == 0 and 16-byte aligned conv_out (every row's q/k/v runs are
+// copied as 16-byte pieces).
 static __global__ void __launch_bounds__(128) gdn_scan_kernel(const __grid_constant__ GdnParams p) {
-  constexpr int D = 128;
+  constexpr int D = 128, TC = kGdnScanChunk, RC = kGdnScanRowsPerCta;
+  extern __shared__ __align__(16) float gs_smem[];
   const int h = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int r0 = (blockIdx.y * 4 + warp) * kGdnScanRows;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = lane & 7;
+  const int row_base = blockIdx.y * RC;
+  const int row = row_base + warp * 4 + (lane >> 3);
   const int kh = h % p.key_heads;
   const int key_dim = p.key_heads * D;
-  float* S = p.state + static_cast<size_t>(h) * D * D;
-  float4 s[kGdnScanRows];
+  float* S = p.state + (static_cast<size_t>(h) * D + row) * D;
+  float4 s[4];
 #pragma unroll
-  for (int r = 0; r < kGdnScanRows; ++r) s[r] = *reinterpret_cast<const float4*>(S + static_cast<size_t>(r0 + r) * D + 4 * lane);
+  for (int j = 0; j < 4; ++j) s[j] = *reinterpret_cast<const float4*>(S + 32 * j + 4 * c);
   pdl_wait();
   pdl_launch_dependents();
-  const float scale = 1.0f / sqrtf(static_cast<float>(D));
-  auto load_tok = [&](int t, float4& q4, float4& k4, float (&vv)[kGdnScanRows], float& g, float& b) {
-    const float* row = p.conv_out + static_cast<size_t>(t) * p.C;
-    q4 = *reinterpret_cast<const float4*>(row + kh * D + 4 * lane);
-    k4 = *reinterpret_cast<const float4*>(row + key_dim + kh * D + 4 * lane);
-#pragma unroll
-    for (int r = 0; r < kGdnScanRows; ++r) vv[r] = row[2 * key_dim + h * D + r0 + r];
-    g = p.alpha_raw[static_cast<size_t>(t) * p.ld_ba + h];
-    b = p.beta_raw[static_cast<size_t>(t) * p.ld_ba + h];
+
+  // buffer layout: q[TC][128] | k[TC][128] | v[TC][RC] | g[TC] | beta[TC]
+  auto load_chunk = [&](int t0, float* buf) {
+    const int n = min(TC, p.T - t0);
+    for (int i = tid; i < n * 64; i += 128) {
+      const int u = i >> 6, w = i & 63;  // w < 32: q piece, else k piece
+      const float* src = p.conv_out + static_cast<size_t>(t0 + u) * p.C + (w < 32 ? kh * D + 4 * w
+                                                                                  : key_dim + kh * D + 4 * (w - 32));
+      gs_cp16(buf + (w < 32 ? 0 : TC * D) + u * D + 4 * (w & 31), src);
+    }
+    for (int i = tid; i < n * (RC / 4); i += 128) {
+      const int u = i / (RC / 4), w = i % (RC / 4);
+      gs_cp16(buf + 2 * TC * D + u * RC + 4 * w,
+              p.conv_out + static_cast<size_t>(t0 + u) * p.C + 2 * key_dim + h * D + row_base + 4 * w);
+    }
+    for (int i = tid; i < 2 * n; i += 128) {
+      const int u = i >> 1;
+      if (i & 1) gs_cp4(buf + 2 * TC * D + TC * RC + TC + u, p.beta_raw + static_cast<size_t>(t0 + u) * p.ld_ba + h);
+      else gs_cp4(buf + 2 * TC * D + TC * RC + u, p.alpha_raw + static_cast<size_t>(t0 + u) * p.ld_ba + h);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  // inputs of the next kPf tokens stay in flight (a global round trip is
-  // several times one token's arithmetic)
-  constexpr int kPf = 4;
-  float4 bq[kPf], bk[kPf];
-  float bv[kPf][kGdnScanRows], bg[kPf], bb[kPf];
+
+  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  float* out = p.out + static_cast<size_t>(h) * D + row;
+  const size_t out_ld = static_cast<size_t>(p.value_heads) * D;
+  const int nchunks = (p.T + TC - 1) / TC;
+  load_chunk(0, gs_smem);
+  for (int ci = 0; ci < nchunks; ++ci) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();  // chunk ci landed for all threads; chunk ci-1's buffer is free
+    float* buf = gs_smem + (ci & 1) * kGdnScanStage;
+    if (ci + 1 < nchunks) load_chunk((ci + 1) * TC, gs_smem + ((ci + 1) & 1) * kGdnScanStage);
+    const float* qb = buf;
+    const float* kb = buf + TC * D;
+    const float* vb = buf + 2 * TC * D + (row - row_base);
+    const float* gb = buf + 2 * TC * D + TC * RC;
+    const int n = min(TC, p.T - ci * TC);
+#pragma unroll 2
+    for (int u = 0; u < n; ++u) {
+      float4 k4[4], q4[4];
 #pragma unroll
-  for (int u = 0; u < kPf; ++u)
-    if (u < p.T) load_tok(u, bq[u], bk[u], bv[u], bg[u], bb[u]);
-  for (int t0 = 0; t0 < p.T; t0 += kPf) {
-#pragma unroll
-    for (int u = 0; u < kPf; ++u) {
-      const int t = t0 + u;
-      if (t >= p.T) break;
-      const float4 q4 = bq[u], k4 = bk[u];
-      float v[kGdnScanRows];
-#pragma unroll
-      for (int r = 0; r < kGdnScanRows; ++r) v[r] = bv[u][r];
-      const float ge = expf(bg[u]), beta = bb[u];
-      if (t + kPf < p.T) load_tok(t + kPf, bq[u], bk[u], bv[u], bg[u], bb[u]);
-#pragma unroll
-      for (int r = 0; r < kGdnScanRows; ++r) {
-        float4 st = s[r];
-        st.x *= ge;
-        st.y *= ge;
-        st.z *= ge;
-        st.w *= ge;
-        const float sk = warp_sum(st.x * k4.x + st.y * k4.y + st.z * k4.z + st.w * k4.w);
-        const float delta = (v[r] - sk) * beta;
-        st.x += k4.x * delta;
-        st.y += k4.y * delta;
-        st.z += k4.z * delta;
-        st.w += k4.w * delta;
-        const float y = warp_sum(st.x * q4.x + st.y * q4.y + st.z * q4.z + st.w * q4.w);
-        if (lane == 0) p.out[static_cast<size_t>(t) * p.value_heads * D + h * D + r0 + r] = y * scale;
-        s[r] = st;
+      for (int j = 0; j < 4; ++j) {
+        k4[j] = *reinterpret_cast<const float4*>(kb + u * D + 32 * j + 4 * c);
+        q4[j] = *reinterpret_cast<const float4*>(qb + u * D + 32 * j + 4 * c);
       }
+      const float ge = expf(gb[u]), beta = gb[TC + u], v = vb[u * RC];
+      float pk[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[j].x *= ge;
+        s[j].y *= ge;
+        s[j].z *= ge;
+        s[j].w *= ge;
+        pk[j] = s[j].x * k4[j].x + s[j].y * k4[j].y + s[j].z * k4[j].z + s[j].w * k4[j].w;
+      }
+      float sk = (pk[0] + pk[1]) + (pk[2] + pk[3]);
+      sk += __shfl_xor_sync(0xffffffffu, sk, 1);
+      sk += __shfl_xor_sync(0xffffffffu, sk, 2);
+      sk += __shfl_xor_sync(0xffffffffu, sk, 4);
+      const float delta = (v - sk) * beta;
+      float pq[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[j].x += k4[j].x * delta;
+        s[j].y += k4[j].y * delta;
+        s[j].z += k4[j].z * delta;
+        s[j].w += k4[j].w * delta;
+        pq[j] = s[j].x * q4[j].x + s[j].y * q4[j].y + s[j].z * q4[j].z + s[j].w * q4[j].w;
+      }
+      float y = (pq[0] + pq[1]) + (pq[2] + pq[3]);
+      y += __shfl_xor_sync(0xffffffffu, y, 1);
+      y += __shfl_xor_sync(0xffffffffu, y, 2);
+      y += __shfl_xor_sync(0xffffffffu, y, 4);
+      if (c == 0) out[static_cast<size_t>(ci * TC + u) * out_ld] = y * scale;
     }
   }
 #pragma unroll
-  for (int r = 0; r < kGdnScanRows; ++r) *reinterpret_cast<float4*>(S + static_cast<size_t>(r0 + r) * D + 4 * lane) = s[r];
+  for (int j = 0; j < 4; ++j) *reinterpret_cast<float4*>(S + 32 * j + 4 * c) = s[j];
 }
 
 // =============================================================== attention
