@@ -465,7 +465,19 @@ void attention_block_prefill(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc
   gemm(q, L.v, m->d_norm, m->H, T, m->d_vp, m->KD);
   const AttnParams a = attn_params(m, L, kc, vc, pos, T);
   q.run(launch_pdl(attn_prep_kernel, dim3(T), dim3(256), 8 * kHd * sizeof(float), q.st, a), "attn_prep");
-  q.run(launch_pdl(attn_prefill_kernel, dim3((T + 7) / 8, m->heads), dim3(256), 0, q.st, a), "attn_prefill");
+  if (a.round_q && m->heads % m->kvh == 0) {
+    static bool fa_cfg = false;
+    if (!fa_cfg) {
+      q.run(cudaFuncSetAttribute(attn_prefill_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kFaSmem)),
+            "attn_prefill_mma_attr");
+      fa_cfg = true;
+    }
+    q.run(launch_pdl(attn_prefill_mma_kernel, dim3((T + kFaQ - 1) / kFaQ, m->heads), dim3(128), kFaSmem, q.st, a),
+          "attn_prefill_mma");
+  } else {
+    q.run(launch_pdl(attn_prefill_kernel, dim3((T + 7) / 8, m->heads), dim3(256), 0, q.st, a), "attn_prefill");
+  }
   gemm(q, L.o, m->d_att, m->AD, T, x_mid, m->H, x_in);
 }
 

@@ -966,4 +966,184 @@ __global__ void __launch_bounds__(256, 2) kquant_gemm_f16_kernel(const __grid_co
       }
 }
 
+// ======================================================= prefill attention (tensor cores)
+// Prefill step 2 for T >= 64 (flash256 numerics, attention_f32_batched_flash256_f16_kv,
+// mps_backend.mm:3398-3640): Q rounded to half, K and V f16 from the cache,
+// scores and the online softmax in fp32 (running max and normaliser per block
+// of keys, masked keys get weight 0), weights kept in fp32 against f16 V, the
+// output divided by the normaliser and multiplied by sigmoid(gate).
+// On the tensor cores (mma.sync m16n8k16 f16 x f16 -> f32): S = Q K^T is exact
+// per product; P V runs as P_hi V + P_lo V with P_hi = half(P), P_lo =
+// half(P - P_hi), so the weights keep ~22 bits against V as in fp32.
+// A CTA owns 64 queries of one head (4 warps x 16 rows, the output rows in
+// registers); K and V tiles of 32 keys are double-buffered by cp.async.
+// Shared rows are padded to 264 halves so the ldmatrix rows spread over banks.
+constexpr int kFaQ = 64, kFaK = 32, kFaLd = 264;
+constexpr size_t kFaSmem = static_cast<size_t>(kFaQ + 4 * kFaK) * kFaLd * 2;
+
+KIB_DEV void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+KIB_DEV uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+static __global__ void __launch_bounds__(128, 2) attn_prefill_mma_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ __align__(16) uint16_t fa_sm[];
+  uint16_t* qs = fa_sm;                   // [64][264]
+  uint16_t* ks = fa_sm + kFaQ * kFaLd;    // [2][32][264]
+  uint16_t* vs = ks + 2 * kFaK * kFaLd;   // [2][32][264]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int head = blockIdx.y, q0 = blockIdx.x * kFaQ;
+  const int kvh = head / (p.heads / p.kv_heads);
+  const int kvd = p.kv_heads * kHd;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pos0 = *p.pos;
+  const int last_q = min(q0 + kFaQ, p.T) - 1;
+  const int nkeys = pos0 + last_q + 1;
+  const int nblocks = (nkeys + kFaK - 1) / kFaK;
+  const uint16_t* kg = p.kcache + static_cast<size_t>(kvh) * kHd;
+  const uint16_t* vg = p.vcache + static_cast<size_t>(kvh) * kHd;
+  auto load_kv = [&](int b, int stage) {
+    uint16_t* kd = ks + stage * kFaK * kFaLd;
+    uint16_t* vd = vs + stage * kFaK * kFaLd;
+#pragma unroll
+    for (int it = 0; it < kFaK * 32 / 128; ++it) {
+      const int i = tid + 128 * it, r = i >> 5, piece = i & 31;
+      const size_t key = static_cast<size_t>(min(b * kFaK + r, nkeys - 1));
+      gs_cp16(kd + r * kFaLd + 8 * piece, kg + key * kvd + 8 * piece);
+      gs_cp16(vd + r * kFaLd + 8 * piece, vg + key * kvd + 8 * piece);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  load_kv(0, 0);
+  // Q rows, rounded to half (rows past T are zero and never written out)
+  for (int i = tid; i < kFaQ * (kHd / 4); i += 128) {
+    const int r = i / (kHd / 4), c4 = i % (kHd / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + r < p.T)
+      v = *reinterpret_cast<const float4*>(p.q_out + (static_cast<size_t>(q0 + r) * p.heads + head) * kHd + 4 * c4);
+    __half2* d = reinterpret_cast<__half2*>(qs + r * kFaLd + 4 * c4);
+    d[0] = __floats2half2_rn(v.x, v.y);
+    d[1] = __floats2half2_rn(v.z, v.w);
+  }
+  const int g = lane >> 2, c = lane & 3;
+  const int qpos0 = pos0 + q0 + 16 * warp + g, qpos1 = qpos0 + 8;
+  const int warp_last = pos0 + q0 + 16 * warp + 15;  // last key any row of this warp sees
+  const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
+  const uint32_t qs_base = smem_u32(qs), ks_base = smem_u32(ks), vs_base = smem_u32(vs);
+  float o[kHd / 8][4];
+#pragma unroll
+  for (int n = 0; n < kHd / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // l: this lane's share
+  for (int b = 0; b < nblocks; ++b) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();  // block b landed (and Q, at b == 0); the other stage is free
+    if (b + 1 < nblocks) load_kv(b + 1, (b + 1) & 1);
+    if (b * kFaK > warp_last) continue;
+    const uint32_t kst = ks_base + static_cast<uint32_t>((b & 1) * kFaK * kFaLd) * 2;
+    const uint32_t vst = vs_base + static_cast<uint32_t>((b & 1) * kFaK * kFaLd) * 2;
+    float s[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll 4
+    for (int k0 = 0; k0 < kHd; k0 += 16) {
+      uint32_t a[4];
+      ldsm_x4(qs_base + static_cast<uint32_t>((16 * warp + (lane & 15)) * kFaLd + k0 + (lane >> 4) * 8) * 2, a[0], a[1],
+              a[2], a[3]);
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        const int n = 8 * j + (lane & 7) + ((lane >> 4) << 3), col = k0 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kst + static_cast<uint32_t>(n * kFaLd + col) * 2, b0, b1, b2, b3);
+        mma_f16_16816(s[j], a, b0, b1);
+        mma_f16_16816(s[j + 1], a, b2, b3);
+      }
+    }
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int key = b * kFaK + 8 * j + 2 * c;
+      s[j][0] = key <= qpos0 ? s[j][0] * scale : -INFINITY;
+      s[j][1] = key + 1 <= qpos0 ? s[j][1] * scale : -INFINITY;
+      s[j][2] = key <= qpos1 ? s[j][2] * scale : -INFINITY;
+      s[j][3] = key + 1 <= qpos1 ? s[j][3] * scale : -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    // key 0 is in block 0 for every row, so the running max is finite from then on
+    const float ps0 = expf(m0 - mx0), ps1 = expf(m1 - mx1);
+    m0 = mx0;
+    m1 = mx1;
+    float rs0 = 0.0f, rs1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      s[j][0] = expf(s[j][0] - m0);
+      s[j][1] = expf(s[j][1] - m0);
+      s[j][2] = expf(s[j][2] - m1);
+      s[j][3] = expf(s[j][3] - m1);
+      rs0 += s[j][0] + s[j][1];
+      rs1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * ps0 + rs0;
+    l1 = l1 * ps1 + rs1;
+#pragma unroll
+    for (int n = 0; n < kHd / 8; ++n) {
+      o[n][0] *= ps0;
+      o[n][1] *= ps0;
+      o[n][2] *= ps1;
+      o[n][3] *= ps1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t ahi[4], alo[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        // a0: row g keys 2c.. of tile 2kk; a1: row g+8; a2/a3: tile 2kk+1
+        const float x = s[2 * kk + (h >> 1)][(h & 1) * 2], y = s[2 * kk + (h >> 1)][(h & 1) * 2 + 1];
+        const __half2 hi = __floats2half2_rn(x, y);
+        const float2 hf = __half22float2(hi);
+        ahi[h] = h2_bits(hi);
+        alo[h] = h2_bits(__floats2half2_rn(x - hf.x, y - hf.y));
+      }
+      const int key = 16 * kk + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int nd = 0; nd < kHd / 16; ++nd) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vst + static_cast<uint32_t>(key * kFaLd + 16 * nd + (lane >> 4) * 8) * 2, b0, b1, b2, b3);
+        mma_f16_16816(o[2 * nd], ahi, b0, b1);
+        mma_f16_16816(o[2 * nd + 1], ahi, b2, b3);
+        mma_f16_16816(o[2 * nd], alo, b0, b1);
+        mma_f16_16816(o[2 * nd + 1], alo, b2, b3);
+      }
+    }
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = l0 == 0.0f ? 0.0f : 1.0f / l0, inv1 = l1 == 0.0f ? 0.0f : 1.0f / l1;
+  const int t0 = q0 + 16 * warp + g, t1 = t0 + 8;
+#pragma unroll
+  for (int n = 0; n < kHd / 8; ++n) {
+    const int d = 8 * n + 2 * c;
+    if (t0 < p.T) {
+      const float* gt = p.qg + (static_cast<size_t>(t0) * p.heads + head) * 2 * kHd + kHd + d;
+      *reinterpret_cast<float2*>(p.out + static_cast<size_t>(t0) * p.heads * kHd + head * kHd + d) =
+          make_float2(o[n][0] * inv0 * sigmoid_f(gt[0]), o[n][1] * inv0 * sigmoid_f(gt[1]));
+    }
+    if (t1 < p.T) {
+      const float* gt = p.qg + (static_cast<size_t>(t1) * p.heads + head) * 2 * kHd + kHd + d;
+      *reinterpret_cast<float2*>(p.out + static_cast<size_t>(t1) * p.heads * kHd + head * kHd + d) =
+          make_float2(o[n][2] * inv1 * sigmoid_f(gt[0]), o[n][3] * inv1 * sigmoid_f(gt[1]));
+    }
+  }
+}
+
 }  // namespace kib
