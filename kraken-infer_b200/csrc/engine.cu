@@ -36,6 +36,11 @@
 namespace kib {
 cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const float* x, int x_ld, int T, float* y,
                             int y_ld, const float* resid, cudaStream_t st);
+cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident, int rows, int cols, const float* x,
+                             int x_ld, int T, float* y, int y_ld, const float* resid, __half* w16, __half* x16,
+                             bool convert_x, int num_sms, cudaStream_t st);
+cudaError_t kquant_to_f16_launch(int type, const void* w, int rows, int cols, __half* out, int num_sms,
+                                 cudaStream_t st);
 cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const int* ids, int T, float* out,
                             int out_ld, cudaStream_t st);
 cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st);
@@ -55,6 +60,7 @@ constexpr int64_t kQwenEndOfText = 151643;  // qwen_tokenizer.hpp:44
 
 struct DevT {
   uint8_t* p = nullptr;
+  __half* h = nullptr;  // K-quant matrices used by prefill GEMMs: resident f16 copy (or nullptr)
   int type = -1;
   std::vector<uint64_t> shape;
   int cols() const { return shape.empty() ? 0 : static_cast<int>(shape[0]); }
@@ -103,6 +109,8 @@ struct kib_qwen35 {
   float *d_att = nullptr, *d_qout = nullptr, *d_norm = nullptr, *d_norm2 = nullptr, *d_hn = nullptr;
   float *d_logits = nullptr, *d_e = nullptr, *d_cat = nullptr, *d_hm = nullptr, *d_hm1 = nullptr, *d_mtp_h = nullptr;
   float *d_part = nullptr;
+  __half *d_w16 = nullptr, *d_x16 = nullptr;  // prefill GEMM scratch: one f16 weight matrix, one f16 x
+  void* d_w16_all = nullptr;                  // resident f16 prefill weights (DevT::h points inside)
   unsigned* d_attn_cnt = nullptr;
   float *d_cand_max = nullptr, *d_cand_sum = nullptr;
   int* d_cand_idx = nullptr;
@@ -406,8 +414,16 @@ void main_layers_small(Enq& q, int T, const int* pos) {
 
 // ---- prefill (T > 8) blocks ----------------------------------------------------
 
-void gemm(Enq& q, const DevT& w, const float* x, int x_ld, int T, float* y, int y_ld, const float* resid = nullptr) {
-  q.run(gemm_f16_launch(w.type, w.p, w.rows(), w.cols(), x, x_ld, T, y, y_ld, resid, q.st), "gemm");
+// same_x: x is the input of the previous gemm() call, unchanged since (its f16
+// copy is reused).
+void gemm(Enq& q, const DevT& w, const float* x, int x_ld, int T, float* y, int y_ld, const float* resid = nullptr,
+          bool same_x = false) {
+  if (q.m->d_w16 && w.cols() % 64 == 0 && x_ld % 4 == 0)
+    q.run(gemm_f16w_launch(w.type, w.p, w.h, w.rows(), w.cols(), x, x_ld, T, y, y_ld, resid, q.m->d_w16, q.m->d_x16,
+                           !same_x, q.m->ctx->num_sms, q.st),
+          "gemm_f16w");
+  else
+    q.run(gemm_f16_launch(w.type, w.p, w.rows(), w.cols(), x, x_ld, T, y, y_ld, resid, q.st), "gemm");
 }
 
 void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, float* x_mid) {
@@ -418,9 +434,9 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
   q.run(conv_launch(m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1), m->d_qkv, m->C, L.conv1d.f(), m->convk,
                     m->C, T, m->d_qkv, m->C, 1, q.st),
         "conv");
-  gemm(q, L.zgate, m->d_norm, m->H, T, m->d_z, m->VD);
-  gemm(q, L.beta, m->d_norm, m->H, T, m->d_beta, m->lvh);
-  gemm(q, L.alpha, m->d_norm, m->H, T, m->d_alpha, m->lvh);
+  gemm(q, L.zgate, m->d_norm, m->H, T, m->d_z, m->VD, nullptr, true);
+  gemm(q, L.beta, m->d_norm, m->H, T, m->d_beta, m->lvh, nullptr, true);
+  gemm(q, L.alpha, m->d_norm, m->H, T, m->d_alpha, m->lvh, nullptr, true);
   GdnParams g;
   g.conv_out = m->d_qkv;
   g.C = m->C;
@@ -461,8 +477,8 @@ void attention_block_prefill(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc
   kib_qwen35* m = q.m;
   q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
   gemm(q, L.q, m->d_norm, m->H, T, m->d_qg, 2 * m->AD);
-  gemm(q, L.k, m->d_norm, m->H, T, m->d_kp, m->KD);
-  gemm(q, L.v, m->d_norm, m->H, T, m->d_vp, m->KD);
+  gemm(q, L.k, m->d_norm, m->H, T, m->d_kp, m->KD, nullptr, true);
+  gemm(q, L.v, m->d_norm, m->H, T, m->d_vp, m->KD, nullptr, true);
   const AttnParams a = attn_params(m, L, kc, vc, pos, T);
   q.run(launch_pdl(attn_prep_kernel, dim3(T), dim3(256), 8 * kHd * sizeof(float), q.st, a), "attn_prep");
   if (a.round_q && m->heads % m->kvh == 0) {
@@ -485,7 +501,7 @@ void ffn_prefill(Enq& q, const LayerW& L, int T, const float* x_mid, float* x_ou
   kib_qwen35* m = q.m;
   q.run(rms_rows_launch(x_mid, L.post_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
   gemm(q, L.ffn_gate, m->d_norm, m->H, T, m->d_act, m->I);
-  gemm(q, L.ffn_up, m->d_norm, m->H, T, m->d_act2, m->I);
+  gemm(q, L.ffn_up, m->d_norm, m->H, T, m->d_act2, m->I, nullptr, true);
   q.run(silu_mul_launch(m->d_act, m->d_act2, static_cast<size_t>(T) * m->I, q.st), "silu_mul");
   gemm(q, L.ffn_down, m->d_act, m->I, T, x_out, m->H, x_mid);
 }
@@ -1185,6 +1201,9 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
             dalloc(&m->d_e, T * H) == cudaSuccess && dalloc(&m->d_cat, T * 2 * H) == cudaSuccess &&
             dalloc(&m->d_hm, T * H) == cudaSuccess && dalloc(&m->d_hm1, T * H) == cudaSuccess &&
             dalloc(&m->d_mtp_h, T * H) == cudaSuccess &&
+            dalloc(&m->d_w16, std::max<uint64_t>({C, 2 * AD, I, VD, H, KD}) * std::max<uint64_t>({H, I, VD, AD})) ==
+                cudaSuccess &&
+            dalloc(&m->d_x16, T * std::max<uint64_t>({2 * H, I, VD, AD})) == cudaSuccess &&
             dalloc(&m->d_part, static_cast<size_t>(m->nsplit) * kMaxSmallT * m->heads * (kHd + 2)) == cudaSuccess &&
             dalloc(&m->d_attn_cnt, 64) == cudaSuccess && dalloc(&m->d_head_cnt, 4) == cudaSuccess &&
             dalloc(&m->d_cand_max, 1024 * kGemvMaxTok) == cudaSuccess &&
@@ -1201,6 +1220,45 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
     return set_error(ctx, KIB_ERR_INTERNAL, "cache/activation allocation failed");
   }
   cudaMemset(m->d_attn_cnt, 0, 64 * sizeof(unsigned));
+  // Resident f16 copies of the prefill GEMM weights (each value as the GEMM
+  // rounds it), made once here so prefill GEMMs stream f16 tiles directly;
+  // only when they take under a quarter of the free device memory
+  // (KIB_PREFILL_F16_WEIGHTS=0 turns them off: per-call dequantization).
+  if (const char* ev = std::getenv("KIB_PREFILL_F16_WEIGHTS"); !ev || ev[0] != '0') {
+    std::vector<DevT*> ws;
+    auto add = [&](LayerW& L) {
+      for (DevT* d : {&L.qkv, &L.zgate, &L.beta, &L.alpha, &L.ssm_out, &L.q, &L.k, &L.v, &L.o, &L.ffn_gate, &L.ffn_up,
+                      &L.ffn_down, &L.eh_proj})
+        if (d->ok() && (d->type == kTypeQ4K || d->type == kTypeQ5K || d->type == kTypeQ6K) && d->cols() % 256 == 0)
+          ws.push_back(d);
+    };
+    for (LayerW& L : m->layers) add(L);
+    if (m->has_mtp) add(m->mtp);
+    auto bytes = [](const DevT* d) {
+      return (static_cast<size_t>(d->rows()) * d->cols() * 2 + 255) & ~static_cast<size_t>(255);
+    };
+    size_t total = 0;
+    for (DevT* d : ws) total += bytes(d);
+    size_t free_b = 0, total_b = 0;
+    if (!ws.empty() && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && total < free_b / 4 &&
+        cudaMalloc(&m->d_w16_all, total) == cudaSuccess) {
+      size_t off = 0;
+      cudaError_t e2 = cudaSuccess;
+      for (DevT* d : ws) {
+        d->h = reinterpret_cast<__half*>(static_cast<uint8_t*>(m->d_w16_all) + off);
+        off += bytes(d);
+        if (e2 == cudaSuccess)
+          e2 = kquant_to_f16_launch(d->type, d->p, d->rows(), d->cols(), d->h, ctx->num_sms, ctx->stream);
+      }
+      if (e2 == cudaSuccess) e2 = cudaStreamSynchronize(ctx->stream);
+      if (e2 != cudaSuccess) {
+        for (DevT* d : ws) d->h = nullptr;
+        cudaFree(m->d_w16_all);
+        m->d_w16_all = nullptr;
+        cudaGetLastError();
+      }
+    }
+  }
   if (const char* tr = std::getenv("KIB_TRACE"); tr && tr[0] == '1') {
     m->trace_on = cudaMalloc(&m->d_trace, 4096 * 8 * sizeof(unsigned long long)) == cudaSuccess;
   }
@@ -1237,7 +1295,8 @@ void kib_qwen35_free(kib_qwen35* m) {
                   m->d_act2, m->d_qg, m->d_kp, m->d_vp, m->d_att, m->d_qout, m->d_norm, m->d_norm2, m->d_hn,
                   m->d_logits, m->d_e, m->d_cat, m->d_hm, m->d_hm1, m->d_mtp_h, m->d_part, m->d_attn_cnt,
                   m->d_head_cnt, m->d_cand_max, m->d_cand_sum, m->d_cand_idx, m->d_pos, m->d_mtp_pos,
-                  m->d_tokens, m->d_argmax, m->d_prob, m->d_log, m->d_step, m->d_mtp_tok, m->d_trace};
+                  m->d_tokens, m->d_argmax, m->d_prob, m->d_log, m->d_step, m->d_mtp_tok, m->d_trace,
+                  m->d_w16, m->d_x16, m->d_w16_all};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (m->h_pin) cudaFreeHost(m->h_pin);

@@ -966,6 +966,161 @@ __global__ void __launch_bounds__(256, 2) kquant_gemm_f16_kernel(const __grid_co
       }
 }
 
+// ---- f16-operand GEMM for prefill ---------------------------------------------
+// The same products as kquant_gemm_f16_kernel (weights exactly as
+// unit_dequant_h2 rounds them, x rounded to half, fp32 accumulation in the same
+// k order), with the dequantization taken out of the GEMM: kquant_to_f16_kernel
+// writes a weight matrix as f16 [rows][cols] (once at load for the resident
+// copies, or per call into scratch), x_to_f16_kernel rounds x once, and
+// gemm_f16w_kernel streams both through a three-stage cp.async ring into
+// mma.sync m16n8k16.
+template <int QT>
+__global__ void __launch_bounds__(256) kquant_to_f16_kernel(const uint8_t* w, int rows, int cols, __half* out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int bpr = cols / 256;
+  const size_t units = static_cast<size_t>(rows) * bpr * 4;
+  for (size_t u = blockIdx.x * 256ull + threadIdx.x; u < units; u += static_cast<size_t>(gridDim.x) * 256) {
+    const size_t blk = u >> 2;
+    const int unit = static_cast<int>(u & 3);
+    const size_t row = blk / bpr;
+    const int kb = static_cast<int>(blk % bpr);
+    __half2 v[32];
+    unit_dequant_h2<QT>(w + blk * kquant_block_bytes(QT), unit, v);
+    __half* dst = out + row * cols + kb * 256;
+#pragma unroll
+    for (int e = 0; e < 64; e += 2) *reinterpret_cast<__half2*>(dst + unit_col<QT>(unit, e)) = v[e / 2];
+  }
+}
+
+static __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* x, int x_ld, int T, int cols, __half* out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int q4 = cols / 4;
+  const size_t n = static_cast<size_t>(T) * q4;
+  for (size_t i = blockIdx.x * 256ull + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * 256) {
+    const size_t t = i / q4;
+    const int c = static_cast<int>(i % q4) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(x + t * x_ld + c);
+    __half2* d = reinterpret_cast<__half2*>(out + t * cols + c);
+    d[0] = __floats2half2_rn(v.x, v.y);
+    d[1] = __floats2half2_rn(v.z, v.w);
+  }
+}
+
+struct GemmF16Params {
+  const __half* w;  // [rows][cols]
+  const __half* x;  // [T][cols]
+  int rows, cols, T;
+  float* y;         // [T][y_ld]
+  int y_ld;
+  const float* resid;
+};
+
+// 16-byte cp.async; src_bytes 0 fills the destination with zeros.
+KIB_DEV void cp16_zfill(void* sdst, const void* gsrc, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(sdst)), "l"(gsrc), "r"(src_bytes)
+               : "memory");
+}
+
+// CTA tile BM weight rows x BN tokens, K step 64, 8 warps as 2 (rows) x 4
+// (tokens), warp tile BM/2 x BN/4.  Shared rows of 64 halves are padded to 72
+// (144 bytes) so the eight rows of an ldmatrix land on distinct banks.
+constexpr int kGfK = 64, kGfLd = 72, kGfStages = 3;
+template <int BM, int BN>
+constexpr size_t gemm_f16w_smem() {
+  return static_cast<size_t>(kGfStages) * (BM + BN) * kGfLd * 2;
+}
+
+template <int BM, int BN>
+__global__ void __launch_bounds__(256, 2) gemm_f16w_kernel(const __grid_constant__ GemmF16Params p) {
+  constexpr int WM = BM / 2, WN = BN / 4, MI = WM / 16, NJ = WN / 8;
+  static_assert(NJ % 2 == 0, "warp tile needs an even number of n8 tiles");
+  extern __shared__ __align__(16) uint16_t gf_sm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r0 = blockIdx.x * BM, t0 = blockIdx.y * BN;
+  const int wm = (warp & 1) * WM, wn = (warp >> 1) * WN;
+  const int nk = p.cols / kGfK;
+  pdl_wait();
+  pdl_launch_dependents();
+  auto stage_ptr = [&](int s) { return gf_sm + static_cast<size_t>(s) * (BM + BN) * kGfLd; };
+  auto load = [&](int kt, int s) {
+    uint16_t* a = stage_ptr(s);
+    uint16_t* b = a + BM * kGfLd;
+    const int k0 = kt * kGfK;
+#pragma unroll
+    for (int i = tid; i < BM * 8; i += 256) {
+      const int r = i >> 3, piece = i & 7;
+      const int row = r0 + r;
+      const bool ok = row < p.rows;
+      cp16_zfill(a + r * kGfLd + 8 * piece, p.w + static_cast<size_t>(ok ? row : 0) * p.cols + k0 + 8 * piece,
+                 ok ? 16 : 0);
+    }
+#pragma unroll
+    for (int i = tid; i < BN * 8; i += 256) {
+      const int r = i >> 3, piece = i & 7;
+      const int t = t0 + r;
+      const bool ok = t < p.T;
+      cp16_zfill(b + r * kGfLd + 8 * piece, p.x + static_cast<size_t>(ok ? t : 0) * p.cols + k0 + 8 * piece,
+                 ok ? 16 : 0);
+    }
+  };
+  float acc[MI][NJ][4];
+#pragma unroll
+  for (int i = 0; i < MI; ++i)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0f;
+#pragma unroll
+  for (int s = 0; s < kGfStages - 1; ++s) {
+    if (s < nk) load(s, s);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  for (int kt = 0; kt < nk; ++kt) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kGfStages - 2) : "memory");
+    __syncthreads();  // tile kt landed; the stage loaded below was read at kt-1 by everyone
+    if (kt + kGfStages - 1 < nk) load(kt + kGfStages - 1, (kt + kGfStages - 1) % kGfStages);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint32_t a_base = smem_u32(stage_ptr(kt % kGfStages));
+    const uint32_t b_base = a_base + BM * kGfLd * 2;
+#pragma unroll
+    for (int k0 = 0; k0 < kGfK; k0 += 16) {
+      uint32_t a[MI][4];
+#pragma unroll
+      for (int i = 0; i < MI; ++i) {
+        const int row = wm + 16 * i + (lane & 15), col = k0 + (lane >> 4) * 8;
+        ldsm_x4(a_base + static_cast<uint32_t>(row * kGfLd + col) * 2, a[i][0], a[i][1], a[i][2], a[i][3]);
+      }
+#pragma unroll
+      for (int j = 0; j < NJ; j += 2) {
+        const int n = wn + 8 * j + (lane & 7) + ((lane >> 4) << 3), col = k0 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(b_base + static_cast<uint32_t>(n * kGfLd + col) * 2, b0, b1, b2, b3);
+#pragma unroll
+        for (int i = 0; i < MI; ++i) {
+          mma_f16_16816(acc[i][j], a[i], b0, b1);
+          mma_f16_16816(acc[i][j + 1], a[i], b2, b3);
+        }
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int i = 0; i < MI; ++i)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int row = r0 + wm + 16 * i + g + (c >> 1) * 8;
+        const int t = t0 + wn + 8 * j + 2 * q + (c & 1);
+        if (row < p.rows && t < p.T) {
+          float v = acc[i][j][c];
+          if (p.resid) v += p.resid[static_cast<size_t>(t) * p.y_ld + row];
+          p.y[static_cast<size_t>(t) * p.y_ld + row] = v;
+        }
+      }
+}
+
 // ======================================================= prefill attention (tensor cores)
 // Prefill step 2 for T >= 64 (flash256 numerics, attention_f32_batched_flash256_f16_kv,
 // mps_backend.mm:3398-3640): Q rounded to half, K and V f16 from the cache,

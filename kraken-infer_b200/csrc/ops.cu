@@ -493,6 +493,69 @@ cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const f
   }
 }
 
+template <int BM, int BN>
+static cudaError_t gemm_f16w_tile(const GemmF16Params& p, cudaStream_t st) {
+  static bool cfg = false;
+  constexpr size_t smem = gemm_f16w_smem<BM, BN>();
+  if (!cfg) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemm_f16w_kernel<BM, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cfg = true;
+  }
+  return launch_pdl(gemm_f16w_kernel<BM, BN>, dim3((p.rows + BM - 1) / BM, (p.T + BN - 1) / BN), dim3(256), smem, st,
+                    p);
+}
+
+cudaError_t kquant_to_f16_launch(int type, const void* w, int rows, int cols, __half* out, int num_sms,
+                                 cudaStream_t st) {
+  if (cols % 256 != 0) return cudaErrorInvalidValue;
+  const uint8_t* wb = static_cast<const uint8_t*>(w);
+  const size_t units = static_cast<size_t>(rows) * (cols / 256) * 4;
+  const int grid = static_cast<int>(std::min<size_t>((units + 255) / 256, static_cast<size_t>(num_sms) * 8));
+  switch (type) {
+    case kTypeQ4K: return launch_pdl(kquant_to_f16_kernel<kTypeQ4K>, dim3(grid), dim3(256), 0, st, wb, rows, cols, out);
+    case kTypeQ5K: return launch_pdl(kquant_to_f16_kernel<kTypeQ5K>, dim3(grid), dim3(256), 0, st, wb, rows, cols, out);
+    default: return launch_pdl(kquant_to_f16_kernel<kTypeQ6K>, dim3(grid), dim3(256), 0, st, wb, rows, cols, out);
+  }
+}
+
+// Prefill GEMM on f16 operands.  w16_resident: the weight's f16 copy made at
+// load (nullptr: dequantize into the w16 scratch, rows * cols halves, now).
+// convert_x false: x16 (T * cols halves) already holds this x, because the
+// previous GEMM read the same input.  The tile is the largest that still
+// gives two CTAs per SM.
+cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident, int rows, int cols, const float* x,
+                             int x_ld, int T, float* y, int y_ld, const float* resid, __half* w16, __half* x16,
+                             bool convert_x, int num_sms, cudaStream_t st) {
+  if (cols % kGfK != 0 || x_ld % 4 != 0) return cudaErrorInvalidValue;
+  cudaError_t e;
+  if (!w16_resident) {
+    e = kquant_to_f16_launch(type, w, rows, cols, w16, num_sms, st);
+    if (e != cudaSuccess) return e;
+  }
+  if (convert_x) {
+    const size_t xn = static_cast<size_t>(T) * (cols / 4);
+    const int x_grid = static_cast<int>(std::min<size_t>((xn + 255) / 256, static_cast<size_t>(num_sms) * 8));
+    e = launch_pdl(x_to_f16_kernel, dim3(x_grid), dim3(256), 0, st, x, x_ld, T, cols, x16);
+    if (e != cudaSuccess) return e;
+  }
+  GemmF16Params p;
+  p.w = w16_resident ? w16_resident : w16;
+  p.x = x16;
+  p.rows = rows;
+  p.cols = cols;
+  p.T = T;
+  p.y = y;
+  p.y_ld = y_ld;
+  p.resid = resid;
+  auto ctas = [&](int bm, int bn) { return ((rows + bm - 1) / bm) * ((T + bn - 1) / bn); };
+  const int fill = 2 * num_sms;
+  if (ctas(128, 128) >= fill) return gemm_f16w_tile<128, 128>(p, st);
+  if (ctas(128, 64) >= fill) return gemm_f16w_tile<128, 64>(p, st);
+  return gemm_f16w_tile<64, 64>(p, st);
+}
+
 cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const int* ids, int T, float* out,
                             int out_ld, cudaStream_t st) {
   const uint8_t* wb = static_cast<const uint8_t*>(w);

@@ -50,6 +50,23 @@ def test_prefill_logits_match_oracle(ctx, oracle, small_model, plen, chunk):
     m.close()
 
 
+def test_prefill_resident_f16_weights_match_per_call_dequant(ctx, small_model, monkeypatch):
+    """Prefill GEMMs on the load-time f16 weight copies and on per-call
+    dequantization into scratch compute the same products in the same order:
+    the logits after a two-chunk prefill are bit-identical."""
+    p = prompt(300, SMALL["vocab"], 7)
+    out = []
+    for flag in ("1", "0"):
+        monkeypatch.setenv("KIB_PREFILL_F16_WEIGHTS", flag)
+        m = kib.Qwen35(ctx, small_model, context_tokens=512, decode_tokens=16, prefill_chunk=1024)
+        nxt = m.prefill(p, 160)
+        _, glg, _ = m.forward([nxt], advance=True, logits=True, normed=True)
+        out.append((nxt, np.array(glg[0])))
+        m.close()
+    assert out[0][0] == out[1][0]
+    assert np.array_equal(out[0][1], out[1][1])
+
+
 def test_greedy_decode_tokens_identical(ctx, oracle, small_model):
     m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=128)
     om = oracle_lib.OracleModel(oracle, small_model, m.plan.attention_capacity_tokens)
