@@ -111,6 +111,60 @@ __global__ void conv_stateful_kernel(float* state, const float* in, int in_ld, c
   if (t1 == T && t0 < T) for (int j = 0; j < K - 1; ++j) state[static_cast<size_t>(c) * (K - 1) + j] = win[j];
 }
 
+// The same with the kernel size fixed at compile time: the window lives in
+// registers and four tokens' inputs are loaded together.  Identical sums.
+template <int K>
+__global__ void conv_stateful_k_kernel(float* state, const float* in, int in_ld, const float* w, int C, int T,
+                                       float* out, int out_ld, int apply_silu) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  const int ntiles = blockDim.y, tile = threadIdx.y;
+  const int len = (T + ntiles - 1) / ntiles;
+  const int t0 = min(tile * len, T), t1 = min(t0 + len, T);
+  float win[K], wc[K];
+  if (c < C) {
+#pragma unroll
+    for (int j = 0; j < K; ++j) wc[j] = w[static_cast<size_t>(c) * K + j];
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) {
+      const int t = t0 - (K - 1) + j;
+      win[j] = t >= 0 ? in[static_cast<size_t>(t) * in_ld + c] : state[static_cast<size_t>(c) * (K - 1) + (t + K - 1)];
+    }
+  }
+  __syncthreads();
+  if (c >= C) return;
+  constexpr int U = 4;
+  int t = t0;
+  for (; t + U <= t1; t += U) {
+    float x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) x[u] = in[static_cast<size_t>(t + u) * in_ld + c];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      win[K - 1] = x[u];
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < K; ++j) s += win[j] * wc[j];
+      out[static_cast<size_t>(t + u) * out_ld + c] = apply_silu ? silu_k(s) : s;
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+    }
+  }
+  for (; t < t1; ++t) {
+    win[K - 1] = in[static_cast<size_t>(t) * in_ld + c];
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) s += win[j] * wc[j];
+    out[static_cast<size_t>(t) * out_ld + c] = apply_silu ? silu_k(s) : s;
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+  }
+  if (t1 == T && t0 < T)
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) state[static_cast<size_t>(c) * (K - 1) + j] = win[j];
+}
+
 __global__ void prepare_gate_beta_kernel(float* gate, float* beta, const float* bias, const float* scale, int total,
                                          int heads) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -579,6 +633,9 @@ cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w
                         int out_ld, int silu, cudaStream_t st) {
   // tiles of >= 16 tokens, at most 32 per CTA (32 x 32 threads)
   const int ntiles = T >= 512 ? 32 : (T + 15) / 16;
+  if (K == 4)
+    return launch_pdl(conv_stateful_k_kernel<4>, dim3((C + 31) / 32), dim3(32, ntiles), 0, st, state, in, in_ld, w, C, T,
+                      out, out_ld, silu);
   return launch_pdl(conv_stateful_kernel, dim3((C + 31) / 32), dim3(32, ntiles), 0, st, state, in, in_ld, w, K, C, T, out,
                     out_ld, silu);
 }
