@@ -1023,8 +1023,8 @@ KIB_DEV void cp16_zfill(void* sdst, const void* gsrc, int src_bytes) {
                : "memory");
 }
 
-// CTA tile BM weight rows x BN tokens, K step 64, 8 warps as 2 (rows) x 4
-// (tokens), warp tile BM/2 x BN/4.  Shared rows of 64 halves are padded to 72
+// CTA tile BM weight rows x BN tokens, K step 64, WR x WC warps (rows x
+// tokens), warp tile BM/WR x BN/WC.  Shared rows of 64 halves are padded to 72
 // (144 bytes) so the eight rows of an ldmatrix land on distinct banks.
 constexpr int kGfK = 64, kGfLd = 72, kGfStages = 3;
 template <int BM, int BN>
@@ -1032,14 +1032,15 @@ constexpr size_t gemm_f16w_smem() {
   return static_cast<size_t>(kGfStages) * (BM + BN) * kGfLd * 2;
 }
 
-template <int BM, int BN>
-__global__ void __launch_bounds__(256, 2) gemm_f16w_kernel(const __grid_constant__ GemmF16Params p) {
-  constexpr int WM = BM / 2, WN = BN / 4, MI = WM / 16, NJ = WN / 8;
+template <int BM, int BN, int WR, int WC>
+__global__ void __launch_bounds__(32 * WR * WC, 16 / (WR * WC)) gemm_f16w_kernel(const __grid_constant__ GemmF16Params p) {
+  constexpr int NT = 32 * WR * WC;
+  constexpr int WM = BM / WR, WN = BN / WC, MI = WM / 16, NJ = WN / 8;
   static_assert(NJ % 2 == 0, "warp tile needs an even number of n8 tiles");
   extern __shared__ __align__(16) uint16_t gf_sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r0 = blockIdx.x * BM, t0 = blockIdx.y * BN;
-  const int wm = (warp & 1) * WM, wn = (warp >> 1) * WN;
+  const int wm = (warp % WR) * WM, wn = (warp / WR) * WN;
   const int nk = p.cols / kGfK;
   pdl_wait();
   pdl_launch_dependents();
@@ -1049,7 +1050,7 @@ __global__ void __launch_bounds__(256, 2) gemm_f16w_kernel(const __grid_constant
     uint16_t* b = a + BM * kGfLd;
     const int k0 = kt * kGfK;
 #pragma unroll
-    for (int i = tid; i < BM * 8; i += 256) {
+    for (int i = tid; i < BM * 8; i += NT) {
       const int r = i >> 3, piece = i & 7;
       const int row = r0 + r;
       const bool ok = row < p.rows;
@@ -1057,7 +1058,7 @@ __global__ void __launch_bounds__(256, 2) gemm_f16w_kernel(const __grid_constant
                  ok ? 16 : 0);
     }
 #pragma unroll
-    for (int i = tid; i < BN * 8; i += 256) {
+    for (int i = tid; i < BN * 8; i += NT) {
       const int r = i >> 3, piece = i & 7;
       const int t = t0 + r;
       const bool ok = t < p.T;

@@ -547,18 +547,19 @@ cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const f
   }
 }
 
-template <int BM, int BN>
+template <int BM, int BN, int WR, int WC>
 static cudaError_t gemm_f16w_tile(const GemmF16Params& p, cudaStream_t st) {
   static bool cfg = false;
   constexpr size_t smem = gemm_f16w_smem<BM, BN>();
   if (!cfg) {
     const cudaError_t e =
-        cudaFuncSetAttribute(gemm_f16w_kernel<BM, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        cudaFuncSetAttribute(gemm_f16w_kernel<BM, BN, WR, WC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     cfg = true;
   }
-  return launch_pdl(gemm_f16w_kernel<BM, BN>, dim3((p.rows + BM - 1) / BM, (p.T + BN - 1) / BN), dim3(256), smem, st,
-                    p);
+  return launch_pdl(gemm_f16w_kernel<BM, BN, WR, WC>, dim3((p.rows + BM - 1) / BM, (p.T + BN - 1) / BN),
+                    dim3(32 * WR * WC), smem, st, p);
 }
 
 cudaError_t kquant_to_f16_launch(int type, const void* w, int rows, int cols, __half* out, int num_sms,
@@ -605,9 +606,9 @@ cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident
   p.resid = resid;
   auto ctas = [&](int bm, int bn) { return ((rows + bm - 1) / bm) * ((T + bn - 1) / bn); };
   const int fill = 2 * num_sms;
-  if (ctas(128, 128) >= fill) return gemm_f16w_tile<128, 128>(p, st);
-  if (ctas(128, 64) >= fill) return gemm_f16w_tile<128, 64>(p, st);
-  return gemm_f16w_tile<64, 64>(p, st);
+  if (ctas(128, 128) >= fill) return gemm_f16w_tile<128, 128, 2, 4>(p, st);
+  if (ctas(128, 64) >= fill) return gemm_f16w_tile<128, 64, 2, 4>(p, st);
+  return gemm_f16w_tile<64, 64, 2, 2>(p, st);  // 4 warps of 32 x 32, up to four CTAs per SM
 }
 
 cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const int* ids, int T, float* out,
