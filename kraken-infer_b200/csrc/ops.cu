@@ -579,7 +579,7 @@ cudaError_t kquant_to_f16_launch(int type, const void* w, int rows, int cols, __
 // load (nullptr: dequantize into the w16 scratch, rows * cols halves, now).
 // convert_x false: x16 (T * cols halves) already holds this x, because the
 // previous GEMM read the same input.  The tile is the largest that still
-// gives two CTAs per SM.
+// fills two CTA slots per SM; the two smaller tiles run four warps each.
 cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident, int rows, int cols, const float* x,
                              int x_ld, int T, float* y, int y_ld, const float* resid, __half* w16, __half* x16,
                              bool convert_x, int num_sms, cudaStream_t st) {
@@ -607,7 +607,7 @@ cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident
   auto ctas = [&](int bm, int bn) { return ((rows + bm - 1) / bm) * ((T + bn - 1) / bn); };
   const int fill = 2 * num_sms;
   if (ctas(128, 128) >= fill) return gemm_f16w_tile<128, 128, 2, 4>(p, st);
-  if (ctas(128, 64) >= fill) return gemm_f16w_tile<128, 64, 2, 4>(p, st);
+  if (ctas(128, 64) >= fill) return gemm_f16w_tile<128, 64, 2, 2>(p, st);
   return gemm_f16w_tile<64, 64, 2, 2>(p, st);  // 4 warps of 32 x 32, up to four CTAs per SM
 }
 
