@@ -41,11 +41,10 @@ WORKLOAD = "qwen35-0.8b-shape-q4_k_m-bs1-greedy-decode-ctx4096"
 # (24 layers 304.7 + Q6_K LM head 208.6), GDN S r+w 37.7, conv R r+w 2.7,
 # KV read 50.3 (6 layers x 4096 x 2 heads x 256 x 2 B x K,V).
 TOKEN_BYTES = 604.0e6
-# DRAM bytes per token of decode_persistent_kernel from ncu (dram__bytes_read.sum
-# + dram__bytes_write.sum), the capture summarised in
-# profiles/decode_persistent_small_full.md: a 4-layer capture (70.51 MB read +
-# 0.46 MB written against 72.44 MB algorithmic) scaled to the full model by
-# algorithmic bytes, traffic/algorithmic = 0.980.
+# DRAM bytes per token of decode_persistent_kernel from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of a 4-layer model: 70.51 MB
+# read + 0.46 MB written against 72.44 MB algorithmic, scaled to the full model
+# by algorithmic bytes, traffic/algorithmic = 0.980.
 PK_TRAFFIC = 591.7e6  # 0.980 x 604 MB
 
 

@@ -102,7 +102,10 @@ int kib_matvec_kquant_f32_argmax(kib_ctx* ctx, int type, const void* weight, uin
  * 256 or above 16384).  The first call on a device looks up that array's
  * address; make it before any stream capture.  Every call shares the array:
  * calls whose kernels may overlap on the GPU race and must be ordered by the
- * caller. */
+ * caller.  The return code covers argument checks and the launch only: a
+ * bounded device wait that gives up inside the kernel (reported as
+ * KIB_ERR_TIMEOUT by kib_matvec_kquant_f32_argmax) shows here as
+ * token_out = -1 and prob_out = 0 once the stream has been synchronised. */
 int kib_matvec_kquant_f32_argmax_noalloc(int type, const void* weight, uint64_t rows, uint64_t cols,
                                          const float* input, int32_t* token_out, float* prob_out, void* stream);
 /* dequantize_rows_q{4,5,6}_k_f32 / q*_k_get_rows (mps_backend.hpp:201-221;

@@ -1,4 +1,7 @@
-"""Builds the B200 backend in-tree: kraken-infer_b200/lib/libkib.so (sm_100a).
+"""Builds the B200 backend in-tree: kraken-infer_b200/lib/libkib.so (sm_100a),
+and lib/libkib_gguf.so, the host-only GGUF tools (synthetic model writer and
+K-quant quantisers, no device code) for processes that must not map the CUDA
+backend.
 
 Usage: python kraken-infer_b200/build.py [--force]
 The CUDA sources are compiled with nvcc for sm_100a only; the host C++ (GGUF
@@ -13,7 +16,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libkib.so")
-SOURCES = ["ops.cu", "engine.cu", "noalloc.cu", "gguf.cpp"]
+SOURCES = ["ops.cu", "engine.cu", "noalloc.cu", "gguf.cpp", "gguf_tools.cpp"]
+TOOLS_LIB = os.path.join(LIB_DIR, "libkib_gguf.so")
+TOOLS_SOURCES = ["gguf.cpp", "gguf_tools.cpp"]
 HEADERS = ["kib_common.cuh", "kquant.cuh", "kquant_gemv.cuh", "kquant_gemv2.cuh", "decode_persistent.cuh", "layer_kernels.cuh", "kib_ctx.cuh", "gguf.hpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -22,7 +27,7 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", 
 
 
 def _stale():
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(TOOLS_LIB):
         return True
     t = os.path.getmtime(LIB)
     deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
@@ -56,6 +61,11 @@ def build(force=False, verbose=False, ptxas_info=False):
     subprocess.check_call(cmd)
     for o in objs:
         os.remove(o)
+    cmd = [os.environ.get("CXX", "g++"), "-O3", "-std=c++17", "-fPIC", "-pthread", "-shared",
+           "-I" + os.path.join(HERE, "..", "include"), "-o", TOOLS_LIB] + [os.path.join(CSRC, f) for f in TOOLS_SOURCES]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.check_call(cmd)
     return LIB
 
 

@@ -381,6 +381,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) kquant_gemv2_kernel(const __g
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  // A CTA whose bounded tile wait gave up raised *p.err before its fence and
+  // ticket, so the last CTA sees it: the token is then -1 (no token), which a
+  // caller without a status read-back (the no-allocation entry) can test.
+  const bool failed = p.err != nullptr && atomicAdd(p.err, 0) != 0;
   if (tid < NT) {
     const int t = tid;
     float m = -INFINITY, s = 0.0f;
@@ -397,6 +401,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) kquant_gemv2_kernel(const __g
       } else {
         s += gs * expf(gm - m);
       }
+    }
+    if (failed) {
+      idx = -1;
+      s = 0.0f;
     }
     p.token_out[t] = idx;
     if (p.prob_out) p.prob_out[(p.token_log ? *p.step_counter : 0) + t] = s > 0.0f ? 1.0f / s : 0.0f;

@@ -632,6 +632,8 @@ cudaError_t norm_gate_launch(float* v, const float* w, const float* gate, int T,
 
 cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w, int K, int C, int T, float* out,
                         int out_ld, int silu, cudaStream_t st) {
+  // conv_stateful_kernel keeps the window in 16-entry register arrays
+  if (K < 1 || K > 16) return cudaErrorInvalidValue;
   // tiles of >= 16 tokens, at most 32 per CTA (32 x 32 threads)
   const int ntiles = T >= 512 ? 32 : (T + 15) / 16;
   if (K == 4)

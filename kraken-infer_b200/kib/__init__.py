@@ -17,6 +17,7 @@ from ctypes import POINTER, byref, c_char_p, c_double, c_float, c_int, c_int32, 
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libkib.so")
+TOOLS_LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libkib_gguf.so")
 HEADER_PATH = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "include", "kib.h")
 
 KIB_OK = 0
@@ -48,6 +49,29 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib = ctypes.CDLL(path)
     _declare(lib)
     _lib = lib
+    return lib
+
+
+_tools = None
+
+
+def load_tools_library(path: str = TOOLS_LIB_PATH) -> ctypes.CDLL:
+    """Loads libkib_gguf.so, the host-only GGUF tools (no device code), which
+    export the same kib_synth_default / kib_write_synthetic_qwen35 /
+    kib_quantize_kquant as libkib.so."""
+    global _tools
+    if _tools is not None:
+        return _tools
+    if not os.path.exists(path):
+        raise KibError(KIB_ERR_UNAVAILABLE, f"{path} is missing: run kraken-infer_b200/build.py")
+    lib = ctypes.CDLL(path)
+    lib.kib_synth_default.restype = None
+    lib.kib_synth_default.argtypes = [POINTER(SynthConfig)]
+    lib.kib_write_synthetic_qwen35.restype = c_int
+    lib.kib_write_synthetic_qwen35.argtypes = [c_char_p, POINTER(SynthConfig), c_char_p, c_int]
+    lib.kib_quantize_kquant.restype = c_int
+    lib.kib_quantize_kquant.argtypes = [c_int, c_void_p, c_uint64, c_void_p]
+    _tools = lib
     return lib
 
 
@@ -348,7 +372,7 @@ class Qwen35:
 
 
 def synth_config(**overrides) -> SynthConfig:
-    lib = load_library()
+    lib = load_tools_library()
     cfg = SynthConfig()
     lib.kib_synth_default(byref(cfg))
     for k, v in overrides.items():
@@ -358,7 +382,7 @@ def synth_config(**overrides) -> SynthConfig:
 
 def write_synthetic_qwen35(path: str, **overrides) -> str:
     """Writes a random-init Qwen3.5-shaped GGUF (Q4_K_M mix by default)."""
-    lib = load_library()
+    lib = load_tools_library()
     cfg = synth_config(**overrides)
     err = ctypes.create_string_buffer(512)
     rc = lib.kib_write_synthetic_qwen35(path.encode(), byref(cfg), err, 512)
@@ -370,7 +394,7 @@ def write_synthetic_qwen35(path: str, **overrides) -> str:
 def quantize(qtype: int, x):
     """K-quant super-blocks of a float32 array (length a multiple of 256)."""
     import numpy as np
-    lib = load_library()
+    lib = load_tools_library()
     a = np.ascontiguousarray(x, dtype=np.float32).ravel()
     out = np.zeros(a.size // 256 * BLOCK_BYTES[qtype], np.uint8)
     rc = lib.kib_quantize_kquant(qtype, a.ctypes.data, a.size, out.ctypes.data)

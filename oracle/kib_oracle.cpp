@@ -1048,7 +1048,7 @@ int orc_model_state(void* h, int write_into_model, uint16_t* k, uint16_t* v, flo
 // last prompt row.  mtp_draft_tokens == 0 selects the plain greedy loop.
 // Returns the number of generated tokens written to out_tokens.
 int64_t orc_generate_from(void* h, int64_t pos, int32_t first_token, int64_t max_new, int mtp_draft_tokens,
-                          int adaptive, int ignore_eos, int32_t* out_tokens, orc_mtp_stats* stats) {
+                          int adaptive, double p_min, int ignore_eos, int32_t* out_tokens, orc_mtp_stats* stats) {
   auto* m = static_cast<Model*>(h);
   int64_t n = 0;
   std::vector<float> hid, hn, lg;
@@ -1071,7 +1071,12 @@ int64_t orc_generate_from(void* h, int64_t pos, int32_t first_token, int64_t max
     return n;
   }
   // MTP greedy loop.  Budget control follows update_mtp_adaptive_budget
-  // (qwen35_runtime.cpp:6421-6455); p_min = 0 (argmax drafts, no confidence stop).
+  // (qwen35_runtime.cpp:6421-6455).  With p_min > 0 a draft whose head p(top1)
+  // is below p_min ends the chain and is not drafted (read_mtp_draft_token,
+  // qwen35_runtime.cpp:6184-6210; confidence_stops counts these).  The
+  // reference runs every forward of the chain before reading the tokens
+  // (6339-6364); forwards past the stop only write MTP cache positions that the
+  // next chain rewrites before it reads them, so stopping early is equivalent.
   const size_t K = static_cast<size_t>(mtp_draft_tokens);
   size_t budget = adaptive ? 1 : K;
   size_t win_d = 0, win_a = 0;
@@ -1094,6 +1099,10 @@ int64_t orc_generate_from(void* h, int64_t pos, int32_t first_token, int64_t max
       const std::string head = m->g->tensors.count("output.weight") ? "output.weight" : "token_embd.weight";
       m->matmul(head, hnext.data(), 1, lg.data());
       dt = static_cast<int32_t>(argmax(lg.data(), V));
+      if (p_min > 0.0 && static_cast<double>(orc_top1_prob(lg.data(), V)) < p_min) {
+        ++stats->confidence_stops;
+        break;
+      }
       drafts.push_back(dt);
       ++stats->drafted;
       hin = hnext;

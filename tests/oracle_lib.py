@@ -53,7 +53,8 @@ class Oracle:
             "orc_model_dim": (c_int64, [_P, c_int]),
             "orc_model_forward": (c_int, [_P, _P, _I64, _I64, _P, _P, _P]),
             "orc_model_state": (c_int, [_P, c_int, _P, _P, _P, _P, _P, _P, _P]),
-            "orc_generate_from": (c_int64, [_P, _I64, c_int32, _I64, c_int, c_int, c_int, _P, POINTER(MtpStats)]),
+            "orc_generate_from": (c_int64, [_P, _I64, c_int32, _I64, c_int, c_int, ctypes.c_double, c_int, _P,
+                                           POINTER(MtpStats)]),
             "orc_mtp_process_chunk": (c_int, [_P, _P, _P, _I64, _I64]),
         }
         for n, (r, a) in sig.items():
@@ -118,10 +119,10 @@ class OracleModel:
         r = np.ascontiguousarray(normed_rows, np.float32)
         assert self.L.orc_mtp_process_chunk(self.h, _a(t), _a(r), len(t), pos) == 0
 
-    def generate_from(self, pos, first_token, max_new, mtp_draft_tokens=0, adaptive=True, ignore_eos=True):
+    def generate_from(self, pos, first_token, max_new, mtp_draft_tokens=0, adaptive=True, ignore_eos=True, p_min=0.0):
         out = np.zeros(max(max_new, 1), np.int32)
         st = MtpStats()
-        n = self.L.orc_generate_from(self.h, pos, int(first_token), max_new, mtp_draft_tokens, 1 if adaptive else 0,
+        n = self.L.orc_generate_from(self.h, pos, int(first_token), max_new, mtp_draft_tokens, 1 if adaptive else 0, p_min,
                                      1 if ignore_eos else 0, _a(out), ctypes.byref(st))
         return out[:n].copy(), st
 
