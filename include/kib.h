@@ -186,6 +186,79 @@ int kib_copy_f32_rows_to_f16(kib_ctx* ctx, const float* source, uint16_t* destin
 /* argmax_f32_i32 / argmax_prob_f32_i32 (mps_backend.hpp:384-387; mps_backend.mm:2681-2779). */
 int kib_argmax_f32_i32(kib_ctx* ctx, const float* values, uint64_t size, int32_t* token_out, float* prob_out);
 
+/* ------------------------------------------------- named and offset forms
+ * The remaining MpsContext members on the Qwen3.5 path, same argument order
+ * and meaning (offsets in elements, as the reference's validate_*_region). */
+/* copy_to_buffer_at / copy_from_buffer_at (mps_backend.hpp:100-109; mps_backend.mm:5768-5830). */
+int kib_copy_to_buffer_at(kib_ctx* ctx, void* buffer, uint64_t destination_offset, const void* data, uint64_t bytes);
+int kib_copy_from_buffer_at(kib_ctx* ctx, const void* buffer, uint64_t source_offset, void* data, uint64_t bytes);
+/* copy_f32_region (mps_backend.hpp:362-365; mps_backend.mm:2631-2640, 9634):
+ * destination[destination_offset + i] = source[source_offset + i], i < size. */
+int kib_copy_f32_region(kib_ctx* ctx, const float* source, float* destination, uint64_t source_offset,
+                        uint64_t destination_offset, uint64_t size);
+/* copy_f16_rows (mps_backend.hpp:377-383; mps_backend.mm:2668-2679, 9900). */
+int kib_copy_f16_rows(kib_ctx* ctx, const uint16_t* source, uint16_t* destination, uint64_t rows, uint64_t row_size,
+                      uint64_t source_stride, uint64_t source_offset, uint64_t destination_stride,
+                      uint64_t destination_offset);
+/* ssm_conv_f32 (mps_backend.hpp:301-307; mps_backend.mm:2376-2400, 8703): input
+ * [sequences][channels][conv_kernel-1+tokens], kernel [channels][conv_kernel],
+ * output [sequences][tokens][channels]; no activation. */
+int kib_ssm_conv_f32(kib_ctx* ctx, const float* input, const float* kernel, uint64_t conv_kernel, uint64_t channels,
+                     uint64_t tokens, uint64_t sequences, float* output);
+/* build_ssm_conv_state_f32 (mps_backend.hpp:308-314; mps_backend.mm:2428-2456, 8801):
+ * conv_input[channel] = [state row | the new inputs]; the state row (at
+ * state + state_offset, [channels][conv_kernel-1]) becomes the window's tail. */
+int kib_build_ssm_conv_state_f32(kib_ctx* ctx, float* state, uint64_t state_offset, const float* input,
+                                 uint64_t conv_kernel, uint64_t channels, uint64_t tokens, float* conv_input);
+/* ssm_conv1_f32_stateful(_at) (mps_backend.hpp:315-327; mps_backend.mm:2402-2426, 8904-8990). */
+int kib_ssm_conv1_f32_stateful(kib_ctx* ctx, float* state, const float* input, const float* kernel,
+                               uint64_t conv_kernel, uint64_t channels, float* output);
+int kib_ssm_conv1_f32_stateful_at(kib_ctx* ctx, float* state, uint64_t state_offset, const float* input,
+                                  const float* kernel, uint64_t conv_kernel, uint64_t channels, float* output);
+/* gated_delta_net_f32_in_place(_at), gated_delta_net_f32_batched_in_place_at
+ * (mps_backend.hpp:270-300): the batched op with tokens = 1 and/or the state at
+ * state + state_offset. */
+int kib_gated_delta_net_f32_in_place(kib_ctx* ctx, const float* query, const float* key, const float* value,
+                                     const float* gate, const float* beta, float* state, uint64_t key_heads,
+                                     uint64_t value_heads, uint64_t head_dim, float* output);
+int kib_gated_delta_net_f32_in_place_at(kib_ctx* ctx, const float* query, const float* key, const float* value,
+                                        const float* gate, const float* beta, float* state, uint64_t state_offset,
+                                        uint64_t key_heads, uint64_t value_heads, uint64_t head_dim, float* output);
+int kib_gated_delta_net_f32_batched_in_place_at(kib_ctx* ctx, const float* query, const float* key,
+                                                const float* value, const float* gate, const float* beta,
+                                                float* state, uint64_t state_offset, uint64_t tokens,
+                                                uint64_t key_heads, uint64_t value_heads, uint64_t head_dim,
+                                                float* output);
+/* matvec_q{4,5,6}_k_f32_top1 / _argmax (mps_backend.hpp:141-149, 162-170, 183-191):
+ * the fused LM-head argmax (ties to the lowest row) with and without p(top1). */
+int kib_matvec_q4_k_f32_top1(kib_ctx* ctx, const void* weight, uint64_t rows, uint64_t cols, const float* input,
+                             int32_t* token_out, float* probability_out);
+int kib_matvec_q5_k_f32_top1(kib_ctx* ctx, const void* weight, uint64_t rows, uint64_t cols, const float* input,
+                             int32_t* token_out, float* probability_out);
+int kib_matvec_q6_k_f32_top1(kib_ctx* ctx, const void* weight, uint64_t rows, uint64_t cols, const float* input,
+                             int32_t* token_out, float* probability_out);
+int kib_matvec_q4_k_f32_argmax(kib_ctx* ctx, const void* weight, uint64_t rows, uint64_t cols, const float* input,
+                               int32_t* token_out);
+int kib_matvec_q5_k_f32_argmax(kib_ctx* ctx, const void* weight, uint64_t rows, uint64_t cols, const float* input,
+                               int32_t* token_out);
+int kib_matvec_q6_k_f32_argmax(kib_ctx* ctx, const void* weight, uint64_t rows, uint64_t cols, const float* input,
+                               int32_t* token_out);
+/* argmax_prob_f32_i32 (mps_backend.hpp:387-390). */
+int kib_argmax_prob_f32_i32(kib_ctx* ctx, const float* values, uint64_t size, int32_t* token_out, float* prob_out);
+/* dequantize_row_q{4,5,6}_k_f32 (mps_backend.hpp:196-225; mps_backend.mm:1693-1760): one row. */
+int kib_dequantize_row_q4_k_f32(kib_ctx* ctx, const void* weight, uint64_t row, uint64_t cols, float* output);
+int kib_dequantize_row_q5_k_f32(kib_ctx* ctx, const void* weight, uint64_t row, uint64_t cols, float* output);
+int kib_dequantize_row_q6_k_f32(kib_ctx* ctx, const void* weight, uint64_t row, uint64_t cols, float* output);
+/* rms_norm_f32_f32, qk_norm_f32_f32, attention_f32_f16_kv (mps_backend.hpp:230-250, 397-401):
+ * the batched ops with one token (attention: the query at `position`). */
+int kib_rms_norm_f32_f32(kib_ctx* ctx, const float* input, const float* weight, uint64_t size, float eps,
+                         float* output);
+int kib_qk_norm_f32_f32(kib_ctx* ctx, float* values, const float* weight, uint64_t heads, uint64_t head_dim,
+                        float eps);
+int kib_attention_f32_f16_kv(kib_ctx* ctx, const float* query, const uint16_t* key_cache,
+                             const uint16_t* value_cache, uint64_t layer, uint64_t position, uint64_t capacity_tokens,
+                             uint64_t heads, uint64_t kv_heads, uint64_t head_dim, float* output);
+
 /* ================================================================ runtime */
 
 typedef struct kib_qwen35 kib_qwen35;
@@ -282,6 +355,13 @@ int kib_qwen35_decode_greedy(kib_qwen35* model, int32_t first_token, uint64_t st
 /* Current position (tokens in the KV cache). */
 uint64_t kib_qwen35_position(const kib_qwen35* model);
 int kib_qwen35_set_position(kib_qwen35* model, uint64_t position);
+/* Test hook, no counterpart in the reference: lowers the persistent decode
+ * kernel's cell-poll limit to poll_limit (0 restores the default) and, when
+ * stage >= 0, makes that GEMV stage wait for an input tag no stage writes, so
+ * the next decode step's bounded waits run out: the step returns
+ * KIB_ERR_TIMEOUT and the model stays usable (state of the aborted step is
+ * undefined; reset and prefill again).  stage = -1 restores the stage list. */
+int kib_qwen35_debug_stall(kib_qwen35* model, uint32_t poll_limit, int stage);
 /* Copies cache state out of (write_into_model = 0) or into (1) the engine: any
  * pointer may be null.  Host buffers; sizes from kib_qwen35_plan. */
 int kib_qwen35_state_io(kib_qwen35* model, int write_into_model, uint16_t* k_cache, uint16_t* v_cache,
@@ -306,6 +386,11 @@ void kib_synth_default(kib_synth_config* cfg);
 int kib_write_synthetic_qwen35(const char* path, const kib_synth_config* cfg, char* err, int err_len);
 /* Raw K-quant quantizers used by the writer (n multiple of 256). */
 int kib_quantize_kquant(int type, const float* x, uint64_t n, void* out);
+/* Opens and validates a GGUF file on the host only (header, metadata, tensor
+ * directory, every tensor's data inside the file), as the loader does before
+ * it touches the device: KIB_ERR_INVALID_ARGUMENT with the reason in err for a
+ * truncated or corrupt file (gguf_reader.cpp's checks). */
+int kib_gguf_check(const char* path, char* err, int err_len, uint64_t* n_tensors);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libkib.so")
-SOURCES = ["ops.cu", "engine.cu", "noalloc.cu", "gguf.cpp", "gguf_tools.cpp"]
+SOURCES = ["ops.cu", "ops_seam.cu", "engine.cu", "noalloc.cu", "gguf.cpp", "gguf_tools.cpp"]
 TOOLS_LIB = os.path.join(LIB_DIR, "libkib_gguf.so")
 TOOLS_SOURCES = ["gguf.cpp", "gguf_tools.cpp"]
 HEADERS = ["kib_common.cuh", "kquant.cuh", "kquant_gemv.cuh", "kquant_gemv2.cuh", "decode_persistent.cuh", "layer_kernels.cuh", "kib_ctx.cuh", "gguf.hpp"]

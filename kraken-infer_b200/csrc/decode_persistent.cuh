@@ -77,6 +77,9 @@ constexpr int kPkRows = 2;           // rows a lane dots per pass (independent c
 constexpr int kPkMaxStages = 254;    // stage tags are 1..254 in the low byte
 constexpr int kPkRopePairs = 128;    // rotary pairs with a precomputed frequency
 constexpr uint32_t kPkPollLimit = 1u << 21;
+// Poll limit the kernel uses (kPkPollLimit unless a test lowers it through
+// kib_qwen35_debug_stall to make a wait run out on purpose).
+__device__ uint32_t g_pk_poll_limit = kPkPollLimit;
 
 enum PkKind : int { kPkGemv = 0, kPkGdn = 1, kPkAttn = 2, kPkMerge = 3, kPkHead = 4 };
 
@@ -118,8 +121,9 @@ KIB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory
 // cell, or 0 (tag 0 is never a stage tag) when the poll limit runs out or
 // another CTA raised the error flag.
 __device__ __noinline__ uint64_t pk_poll1(const uint64_t* p, uint32_t tag, const int* err) {
+  const uint32_t limit = *reinterpret_cast<const volatile uint32_t*>(&g_pk_poll_limit);
   #pragma unroll 1
-  for (uint32_t i = 0; i < kPkPollLimit; ++i) {
+  for (uint32_t i = 0; i < limit; ++i) {
     const uint64_t c = cell_ld1(p);
     if (cell_ok(c, tag)) return c;
     if ((i & 255u) == 255u && *reinterpret_cast<const volatile int*>(err) != 0) break;
@@ -531,6 +535,7 @@ __device__ __noinline__ float pk_poll_input(const uint64_t* c, uint32_t t, int c
   }
   float ss = 0.0f;
   uint32_t iter = 0;
+  const uint32_t limit = *reinterpret_cast<const volatile uint32_t*>(&g_pk_poll_limit);
   #pragma unroll 1
   while (true) {
     bool ready = true;
@@ -555,7 +560,7 @@ __device__ __noinline__ float pk_poll_input(const uint64_t* c, uint32_t t, int c
       }
     }
     if (ready) break;
-    if (++iter > kPkPollLimit || ((iter & 255u) == 0u && *reinterpret_cast<const volatile int*>(err) != 0)) {
+    if (++iter > limit || ((iter & 255u) == 0u && *reinterpret_cast<const volatile int*>(err) != 0)) {
       ok = false;
       break;
     }

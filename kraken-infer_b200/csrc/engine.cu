@@ -137,6 +137,7 @@ struct kib_qwen35 {
   bool pk_on = false;
   std::string pk_why;
   PkStage* d_pk = nullptr;
+  std::vector<PkStage> pk_host;  // host copy of the stage list (kib_qwen35_debug_stall restores from it)
   int pk_n = 0;
   int pk_grid = 0;
   unsigned* d_pk_ctr = nullptr;  // [1] LM-head ticket, [2] cell tag epoch
@@ -934,6 +935,7 @@ static int build_pk(kib_qwen35* m) {
   if (cudaMalloc(&m->d_pk, st.size() * sizeof(PkStage)) != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, "pk alloc");
   ENG_CUDA(cudaMemcpy(m->d_pk, st.data(), st.size() * sizeof(PkStage), cudaMemcpyHostToDevice));
   m->pk_n = static_cast<int>(st.size());
+  m->pk_host = st;
   m->pk_grid = grid;
   m->pk_coop = coop != 0;
   ENG_CUDA(cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1329,16 +1331,43 @@ int kib_qwen35_reset(kib_qwen35* m) {
 
 uint64_t kib_qwen35_position(const kib_qwen35* m) { return m ? m->pos : 0; }
 
+int kib_qwen35_debug_stall(kib_qwen35* m, uint32_t poll_limit, int stage) {
+  if (!m) return KIB_ERR_INVALID_ARGUMENT;
+  if (!m->pk_on) return fail(m, KIB_ERR_UNAVAILABLE, "debug_stall: the persistent decode kernel is not in use");
+  if (stage >= m->pk_n) return fail(m, KIB_ERR_INVALID_ARGUMENT, "debug_stall: no such stage");
+  std::vector<PkStage> st = m->pk_host;
+  if (stage >= 0) {
+    PkStage& S = st[static_cast<size_t>(stage)];
+    if (S.kind != kPkGemv || S.in_tag == 0)
+      return fail(m, KIB_ERR_INVALID_ARGUMENT, "debug_stall: the stage must be a GEMV reading cells");
+    S.in_tag = 255;  // no stage writes tag 255: the input never arrives
+  }
+  const uint32_t limit = poll_limit ? poll_limit : kPkPollLimit;
+  ENG_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  ENG_CUDA(cudaMemcpyToSymbol(g_pk_poll_limit, &limit, sizeof(limit)));
+  ENG_CUDA(cudaMemcpy(m->d_pk, st.data(), st.size() * sizeof(PkStage), cudaMemcpyHostToDevice));
+  return KIB_OK;
+}
+
 int kib_qwen35_set_position(kib_qwen35* m, uint64_t position) {
   if (!m || position >= static_cast<uint64_t>(m->cap)) return KIB_ERR_INVALID_ARGUMENT;
   m->pos = position;
   return set_pos(m, m->d_pos, position);
 }
 
+// Token ids must name embedding rows (qwen35_runtime.cpp:1575-1578 rejects
+// the others as invalid arguments).
+static int check_tokens(kib_qwen35* m, const int32_t* t, uint64_t n) {
+  for (uint64_t i = 0; i < n; ++i)
+    if (t[i] < 0 || t[i] >= m->V) return fail(m, KIB_ERR_INVALID_ARGUMENT, "Qwen3.5 token id is outside embedding rows");
+  return KIB_OK;
+}
+
 int kib_qwen35_forward(kib_qwen35* m, const int32_t* tokens, uint64_t n, int advance, int32_t* argmax_out,
                        float* logits, float* normed_hidden) {
   if (!m || !tokens || n < 1 || n > kMaxSmallT) return KIB_ERR_INVALID_ARGUMENT;
   if (m->pos + n > static_cast<uint64_t>(m->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "forward exceeds cache capacity");
+  if (int rc = check_tokens(m, tokens, n)) return rc;
   cudaStream_t st = m->ctx->stream;
   if (n == 1 && !logits && !normed_hidden && m->pk_on) {
     // one token, argmax only: the persistent decode path (its head writes the
@@ -1383,6 +1412,7 @@ int kib_qwen35_forward(kib_qwen35* m, const int32_t* tokens, uint64_t n, int adv
 int kib_qwen35_prefill(kib_qwen35* m, const int32_t* tokens, uint64_t n, uint64_t chunk, int32_t* next_token) {
   if (!m || !tokens || n == 0) return KIB_ERR_INVALID_ARGUMENT;
   if (m->pos + n > static_cast<uint64_t>(m->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "prefill exceeds cache capacity");
+  if (int rc = check_tokens(m, tokens, n)) return rc;
   if (chunk == 0) chunk = static_cast<uint64_t>(m->chunk);
   if (chunk > static_cast<uint64_t>(m->tmax)) chunk = static_cast<uint64_t>(m->tmax);
   cudaStream_t st = m->ctx->stream;
@@ -1437,6 +1467,7 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   if (!m || steps == 0) return KIB_ERR_INVALID_ARGUMENT;
   if (m->pos + steps > static_cast<uint64_t>(m->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "decode exceeds cache capacity");
   if (steps > (1u << 20)) return KIB_ERR_INVALID_ARGUMENT;
+  if (int rc = check_tokens(m, &first_token, 1)) return rc;
   cudaStream_t st = m->ctx->stream;
   const bool use_pk = m->pk_on;
   if (use_pk) {
@@ -1549,6 +1580,7 @@ int kib_qwen35_mtp_forward(kib_qwen35* m, const int32_t* tokens, const float* h_
                            int32_t* argmax_out, float* h_nextn_out) {
   if (!m || !tokens || !h_rows || n < 1 || n > kMaxSmallT) return KIB_ERR_INVALID_ARGUMENT;
   if (!m->has_mtp) return fail(m, KIB_ERR_UNAVAILABLE, "model has no MTP/NextN layer");
+  if (int rc = check_tokens(m, tokens, n)) return rc;
   cudaStream_t st = m->ctx->stream;
   std::memcpy(m->h_pin + 16, tokens, n * sizeof(int32_t));
   m->h_pin[0] = static_cast<int>(position);
@@ -1572,6 +1604,7 @@ int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t
                         kib_generation_result* res) {
   if (!m || !rq || !rq->prompt_tokens || rq->prompt_count == 0 || !res) return KIB_ERR_INVALID_ARGUMENT;
   std::memset(res, 0, sizeof(*res));
+  if (int rc = check_tokens(m, rq->prompt_tokens, rq->prompt_count)) return rc;
   const uint64_t max_new = std::min<uint64_t>(rq->max_new_tokens, cap_out);
   if (rq->prompt_count + max_new + 8 > static_cast<uint64_t>(m->cap))
     return fail(m, KIB_ERR_INVALID_ARGUMENT, "prompt + max_new_tokens exceeds the attention capacity");

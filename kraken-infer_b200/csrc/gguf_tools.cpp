@@ -5,6 +5,7 @@
 // bench) can still write the benchmark's model file.
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <string>
 
 #include "gguf.hpp"
@@ -82,6 +83,21 @@ int kib_quantize_kquant(int type, const float* x, uint64_t n, void* out) {
     case 14: quantize_q6_k(x, static_cast<int64_t>(n), o); return KIB_OK;
     default: return KIB_ERR_INVALID_ARGUMENT;
   }
+}
+
+int kib_gguf_check(const char* path, char* err, int err_len, uint64_t* n_tensors) {
+  if (!path) return KIB_ERR_INVALID_ARGUMENT;
+  std::string e;
+  std::unique_ptr<GgufFile> g = GgufFile::open(path, &e);
+  if (!g) {
+    if (err && err_len > 0) {
+      std::strncpy(err, e.c_str(), static_cast<size_t>(err_len - 1));
+      err[err_len - 1] = 0;
+    }
+    return KIB_ERR_INVALID_ARGUMENT;
+  }
+  if (n_tensors) *n_tensors = static_cast<uint64_t>(g->tensors().size());
+  return KIB_OK;
 }
 
 }  // extern "C"

@@ -133,3 +133,13 @@ struct GemvDesc {
 cudaError_t gemv_launch(const GemvDesc& d, int num_sms, cudaStream_t st, std::string* why);
 
 }  // namespace kib
+
+// C-ABI argument checks (the reference's Status::unavailable / invalid_argument)
+#define KIB_REQUIRE_CTX(ctx)                       \
+  do {                                             \
+    if (!(ctx) || !(ctx)->stream) return KIB_ERR_UNAVAILABLE; \
+  } while (0)
+#define KIB_ARG(cond, msg)                                              \
+  do {                                                                  \
+    if (!(cond)) return set_error(ctx, KIB_ERR_INVALID_ARGUMENT, msg);  \
+  } while (0)

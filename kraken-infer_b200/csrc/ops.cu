@@ -665,14 +665,6 @@ int finish_op(kib_ctx* ctx, const char* what) {
 }  // namespace kib
 
 // =============================================================== C ABI
-#define KIB_REQUIRE_CTX(ctx)                       \
-  do {                                             \
-    if (!(ctx) || !(ctx)->stream) return KIB_ERR_UNAVAILABLE; \
-  } while (0)
-#define KIB_ARG(cond, msg)                                              \
-  do {                                                                  \
-    if (!(cond)) return set_error(ctx, KIB_ERR_INVALID_ARGUMENT, msg);  \
-  } while (0)
 
 extern "C" {
 

@@ -71,6 +71,8 @@ def load_tools_library(path: str = TOOLS_LIB_PATH) -> ctypes.CDLL:
     lib.kib_write_synthetic_qwen35.argtypes = [c_char_p, POINTER(SynthConfig), c_char_p, c_int]
     lib.kib_quantize_kquant.restype = c_int
     lib.kib_quantize_kquant.argtypes = [c_int, c_void_p, c_uint64, c_void_p]
+    lib.kib_gguf_check.restype = c_int
+    lib.kib_gguf_check.argtypes = [c_char_p, c_char_p, c_int, POINTER(c_uint64)]
     _tools = lib
     return lib
 
@@ -157,6 +159,22 @@ def _declare(lib):
         "kib_copy_f32_rows": (c_int, [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _U64]),
         "kib_copy_f32_rows_to_f16": (c_int, [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _U64]),
         "kib_argmax_f32_i32": (c_int, [_P, _P, _U64, _P, _P]),
+        "kib_copy_to_buffer_at": (c_int, [_P, _P, _U64, _P, _U64]),
+        "kib_copy_from_buffer_at": (c_int, [_P, _P, _U64, _P, _U64]),
+        "kib_copy_f32_region": (c_int, [_P, _P, _P, _U64, _U64, _U64]),
+        "kib_copy_f16_rows": (c_int, [_P, _P, _P, _U64, _U64, _U64, _U64, _U64, _U64]),
+        "kib_ssm_conv_f32": (c_int, [_P, _P, _P, _U64, _U64, _U64, _U64, _P]),
+        "kib_build_ssm_conv_state_f32": (c_int, [_P, _P, _U64, _P, _U64, _U64, _U64, _P]),
+        "kib_ssm_conv1_f32_stateful": (c_int, [_P, _P, _P, _P, _U64, _U64, _P]),
+        "kib_ssm_conv1_f32_stateful_at": (c_int, [_P, _P, _U64, _P, _P, _U64, _U64, _P]),
+        "kib_gated_delta_net_f32_in_place": (c_int, [_P, _P, _P, _P, _P, _P, _P, _U64, _U64, _U64, _P]),
+        "kib_gated_delta_net_f32_in_place_at": (c_int, [_P, _P, _P, _P, _P, _P, _P, _U64, _U64, _U64, _U64, _P]),
+        "kib_gated_delta_net_f32_batched_in_place_at": (c_int, [_P, _P, _P, _P, _P, _P, _P, _U64, _U64, _U64, _U64,
+                                                                _U64, _P]),
+        "kib_argmax_prob_f32_i32": (c_int, [_P, _P, _U64, _P, _P]),
+        "kib_rms_norm_f32_f32": (c_int, [_P, _P, _P, _U64, c_float, _P]),
+        "kib_qk_norm_f32_f32": (c_int, [_P, _P, _P, _U64, _U64, c_float]),
+        "kib_attention_f32_f16_kv": (c_int, [_P, _P, _P, _P, _U64, _U64, _U64, _U64, _U64, _U64, _P]),
         "kib_qwen35_load": (c_int, [_P, c_char_p, POINTER(Qwen35Options), POINTER(c_void_p)]),
         "kib_qwen35_free": (None, [_P]),
         "kib_qwen35_get_plan": (c_int, [_P, POINTER(Qwen35Plan)]),
@@ -167,6 +185,7 @@ def _declare(lib):
         "kib_qwen35_decode_greedy": (c_int, [_P, c_int32, _U64, _P]),
         "kib_qwen35_position": (c_uint64, [_P]),
         "kib_qwen35_set_position": (c_int, [_P, _U64]),
+        "kib_qwen35_debug_stall": (c_int, [_P, c_uint32, c_int]),
         "kib_qwen35_state_io": (c_int, [_P, c_int, _P, _P, _P, _P, _P, _P, _P]),
         "kib_qwen35_mtp_forward": (c_int, [_P, _P, _P, _U64, _U64, _P, _P]),
         "kib_synth_default": (None, [POINTER(SynthConfig)]),
@@ -175,6 +194,9 @@ def _declare(lib):
     }
     for name in ("q4_k", "q5_k", "q6_k"):
         sig[f"kib_matvec_{name}_f32_device"] = (c_int, [_P, _P, _U64, _U64, _P, _P])
+        sig[f"kib_matvec_{name}_f32_top1"] = (c_int, [_P, _P, _U64, _U64, _P, _P, _P])
+        sig[f"kib_matvec_{name}_f32_argmax"] = (c_int, [_P, _P, _U64, _U64, _P, _P])
+        sig[f"kib_dequantize_row_{name}_f32"] = (c_int, [_P, _P, _U64, _U64, _P])
         sig[f"kib_matmul_{name}_f32_device"] = (c_int, [_P, _P, _U64, _U64, _U64, _P, _P])
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -389,6 +411,18 @@ def write_synthetic_qwen35(path: str, **overrides) -> str:
     if rc != KIB_OK:
         raise KibError(rc, err.value.decode())
     return path
+
+
+def gguf_check(path: str):
+    """Host-only validation of a GGUF file; returns its tensor count or raises
+    KibError(KIB_ERR_INVALID_ARGUMENT, reason)."""
+    lib = load_tools_library()
+    err = ctypes.create_string_buffer(512)
+    n = c_uint64(0)
+    rc = lib.kib_gguf_check(path.encode(), err, 512, byref(n))
+    if rc != KIB_OK:
+        raise KibError(rc, err.value.decode())
+    return n.value
 
 
 def quantize(qtype: int, x):

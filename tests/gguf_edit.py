@@ -24,9 +24,11 @@ class GGUF:
             k = self._str()
             self.kv[k] = self._value(self._u32())
         self.tensors = {}
+        self.dim_offsets = {}
         for _ in range(n_tensors):
             name = self._str()
             nd = self._u32()
+            self.dim_offsets[name] = [self._o + 8 * d for d in range(nd)]
             shape = [self._u64() for _ in range(nd)]
             typ = self._u32()
             off = self._u64()
@@ -60,6 +62,12 @@ class GGUF:
         v = struct.unpack_from(fmt, self._b, self._o)[0]
         self._o += struct.calcsize(fmt)
         return v
+
+    def set_dim(self, name, d, value):
+        """Rewrites dimension d of tensor `name` in the tensor directory."""
+        with open(self.path, "r+b") as f:
+            f.seek(self.dim_offsets[name][d])
+            f.write(struct.pack("<Q", value))
 
     def replace(self, name, data):
         """Overwrites the stored bytes of tensor `name` (same size)."""
