@@ -38,7 +38,7 @@ cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const f
                             int y_ld, const float* resid, cudaStream_t st);
 cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident, int rows, int cols, const float* x,
                              int x_ld, int T, float* y, int y_ld, const float* resid, __half* w16, __half* x16,
-                             bool convert_x, int num_sms, cudaStream_t st);
+                             bool convert_x, int num_sms, cudaStream_t st, int* err);
 cudaError_t kquant_to_f16_launch(int type, const void* w, int rows, int cols, __half* out, int num_sms,
                                  cudaStream_t st);
 cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const int* ids, int T, float* out,
@@ -421,7 +421,7 @@ void gemm(Enq& q, const DevT& w, const float* x, int x_ld, int T, float* y, int 
           bool same_x = false) {
   if (q.m->d_w16 && w.cols() % 64 == 0 && x_ld % 4 == 0)
     q.run(gemm_f16w_launch(w.type, w.p, w.h, w.rows(), w.cols(), x, x_ld, T, y, y_ld, resid, q.m->d_w16, q.m->d_x16,
-                           !same_x, q.m->ctx->num_sms, q.st),
+                           !same_x, q.m->ctx->num_sms, q.st, q.m->ctx->d_err),
           "gemm_f16w");
   else
     q.run(gemm_f16_launch(w.type, w.p, w.rows(), w.cols(), x, x_ld, T, y, y_ld, resid, q.st), "gemm");

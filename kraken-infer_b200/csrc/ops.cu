@@ -11,6 +11,9 @@
 #include "kib_ctx.cuh"
 #include "kquant_gemv2.cuh"
 #include "layer_kernels.cuh"
+#include "gemm_tc.cuh"
+
+#include <cudaTypedefs.h>
 
 using namespace kib;
 
@@ -580,9 +583,63 @@ cudaError_t kquant_to_f16_launch(int type, const void* w, int rows, int cols, __
 // convert_x false: x16 (T * cols halves) already holds this x, because the
 // previous GEMM read the same input.  The tile is the largest that still
 // fills two CTA slots per SM; the two smaller tiles run four warps each.
+// ---- tcgen05 GEMM host side: 2-D tensor maps over row-major f16 matrices
+namespace tc_host {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// [rows][cols] halves, boxes of box_rows x 64 columns, 128-byte swizzle,
+// out-of-range rows read as zeros.
+bool f16_tensor_map(CUtensorMap* map, const __half* base, int rows, int cols, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || (cols * 2) % 16) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool gemm_tc_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("KIB_GEMM_TC");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <int BN>
+cudaError_t gemm_tc_launch(const __half* w16, const __half* x16, const GemmTcParams& p, cudaStream_t st) {
+  CUtensorMap wm, xm;
+  if (!f16_tensor_map(&wm, w16, p.rows, p.cols, kTcBM) || !f16_tensor_map(&xm, x16, p.T, p.cols, BN))
+    return cudaErrorInvalidValue;
+  static bool cfg = false;
+  constexpr size_t smem = gemm_tc_smem<BN>();
+  if (!cfg) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cfg = true;
+  }
+  return launch_pdl(gemm_tc_kernel<BN>, dim3((p.rows + kTcBM - 1) / kTcBM, (p.T + BN - 1) / BN), dim3(kTcThreads),
+                    smem, st, wm, xm, p);
+}
+}  // namespace tc_host
+
 cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident, int rows, int cols, const float* x,
                              int x_ld, int T, float* y, int y_ld, const float* resid, __half* w16, __half* x16,
-                             bool convert_x, int num_sms, cudaStream_t st) {
+                             bool convert_x, int num_sms, cudaStream_t st, int* err) {
   if (cols % kGfK != 0 || x_ld % 4 != 0) return cudaErrorInvalidValue;
   cudaError_t e;
   if (!w16_resident) {
@@ -595,8 +652,23 @@ cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident
     e = launch_pdl(x_to_f16_kernel, dim3(x_grid), dim3(256), 0, st, x, x_ld, T, cols, x16);
     if (e != cudaSuccess) return e;
   }
+  const __half* wsrc = w16_resident ? w16_resident : w16;
+  if (tc_host::gemm_tc_enabled() && rows >= kTcBM && T >= 128 && cols % kTcBK == 0) {
+    // tcgen05 path; the mma.sync tiles below remain for small or unaligned cases
+    GemmTcParams tp;
+    tp.rows = rows;
+    tp.cols = cols;
+    tp.T = T;
+    tp.y = y;
+    tp.y_ld = y_ld;
+    tp.resid = resid;
+    tp.err = err;
+    e = tc_host::gemm_tc_launch<128>(wsrc, x16, tp, st);
+    if (e != cudaErrorInvalidValue) return e;
+    cudaGetLastError();
+  }
   GemmF16Params p;
-  p.w = w16_resident ? w16_resident : w16;
+  p.w = wsrc;
   p.x = x16;
   p.rows = rows;
   p.cols = cols;
