@@ -32,6 +32,7 @@
 #include "kib_ctx.cuh"
 #include "layer_kernels.cuh"
 #include "decode_persistent.cuh"
+#include "gdn_chunk.cuh"
 
 namespace kib {
 cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const float* x, int x_ld, int T, float* y,
@@ -111,6 +112,7 @@ struct kib_qwen35 {
   float *d_part = nullptr;
   __half *d_w16 = nullptr, *d_x16 = nullptr;  // prefill GEMM scratch: one f16 weight matrix, one f16 x
   void* d_w16_all = nullptr;                  // resident f16 prefill weights (DevT::h points inside)
+  float* d_gdn_ws = nullptr;                  // chunked delta rule: Tb, P, Kt, G per (value head, 64-token chunk)
   unsigned* d_attn_cnt = nullptr;
   float *d_cand_max = nullptr, *d_cand_sum = nullptr;
   int* d_cand_idx = nullptr;
@@ -400,6 +402,15 @@ void head_small(Enq& q, int T, const float* x, const DevT& norm_w, const DevT& h
   q.run(gemv_launch(d, m->ctx->num_sms, q.st, &why), "lm_head");
 }
 
+// KIB_GDN_CHUNKED=0: prefill keeps the token-by-token delta-rule scan (A/B runs).
+bool gdn_chunked_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("KIB_GDN_CHUNKED");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 void main_layers_small(Enq& q, int T, const int* pos) {
   kib_qwen35* m = q.m;
   for (const LayerW& L : m->layers) {
@@ -453,7 +464,39 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
   g.value_heads = m->lvh;
   g.eps = m->eps;
   g.trace = nullptr;
-  if (m->lhd == 128 && m->lkh <= m->lvh && m->C % 4 == 0) {
+  if (m->lhd == 128 && m->lkh <= m->lvh && m->C % 4 == 0 && T >= kGc && gdn_chunked_enabled()) {
+    // token-parallel norms and gate/beta, then the chunked delta rule: the
+    // per-chunk matrices for every chunk at once, then the scan over chunks
+    q.run(launch_pdl(gdn_prep_kernel, dim3(T, m->lkh), dim3(128), 0, q.st, m->d_qkv, m->C, m->d_alpha, m->d_beta, m->lvh,
+                     L.dt_bias.f(), L.ssm_a.f(), m->lkh, m->lvh, m->eps),
+          "gdn_prep");
+    static bool chunk_cfg = false;
+    if (!chunk_cfg) {
+      q.run(cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kGcPrepSmem)),
+            "gdn_chunk_attr");
+      q.run(cudaFuncSetAttribute(gdn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kGcScanSmem)),
+            "gdn_chunk_attr");
+      chunk_cfg = true;
+    }
+    GdnChunkParams gc;
+    gc.conv_out = m->d_qkv;
+    gc.C = m->C;
+    gc.g = m->d_alpha;
+    gc.beta = m->d_beta;
+    gc.ld_ba = m->lvh;
+    gc.state = g.state;
+    gc.out = m->d_y;
+    gc.ws = m->d_gdn_ws;
+    gc.T = T;
+    gc.key_heads = m->lkh;
+    gc.value_heads = m->lvh;
+    q.run(launch_pdl(gdn_chunk_prep_kernel, dim3(m->lvh, (T + kGc - 1) / kGc), dim3(256), kGcPrepSmem, q.st, gc),
+          "gdn_chunk_prep");
+    q.run(launch_pdl(gdn_chunk_scan_kernel, dim3(m->lvh, kGcD / kGcRows), dim3(256), kGcScanSmem, q.st, gc),
+          "gdn_chunk_scan");
+  } else if (m->lhd == 128 && m->lkh <= m->lvh && m->C % 4 == 0) {
     // token-parallel norms and gate/beta first, then the sequential scan alone
     q.run(launch_pdl(gdn_prep_kernel, dim3(T, m->lkh), dim3(128), 0, q.st, m->d_qkv, m->C, m->d_alpha, m->d_beta, m->lvh,
                      L.dt_bias.f(), L.ssm_a.f(), m->lkh, m->lvh, m->eps),
@@ -1206,6 +1249,7 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
             dalloc(&m->d_w16, std::max<uint64_t>({C, 2 * AD, I, VD, H, KD}) * std::max<uint64_t>({H, I, VD, AD})) ==
                 cudaSuccess &&
             dalloc(&m->d_x16, T * std::max<uint64_t>({2 * H, I, VD, AD})) == cudaSuccess &&
+            dalloc(&m->d_gdn_ws, static_cast<size_t>(lvh) * ((T + kGc - 1) / kGc) * kGcWs) == cudaSuccess &&
             dalloc(&m->d_part, static_cast<size_t>(m->nsplit) * kMaxSmallT * m->heads * (kHd + 2)) == cudaSuccess &&
             dalloc(&m->d_attn_cnt, 64) == cudaSuccess && dalloc(&m->d_head_cnt, 4) == cudaSuccess &&
             dalloc(&m->d_cand_max, 1024 * kGemvMaxTok) == cudaSuccess &&
@@ -1298,7 +1342,7 @@ void kib_qwen35_free(kib_qwen35* m) {
                   m->d_logits, m->d_e, m->d_cat, m->d_hm, m->d_hm1, m->d_mtp_h, m->d_part, m->d_attn_cnt,
                   m->d_head_cnt, m->d_cand_max, m->d_cand_sum, m->d_cand_idx, m->d_pos, m->d_mtp_pos,
                   m->d_tokens, m->d_argmax, m->d_prob, m->d_log, m->d_step, m->d_mtp_tok, m->d_trace,
-                  m->d_w16, m->d_x16, m->d_w16_all};
+                  m->d_w16, m->d_x16, m->d_w16_all, m->d_gdn_ws};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (m->h_pin) cudaFreeHost(m->h_pin);

@@ -1,0 +1,344 @@
+// gdn_chunk.cuh -- chunked delta rule for prefill (T >= 64 tokens).
+//
+// The reference runs the gated delta rule token by token
+// (gated_delta_net_f32_batched_qwen35, mps_backend.mm:2307-2374):
+//   S_v *= exp(g);  u = (v_v - S_v . k) * beta;  S_v += u * k;  y_v = S_v . q / sqrt(128)
+// for every value row v of a head's 128 x 128 state.  Over a chunk of C = 64
+// tokens with log-decay prefix sums G_i = g_1 + .. + g_i the same recurrence
+// has a closed form (the WY / UT representation of a product of rank-one
+// updates).  With S0 the state before the chunk,
+//   u_i = beta_i (v_i - e^{G_i} S0 k_i - sum_{j<i} e^{G_i - G_j} (k_j . k_i) u_j)
+// i.e. (I + L) U = diag(beta) (V - diag(e^G) K S0^T),
+//   L_ij = beta_i e^{G_i - G_j} (k_i . k_j) for j < i,
+// so with Tb = (I + L)^{-1} diag(beta) and Kt = Tb diag(e^G) K:
+//   U   = Tb V - Kt S0^T
+//   Y   = (diag(e^G) Q S0^T + P U) / sqrt(128),  P_ij = e^{G_i - G_j} (q_i . k_j), j <= i
+//   S_C = e^{G_C} S0 + U^T diag(e^{G_C - G}) K.
+// gdn_chunk_prep_kernel computes Tb, P, Kt and G for every (head, chunk) at
+// once -- they do not depend on the state -- and gdn_chunk_scan_kernel walks
+// the chunks in order for 16 value rows of one head per CTA: the per-token
+// dependent chain of the reference becomes 16 steps of small fp32 matrix
+// products.  Same arithmetic type (fp32) as the reference; only the order of
+// the roundings differs.  Tokens past the end of the prompt are zero (beta = 0
+// and g = 0), so they contribute nothing to U, Y or the state.
+#pragma once
+
+#include "kib_common.cuh"
+
+namespace kib {
+
+constexpr int kGc = 64;     // tokens per chunk
+constexpr int kGcD = 128;   // head dimension (keys and values)
+constexpr int kGcRows = 16; // value rows per scan CTA
+constexpr int kGcWs = kGc * kGc * 2 + kGc * kGcD + kGc;  // workspace floats per (head, chunk)
+
+struct GdnChunkParams {
+  const float* conv_out;  // [T][C]: q | k (L2-normalised) | v
+  int C;
+  const float* g;         // [T][ld_ba] log-decay (softplus(alpha + dt_bias) * ssm_a)
+  const float* beta;      // [T][ld_ba] sigmoid(beta)
+  int ld_ba;
+  float* state;           // [value_heads][128][128]
+  float* out;             // [T][value_heads * 128]
+  float* ws;              // [value_heads][nchunks][kGcWs]
+  int T;
+  int key_heads;
+  int value_heads;
+};
+
+// 16-byte global -> shared copy without a register destination; valid false
+// writes zeros (source size 0), so every copy of a chunk is in flight at once.
+KIB_DEV void gc_cp16(void* sdst, const void* gsrc, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(sdst)), "l"(gsrc), "r"(valid ? 16 : 0)
+               : "memory");
+}
+KIB_DEV void gc_cp_wait() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- prep
+// One CTA per (value head, chunk), 256 threads.
+constexpr int kGcTs = 68;  // padded token stride of the transposed q/k tiles
+constexpr size_t kGcPrepSmem = (2 * kGcD * kGcTs + 2 * kGc * kGcD + 2 * kGc * (kGc + 1) + 3 * kGc) * sizeof(float);
+
+__global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const __grid_constant__ GdnChunkParams p) {
+  extern __shared__ __align__(16) float gc_sm[];
+  float* kT = gc_sm;                      // [128][68]: k^T
+  float* qT = kT + kGcD * kGcTs;          // [128][68]: q^T
+  float* kr = qT + kGcD * kGcTs;          // [64][128]: k rows
+  float* qr = kr + kGc * kGcD;            // [64][128]: q rows
+  float* Lm = qr + kGc * kGcD;            // [64][65]: L, then X = (I + L)^{-1}
+  float* Xm = Lm + kGc * (kGc + 1);       // [64][65]
+  float* G = Xm + kGc * (kGc + 1);        // [64]
+  float* bt = G + kGc;                    // [64]
+  float* eG = bt + kGc;                   // [64]
+  const int h = blockIdx.x, c = blockIdx.y, tid = threadIdx.x;
+  const int kh = h % p.key_heads;
+  const int t0 = c * kGc, n = min(kGc, p.T - t0);
+  const int key_dim = p.key_heads * kGcD;
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = tid; i < kGc * kGcD / 4; i += 256) {
+    const int t = i >> 5, d4 = i & 31;
+    const bool ok = t < n;
+    const float* row = p.conv_out + static_cast<size_t>(t0 + (ok ? t : 0)) * p.C;
+    gc_cp16(qr + t * kGcD + 4 * d4, row + kh * kGcD + 4 * d4, ok);
+    gc_cp16(kr + t * kGcD + 4 * d4, row + key_dim + kh * kGcD + 4 * d4, ok);
+  }
+  if (tid < kGc) {
+    const bool ok = tid < n;
+    G[tid] = ok ? p.g[static_cast<size_t>(t0 + tid) * p.ld_ba + h] : 0.0f;
+    bt[tid] = ok ? p.beta[static_cast<size_t>(t0 + tid) * p.ld_ba + h] : 0.0f;
+  }
+  gc_cp_wait();
+  __syncthreads();
+  // transposed copies for the K K^T / Q K^T tiles
+  for (int i = tid; i < kGc * kGcD; i += 256) {
+    const int t = i & 63, d = i >> 6;
+    kT[d * kGcTs + t] = kr[t * kGcD + d];
+    qT[d * kGcTs + t] = qr[t * kGcD + d];
+  }
+  if (tid == 0) {
+    float acc = 0.0f;
+    for (int i = 0; i < kGc; ++i) {
+      acc += G[i];
+      G[i] = acc;
+    }
+  }
+  __syncthreads();
+  if (tid < kGc) eG[tid] = expf(G[tid]);
+  // KK and QK in 4 x 4 register tiles: thread (ti, tj) owns rows 4ti.., cols 4tj..
+  const int ti = tid >> 4, tj = tid & 15;
+  float kk[4][4], qk[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) kk[a][b] = qk[a][b] = 0.0f;
+#pragma unroll 4
+  for (int d = 0; d < kGcD; ++d) {
+    const float4 ki = *reinterpret_cast<const float4*>(kT + d * kGcTs + 4 * ti);
+    const float4 qi = *reinterpret_cast<const float4*>(qT + d * kGcTs + 4 * ti);
+    const float4 kj = *reinterpret_cast<const float4*>(kT + d * kGcTs + 4 * tj);
+    const float kia[4] = {ki.x, ki.y, ki.z, ki.w}, qia[4] = {qi.x, qi.y, qi.z, qi.w};
+    const float kja[4] = {kj.x, kj.y, kj.z, kj.w};
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        kk[a][b] = fmaf(kia[a], kja[b], kk[a][b]);
+        qk[a][b] = fmaf(qia[a], kja[b], qk[a][b]);
+      }
+  }
+  __syncthreads();
+  float* ws = p.ws + (static_cast<size_t>(h) * gridDim.y + c) * kGcWs;
+  float* wTb = ws;
+  float* wP = ws + kGc * kGc;
+  float* wKt = wP + kGc * kGc;
+  float* wG = wKt + kGc * kGcD;
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int i = 4 * ti + a, j = 4 * tj + b;
+      const float dec = j <= i ? expf(G[i] - G[j]) : 0.0f;
+      Lm[i * (kGc + 1) + j] = j < i ? bt[i] * dec * kk[a][b] : 0.0f;
+      wP[i * kGc + j] = dec * qk[a][b];
+    }
+  __syncthreads();
+  // X = (I + L)^{-1} by forward substitution, row by row: four threads per
+  // column split the sum over j < i
+  {
+    const int col = tid >> 2, part = tid & 3;
+    for (int i = 0; i < kGc; ++i) {
+      float s = 0.0f;
+      for (int j = part; j < i; j += 4) s = fmaf(Lm[i * (kGc + 1) + j], Xm[j * (kGc + 1) + col], s);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      if (part == 0) Xm[i * (kGc + 1) + col] = (i == col ? 1.0f : 0.0f) - s;
+      __syncthreads();
+    }
+  }
+  // Tb = X diag(beta), then Kt = Tb diag(e^G) K (thread: 4 rows x 8 columns)
+  for (int e = tid; e < kGc * kGc; e += 256) {
+    const int i = e >> 6, j = e & 63;
+    const float v = Xm[i * (kGc + 1) + j] * bt[j];
+    wTb[e] = v;
+    Lm[i * (kGc + 1) + j] = v * eG[j];  // Tb diag(e^G), reused below
+  }
+  if (tid < kGc) wG[tid] = G[tid];
+  __syncthreads();
+  {
+    const int ig = tid >> 4, dg = tid & 15;
+    float acc[4][8];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 8; ++b) acc[a][b] = 0.0f;
+#pragma unroll 2
+    for (int j = 0; j < kGc; ++j) {
+      const float4 k0 = *reinterpret_cast<const float4*>(kr + j * kGcD + 8 * dg);
+      const float4 k1 = *reinterpret_cast<const float4*>(kr + j * kGcD + 8 * dg + 4);
+      const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const float t = Lm[(4 * ig + a) * (kGc + 1) + j];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) acc[a][b] = fmaf(t, kv[b], acc[a][b]);
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      float* o = wKt + (4 * ig + a) * kGcD + 8 * dg;
+      *reinterpret_cast<float4*>(o) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+      *reinterpret_cast<float4*>(o + 4) = make_float4(acc[a][4], acc[a][5], acc[a][6], acc[a][7]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- scan
+// One CTA per (value head, 16 value rows), 256 threads; walks the chunks.
+constexpr int kGcSr = kGcD + 4;  // padded state row
+constexpr size_t kGcScanSmem =
+    (3 * kGc * kGcD + 2 * kGc * kGc + kGc * kGcRows * 4 + kGcRows * kGcSr + 2 * kGc) * sizeof(float);
+
+__global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(const __grid_constant__ GdnChunkParams p) {
+  extern __shared__ __align__(16) float gs_sm[];
+  float* sKt = gs_sm;                 // [64][128]
+  float* sKd = sKt + kGc * kGcD;      // [64][128]: e^{G_C - G_j} k_j
+  float* sQg = sKd + kGc * kGcD;      // [64][128]: e^{G_i} q_i
+  float* sTb = sQg + kGc * kGcD;      // [64][64]
+  float* sP = sTb + kGc * kGc;        // [64][64]
+  float* sV = sP + kGc * kGc;         // [64][16]
+  float* sX1 = sV + kGc * kGcRows;    // [64][16]
+  float* sX2 = sX1 + kGc * kGcRows;   // [64][16]
+  float* sU = sX2 + kGc * kGcRows;    // [64][16]
+  float* sS = sU + kGc * kGcRows;     // [16][132]: the state rows
+  float* sG = sS + kGcRows * kGcSr;   // [64]
+  float* sE = sG + kGc;               // [64]: e^{G}
+  const int h = blockIdx.x, r0 = blockIdx.y * kGcRows, tid = threadIdx.x;
+  const int kh = h % p.key_heads;
+  const int key_dim = p.key_heads * kGcD;
+  const int nchunks = (p.T + kGc - 1) / kGc;
+  float* S = p.state + (static_cast<size_t>(h) * kGcD + r0) * kGcD;
+  for (int i = tid; i < kGcRows * kGcD / 4; i += 256) {
+    const int r = i >> 5, d4 = i & 31;
+    *reinterpret_cast<float4*>(sS + r * kGcSr + 4 * d4) = reinterpret_cast<const float4*>(S + r * kGcD)[d4];
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  const float scale = 1.0f / sqrtf(static_cast<float>(kGcD));
+  const size_t out_ld = static_cast<size_t>(p.value_heads) * kGcD;
+  const int r = tid & 15, ig = tid >> 4;  // output mapping: value row r, chunk rows 4ig..4ig+3
+  for (int c = 0; c < nchunks; ++c) {
+    const int t0 = c * kGc, n = min(kGc, p.T - t0);
+    const float* ws = p.ws + (static_cast<size_t>(h) * nchunks + c) * kGcWs;
+    for (int i = tid; i < kGc * kGc / 4; i += 256) {
+      gc_cp16(sTb + 4 * i, ws + 4 * i, true);
+      gc_cp16(sP + 4 * i, ws + kGc * kGc + 4 * i, true);
+    }
+    for (int i = tid; i < kGc * kGcD / 4; i += 256) {
+      const int t = i >> 5, d4 = i & 31;
+      const bool ok = t < n;
+      const float* row = p.conv_out + static_cast<size_t>(t0 + (ok ? t : 0)) * p.C;
+      gc_cp16(sKt + 4 * i, ws + 2 * kGc * kGc + 4 * i, true);
+      gc_cp16(sQg + 4 * i, row + kh * kGcD + 4 * d4, ok);
+      gc_cp16(sKd + 4 * i, row + key_dim + kh * kGcD + 4 * d4, ok);
+    }
+    {
+      const int t = tid >> 2, q4 = tid & 3;  // 64 tokens x 4 pieces of the CTA's 16 value rows
+      const bool ok = t < n;
+      gc_cp16(sV + t * kGcRows + 4 * q4,
+              p.conv_out + static_cast<size_t>(t0 + (ok ? t : 0)) * p.C + 2 * key_dim + h * kGcD + r0 + 4 * q4, ok);
+    }
+    if (tid < kGc / 4) gc_cp16(sG + 4 * tid, ws + 2 * kGc * kGc + kGc * kGcD + 4 * tid, true);
+    gc_cp_wait();
+    __syncthreads();
+    const float gend = sG[kGc - 1];
+    if (tid < kGc) sE[tid] = expf(sG[tid]);
+    // scale in place: k rows by e^{G_C - G_j}, q rows by e^{G_i}
+    for (int i = tid; i < kGc * kGcD / 4; i += 256) {
+      const int t = i >> 5;
+      const float fk = expf(gend - sG[t]), fq = expf(sG[t]);
+      float4 kq = reinterpret_cast<float4*>(sKd)[i], qq = reinterpret_cast<float4*>(sQg)[i];
+      reinterpret_cast<float4*>(sKd)[i] = make_float4(kq.x * fk, kq.y * fk, kq.z * fk, kq.w * fk);
+      reinterpret_cast<float4*>(sQg)[i] = make_float4(qq.x * fq, qq.y * fq, qq.z * fq, qq.w * fq);
+    }
+    __syncthreads();
+    // X1 = Kt S0^T, X2 = (e^G Q) S0^T for rows 4ig.. and value row r
+    {
+      float x1[4] = {0.f, 0.f, 0.f, 0.f}, x2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int d = 0; d < kGcD; d += 4) {
+        const float4 s4 = *reinterpret_cast<const float4*>(sS + r * kGcSr + d);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const float4 kt = *reinterpret_cast<const float4*>(sKt + (4 * ig + a) * kGcD + d);
+          const float4 qg = *reinterpret_cast<const float4*>(sQg + (4 * ig + a) * kGcD + d);
+          x1[a] = fmaf(kt.x, s4.x, fmaf(kt.y, s4.y, fmaf(kt.z, s4.z, fmaf(kt.w, s4.w, x1[a]))));
+          x2[a] = fmaf(qg.x, s4.x, fmaf(qg.y, s4.y, fmaf(qg.z, s4.z, fmaf(qg.w, s4.w, x2[a]))));
+        }
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        sX1[(4 * ig + a) * kGcRows + r] = x1[a];
+        sX2[(4 * ig + a) * kGcRows + r] = x2[a];
+      }
+    }
+    __syncthreads();
+    // U = Tb V - X1
+    {
+      float u[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) u[a] = -sX1[(4 * ig + a) * kGcRows + r];
+#pragma unroll 4
+      for (int j = 0; j < kGc; ++j) {
+        const float v = sV[j * kGcRows + r];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) u[a] = fmaf(sTb[(4 * ig + a) * kGc + j], v, u[a]);
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a) sU[(4 * ig + a) * kGcRows + r] = u[a];
+    }
+    __syncthreads();
+    // Y = (X2 + P U) * scale
+    {
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const int i = 4 * ig + a;
+        float y = sX2[i * kGcRows + r];
+        for (int j = 0; j <= i; ++j) y = fmaf(sP[i * kGc + j], sU[j * kGcRows + r], y);
+        if (i < n) p.out[static_cast<size_t>(t0 + i) * out_ld + h * kGcD + r0 + r] = y * scale;
+      }
+    }
+    // S = e^{G_C} S + U^T Kd (thread: value row r, columns 8dg..8dg+7)
+    {
+      const int dg = tid >> 4;
+      const float eg = expf(gend);
+      float acc[8];
+      const float4 a0 = *reinterpret_cast<const float4*>(sS + r * kGcSr + 8 * dg);
+      const float4 a1 = *reinterpret_cast<const float4*>(sS + r * kGcSr + 8 * dg + 4);
+      acc[0] = a0.x * eg; acc[1] = a0.y * eg; acc[2] = a0.z * eg; acc[3] = a0.w * eg;
+      acc[4] = a1.x * eg; acc[5] = a1.y * eg; acc[6] = a1.z * eg; acc[7] = a1.w * eg;
+#pragma unroll 4
+      for (int j = 0; j < kGc; ++j) {
+        const float u = sU[j * kGcRows + r];
+        const float4 k0 = *reinterpret_cast<const float4*>(sKd + j * kGcD + 8 * dg);
+        const float4 k1 = *reinterpret_cast<const float4*>(sKd + j * kGcD + 8 * dg + 4);
+        acc[0] = fmaf(u, k0.x, acc[0]); acc[1] = fmaf(u, k0.y, acc[1]);
+        acc[2] = fmaf(u, k0.z, acc[2]); acc[3] = fmaf(u, k0.w, acc[3]);
+        acc[4] = fmaf(u, k1.x, acc[4]); acc[5] = fmaf(u, k1.y, acc[5]);
+        acc[6] = fmaf(u, k1.z, acc[6]); acc[7] = fmaf(u, k1.w, acc[7]);
+      }
+      __syncthreads();  // every thread has read the old state rows (X1/X2 long done; the row is shared by 16 threads)
+      *reinterpret_cast<float4*>(sS + r * kGcSr + 8 * dg) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(sS + r * kGcSr + 8 * dg + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+    __syncthreads();
+  }
+  for (int i = tid; i < kGcRows * kGcD / 4; i += 256) {
+    const int rr = i >> 5, d4 = i & 31;
+    reinterpret_cast<float4*>(S + rr * kGcD)[d4] = *reinterpret_cast<const float4*>(sS + rr * kGcSr + 4 * d4);
+  }
+}
+
+}  // namespace kib
