@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const __grid_consta
   __syncthreads();
   // transposed copies for the K K^T / Q K^T tiles
   for (int i = tid; i < kGc * kGcD; i += 256) {
-    const int t = i & 63, d = i >> 6;
+    const int d = i & 127, t = i >> 7;  // lanes along d: conflict-free reads, 4-way writes (stride 68)
     kT[d * kGcTs + t] = kr[t * kGcD + d];
     qT[d * kGcTs + t] = qr[t * kGcD + d];
   }
