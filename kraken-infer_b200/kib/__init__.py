@@ -16,7 +16,7 @@ import os
 from ctypes import POINTER, byref, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_uint16, c_uint32, c_uint64, c_void_p
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libkib.so")
+LIB_PATH = os.environ.get("KIB_LIBRARY", os.path.join(os.path.dirname(_HERE), "lib", "libkib.so"))
 TOOLS_LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libkib_gguf.so")
 HEADER_PATH = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "include", "kib.h")
 
