@@ -372,6 +372,32 @@ int kib_qwen35_state_io(kib_qwen35* model, int write_into_model, uint16_t* k_cac
 int kib_qwen35_mtp_forward(kib_qwen35* model, const int32_t* tokens, const float* h_rows, uint64_t n,
                            uint64_t position, int32_t* argmax_out, float* h_nextn_out);
 
+/* ------------------------------------------------------- batched decode
+ * Independent sequences decoded together, one token per sequence per step:
+ * the plan's sequence_slots (qwen35_runtime.hpp:20, qwen35_runtime.cpp:
+ * 4478-4479), which the reference reserves but does not run.  A batch owns
+ * each slot's KV cache (context_tokens positions), conv and delta-rule state;
+ * it shares the model's weights and scratch, so calls on one model must not
+ * overlap.  The projections of a step are one GEMM over the slots: every slot
+ * gets the reference's M > 8 matmul numerics (half-rounded weights and
+ * inputs, fp32 accumulation), hence 9 <= slots <= the prefill chunk. */
+typedef struct kib_qwen35_batch kib_qwen35_batch;
+int kib_qwen35_batch_create(kib_qwen35* model, uint64_t slots, uint64_t context_tokens, uint64_t max_steps,
+                            kib_qwen35_batch** out);
+void kib_qwen35_batch_free(kib_qwen35_batch* batch);
+/* Prefills one slot through the model's own prefill (the model's
+ * single-sequence state is reset and then holds this prompt), copies the
+ * caches into the slot and returns the prompt's greedy next token. */
+int kib_qwen35_batch_prefill(kib_qwen35_batch* batch, uint64_t slot, const int32_t* tokens, uint64_t count,
+                             int32_t* next_token);
+/* steps greedy steps for every slot, starting from first_tokens[slots];
+ * tokens_out[step * slots + slot] receives the argmax of each step. */
+int kib_qwen35_batch_decode(kib_qwen35_batch* batch, const int32_t* first_tokens, uint64_t steps,
+                            int32_t* tokens_out);
+uint64_t kib_qwen35_batch_position(const kib_qwen35_batch* batch, uint64_t slot);
+/* The logits of the last batched step, [slots][vocab] (host copy). */
+int kib_qwen35_batch_logits(kib_qwen35_batch* batch, float* logits_out);
+
 /* Synthetic BASELINE-shaped Qwen3.5 GGUF writer (random-init weights, Q4_K_M mix). */
 typedef struct kib_synth_config {
   uint64_t hidden, layers, intermediate, vocab, heads, kv_heads, head_dim;

@@ -33,6 +33,7 @@
 #include "layer_kernels.cuh"
 #include "decode_persistent.cuh"
 #include "gdn_chunk.cuh"
+#include "batch_kernels.cuh"
 
 namespace kib {
 cudaError_t gemm_f16_launch(int type, const void* w, int rows, int cols, const float* x, int x_ld, int T, float* y,
@@ -254,7 +255,7 @@ void linear_block_small(Enq& q, const LayerW& L, int T, const float* x_in, float
               {&L.zgate, m->d_z, m->VD, kEpiStore},
               {&L.beta, m->d_beta, m->lvh, kEpiStore},
               {&L.alpha, m->d_alpha, m->lvh, kEpiStore}});
-  GdnParams g;
+  GdnParams g = {};
   g.conv_out = m->d_qkv;
   g.C = m->C;
   g.beta_raw = m->d_beta;
@@ -282,7 +283,7 @@ void linear_block_small(Enq& q, const LayerW& L, int T, const float* x_in, float
 }
 
 AttnParams attn_params(kib_qwen35* m, const LayerW& L, uint16_t* kc, uint16_t* vc, const int* pos, int T) {
-  AttnParams a;
+  AttnParams a = {};
   a.qg = m->d_qg;
   a.kp = m->d_kp;
   a.vp = m->d_vp;
@@ -449,7 +450,7 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
   gemm(q, L.zgate, m->d_norm, m->H, T, m->d_z, m->VD, nullptr, true);
   gemm(q, L.beta, m->d_norm, m->H, T, m->d_beta, m->lvh, nullptr, true);
   gemm(q, L.alpha, m->d_norm, m->H, T, m->d_alpha, m->lvh, nullptr, true);
-  GdnParams g;
+  GdnParams g = {};
   g.conv_out = m->d_qkv;
   g.C = m->C;
   g.beta_raw = m->d_beta;
@@ -1832,6 +1833,233 @@ int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t
   res->finish_reason_stop = stop ? 1 : 0;
   res->kv_used_tokens = m->pos;
   return KIB_OK;
+}
+
+}  // extern "C"
+
+// ================================================================ batched decode
+// `slots` independent sequences decoded together, one token each per step
+// (the plan's sequence_slots, qwen35_runtime.hpp:20 / qwen35_runtime.cpp:4478-4479,
+// which the reference reserves but never runs).  The batch owns each slot's
+// KV cache, conv state R and delta-rule state S; the model's activation and
+// GEMM scratch is shared (one batch step runs at a time on the model's
+// stream).  The projections of a step are one GEMM over the slots, so they
+// take the reference's M > 8 numerics bucket (weights and inputs rounded to
+// half, fp32 accumulation) for every slot.
+struct kib_qwen35_batch {
+  kib_qwen35* m = nullptr;
+  int slots = 0;
+  int cap = 0;                // positions per slot
+  int nsplit = 8;             // attention key splits per slot
+  int max_steps = 0;
+  size_t k_slot = 0, r_slot = 0, s_slot = 0;  // elements per slot
+  uint16_t *d_k = nullptr, *d_v = nullptr;    // [slot][attention layer][cap][KD]
+  float *d_r = nullptr, *d_s = nullptr;       // [slot][linear layer][...]
+  float* d_part = nullptr;                    // [slot][nsplit][heads][256 + 2]
+  unsigned* d_cnt = nullptr;                  // [slot][kv_heads]
+  float* d_logits = nullptr;                  // [slot][vocab]
+  int *d_tok = nullptr, *d_pos = nullptr, *d_log = nullptr, *d_step = nullptr;
+  std::vector<int> pos;                       // host copy of the slot positions
+  cudaGraphExec_t graph = nullptr;
+};
+
+namespace {
+
+void linear_block_batch(Enq& q, kib_qwen35_batch* b, const LayerW& L, int S) {
+  kib_qwen35* m = q.m;
+  const int li = L.cache_index;
+  q.run(rms_rows_launch(m->d_h, L.attn_norm.f(), S, m->H, m->eps, m->d_norm, q.st), "rms");
+  gemm(q, L.qkv, m->d_norm, m->H, S, m->d_qkv, m->C);
+  q.run(launch_pdl(conv_batched_kernel<4>, dim3((m->C + 255) / 256, S), dim3(256), 0, q.st,
+                   b->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1), b->r_slot,
+                   static_cast<const float*>(m->d_qkv), m->C, L.conv1d.f(), m->C, m->d_qkv, m->C),
+        "conv_batched");
+  gemm(q, L.zgate, m->d_norm, m->H, S, m->d_z, m->VD, nullptr, true);
+  gemm(q, L.beta, m->d_norm, m->H, S, m->d_beta, m->lvh, nullptr, true);
+  gemm(q, L.alpha, m->d_norm, m->H, S, m->d_alpha, m->lvh, nullptr, true);
+  GdnParams g = {};
+  g.conv_out = m->d_qkv;
+  g.C = m->C;
+  g.beta_raw = m->d_beta;
+  g.alpha_raw = m->d_alpha;
+  g.ld_ba = m->lvh;
+  g.dt_bias = L.dt_bias.f();
+  g.ssm_a = L.ssm_a.f();
+  g.state = b->d_s + static_cast<size_t>(li) * m->lvh * m->lhd * m->lhd;
+  g.out = m->d_y;
+  g.T = 1;
+  g.key_heads = m->lkh;
+  g.value_heads = m->lvh;
+  g.eps = m->eps;
+  g.batched = 1;
+  g.state_slot_stride = b->s_slot;
+  q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows, S), dim3(128), 0, q.st, g), "gdn_batched");
+  q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, S, m->lvh, m->lhd, m->eps, m->d_norm2, q.st), "norm_gate");
+  gemm(q, L.ssm_out, m->d_norm2, m->VD, S, m->d_h1, m->H, m->d_h);
+}
+
+void attention_block_batch(Enq& q, kib_qwen35_batch* b, const LayerW& L, int S) {
+  kib_qwen35* m = q.m;
+  q.run(rms_rows_launch(m->d_h, L.attn_norm.f(), S, m->H, m->eps, m->d_norm, q.st), "rms");
+  gemm(q, L.q, m->d_norm, m->H, S, m->d_qg, 2 * m->AD);
+  gemm(q, L.k, m->d_norm, m->H, S, m->d_kp, m->KD, nullptr, true);
+  gemm(q, L.v, m->d_norm, m->H, S, m->d_vp, m->KD, nullptr, true);
+  const size_t off = static_cast<size_t>(L.cache_index) * b->cap * m->KD;
+  AttnParams a = attn_params(m, L, b->d_k + off, b->d_v + off, b->d_pos, 1);
+  a.batched = 1;
+  a.cache_slot_stride = b->k_slot;
+  a.nsplit = b->nsplit;
+  a.part = b->d_part;
+  a.counters = b->d_cnt;
+  a.round_q = 0;
+  static bool cfg = false;
+  if (!cfg) {
+    q.run(cudaFuncSetAttribute(attn_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+          "attn_decode_attr");
+    cfg = true;
+  }
+  q.run(launch_pdl(attn_decode_kernel<1>, dim3(b->nsplit, m->kvh, S), dim3(256), attn_decode_smem_bytes(1), q.st, a),
+        "attn_batched");
+  gemm(q, L.o, m->d_att, m->AD, S, m->d_h1, m->H, m->d_h);
+}
+
+// One step for every slot: embedding of d_tok, the layers, the LM head over
+// the batch, argmax per slot into d_tok / d_log, positions advanced.
+void batch_step(Enq& q, kib_qwen35_batch* b) {
+  kib_qwen35* m = q.m;
+  const int S = b->slots;
+  q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, b->d_tok, S, m->d_h, m->H, q.st), "embed");
+  for (const LayerW& L : m->layers) {
+    if (L.kind == 0) linear_block_batch(q, b, L, S);
+    else attention_block_batch(q, b, L, S);
+    ffn_prefill(q, L, S, m->d_h1, m->d_h);
+  }
+  q.run(rms_rows_launch(m->d_h, m->output_norm.f(), S, m->H, m->eps, m->d_hn, q.st), "head_norm");
+  const DevT& hw = head_weight(m);
+  q.run(gemm_f16_launch(hw.type, hw.p, m->V, m->H, m->d_hn, m->H, S, b->d_logits, m->V, nullptr, q.st), "lm_head");
+  q.run(launch_pdl(batch_argmax_kernel, dim3(S), dim3(256), 0, q.st, static_cast<const float*>(b->d_logits), m->V,
+                   b->d_tok, b->d_pos, b->d_log, b->d_step, S),
+        "argmax");
+  q.run(launch_pdl(batch_step_kernel, dim3(1), dim3(32), 0, q.st, b->d_step), "step");
+}
+
+void batch_release(kib_qwen35_batch* b) {
+  if (!b) return;
+  if (b->graph) cudaGraphExecDestroy(b->graph);
+  void* ptrs[] = {b->d_k, b->d_v, b->d_r, b->d_s, b->d_part, b->d_cnt, b->d_logits, b->d_tok, b->d_pos, b->d_log,
+                  b->d_step};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  delete b;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kib_qwen35_batch_create(kib_qwen35* m, uint64_t slots, uint64_t context_tokens, uint64_t max_steps,
+                            kib_qwen35_batch** out) {
+  if (!m || !out) return KIB_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  if (slots <= 8 || slots > static_cast<uint64_t>(m->tmax))
+    return fail(m, KIB_ERR_INVALID_ARGUMENT, "batched decode needs 9 .. prefill-chunk slots (the M > 8 GEMM bucket)");
+  if (context_tokens == 0 || context_tokens > (1u << 20) || max_steps == 0 || max_steps > (1u << 20))
+    return fail(m, KIB_ERR_INVALID_ARGUMENT, "batched decode: context_tokens / max_steps out of range");
+  if (m->convk != 4 || m->lhd != 128 || m->hd != 256 || !m->d_w16)
+    return fail(m, KIB_ERR_UNAVAILABLE, "batched decode needs conv kernel 4, head dims 128/256 and the f16 GEMM scratch");
+  auto* b = new kib_qwen35_batch;
+  b->m = m;
+  b->slots = static_cast<int>(slots);
+  b->cap = static_cast<int>(context_tokens);
+  b->max_steps = static_cast<int>(max_steps);
+  b->nsplit = std::max(1, std::min(32, (b->cap + 255) / 256));
+  const size_t n_full = m->plan.full_attention_layers, n_lin = m->plan.linear_attention_layers;
+  b->k_slot = n_full * static_cast<size_t>(b->cap) * m->KD;
+  b->r_slot = n_lin * static_cast<size_t>(m->C) * (m->convk - 1);
+  b->s_slot = n_lin * static_cast<size_t>(m->lvh) * m->lhd * m->lhd;
+  const size_t S = slots;
+  auto al = [](void** p, size_t bytes) { return cudaMalloc(p, std::max<size_t>(bytes, 16)) == cudaSuccess; };
+  bool ok = al(reinterpret_cast<void**>(&b->d_k), S * b->k_slot * 2) && al(reinterpret_cast<void**>(&b->d_v), S * b->k_slot * 2) &&
+            al(reinterpret_cast<void**>(&b->d_r), S * b->r_slot * 4) && al(reinterpret_cast<void**>(&b->d_s), S * b->s_slot * 4) &&
+            al(reinterpret_cast<void**>(&b->d_part), S * b->nsplit * m->heads * (kHd + 2) * 4) &&
+            al(reinterpret_cast<void**>(&b->d_cnt), S * m->kvh * 4) &&
+            al(reinterpret_cast<void**>(&b->d_logits), S * static_cast<size_t>(m->V) * 4) &&
+            al(reinterpret_cast<void**>(&b->d_tok), S * 4) && al(reinterpret_cast<void**>(&b->d_pos), S * 4) &&
+            al(reinterpret_cast<void**>(&b->d_log), S * max_steps * 4) && al(reinterpret_cast<void**>(&b->d_step), 4);
+  if (!ok) {
+    batch_release(b);
+    return fail(m, KIB_ERR_INTERNAL, "batched decode: device allocation failed");
+  }
+  cudaMemset(b->d_cnt, 0, S * m->kvh * 4);
+  cudaMemset(b->d_k, 0, S * b->k_slot * 2);
+  cudaMemset(b->d_v, 0, S * b->k_slot * 2);
+  cudaMemset(b->d_r, 0, S * b->r_slot * 4);
+  cudaMemset(b->d_s, 0, S * b->s_slot * 4);
+  b->pos.assign(S, 0);
+  *out = b;
+  return KIB_OK;
+}
+
+void kib_qwen35_batch_free(kib_qwen35_batch* b) {
+  if (b && b->m) cudaStreamSynchronize(b->m->ctx->stream);
+  batch_release(b);
+}
+
+int kib_qwen35_batch_prefill(kib_qwen35_batch* b, uint64_t slot, const int32_t* tokens, uint64_t n,
+                             int32_t* next_token) {
+  if (!b || !tokens || n == 0 || slot >= static_cast<uint64_t>(b->slots)) return KIB_ERR_INVALID_ARGUMENT;
+  kib_qwen35* m = b->m;
+  if (n >= static_cast<uint64_t>(b->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "batched prefill exceeds the slot capacity");
+  // the model's own single-sequence caches run the prefill, then the slot takes a copy
+  if (int rc = kib_qwen35_reset(m)) return rc;
+  if (int rc = kib_qwen35_prefill(m, tokens, n, 0, next_token)) return rc;
+  cudaStream_t st = m->ctx->stream;
+  const size_t n_full = m->plan.full_attention_layers;
+  for (size_t l = 0; l < n_full; ++l) {
+    const size_t src = l * static_cast<size_t>(m->cap) * m->KD, dst = slot * b->k_slot + l * static_cast<size_t>(b->cap) * m->KD;
+    ENG_CUDA(cudaMemcpyAsync(b->d_k + dst, m->d_k + src, n * m->KD * 2, cudaMemcpyDeviceToDevice, st));
+    ENG_CUDA(cudaMemcpyAsync(b->d_v + dst, m->d_v + src, n * m->KD * 2, cudaMemcpyDeviceToDevice, st));
+  }
+  ENG_CUDA(cudaMemcpyAsync(b->d_r + slot * b->r_slot, m->d_r, b->r_slot * 4, cudaMemcpyDeviceToDevice, st));
+  ENG_CUDA(cudaMemcpyAsync(b->d_s + slot * b->s_slot, m->d_s, b->s_slot * 4, cudaMemcpyDeviceToDevice, st));
+  ENG_CUDA(cudaStreamSynchronize(st));
+  b->pos[slot] = static_cast<int>(n);
+  return KIB_OK;
+}
+
+int kib_qwen35_batch_decode(kib_qwen35_batch* b, const int32_t* first_tokens, uint64_t steps, int32_t* tokens_out) {
+  if (!b || !first_tokens || steps == 0) return KIB_ERR_INVALID_ARGUMENT;
+  kib_qwen35* m = b->m;
+  if (steps > static_cast<uint64_t>(b->max_steps)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "batched decode: more steps than max_steps");
+  for (int s = 0; s < b->slots; ++s)
+    if (static_cast<uint64_t>(b->pos[s]) + steps > static_cast<uint64_t>(b->cap))
+      return fail(m, KIB_ERR_INVALID_ARGUMENT, "batched decode exceeds a slot's capacity");
+  if (int rc = check_tokens(m, first_tokens, static_cast<uint64_t>(b->slots))) return rc;
+  cudaStream_t st = m->ctx->stream;
+  ENG_CUDA(cudaMemcpyAsync(b->d_tok, first_tokens, b->slots * 4, cudaMemcpyHostToDevice, st));
+  ENG_CUDA(cudaMemcpyAsync(b->d_pos, b->pos.data(), b->slots * 4, cudaMemcpyHostToDevice, st));
+  ENG_CUDA(cudaMemsetAsync(b->d_step, 0, 4, st));
+  if (!b->graph) {
+    int rc = capture(m, &b->graph, [&](Enq& q) { batch_step(q, b); });
+    if (rc) return rc;
+  }
+  for (uint64_t i = 0; i < steps; ++i) ENG_CUDA(cudaGraphLaunch(b->graph, st));
+  if (tokens_out)
+    ENG_CUDA(cudaMemcpyAsync(tokens_out, b->d_log, steps * b->slots * 4, cudaMemcpyDeviceToHost, st));
+  if (int rc = sync_check(m, "batched decode")) return rc;
+  for (int s = 0; s < b->slots; ++s) b->pos[s] += static_cast<int>(steps);
+  return KIB_OK;
+}
+
+int kib_qwen35_batch_logits(kib_qwen35_batch* b, float* logits_out) {
+  if (!b || !logits_out) return KIB_ERR_INVALID_ARGUMENT;
+  kib_qwen35* m = b->m;
+  ENG_CUDA(cudaMemcpy(logits_out, b->d_logits, static_cast<size_t>(b->slots) * m->V * 4, cudaMemcpyDeviceToHost));
+  return KIB_OK;
+}
+
+uint64_t kib_qwen35_batch_position(const kib_qwen35_batch* b, uint64_t slot) {
+  return (b && slot < static_cast<uint64_t>(b->slots)) ? static_cast<uint64_t>(b->pos[slot]) : 0;
 }
 
 }  // extern "C"

@@ -35,6 +35,11 @@ struct GdnParams {
   int value_heads;
   float eps;
   unsigned long long* trace;
+  // batched decode (gdn_core_kernel only): blockIdx.z is a sequence slot with
+  // one token (T = 1); row `slot` of conv_out / alpha / beta / out is its
+  // token and its state starts state_slot_stride floats after slot 0's
+  int batched;
+  size_t state_slot_stride;
 };
 
 constexpr int kGdnRows = 16;  // state rows per CTA
@@ -49,7 +54,12 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kh = h % p.key_heads;
   const int key_dim = p.key_heads * D;
-  float* S = p.state + static_cast<size_t>(h) * D * D;
+  const int slot = p.batched ? static_cast<int>(blockIdx.z) : 0;
+  const float* const conv_out = p.conv_out + static_cast<size_t>(slot) * p.C;
+  const float* const alpha_raw = p.alpha_raw + static_cast<size_t>(slot) * p.ld_ba;
+  const float* const beta_raw = p.beta_raw + static_cast<size_t>(slot) * p.ld_ba;
+  float* const out = p.out + static_cast<size_t>(slot) * p.value_heads * D;
+  float* S = p.state + slot * p.state_slot_stride + static_cast<size_t>(h) * D * D;
   // warp w owns rows grp*16 + 4w .. +3; lane owns columns 4*lane .. +3
   trace_entry(p.trace);
   float4 s[4];
@@ -64,13 +74,13 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
   // the next token's inputs are loaded while the current one is processed
   // (one global round trip per token would otherwise sit on the sequential path)
   auto load_tok = [&](int t, float& qv, float& kv, float (&vv)[4], float& a, float& b) {
-    const float* row = p.conv_out + static_cast<size_t>(t) * p.C;
+    const float* row = conv_out + static_cast<size_t>(t) * p.C;
     qv = row[kh * D + tid];
     kv = row[key_dim + kh * D + tid];
 #pragma unroll
     for (int r = 0; r < 4; ++r) vv[r] = row[2 * key_dim + h * D + grp * kGdnRows + 4 * warp + r];
-    a = p.alpha_raw[static_cast<size_t>(t) * p.ld_ba + h];
-    b = p.beta_raw[static_cast<size_t>(t) * p.ld_ba + h];
+    a = alpha_raw[static_cast<size_t>(t) * p.ld_ba + h];
+    b = beta_raw[static_cast<size_t>(t) * p.ld_ba + h];
   };
   float nq = 0.f, nk = 0.f, nv[4] = {0.f, 0.f, 0.f, 0.f}, na = 0.f, nb = 0.f;
   if (p.T > 0) load_tok(0, nq, nk, nv, na, nb);
@@ -114,7 +124,7 @@ static __global__ void __launch_bounds__(128) gdn_core_kernel(const __grid_const
       st.z += k4.z * delta;
       st.w += k4.w * delta;
       const float y = warp_sum(st.x * q4.x + st.y * q4.y + st.z * q4.z + st.w * q4.w);
-      if (lane == 0) p.out[static_cast<size_t>(t) * p.value_heads * D + h * D + vrow] = y * scale;
+      if (lane == 0) out[static_cast<size_t>(t) * p.value_heads * D + h * D + vrow] = y * scale;
       s[r] = st;
     }
     __syncthreads();
@@ -298,6 +308,12 @@ struct AttnParams {
   int n_dims;             // rotated dims (2 * sum of MRoPE sections)
   int sec0, sec1, sec2, sec3;
   int nsplit;
+  // batched decode (attn_decode_kernel only): blockIdx.z is a sequence slot
+  // with one token (T = 1); pos is then [slots], the caches of slot s start
+  // cache_slot_stride halves after the slot-0 pointers, and the qg/kp/vp/out
+  // rows, the split partials and the counters are indexed by slot
+  int batched;
+  size_t cache_slot_stride;
   float* part;            // [nsplit][T][heads][hd + 2]
   unsigned* counters;     // [kv_heads]
   float* out;             // [T][heads*hd]
@@ -371,11 +387,20 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
   const int split = blockIdx.x, kvh = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kvd = p.kv_heads * kHd;
+  const int slot = p.batched ? static_cast<int>(blockIdx.z) : 0;
+  uint16_t* const kcache = p.kcache + slot * p.cache_slot_stride;
+  uint16_t* const vcache = p.vcache + slot * p.cache_slot_stride;
+  const float* const qg = p.qg + static_cast<size_t>(slot) * p.heads * 2 * kHd;
+  const float* const kp = p.kp + static_cast<size_t>(slot) * kvd;
+  const float* const vp = p.vp + static_cast<size_t>(slot) * kvd;
+  float* const part = p.part + static_cast<size_t>(slot) * p.nsplit * p.heads * (kHd + 2);
+  unsigned* const counters = p.counters + static_cast<size_t>(slot) * p.kv_heads;
+  float* const out = p.out + static_cast<size_t>(slot) * p.heads * kHd;
 
   // the position was written at least two kernels earlier (host copy or the
   // previous step's LM head), so it and the cached keys are readable now
   trace_entry(p.trace);
-  const int pos0 = *p.pos;
+  const int pos0 = p.pos[slot];
   const int nkeys = pos0 + p.T;
   int chunk = (nkeys + p.nsplit - 1) / p.nsplit;
   chunk = (chunk + 7) & ~7;
@@ -392,8 +417,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     if (lane < nk) {
       const size_t src = static_cast<size_t>(k0 + lane) * kvd + kvh * kHd;
       uint16_t* dst = kvbuf + (static_cast<size_t>(st) * kAttnChunk + lane) * 2 * kHd;
-      bulk_g2s(dst, p.kcache + src, kHd * 2, &bar[st]);
-      bulk_g2s(dst + kHd, p.vcache + src, kHd * 2, &bar[st]);
+      bulk_g2s(dst, kcache + src, kHd * 2, &bar[st]);
+      bulk_g2s(dst + kHd, vcache + src, kHd * 2, &bar[st]);
     }
   };
   if (warp == 0) {
@@ -414,7 +439,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
   for (int job = warp; job < G * p.T; job += 8) {
     const int j = job % G, t = job / G;
     const int head = kvh * G + j;
-    norm_rope_head(qs + (t * G + j) * kHd, p.qg + (static_cast<size_t>(t) * p.heads + head) * 2 * kHd, p.q_norm,
+    norm_rope_head(qs + (t * G + j) * kHd, qg + (static_cast<size_t>(t) * p.heads + head) * 2 * kHd, p.q_norm,
                    p.eps, pos0 + t, p, lane);
   }
   // new keys owned by this split
@@ -422,12 +447,12 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     const int kpos = pos0 + t;
     if (kpos < kb || kpos >= ke) continue;
     float* kr = newk + t * kHd;
-    norm_rope_head(kr, p.kp + static_cast<size_t>(t) * kvd + kvh * kHd, p.k_norm, p.eps, kpos, p, lane);
+    norm_rope_head(kr, kp + static_cast<size_t>(t) * kvd + kvh * kHd, p.k_norm, p.eps, kpos, p, lane);
     for (int i = lane; i < kHd; i += 32) {
       const __half kh = __float2half_rn(kr[i]);
-      const __half vh = __float2half_rn(p.vp[static_cast<size_t>(t) * kvd + kvh * kHd + i]);
-      p.kcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] = __half_as_ushort(kh);
-      p.vcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] = __half_as_ushort(vh);
+      const __half vh = __float2half_rn(vp[static_cast<size_t>(t) * kvd + kvh * kHd + i]);
+      kcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] = __half_as_ushort(kh);
+      vcache[static_cast<size_t>(kpos) * kvd + kvh * kHd + i] = __half_as_ushort(vh);
       kr[i] = __half2float(kh);
       newv[t * kHd + i] = __half2float(vh);
     }
@@ -566,7 +591,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     const float M = fmaxf(ma, mb);
     const float ea = ma == -INFINITY ? 0.0f : expf(ma - M);
     const float eb = mb == -INFINITY ? 0.0f : expf(mb - M);
-    float* dst = p.part + ((static_cast<size_t>(split) * p.T + t) * p.heads + kvh * G + jj) * (kHd + 2);
+    float* dst = part + ((static_cast<size_t>(split) * p.T + t) * p.heads + kvh * G + jj) * (kHd + 2);
     dst[i] = a[i] * ea + b[i] * eb;
     if (i == 0) {
       dst[kHd] = M;
@@ -575,7 +600,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
   }
   __threadfence();
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&p.counters[kvh], 1u) == static_cast<unsigned>(p.nsplit - 1);
+  if (tid == 0) s_last = atomicAdd(&counters[kvh], 1u) == static_cast<unsigned>(p.nsplit - 1);
   __syncthreads();
   trace_exit(p.trace);
   if (!s_last) return;
@@ -590,7 +615,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
   for (int idx = tid; idx < pairs * nact; idx += 256) {
     const int pr = idx / nact, sp = idx % nact;
     const int head = kvh * G + pr % G, t = pr / G;
-    const float* src = p.part + ((static_cast<size_t>(sp) * p.T + t) * p.heads + head) * (kHd + 2) + kHd;
+    const float* src = part + ((static_cast<size_t>(sp) * p.T + t) * p.heads + head) * (kHd + 2) + kHd;
     wsm[pr * p.nsplit + sp] = __ldcg(src);
     lsm[pr * p.nsplit + sp] = __ldcg(src + 1);
   }
@@ -613,7 +638,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
   for (int job = tid; job < pairs * (kHd / 2); job += 256) {
     const int i = 2 * (job % (kHd / 2)), pr = job / (kHd / 2), jj = pr % G, t = pr / G;
     const int head = kvh * G + jj;
-    const float* src = p.part + (static_cast<size_t>(t) * p.heads + head) * (kHd + 2) + i;
+    const float* src = part + (static_cast<size_t>(t) * p.heads + head) * (kHd + 2) + i;
     const size_t sstride = static_cast<size_t>(p.T) * p.heads * (kHd + 2);
     float n0 = 0.0f, n1 = 0.0f;
 #pragma unroll 16
@@ -625,14 +650,14 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __grid_constant_
     }
     const float den = dsm[pr];
     const float inv = den == 0.0f ? 0.0f : 1.0f / den;
-    const float* g = p.qg + (static_cast<size_t>(t) * p.heads + head) * 2 * kHd + kHd + i;
-    float* o = p.out + static_cast<size_t>(t) * p.heads * kHd + head * kHd + i;
+    const float* g = qg + (static_cast<size_t>(t) * p.heads + head) * 2 * kHd + kHd + i;
+    float* o = out + static_cast<size_t>(t) * p.heads * kHd + head * kHd + i;
     o[0] = n0 * inv * sigmoid_f(g[0]);
     o[1] = n1 * inv * sigmoid_f(g[1]);
   }
   __syncthreads();
   trace_exit(p.trace);
-  if (tid == 0) p.counters[kvh] = 0u;
+  if (tid == 0) counters[kvh] = 0u;
 }
 
 // Prefill step 1: per token, q norm+rope -> q_out, k norm+rope and v -> f16 cache.

@@ -186,6 +186,12 @@ def _declare(lib):
         "kib_qwen35_position": (c_uint64, [_P]),
         "kib_qwen35_set_position": (c_int, [_P, _U64]),
         "kib_qwen35_debug_stall": (c_int, [_P, c_uint32, c_int]),
+        "kib_qwen35_batch_create": (c_int, [_P, _U64, _U64, _U64, POINTER(c_void_p)]),
+        "kib_qwen35_batch_free": (None, [_P]),
+        "kib_qwen35_batch_prefill": (c_int, [_P, _U64, _P, _U64, _P]),
+        "kib_qwen35_batch_decode": (c_int, [_P, _P, _U64, _P]),
+        "kib_qwen35_batch_position": (c_uint64, [_P, _U64]),
+        "kib_qwen35_batch_logits": (c_int, [_P, _P]),
         "kib_qwen35_state_io": (c_int, [_P, c_int, _P, _P, _P, _P, _P, _P, _P]),
         "kib_qwen35_mtp_forward": (c_int, [_P, _P, _P, _U64, _U64, _P, _P]),
         "kib_synth_default": (None, [POINTER(SynthConfig)]),
@@ -391,6 +397,57 @@ class Qwen35:
         res = GenerationResult()
         self.ctx.check(self.lib.kib_generate_qwen35(self.h, byref(rq), out.ctypes.data, max_new_tokens, byref(res)))
         return out[: res.generated_tokens].copy(), res
+
+
+class Qwen35Batch:
+    """Batched greedy decode of independent sequences on one loaded model
+    (kib_qwen35_batch_*): slot-owned KV / conv / delta-rule state, one GEMM
+    over the slots per projection."""
+
+    def __init__(self, model: "Qwen35", slots: int, context_tokens: int, max_steps: int = 256):
+        self.model = model
+        self.lib = model.lib
+        self.slots = slots
+        h = c_void_p()
+        model.ctx.check(self.lib.kib_qwen35_batch_create(model.h, slots, context_tokens, max_steps, byref(h)))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.lib.kib_qwen35_batch_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def prefill(self, slot: int, tokens) -> int:
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt = np.zeros(1, np.int32)
+        self.model.ctx.check(self.lib.kib_qwen35_batch_prefill(self.h, slot, t.ctypes.data, len(t), nxt.ctypes.data))
+        return int(nxt[0])
+
+    def decode(self, first_tokens, steps: int):
+        """[steps][slots] greedy tokens."""
+        import numpy as np
+        f = np.ascontiguousarray(first_tokens, dtype=np.int32)
+        assert len(f) == self.slots
+        out = np.zeros((steps, self.slots), np.int32)
+        self.model.ctx.check(self.lib.kib_qwen35_batch_decode(self.h, f.ctypes.data, steps, out.ctypes.data))
+        return out
+
+    def position(self, slot: int) -> int:
+        return int(self.lib.kib_qwen35_batch_position(self.h, slot))
+
+    def logits(self):
+        """[slots][vocab] logits of the last step."""
+        import numpy as np
+        out = np.zeros((self.slots, self.model.plan.vocab_size), np.float32)
+        self.model.ctx.check(self.lib.kib_qwen35_batch_logits(self.h, out.ctypes.data))
+        return out
 
 
 def synth_config(**overrides) -> SynthConfig:

@@ -232,6 +232,11 @@ void pfor(int64_t n, int threads, F&& fn) {
 }
 
 int g_threads = 1;
+// Rows the matmul numerics bucket is chosen for, when larger than the actual
+// row count (0: the actual count).  A batched decode step multiplies the
+// tokens of `slots` sequences in one matmul, so each sequence's rows get the
+// bucket of the whole batch; restating one sequence of such a batch sets this.
+int64_t g_bucket_rows = 0;
 
 // ------------------------------------------------------------- quant matmul
 
@@ -240,7 +245,8 @@ void quant_matmul(int type, const uint8_t* w, int64_t rows, int64_t cols, const 
                   int64_t tokens, float* y) {
   const int64_t bpr = cols / 256;
   const int bb = block_bytes(type);
-  if (tokens <= 3) {
+  const int64_t bucket = tokens > g_bucket_rows ? tokens : g_bucket_rows;
+  if (bucket <= 3) {
     // q*_k_matmul (mps_backend.mm:1268-1446): lane b sums block b in order, the
     // 256-wide threadgroup tree-reduces the per-block partials.
     pfor(rows, g_threads, [&](int64_t r) {
@@ -276,7 +282,7 @@ void quant_matmul(int type, const uint8_t* w, int64_t rows, int64_t cols, const 
     });
     return;
   }
-  const bool round_x = tokens > 8;
+  const bool round_x = bucket > 8;
   std::vector<float> xr;
   const float* xs = x;
   if (round_x) {
@@ -882,6 +888,7 @@ struct orc_mtp_stats {
 };
 
 void orc_set_threads(int threads) { g_threads = threads < 1 ? 1 : threads; }
+void orc_set_bucket_rows(int64_t rows) { g_bucket_rows = rows < 0 ? 0 : rows; }
 
 uint16_t orc_f32_to_f16(float v) { return f32_to_f16_bits(v); }
 float orc_f16_to_f32(uint16_t v) { return f16_bits_to_f32(v); }

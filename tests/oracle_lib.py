@@ -33,6 +33,7 @@ class Oracle:
         L = self.lib
         sig = {
             "orc_set_threads": (None, [c_int]),
+            "orc_set_bucket_rows": (None, [_I64]),
             "orc_f32_to_f16": (c_uint16, [c_float]),
             "orc_f16_to_f32": (c_float, [c_uint16]),
             "orc_dequant_rows": (c_int, [c_int, _P, _I64, _I64, _P]),
