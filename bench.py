@@ -302,6 +302,58 @@ def prefill_bench(ctx, path):
 
 
 
+BATCH_SLOTS = 32
+BATCH_CONTEXT = 2048
+BATCH_STEPS = 128
+
+
+def batched_bench(ctx, path, hbm_peak, steps=BATCH_STEPS):
+    """BASELINE config 5 on one GPU: 32 independent sequences, each with a
+    seeded random 2048-token context, then `steps` greedy decode steps for all
+    of them (device time by CUDA events on the engine's stream).  Algorithmic
+    HBM bytes per step: the f16 projection weights read by the slot GEMMs, the
+    Q6_K head, and per slot its KV rows, conv state and delta-rule state."""
+    import numpy as np
+    import torch
+    import kib
+    m = kib.Qwen35(ctx, path, context_tokens=BATCH_CONTEXT + 16, decode_tokens=8, prefill_chunk=1024,
+                   enable_mtp=False)
+    b = kib.Qwen35Batch(m, BATCH_SLOTS, context_tokens=BATCH_CONTEXT + steps + 16, max_steps=steps + 8)
+    rng = np.random.default_rng(5)
+    first = np.array([b.prefill(s, rng.integers(0, m.plan.vocab_size, BATCH_CONTEXT).astype(np.int32))
+                      for s in range(BATCH_SLOTS)], np.int32)
+    warm = b.decode(first, 4)  # captures the step graph
+    stream = torch.cuda.ExternalStream(ctx.lib.kib_stream(ctx.h))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()  # ncu --profile-from-start off captures the timed steps only
+    e0.record(stream)
+    out = b.decode(warm[-1], steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    ms = e0.elapsed_time(e1)
+    p = m.plan
+    ctx_mid = BATCH_CONTEXT + 4 + steps / 2
+    w16 = 2.0 * (p.linear_attention_layers * (1024 * (6144 + 2048 + 32) + 2048 * 1024) +
+                 p.full_attention_layers * (1024 * (4096 + 512 + 512) + 2048 * 1024) +
+                 p.main_layers * 3 * 1024 * 3584)
+    head = p.vocab_size * 4 * 210
+    per_slot = (p.full_attention_layers * ctx_mid * 2 * 512 * 2 +            # K and V rows read
+                p.linear_attention_layers * (16 * 128 * 128 * 4 * 2 + 6144 * 3 * 4 * 2))  # S and R read + written
+    step_bytes = w16 + head + BATCH_SLOTS * per_slot
+    step_ms = ms / steps
+    gbs = step_bytes / (step_ms * 1e-3) / 1e9
+    b.close()
+    m.close()
+    return {"workload": "BASELINE config 5: 32 sequences x 2048-token seeded contexts, greedy steps for all "
+                        "(one GEMM over the slots per projection: the M > 8 numerics bucket)",
+            "slots": BATCH_SLOTS, "steps": steps, "ms_per_step": round(step_ms, 4),
+            "tok_per_s": round(BATCH_SLOTS * steps / (ms * 1e-3), 1), "bytes_per_step": round(step_bytes),
+            "bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(gbs / hbm_peak, 4), "tokens_head": [int(x) for x in out[0][:8]]}
+
+
 def cpu_decode_sample(path, threads, budget_s=20.0, max_tokens=6):
     """The oracle's bs1 decode step at position 4096 on the host cores (state
     content does not change the work)."""
@@ -363,7 +415,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--no-mtp", action="store_true", help="skip the config-3 MTP verify measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
-    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "prefill"],
+    ap.add_argument("--no-batch", action="store_true", help="skip the config-5 batched decode measurement")
+    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "prefill", "batch"],
                     help="matvec: BASELINE config 1 only (Q4_K 3584x1024 GEMV roofline)")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: fewer layers than the BASELINE model (the JSON line says so)")
@@ -399,6 +452,19 @@ def main():
         r = prefill_bench(ctx, path)
         print(json.dumps({"metric": "Qwen3.5-0.8B-shape 8192-token chunked prefill tok/s", "value": r["tok_per_s"],
                           "unit": "tok/s", "prefill_config4": r}), flush=True)
+        ctx.close()
+        return
+    if args.workload == "batch":
+        import torch
+        import kib
+        torch.cuda.set_device(local)
+        path = model_path(rank, world)
+        ensure_model(path, rank, world)
+        ctx = kib.Context(local)
+        hbm, _ = peaks()
+        r = batched_bench(ctx, path, hbm)
+        print(json.dumps({"metric": "Qwen3.5-0.8B-shape 32-sequence batched decode tok/s", "value": r["tok_per_s"],
+                          "unit": "tok/s", "batched_config5": r}), flush=True)
         ctx.close()
         return
     if args.impl == "reference":
@@ -470,6 +536,9 @@ def main():
         pre = None
         if not args.no_prefill and world == 1:
             pre = prefill_bench(ctx, path)
+        bat = None
+        if not args.no_batch and world == 1:
+            bat = batched_bench(ctx, path, hbm_peak)
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             threads = os.cpu_count() or 1
@@ -495,6 +564,7 @@ def main():
                 "matvec_config1": mv,
                 "mtp_verify_config3": mtp,
                 "prefill_config4": pre,
+                "batched_config5": bat,
                 "cpu_baseline": cpu, "gpu_launches": launches_per_step * args.steps,
                 "clocks": clk.summary(),
                 "tokens_head": [int(x) for x in out[:8]]}

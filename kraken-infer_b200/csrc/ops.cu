@@ -680,6 +680,9 @@ cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident
   const int fill = 2 * num_sms;
   if (ctas(128, 128) >= fill) return gemm_f16w_tile<128, 128, 2, 4>(p, st);
   if (ctas(128, 64) >= fill) return gemm_f16w_tile<128, 64, 2, 2>(p, st);
+  // few tokens (batched decode, short chunks): 32 x 32 tiles on two warps give
+  // 4x the CTAs of 64 x 64, so narrow matrices still spread over the SMs
+  if (T <= 32) return gemm_f16w_tile<32, 32, 2, 1>(p, st);
   return gemm_f16w_tile<64, 64, 2, 2>(p, st);  // 4 warps of 32 x 32, up to four CTAs per SM
 }
 
