@@ -43,6 +43,8 @@ cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident
                              bool convert_x, int num_sms, cudaStream_t st, int* err);
 cudaError_t kquant_to_f16_launch(int type, const void* w, int rows, int cols, __half* out, int num_sms,
                                  cudaStream_t st);
+cudaError_t kq_skinny_launch(int type, const void* w, int rows, int cols, const __half* x16, int T, float* y,
+                             int y_ld, const float* resid, float* ws, int num_sms, cudaStream_t st);
 cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const int* ids, int T, float* out,
                             int out_ld, cudaStream_t st);
 cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st);
@@ -1936,7 +1938,16 @@ void batch_step(Enq& q, kib_qwen35_batch* b) {
   }
   q.run(rms_rows_launch(m->d_h, m->output_norm.f(), S, m->H, m->eps, m->d_hn, q.st), "head_norm");
   const DevT& hw = head_weight(m);
-  q.run(gemm_f16_launch(hw.type, hw.p, m->V, m->H, m->d_hn, m->H, S, b->d_logits, m->V, nullptr, q.st), "lm_head");
+  if (S <= 64) {
+    q.run(launch_pdl(x_to_f16_kernel, dim3(std::max(1, S * m->H / 1024)), dim3(256), 0, q.st,
+                     static_cast<const float*>(m->d_hn), m->H, S, m->H, m->d_x16),
+          "head_x16");
+    q.run(kq_skinny_launch(hw.type, hw.p, m->V, m->H, m->d_x16, S, b->d_logits, m->V, nullptr,
+                           reinterpret_cast<float*>(m->d_w16), m->ctx->num_sms, q.st),
+          "lm_head");
+  } else {
+    q.run(gemm_f16_launch(hw.type, hw.p, m->V, m->H, m->d_hn, m->H, S, b->d_logits, m->V, nullptr, q.st), "lm_head");
+  }
   q.run(launch_pdl(batch_argmax_kernel, dim3(S), dim3(256), 0, q.st, static_cast<const float*>(b->d_logits), m->V,
                    b->d_tok, b->d_pos, b->d_log, b->d_step, S),
         "argmax");

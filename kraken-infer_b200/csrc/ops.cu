@@ -12,6 +12,7 @@
 #include "kquant_gemv2.cuh"
 #include "layer_kernels.cuh"
 #include "gemm_tc.cuh"
+#include "kq_skinny.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -637,11 +638,85 @@ cudaError_t gemm_tc_launch(const __half* w16, const __half* x16, const GemmTcPar
 }
 }  // namespace tc_host
 
+namespace skinny_host {
+template <int QT, int NT>
+cudaError_t launch(const SkinnyParams& p, dim3 grid, cudaStream_t st) {
+  static bool cfg = false;
+  constexpr size_t smem = kq_skinny_smem<NT>();
+  if (!cfg) {
+    const cudaError_t e = cudaFuncSetAttribute(kq_skinny_gemm_kernel<QT, NT>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cfg = true;
+  }
+  return launch_pdl(kq_skinny_gemm_kernel<QT, NT>, grid, dim3(128), smem, st, p);
+}
+template <int QT>
+cudaError_t launch_t(const SkinnyParams& p, dim3 grid, cudaStream_t st) {
+  if (p.T <= 16) return launch<QT, 2>(p, grid, st);
+  if (p.T <= 32) return launch<QT, 4>(p, grid, st);
+  return launch<QT, 8>(p, grid, st);
+}
+}  // namespace skinny_host
+
+// Few-token M > 8 projection straight from the K-quant blocks (kq_skinny.cuh).
+// Split-K over the super-blocks when the 64-row tiles alone give fewer than
+// two CTAs per SM; the partials (ws, nsplit * T * rows floats) are then summed
+// in split order by a second kernel.
+cudaError_t kq_skinny_launch(int type, const void* w, int rows, int cols, const __half* x16, int T, float* y,
+                             int y_ld, const float* resid, float* ws, int num_sms, cudaStream_t st) {
+  const int bpr = cols / 256;
+  const int tiles = (rows + kSkRows - 1) / kSkRows;
+  int nsplit = std::min(bpr, std::max(1, (2 * num_sms + tiles - 1) / tiles));
+  const int kps = (bpr + nsplit - 1) / nsplit;
+  nsplit = (bpr + kps - 1) / kps;
+  SkinnyParams p;
+  p.w = static_cast<const uint8_t*>(w);
+  p.rows = rows;
+  p.cols = cols;
+  p.T = T;
+  p.row_bytes = bpr * kquant_block_bytes(type);
+  p.x = x16;
+  p.y = y;
+  p.y_ld = y_ld;
+  p.resid = resid;
+  p.ws = ws;
+  p.kb_per_split = kps;
+  const dim3 grid(tiles, nsplit);
+  cudaError_t e;
+  switch (type) {
+    case kTypeQ4K: e = skinny_host::launch_t<kTypeQ4K>(p, grid, st); break;
+    case kTypeQ5K: e = skinny_host::launch_t<kTypeQ5K>(p, grid, st); break;
+    default: e = skinny_host::launch_t<kTypeQ6K>(p, grid, st); break;
+  }
+  if (e != cudaSuccess || nsplit == 1) return e;
+  const size_t n = static_cast<size_t>(T) * rows;
+  const int rg = static_cast<int>(std::min<size_t>((n + 255) / 256, static_cast<size_t>(num_sms) * 4));
+  return launch_pdl(kq_skinny_reduce_kernel, dim3(rg), dim3(256), 0, st, static_cast<const float*>(ws), nsplit, rows, T,
+                    y, y_ld, resid);
+}
+
 cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident, int rows, int cols, const float* x,
                              int x_ld, int T, float* y, int y_ld, const float* resid, __half* w16, __half* x16,
                              bool convert_x, int num_sms, cudaStream_t st, int* err) {
   if (cols % kGfK != 0 || x_ld % 4 != 0) return cudaErrorInvalidValue;
   cudaError_t e;
+  static const bool skinny_on = [] {
+    const char* v = std::getenv("KIB_GEMM_SKINNY");
+    return !(v && v[0] == '0');
+  }();
+  if (skinny_on && T > 8 && T <= 64 && cols % 256 == 0 && kquant_type_ok(type) && w16 != nullptr) {
+    // few tokens: dequantise the K-quant blocks in shared memory instead of
+    // streaming the f16 copy (same products); w16's scratch holds the split-K
+    // partials
+    if (convert_x) {
+      const size_t xn = static_cast<size_t>(T) * (cols / 4);
+      const int x_grid = static_cast<int>(std::min<size_t>((xn + 255) / 256, static_cast<size_t>(num_sms) * 8));
+      e = launch_pdl(x_to_f16_kernel, dim3(x_grid), dim3(256), 0, st, x, x_ld, T, cols, x16);
+      if (e != cudaSuccess) return e;
+    }
+    return kq_skinny_launch(type, w, rows, cols, x16, T, y, y_ld, resid, reinterpret_cast<float*>(w16), num_sms, st);
+  }
   if (!w16_resident) {
     e = kquant_to_f16_launch(type, w, rows, cols, w16, num_sms, st);
     if (e != cudaSuccess) return e;
