@@ -398,6 +398,24 @@ uint64_t kib_qwen35_batch_position(const kib_qwen35_batch* batch, uint64_t slot)
 /* The logits of the last batched step, [slots][vocab] (host copy). */
 int kib_qwen35_batch_logits(kib_qwen35_batch* batch, float* logits_out);
 
+/* --------------------------------------------------- host prompt cache
+ * Qwen35HostPrefixCache (qwen35_runtime.cpp:516-932) on this backend: after
+ * each full block of a prefill, the block's K/V rows, the conv and delta-rule
+ * state and the block's last hidden row go to host memory under the block's
+ * chained hash; kib_qwen35_prefill_cached resets the model, restores the
+ * longest stored block-aligned prefix of the prompt into the device caches
+ * and prefills only the rest (the whole prompt hit: the next token comes from
+ * the restored hidden row).  block_tokens <= the prefill chunk.  Not for use
+ * with MTP (the reference disables its prompt cache then too). */
+typedef struct kib_qwen35_prefix_cache kib_qwen35_prefix_cache;
+int kib_qwen35_prefix_cache_create(kib_qwen35* model, uint64_t block_tokens, uint64_t capacity_blocks,
+                                   uint64_t min_reuse_tokens, kib_qwen35_prefix_cache** out);
+void kib_qwen35_prefix_cache_free(kib_qwen35_prefix_cache* cache);
+/* stored blocks, hit tokens, miss tokens, committed tokens, evicted blocks, block tokens. */
+void kib_qwen35_prefix_cache_stats(const kib_qwen35_prefix_cache* cache, uint64_t* out6);
+int kib_qwen35_prefill_cached(kib_qwen35* model, kib_qwen35_prefix_cache* cache, const int32_t* tokens,
+                              uint64_t count, int32_t* next_token, uint64_t* hit_tokens);
+
 /* Synthetic BASELINE-shaped Qwen3.5 GGUF writer (random-init weights, Q4_K_M mix). */
 typedef struct kib_synth_config {
   uint64_t hidden, layers, intermediate, vocab, heads, kv_heads, head_dim;
@@ -417,6 +435,24 @@ int kib_quantize_kquant(int type, const float* x, uint64_t n, void* out);
  * it touches the device: KIB_ERR_INVALID_ARGUMENT with the reason in err for a
  * truncated or corrupt file (gguf_reader.cpp's checks). */
 int kib_gguf_check(const char* path, char* err, int err_len, uint64_t* n_tensors);
+
+/* ------------------------------------------------------- host prompt cache
+ * Exact-prefix block index of the host prefix cache (Qwen35PrefixCacheIndex,
+ * include/toyllm/runtime/qwen35_prefix_cache.hpp:52-79;
+ * src/runtime/qwen35_prefix_cache.cpp): blocks of block_tokens chained by
+ * hash, LRU eviction at capacity_blocks, hits below min_reuse_tokens ignored.
+ * Host only (also exported by libkib_gguf.so). */
+typedef struct kib_prefix_index kib_prefix_index;
+kib_prefix_index* kib_prefix_index_create(uint64_t block_tokens, uint64_t capacity_blocks, uint64_t min_reuse_tokens);
+void kib_prefix_index_free(kib_prefix_index* index);
+/* Tokens of the longest stored prefix; its block hashes (up to max_hashes) into hashes_out. */
+uint64_t kib_prefix_index_lookup(kib_prefix_index* index, const int64_t* tokens, uint64_t count, uint64_t* hashes_out,
+                                 uint64_t max_hashes);
+/* Commits block [start, start + block_tokens): returns inserted | evicted << 1, -1 on bad arguments. */
+int kib_prefix_index_commit(kib_prefix_index* index, const int64_t* tokens, uint64_t count, uint64_t start,
+                            uint64_t* hash_out, uint64_t* evicted_hash_out);
+/* stored blocks, hit tokens, miss tokens, committed tokens, evicted blocks, block tokens. */
+void kib_prefix_index_stats(const kib_prefix_index* index, uint64_t* out6);
 
 #ifdef __cplusplus
 }

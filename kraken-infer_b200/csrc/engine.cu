@@ -29,6 +29,7 @@
 #include <vector>
 
 #include "gguf.hpp"
+#include "prefix_cache.hpp"
 #include "kib_ctx.cuh"
 #include "layer_kernels.cuh"
 #include "decode_persistent.cuh"
@@ -44,7 +45,7 @@ cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident
 cudaError_t kquant_to_f16_launch(int type, const void* w, int rows, int cols, __half* out, int num_sms,
                                  cudaStream_t st);
 cudaError_t kq_skinny_launch(int type, const void* w, int rows, int cols, const __half* x16, int T, float* y,
-                             int y_ld, const float* resid, float* ws, int num_sms, cudaStream_t st);
+                             int y_ld, const float* resid, float* ws, int num_sms, cudaStream_t st, bool xsplit);
 cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const int* ids, int T, float* out,
                             int out_ld, cudaStream_t st);
 cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st);
@@ -405,6 +406,15 @@ void head_small(Enq& q, int T, const float* x, const DevT& norm_w, const DevT& h
   q.run(gemv_launch(d, m->ctx->num_sms, q.st, &why), "lm_head");
 }
 
+// KIB_SMALL_BLOCKS=0: 4..8-token forwards keep the fused GEMV path (A/B runs).
+bool small_blocks_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("KIB_SMALL_BLOCKS");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 // KIB_GDN_CHUNKED=0: prefill keeps the token-by-token delta-rule scan (A/B runs).
 bool gdn_chunked_enabled() {
   static const bool on = [] {
@@ -566,6 +576,64 @@ void main_layers_prefill(Enq& q, int T, const int* pos) {
   }
 }
 
+// 4..8 tokens (MTP verify): the projections as few-token tensor-core GEMMs
+// (kq_skinny, x split into halves: the 4..8 bucket numerics), the delta rule
+// and the split-K attention of the decode path.
+void linear_block_mid(Enq& q, const LayerW& L, int T, const float* x_in, float* x_mid) {
+  kib_qwen35* m = q.m;
+  const int li = L.cache_index;
+  q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
+  gemm(q, L.qkv, m->d_norm, m->H, T, m->d_qkv, m->C);
+  q.run(conv_launch(m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1), m->d_qkv, m->C, L.conv1d.f(), m->convk,
+                    m->C, T, m->d_qkv, m->C, 1, q.st),
+        "conv");
+  gemm(q, L.zgate, m->d_norm, m->H, T, m->d_z, m->VD, nullptr, true);
+  gemm(q, L.beta, m->d_norm, m->H, T, m->d_beta, m->lvh, nullptr, true);
+  gemm(q, L.alpha, m->d_norm, m->H, T, m->d_alpha, m->lvh, nullptr, true);
+  GdnParams g = {};
+  g.conv_out = m->d_qkv;
+  g.C = m->C;
+  g.beta_raw = m->d_beta;
+  g.alpha_raw = m->d_alpha;
+  g.ld_ba = m->lvh;
+  g.dt_bias = L.dt_bias.f();
+  g.ssm_a = L.ssm_a.f();
+  g.state = m->d_s + static_cast<size_t>(li) * m->lvh * m->lhd * m->lhd;
+  g.out = m->d_y;
+  g.T = T;
+  g.key_heads = m->lkh;
+  g.value_heads = m->lvh;
+  g.eps = m->eps;
+  q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
+  q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, T, m->lvh, m->lhd, m->eps, m->d_norm2, q.st), "norm_gate");
+  gemm(q, L.ssm_out, m->d_norm2, m->VD, T, x_mid, m->H, x_in);
+}
+
+void attention_block_mid(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc, const int* pos, int T,
+                         const float* x_in, float* x_mid) {
+  kib_qwen35* m = q.m;
+  q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
+  gemm(q, L.q, m->d_norm, m->H, T, m->d_qg, 2 * m->AD);
+  gemm(q, L.k, m->d_norm, m->H, T, m->d_kp, m->KD, nullptr, true);
+  gemm(q, L.v, m->d_norm, m->H, T, m->d_vp, m->KD, nullptr, true);
+  AttnParams a = attn_params(m, L, kc, vc, pos, T);
+  q.run(launch_attn_decode<8>(a, m->kvh, m->nsplit, q.st), "attn_decode");
+  gemm(q, L.o, m->d_att, m->AD, T, x_mid, m->H, x_in);
+}
+
+void main_layers_mid(Enq& q, int T, const int* pos) {
+  kib_qwen35* m = q.m;
+  for (const LayerW& L : m->layers) {
+    if (L.kind == 0) {
+      linear_block_mid(q, L, T, m->d_h, m->d_h1);
+    } else {
+      const size_t off = static_cast<size_t>(L.cache_index) * m->cap * m->KD;
+      attention_block_mid(q, L, m->d_k + off, m->d_v + off, pos, T, m->d_h, m->d_h1);
+    }
+    ffn_prefill(q, L, T, m->d_h1, m->d_h);
+  }
+}
+
 const DevT& head_weight(kib_qwen35* m) { return m->output.ok() ? m->output : m->tok_embd; }
 
 // ------------------------------------------------------------------ loading
@@ -628,7 +696,11 @@ int forward_small(kib_qwen35* m, int T, bool want_logits) {
     m->fwd_graph[T] = nullptr;
     int rc = capture(m, &m->fwd_graph[T], [&](Enq& q) {
       q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, m->d_tokens, T, m->d_h, m->H, q.st), "embed");
-      main_layers_small(q, T, m->d_pos);
+      // 4..8 tokens (MTP verify): projections on the few-token tensor-core
+      // GEMM with x split into halves (the same 4..8 bucket numerics as the
+      // GEMV path), delta rule and attention as on the decode path
+      if (T >= 4 && m->d_w16 && small_blocks_enabled()) main_layers_mid(q, T, m->d_pos);
+      else main_layers_small(q, T, m->d_pos);
       head_small(q, T, m->d_h, m->output_norm, head_weight(m), m->d_argmax, m->d_prob, m->d_hn,
                  want_logits ? m->d_logits : nullptr, nullptr, nullptr, nullptr);
     });
@@ -1943,7 +2015,7 @@ void batch_step(Enq& q, kib_qwen35_batch* b) {
                      static_cast<const float*>(m->d_hn), m->H, S, m->H, m->d_x16),
           "head_x16");
     q.run(kq_skinny_launch(hw.type, hw.p, m->V, m->H, m->d_x16, S, b->d_logits, m->V, nullptr,
-                           reinterpret_cast<float*>(m->d_w16), m->ctx->num_sms, q.st),
+                           reinterpret_cast<float*>(m->d_w16), m->ctx->num_sms, q.st, false),
           "lm_head");
   } else {
     q.run(gemm_f16_launch(hw.type, hw.p, m->V, m->H, m->d_hn, m->H, S, b->d_logits, m->V, nullptr, q.st), "lm_head");
@@ -2071,6 +2143,133 @@ int kib_qwen35_batch_logits(kib_qwen35_batch* b, float* logits_out) {
 
 uint64_t kib_qwen35_batch_position(const kib_qwen35_batch* b, uint64_t slot) {
   return (b && slot < static_cast<uint64_t>(b->slots)) ? static_cast<uint64_t>(b->pos[slot]) : 0;
+}
+
+}  // extern "C"
+
+// ================================================================ host prompt cache
+// The reference's host prefix cache (Qwen35HostPrefixCache,
+// qwen35_runtime.cpp:516-932): prompts are prefilled in blocks of
+// block_tokens; after each full block the block's K/V rows of every attention
+// layer, the whole conv and delta-rule state and the block's last hidden row
+// are copied to host memory under the block's chained hash; a later prompt
+// with the same block-aligned prefix restores those bytes into the device
+// caches and prefills only the rest (or, when the whole prompt hit, samples
+// its next token from the restored hidden row).  Restored bytes are the ones
+// the prefill computed, so a hit leaves exactly the state of a fresh prefill
+// in the same blocks.
+struct kib_qwen35_prefix_cache {
+  kib_qwen35* m = nullptr;
+  std::unique_ptr<kib::PrefixIndex> idx;
+  struct Payload {
+    std::vector<uint16_t> k, v;  // [attention layer][block_tokens][kv_dim]
+    std::vector<float> r, s, h;  // whole R, whole S, last hidden row
+  };
+  std::map<uint64_t, Payload> payloads;
+};
+
+namespace {
+
+int prefix_read_payload(kib_qwen35_prefix_cache* pc, uint64_t start, uint64_t block, int last_row,
+                        kib_qwen35_prefix_cache::Payload* out) {
+  kib_qwen35* m = pc->m;
+  const size_t n_full = m->plan.full_attention_layers, kd = static_cast<size_t>(m->KD);
+  out->k.resize(n_full * block * kd);
+  out->v.resize(n_full * block * kd);
+  for (size_t l = 0; l < n_full; ++l) {
+    const size_t src = (l * static_cast<size_t>(m->cap) + start) * kd, dst = l * block * kd;
+    ENG_CUDA(cudaMemcpy(out->k.data() + dst, m->d_k + src, block * kd * 2, cudaMemcpyDeviceToHost));
+    ENG_CUDA(cudaMemcpy(out->v.data() + dst, m->d_v + src, block * kd * 2, cudaMemcpyDeviceToHost));
+  }
+  out->r.resize(m->r_elems);
+  out->s.resize(m->s_elems);
+  out->h.resize(static_cast<size_t>(m->H));
+  ENG_CUDA(cudaMemcpy(out->r.data(), m->d_r, m->r_elems * 4, cudaMemcpyDeviceToHost));
+  ENG_CUDA(cudaMemcpy(out->s.data(), m->d_s, m->s_elems * 4, cudaMemcpyDeviceToHost));
+  ENG_CUDA(cudaMemcpy(out->h.data(), m->d_h + static_cast<size_t>(last_row) * m->H, static_cast<size_t>(m->H) * 4,
+                      cudaMemcpyDeviceToHost));
+  return KIB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kib_qwen35_prefix_cache_create(kib_qwen35* m, uint64_t block_tokens, uint64_t capacity_blocks,
+                                   uint64_t min_reuse_tokens, kib_qwen35_prefix_cache** out) {
+  if (!m || !out) return KIB_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  if (block_tokens == 0 || block_tokens > static_cast<uint64_t>(m->tmax) || capacity_blocks == 0)
+    return fail(m, KIB_ERR_INVALID_ARGUMENT, "prefix cache: block_tokens must be 1 .. the prefill chunk, capacity > 0");
+  auto* pc = new kib_qwen35_prefix_cache;
+  pc->m = m;
+  pc->idx.reset(new kib::PrefixIndex(block_tokens, capacity_blocks, min_reuse_tokens));
+  *out = pc;
+  return KIB_OK;
+}
+
+void kib_qwen35_prefix_cache_free(kib_qwen35_prefix_cache* pc) { delete pc; }
+
+void kib_qwen35_prefix_cache_stats(const kib_qwen35_prefix_cache* pc, uint64_t* out6) {
+  if (pc && out6) pc->idx->stats(out6);
+}
+
+int kib_qwen35_prefill_cached(kib_qwen35* m, kib_qwen35_prefix_cache* pc, const int32_t* tokens, uint64_t n,
+                              int32_t* next_token, uint64_t* hit_tokens) {
+  if (!m || !pc || pc->m != m || !tokens || n == 0 || !next_token) return KIB_ERR_INVALID_ARGUMENT;
+  if (n > static_cast<uint64_t>(m->cap)) return fail(m, KIB_ERR_INVALID_ARGUMENT, "prefill exceeds cache capacity");
+  if (int rc = check_tokens(m, tokens, n)) return rc;
+  const uint64_t block = pc->idx->block_tokens();
+  std::vector<int64_t> t64(tokens, tokens + n);
+  std::vector<uint64_t> hashes;
+  const uint64_t hit = pc->idx->lookup(t64.data(), n, &hashes);
+  if (hit_tokens) *hit_tokens = hit;
+  if (int rc = kib_qwen35_reset(m)) return rc;
+  if (hit > 0) {
+    // restore_kv_block per hit block, then the state and hidden row of the last one
+    const size_t n_full = m->plan.full_attention_layers, kd = static_cast<size_t>(m->KD);
+    for (size_t b = 0; b < hashes.size(); ++b) {
+      auto it = pc->payloads.find(hashes[b]);
+      if (it == pc->payloads.end()) return fail(m, KIB_ERR_INTERNAL, "prefix cache payload is missing");
+      for (size_t l = 0; l < n_full; ++l) {
+        const size_t dst = (l * static_cast<size_t>(m->cap) + b * block) * kd, src = l * block * kd;
+        ENG_CUDA(cudaMemcpy(m->d_k + dst, it->second.k.data() + src, block * kd * 2, cudaMemcpyHostToDevice));
+        ENG_CUDA(cudaMemcpy(m->d_v + dst, it->second.v.data() + src, block * kd * 2, cudaMemcpyHostToDevice));
+      }
+    }
+    const auto& last = pc->payloads.at(hashes.back());
+    ENG_CUDA(cudaMemcpy(m->d_r, last.r.data(), m->r_elems * 4, cudaMemcpyHostToDevice));
+    ENG_CUDA(cudaMemcpy(m->d_s, last.s.data(), m->s_elems * 4, cudaMemcpyHostToDevice));
+    m->pos = hit;
+    if (int rc = set_pos(m, m->d_pos, hit)) return rc;
+    if (hit == n) {
+      // the whole prompt hit: the next token from the restored last hidden row
+      ENG_CUDA(cudaMemcpy(m->d_h, last.h.data(), static_cast<size_t>(m->H) * 4, cudaMemcpyHostToDevice));
+      Enq q{m, m->ctx->stream};
+      head_small(q, 1, m->d_h, m->output_norm, head_weight(m), m->d_argmax, m->d_prob, nullptr, nullptr, nullptr,
+                 nullptr, nullptr);
+      if (!q.ok()) return fail(m, KIB_ERR_INTERNAL, "prefix cache head: " + q.why);
+      ENG_CUDA(cudaMemcpyAsync(m->h_pin, m->d_argmax, 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+      if (int rc = sync_check(m, "prefix cache head")) return rc;
+      *next_token = m->h_pin[0];
+      return KIB_OK;
+    }
+  }
+  // the rest in blocks; every full block is committed with its payload
+  for (uint64_t start = hit; start < n; start += block) {
+    const uint64_t c = std::min<uint64_t>(block, n - start);
+    if (int rc = kib_qwen35_prefill(m, tokens + start, c, c, next_token)) return rc;
+    if (c != block) continue;
+    const uint64_t h = pc->idx->hash_for(t64.data(), start);
+    if (pc->payloads.count(h)) continue;
+    kib_qwen35_prefix_cache::Payload pl;
+    if (int rc = prefix_read_payload(pc, start, block, static_cast<int>(c) - 1, &pl)) return rc;
+    const kib::PrefixCommit cm = pc->idx->commit(t64.data(), n, start);
+    if (!cm.inserted) continue;
+    if (cm.evicted) pc->payloads.erase(cm.evicted_hash);
+    pc->payloads[cm.hash] = std::move(pl);
+  }
+  return KIB_OK;
 }
 
 }  // extern "C"

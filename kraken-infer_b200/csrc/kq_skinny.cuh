@@ -39,6 +39,8 @@ struct SkinnyParams {
   const float* resid; // may alias y
   float* ws;          // split partials [nsplit][T][rows]
   int kb_per_split;
+  int xrows;          // rows of x in the shared tile (T, or 16 with xsplit)
+  int xsplit;         // x rows 0..7 = half(x), 8..15 = half(x - half(x)): the 4..8 bucket
 };
 
 template <int NT>
@@ -82,7 +84,7 @@ __global__ void __launch_bounds__(128) kq_skinny_gemm_kernel(const __grid_consta
     __half* xb = X + static_cast<size_t>(buf) * NTOK * kSkLd;
     for (int i = tid; i < NTOK * 32; i += 128) {  // 32 pieces of 8 halves per token row
       const int t = i >> 5, piece = i & 31;
-      const bool ok = t < p.T;
+      const bool ok = t < p.xrows;
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(xb + t * kSkLd + 8 * piece)),
                    "l"(p.x + static_cast<size_t>(ok ? t : 0) * p.cols + kb * 256 + 8 * piece), "r"(ok ? 16 : 0)
                    : "memory");
@@ -134,13 +136,19 @@ __global__ void __launch_bounds__(128) kq_skinny_gemm_kernel(const __grid_consta
   }
   const int g = lane >> 2, q = lane & 3;
   const bool split = gridDim.y > 1;
+  if (p.xsplit) {
+    // token t's product is the sum of its high-half row (tile 0) and its
+    // low-half row (tile 1)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[0][c] += acc[1 % NT][c];
+  }
 #pragma unroll
   for (int j = 0; j < NT; ++j)
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int row = row0 + 16 * warp + g + (c >> 1) * 8;
       const int t = 8 * j + 2 * q + (c & 1);
-      if (row < p.rows && t < p.T) {
+      if (row < p.rows && t < p.T && !(p.xsplit && j > 0)) {
         if (split) {
           p.ws[(static_cast<size_t>(blockIdx.y) * p.T + t) * p.rows + row] = acc[j][c];
         } else {
@@ -166,6 +174,23 @@ static __global__ void __launch_bounds__(256) kq_skinny_reduce_kernel(const floa
     const size_t o = static_cast<size_t>(t) * y_ld + row;
     if (resid) v += resid[o];
     y[o] = v;
+  }
+}
+
+// The 4..8-token bucket keeps x in fp32 against half weights: x becomes two
+// half rows per token, rows 0..7 the rounded value and rows 8..15 the rounding
+// remainder, so W_h . x = W_h . x_hi + W_h . x_lo to ~22 bits of x.
+static __global__ void __launch_bounds__(256) x_split_f16_kernel(const float* x, int x_ld, int T, int cols,
+                                                                 __half* out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const size_t n = static_cast<size_t>(8) * cols;
+  for (size_t i = blockIdx.x * 256ull + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * 256) {
+    const int t = static_cast<int>(i / cols), c = static_cast<int>(i % cols);
+    const float v = t < T ? x[static_cast<size_t>(t) * x_ld + c] : 0.0f;
+    const __half hi = __float2half_rn(v);
+    out[i] = hi;
+    out[n + i] = __float2half_rn(v - __half2float(hi));
   }
 }
 

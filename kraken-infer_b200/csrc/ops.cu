@@ -653,8 +653,8 @@ cudaError_t launch(const SkinnyParams& p, dim3 grid, cudaStream_t st) {
 }
 template <int QT>
 cudaError_t launch_t(const SkinnyParams& p, dim3 grid, cudaStream_t st) {
-  if (p.T <= 16) return launch<QT, 2>(p, grid, st);
-  if (p.T <= 32) return launch<QT, 4>(p, grid, st);
+  if (p.xrows <= 16) return launch<QT, 2>(p, grid, st);
+  if (p.xrows <= 32) return launch<QT, 4>(p, grid, st);
   return launch<QT, 8>(p, grid, st);
 }
 }  // namespace skinny_host
@@ -664,7 +664,7 @@ cudaError_t launch_t(const SkinnyParams& p, dim3 grid, cudaStream_t st) {
 // two CTAs per SM; the partials (ws, nsplit * T * rows floats) are then summed
 // in split order by a second kernel.
 cudaError_t kq_skinny_launch(int type, const void* w, int rows, int cols, const __half* x16, int T, float* y,
-                             int y_ld, const float* resid, float* ws, int num_sms, cudaStream_t st) {
+                             int y_ld, const float* resid, float* ws, int num_sms, cudaStream_t st, bool xsplit) {
   const int bpr = cols / 256;
   const int tiles = (rows + kSkRows - 1) / kSkRows;
   int nsplit = std::min(bpr, std::max(1, (2 * num_sms + tiles - 1) / tiles));
@@ -682,6 +682,8 @@ cudaError_t kq_skinny_launch(int type, const void* w, int rows, int cols, const 
   p.resid = resid;
   p.ws = ws;
   p.kb_per_split = kps;
+  p.xsplit = xsplit ? 1 : 0;
+  p.xrows = xsplit ? 16 : T;
   const dim3 grid(tiles, nsplit);
   cudaError_t e;
   switch (type) {
@@ -705,6 +707,18 @@ cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident
     const char* v = std::getenv("KIB_GEMM_SKINNY");
     return !(v && v[0] == '0');
   }();
+  if (T >= 4 && T <= 8 && cols % 256 == 0 && kquant_type_ok(type) && w16 != nullptr) {
+    // the reference's 4..8-token bucket: half weights against fp32 x, as x's
+    // high and low halves on the tensor cores
+    if (convert_x) {
+      const size_t xn = static_cast<size_t>(8) * cols;
+      const int x_grid = static_cast<int>(std::min<size_t>((xn + 255) / 256, static_cast<size_t>(num_sms) * 4));
+      e = launch_pdl(x_split_f16_kernel, dim3(x_grid), dim3(256), 0, st, x, x_ld, T, cols, x16);
+      if (e != cudaSuccess) return e;
+    }
+    return kq_skinny_launch(type, w, rows, cols, x16, T, y, y_ld, resid, reinterpret_cast<float*>(w16), num_sms, st,
+                            true);
+  }
   if (skinny_on && T > 8 && T <= 64 && cols % 256 == 0 && kquant_type_ok(type) && w16 != nullptr) {
     // few tokens: dequantise the K-quant blocks in shared memory instead of
     // streaming the f16 copy (same products); w16's scratch holds the split-K
@@ -715,7 +729,8 @@ cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident
       e = launch_pdl(x_to_f16_kernel, dim3(x_grid), dim3(256), 0, st, x, x_ld, T, cols, x16);
       if (e != cudaSuccess) return e;
     }
-    return kq_skinny_launch(type, w, rows, cols, x16, T, y, y_ld, resid, reinterpret_cast<float*>(w16), num_sms, st);
+    return kq_skinny_launch(type, w, rows, cols, x16, T, y, y_ld, resid, reinterpret_cast<float*>(w16), num_sms, st,
+                            false);
   }
   if (!w16_resident) {
     e = kquant_to_f16_launch(type, w, rows, cols, w16, num_sms, st);

@@ -73,6 +73,17 @@ def load_tools_library(path: str = TOOLS_LIB_PATH) -> ctypes.CDLL:
     lib.kib_quantize_kquant.argtypes = [c_int, c_void_p, c_uint64, c_void_p]
     lib.kib_gguf_check.restype = c_int
     lib.kib_gguf_check.argtypes = [c_char_p, c_char_p, c_int, POINTER(c_uint64)]
+    lib.kib_prefix_index_create.restype = c_void_p
+    lib.kib_prefix_index_create.argtypes = [c_uint64, c_uint64, c_uint64]
+    lib.kib_prefix_index_free.restype = None
+    lib.kib_prefix_index_free.argtypes = [c_void_p]
+    lib.kib_prefix_index_lookup.restype = c_uint64
+    lib.kib_prefix_index_lookup.argtypes = [c_void_p, c_void_p, c_uint64, c_void_p, c_uint64]
+    lib.kib_prefix_index_commit.restype = c_int
+    lib.kib_prefix_index_commit.argtypes = [c_void_p, c_void_p, c_uint64, c_uint64, POINTER(c_uint64),
+                                            POINTER(c_uint64)]
+    lib.kib_prefix_index_stats.restype = None
+    lib.kib_prefix_index_stats.argtypes = [c_void_p, c_void_p]
     _tools = lib
     return lib
 
@@ -192,6 +203,10 @@ def _declare(lib):
         "kib_qwen35_batch_decode": (c_int, [_P, _P, _U64, _P]),
         "kib_qwen35_batch_position": (c_uint64, [_P, _U64]),
         "kib_qwen35_batch_logits": (c_int, [_P, _P]),
+        "kib_qwen35_prefix_cache_create": (c_int, [_P, _U64, _U64, _U64, POINTER(c_void_p)]),
+        "kib_qwen35_prefix_cache_free": (None, [_P]),
+        "kib_qwen35_prefix_cache_stats": (None, [_P, _P]),
+        "kib_qwen35_prefill_cached": (c_int, [_P, _P, _P, _U64, _P, _P]),
         "kib_qwen35_state_io": (c_int, [_P, c_int, _P, _P, _P, _P, _P, _P, _P]),
         "kib_qwen35_mtp_forward": (c_int, [_P, _P, _P, _U64, _U64, _P, _P]),
         "kib_synth_default": (None, [POINTER(SynthConfig)]),
@@ -399,6 +414,44 @@ class Qwen35:
         return out[: res.generated_tokens].copy(), res
 
 
+class PromptCache:
+    """Host prefix cache of one model (kib_qwen35_prefix_cache_*)."""
+
+    def __init__(self, model: "Qwen35", block_tokens: int, capacity_blocks: int, min_reuse_tokens: int = 0):
+        self.model = model
+        self.lib = model.lib
+        h = c_void_p()
+        model.ctx.check(self.lib.kib_qwen35_prefix_cache_create(model.h, block_tokens, capacity_blocks,
+                                                                min_reuse_tokens, byref(h)))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.lib.kib_qwen35_prefix_cache_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def prefill(self, tokens):
+        """(next token, hit tokens): reset, restore the longest cached prefix, prefill the rest."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt, hit = np.zeros(1, np.int32), np.zeros(1, np.uint64)
+        self.model.ctx.check(self.lib.kib_qwen35_prefill_cached(self.model.h, self.h, t.ctypes.data, len(t),
+                                                                nxt.ctypes.data, hit.ctypes.data))
+        return int(nxt[0]), int(hit[0])
+
+    def stats(self):
+        import numpy as np
+        out = np.zeros(6, np.uint64)
+        self.lib.kib_qwen35_prefix_cache_stats(self.h, out.ctypes.data)
+        return [int(x) for x in out]
+
+
 class Qwen35Batch:
     """Batched greedy decode of independent sequences on one loaded model
     (kib_qwen35_batch_*): slot-owned KV / conv / delta-rule state, one GEMM
@@ -480,6 +533,45 @@ def gguf_check(path: str):
     if rc != KIB_OK:
         raise KibError(rc, err.value.decode())
     return n.value
+
+
+class PrefixIndex:
+    """Host exact-prefix block index of the prompt cache (no device needed)."""
+
+    def __init__(self, block_tokens: int, capacity_blocks: int, min_reuse_tokens: int = 0):
+        self.lib = load_tools_library()
+        self.h = self.lib.kib_prefix_index_create(block_tokens, capacity_blocks, min_reuse_tokens)
+
+    def close(self):
+        if self.h:
+            self.lib.kib_prefix_index_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def lookup(self, tokens):
+        """(hit tokens, block hashes)."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int64)
+        hashes = np.zeros(max(1, len(t)), np.uint64)
+        hit = self.lib.kib_prefix_index_lookup(self.h, t.ctypes.data, len(t), hashes.ctypes.data, len(hashes))
+        return int(hit), [int(x) for x in hashes[: hit // max(1, self.stats()[5])]] if hit else []
+
+    def commit(self, tokens, start: int):
+        """(inserted, evicted, hash)."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int64)
+        hh, ev = c_uint64(0), c_uint64(0)
+        r = self.lib.kib_prefix_index_commit(self.h, t.ctypes.data, len(t), start, byref(hh), byref(ev))
+        return bool(r & 1), bool(r & 2), int(hh.value)
+
+    def stats(self):
+        """stored blocks, hit tokens, miss tokens, committed tokens, evicted blocks, block tokens."""
+        import numpy as np
+        out = np.zeros(6, np.uint64)
+        self.lib.kib_prefix_index_stats(self.h, out.ctypes.data)
+        return [int(x) for x in out]
 
 
 def quantize(qtype: int, x):

@@ -88,4 +88,43 @@ int ref_check_gguf(const char* path, unsigned long long context_tokens, long lon
   return 0;
 }
 
+// Qwen35PrefixCacheIndex (src/runtime/qwen35_prefix_cache.cpp) driven by a
+// script, to pin the repository's restatement against the reference's own
+// index.  ops[i] = 0: lookup of prompt i, 1: commit of the block of prompt i
+// at starts[i].  prompts[i] has lens[i] tokens at offs[i] in tokens.  For
+// every op, out[2*i] = hit tokens (lookup) or inserted | evicted << 1
+// (commit), out[2*i+1] = the last block hash (lookup) or the block hash
+// (commit); stats6 = stored, hit, miss, committed, evicted, block tokens.
+int ref_prefix_script(unsigned long long block_tokens, unsigned long long capacity, unsigned long long min_reuse,
+                      int nops, const int* ops, const long long* tokens, const unsigned long long* offs,
+                      const unsigned long long* lens, const unsigned long long* starts, unsigned long long* out,
+                      unsigned long long* stats6) {
+  toyllm::Qwen35PrefixCacheConfig cfg;
+  cfg.enabled = true;
+  cfg.block_tokens = block_tokens;
+  cfg.capacity_blocks = capacity;
+  cfg.min_reuse_tokens = min_reuse;
+  toyllm::Qwen35PrefixCacheIndex idx(cfg);
+  for (int i = 0; i < nops; ++i) {
+    std::vector<std::int64_t> t(tokens + offs[i], tokens + offs[i] + lens[i]);
+    if (ops[i] == 0) {
+      auto r = idx.lookup(t);
+      out[2 * i] = r.hit_tokens;
+      out[2 * i + 1] = r.block_hashes.empty() ? 0 : r.block_hashes.back();
+    } else {
+      auto r = idx.commit_block(t, starts[i]);
+      out[2 * i] = (r.inserted ? 1u : 0u) | (r.evicted ? 2u : 0u);
+      out[2 * i + 1] = r.hash;
+    }
+  }
+  auto st = idx.stats();
+  stats6[0] = st.stored_blocks;
+  stats6[1] = st.hit_tokens;
+  stats6[2] = st.miss_tokens;
+  stats6[3] = st.committed_tokens;
+  stats6[4] = st.evicted_blocks;
+  stats6[5] = st.block_tokens;
+  return 0;
+}
+
 }  // extern "C"
