@@ -239,4 +239,167 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   }
 }
 
+// ---------------------------------------------------------------- persistent
+// gemm_tc_persist_kernel: the same tile and numerics, one CTA per SM walking
+// the tiles t = blockIdx.x, + gridDim.x, ... (row tile fastest).  Two TMEM
+// accumulators of BN columns alternate between tiles: the MMA warp fills one
+// while the epilogue warps drain the other (acc_full / acc_empty barriers),
+// and the TMA ring of kTcPStages stages runs across tile boundaries, so
+// neither the epilogue nor the next tile's pipeline fill stalls the tensor
+// pipe.
+template <int BN>
+constexpr int tc_persist_stages() {
+  return BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);  // 192 KB of stages in each case
+}
+
+template <int BN>
+constexpr size_t gemm_tc_persist_smem() {
+  return static_cast<size_t>(tc_persist_stages<BN>()) * (kTcBM + BN) * kTcBK * 2 + 1024 + 256;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_persist_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                           const __grid_constant__ GemmTcParams p) {
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "N must be a multiple of 32 up to 256");
+  constexpr uint32_t kABytes = kTcBM * kTcBK * 2, kBBytes = BN * kTcBK * 2;
+  constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+  constexpr int kTcPStages = tc_persist_stages<BN>();
+  static_assert(kTmemCols <= 512 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation");
+  extern __shared__ __align__(1024) uint8_t tcp_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tcp_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* a_st = smem;
+  uint8_t* b_st = smem + kTcPStages * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(b_st + kTcPStages * kBBytes);
+  uint64_t* empty = full + kTcPStages;
+  uint64_t* acc_full = empty + kTcPStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = (p.rows + kTcBM - 1) / kTcBM, nt = (p.T + BN - 1) / BN;
+  const int ntiles = mt * nt;
+  const int nk = p.cols / kTcBK;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < kTcPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&wmap);
+    tma_prefetch_desc(&xmap);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;  // stage uses across all tiles of this CTA
+      bool ok = true;
+      #pragma unroll 1
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % mt) * kTcBM, t0 = (tile / mt) * BN;
+        #pragma unroll 1
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = static_cast<int>(it % kTcPStages);
+          ok = tc_wait(&empty[s], ((it / kTcPStages) & 1) ^ 1, p.err);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+          tma_load_2d(a_st + s * kABytes, &wmap, kt * kTcBK, m0, &full[s]);
+          tma_load_2d(b_st + s * kBBytes, &xmap, kt * kTcBK, t0, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(BN);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      #pragma unroll 1
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++local) {
+        const int b = local & 1;
+        // the epilogue has drained this accumulator (its previous use)
+        ok = tc_wait(&acc_empty[b], static_cast<uint32_t>(((local >> 1) & 1) ^ 1), p.err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + static_cast<uint32_t>(b * BN);
+        #pragma unroll 1
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = static_cast<int>(it % kTcPStages);
+          ok = tc_wait(&full[s], (it / kTcPStages) & 1, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(a_st + s * kABytes), b0 = smem_u32(b_st + s * kBBytes);
+#pragma unroll
+          for (int k = 0; k < kTcBK / 16; ++k)
+            umma_f16(acc, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (kt | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[b]);
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    int local = 0;
+    bool ok = true;
+    #pragma unroll 1
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++local) {
+      const int b = local & 1;
+      const int m0 = (tile % mt) * kTcBM, t0 = (tile / mt) * BN;
+      const int row = m0 + quad * 32 + lane;
+      ok = tc_wait(&acc_full[b], static_cast<uint32_t>((local >> 1) & 1), p.err);
+      tc_fence_after();
+      if (!ok) break;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(b * BN + c0), v);
+        if (row < p.rows) {
+          if (p.resid) {
+            float r[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int t = t0 + c0 + j;
+              r[j] = t < p.T ? p.resid[static_cast<size_t>(t) * p.y_ld + row] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += r[j];
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int t = t0 + c0 + j;
+            if (t < p.T) p.y[static_cast<size_t>(t) * p.y_ld + row] = v[j];
+          }
+        }
+      }
+      // this accumulator may be overwritten by the tile after next
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
 }  // namespace kib

@@ -620,6 +620,32 @@ bool gemm_tc_enabled() {
   return on;
 }
 
+bool gemm_tc_persist_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("KIB_GEMM_TC_PERSIST");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <int BN>
+cudaError_t gemm_tc_persist_launch(const __half* w16, const __half* x16, const GemmTcParams& p, int num_sms,
+                                   cudaStream_t st) {
+  CUtensorMap wm, xm;
+  if (!f16_tensor_map(&wm, w16, p.rows, p.cols, kTcBM) || !f16_tensor_map(&xm, x16, p.T, p.cols, BN))
+    return cudaErrorInvalidValue;
+  static bool cfg = false;
+  constexpr size_t smem = gemm_tc_persist_smem<BN>();
+  if (!cfg) {
+    const cudaError_t e = cudaFuncSetAttribute(gemm_tc_persist_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cfg = true;
+  }
+  const int tiles = ((p.rows + kTcBM - 1) / kTcBM) * ((p.T + BN - 1) / BN);
+  return launch_pdl(gemm_tc_persist_kernel<BN>, dim3(std::min(tiles, num_sms)), dim3(kTcThreads), smem, st, wm, xm, p);
+}
+
 template <int BN>
 cudaError_t gemm_tc_launch(const __half* w16, const __half* x16, const GemmTcParams& p, cudaStream_t st) {
   CUtensorMap wm, xm;
@@ -753,7 +779,18 @@ cudaError_t gemm_f16w_launch(int type, const void* w, const __half* w16_resident
     tp.y_ld = y_ld;
     tp.resid = resid;
     tp.err = err;
-    e = tc_host::gemm_tc_launch<128>(wsrc, x16, tp, st);
+    static const int tc_bn = [] {
+      const char* v = std::getenv("KIB_GEMM_TC_BN");
+      return v && std::atoi(v) == 256 ? 256 : 128;
+    }();
+    // tile width by the cost model rounds x width: 64-token tiles when they
+    // halve the rounds (narrow matrices whose 128-wide tiles leave SMs idle)
+    const int mt = (rows + kTcBM - 1) / kTcBM;
+    const int r128 = (mt * ((T + 127) / 128) + num_sms - 1) / num_sms, r64 = (mt * ((T + 63) / 64) + num_sms - 1) / num_sms;
+    if (!tc_host::gemm_tc_persist_enabled()) e = tc_host::gemm_tc_launch<128>(wsrc, x16, tp, st);
+    else if (tc_bn == 256 && T >= 256) e = tc_host::gemm_tc_persist_launch<256>(wsrc, x16, tp, num_sms, st);
+    else if (64 * r64 < 128 * r128) e = tc_host::gemm_tc_persist_launch<64>(wsrc, x16, tp, num_sms, st);
+    else e = tc_host::gemm_tc_persist_launch<128>(wsrc, x16, tp, num_sms, st);
     if (e != cudaErrorInvalidValue) return e;
     cudaGetLastError();
   }
