@@ -454,6 +454,44 @@ int kib_prefix_index_commit(kib_prefix_index* index, const int64_t* tokens, uint
 /* stored blocks, hit tokens, miss tokens, committed tokens, evicted blocks, block tokens. */
 void kib_prefix_index_stats(const kib_prefix_index* index, uint64_t* out6);
 
+/* ------------------------------------------------------- GGUF tokenizer
+ * Byte-level BPE from the GGUF's tokenizer.ggml.* metadata, the Qwen3.5
+ * pre-tokenizer and chat prompt (GgufTokenizer,
+ * include/toyllm/runtime/gguf_tokenizer.hpp:27-66; src/runtime/gguf_tokenizer.cpp).
+ * Host only (also exported by libkib_gguf.so).  Calls that produce ids or text
+ * return the element count of the full result and write it only when it fits
+ * in cap (call with out = NULL, cap = 0 to size the buffer); -1 on error, the
+ * reference's message in kib_tokenizer_last_error. */
+typedef struct kib_tokenizer kib_tokenizer;
+/* load_gguf_tokenizer (gguf_tokenizer.cpp:628-677); NULL on error, reason in kib_tokenizer_load_error(). */
+kib_tokenizer* kib_tokenizer_load(const char* gguf_path);
+const char* kib_tokenizer_load_error(void);
+void kib_tokenizer_free(kib_tokenizer* tok);
+const char* kib_tokenizer_last_error(const kib_tokenizer* tok);
+/* info9: tokens, merges, bos, eos, pad, add_bos, add_eos, <|im_start|> id, <|im_end|> id (-1 when absent). */
+void kib_tokenizer_info(const kib_tokenizer* tok, int64_t* info9);
+/* which: 0 tokenizer.ggml.model, 1 tokenizer.ggml.pre, 2 tokenizer.chat_template. */
+int64_t kib_tokenizer_meta(const kib_tokenizer* tok, int which, char* out, uint64_t cap);
+/* gguf_token_id (gguf_tokenizer.cpp:679-686): -1 when absent. */
+int64_t kib_tokenizer_token_id(const kib_tokenizer* tok, const char* text, uint64_t len);
+int64_t kib_tokenizer_token_text(const kib_tokenizer* tok, int64_t id, char* out, uint64_t cap);
+int64_t kib_tokenizer_token_type(const kib_tokenizer* tok, int64_t id);
+/* gguf_token_is_control (gguf_tokenizer.cpp:688-695): control or unused. */
+int kib_tokenizer_is_control(const kib_tokenizer* tok, int64_t id);
+/* gguf_encode_text (gguf_tokenizer.cpp:697-738). */
+int64_t kib_tokenizer_encode(kib_tokenizer* tok, const char* text, uint64_t len, int add_special, int parse_special,
+                             int64_t* out, uint64_t cap);
+/* gguf_decode_token_text (gguf_tokenizer.cpp:751-775). */
+int64_t kib_tokenizer_decode(kib_tokenizer* tok, const int64_t* ids, uint64_t count, int skip_control, char* out,
+                             uint64_t cap);
+/* format_qwen35_chat_prompt (gguf_tokenizer.cpp:777-809): n messages of (role, content), NUL-terminated. */
+int64_t kib_tokenizer_format_chat(kib_tokenizer* tok, const char* const* roles, const char* const* contents,
+                                  uint64_t n, int add_generation_prompt, int enable_thinking, char* out, uint64_t cap);
+/* gguf_encode_qwen35_chat_prompt (gguf_tokenizer.cpp:740-749). */
+int64_t kib_tokenizer_encode_chat(kib_tokenizer* tok, const char* const* roles, const char* const* contents,
+                                  uint64_t n, int add_generation_prompt, int enable_thinking, int64_t* out,
+                                  uint64_t cap);
+
 #ifdef __cplusplus
 }
 #endif

@@ -16,10 +16,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libkib.so")
-SOURCES = ["ops.cu", "ops_seam.cu", "engine.cu", "noalloc.cu", "gguf.cpp", "gguf_tools.cpp", "prefix_cache.cpp"]
+SOURCES = ["ops.cu", "ops_seam.cu", "engine.cu", "noalloc.cu", "gguf.cpp", "gguf_tools.cpp", "prefix_cache.cpp", "tokenizer.cpp"]
 TOOLS_LIB = os.path.join(LIB_DIR, "libkib_gguf.so")
-TOOLS_SOURCES = ["gguf.cpp", "gguf_tools.cpp", "prefix_cache.cpp"]
-HEADERS = ["prefix_cache.hpp", "kq_skinny.cuh", "batch_kernels.cuh", "gdn_chunk.cuh", "gemm_tc.cuh", "kib_common.cuh", "kquant.cuh", "kquant_gemv.cuh", "kquant_gemv2.cuh", "decode_persistent.cuh", "layer_kernels.cuh", "kib_ctx.cuh", "gguf.hpp"]
+TOOLS_SOURCES = ["gguf.cpp", "gguf_tools.cpp", "prefix_cache.cpp", "tokenizer.cpp"]
+HEADERS = ["tokenizer.hpp", "prefix_cache.hpp", "kq_skinny.cuh", "batch_kernels.cuh", "gdn_chunk.cuh", "gemm_tc.cuh", "kib_common.cuh", "kquant.cuh", "kquant_gemv.cuh", "kquant_gemv2.cuh", "decode_persistent.cuh", "layer_kernels.cuh", "kib_ctx.cuh", "gguf.hpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-pthread",

@@ -310,7 +310,7 @@ std::unique_ptr<GgufFile> GgufFile::open(const std::string& path, std::string* e
       if (!c.ok || n > g->size_) return fail("corrupt GGUF array");
       for (uint64_t j = 0; j < n && c.ok; ++j) {
         if (v.type == kString) {
-          c.str();
+          v.strs.push_back(c.str());
         } else {
           bool ok;
           v.arr.push_back(read_num(c, v.type, &ok));

@@ -30,6 +30,7 @@ struct GgufValue {
   double num = 0.0;
   std::string str;
   std::vector<double> arr;
+  std::vector<std::string> strs;  // elements of a string array
 };
 
 class GgufFile {

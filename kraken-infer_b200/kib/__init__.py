@@ -34,6 +34,7 @@ class KibError(RuntimeError):
     def __init__(self, code, message):
         super().__init__(f"kib error {code}: {message}")
         self.code = code
+        self.message = message
 
 
 _lib = None
@@ -84,8 +85,40 @@ def load_tools_library(path: str = TOOLS_LIB_PATH) -> ctypes.CDLL:
                                             POINTER(c_uint64)]
     lib.kib_prefix_index_stats.restype = None
     lib.kib_prefix_index_stats.argtypes = [c_void_p, c_void_p]
+    _declare_tokenizer(lib)
     _tools = lib
     return lib
+
+
+def _declare_tokenizer(lib):
+    i64 = ctypes.c_int64
+    lib.kib_tokenizer_load.restype = c_void_p
+    lib.kib_tokenizer_load.argtypes = [c_char_p]
+    lib.kib_tokenizer_load_error.restype = c_char_p
+    lib.kib_tokenizer_load_error.argtypes = []
+    lib.kib_tokenizer_free.restype = None
+    lib.kib_tokenizer_free.argtypes = [c_void_p]
+    lib.kib_tokenizer_last_error.restype = c_char_p
+    lib.kib_tokenizer_last_error.argtypes = [c_void_p]
+    lib.kib_tokenizer_info.restype = None
+    lib.kib_tokenizer_info.argtypes = [c_void_p, c_void_p]
+    lib.kib_tokenizer_meta.restype = i64
+    lib.kib_tokenizer_meta.argtypes = [c_void_p, c_int, c_void_p, c_uint64]
+    lib.kib_tokenizer_token_id.restype = i64
+    lib.kib_tokenizer_token_id.argtypes = [c_void_p, c_char_p, c_uint64]
+    lib.kib_tokenizer_token_text.restype = i64
+    lib.kib_tokenizer_token_text.argtypes = [c_void_p, i64, c_void_p, c_uint64]
+    lib.kib_tokenizer_token_type.restype = i64
+    lib.kib_tokenizer_token_type.argtypes = [c_void_p, i64]
+    lib.kib_tokenizer_is_control.restype = c_int
+    lib.kib_tokenizer_is_control.argtypes = [c_void_p, i64]
+    lib.kib_tokenizer_encode.restype = i64
+    lib.kib_tokenizer_encode.argtypes = [c_void_p, c_char_p, c_uint64, c_int, c_int, c_void_p, c_uint64]
+    lib.kib_tokenizer_decode.restype = i64
+    lib.kib_tokenizer_decode.argtypes = [c_void_p, c_void_p, c_uint64, c_int, c_void_p, c_uint64]
+    for f in (lib.kib_tokenizer_format_chat, lib.kib_tokenizer_encode_chat):
+        f.restype = i64
+        f.argtypes = [c_void_p, c_void_p, c_void_p, c_uint64, c_int, c_int, c_void_p, c_uint64]
 
 
 class Qwen35Options(ctypes.Structure):
@@ -413,6 +446,24 @@ class Qwen35:
         self.ctx.check(self.lib.kib_generate_qwen35(self.h, byref(rq), out.ctypes.data, max_new_tokens, byref(res)))
         return out[: res.generated_tokens].copy(), res
 
+    def chat(self, tokenizer: "Tokenizer", messages, max_new_tokens, enable_thinking=False, **generate_kw):
+        """A chat request end to end, as the reference's Qwen3.5 generate does
+        it (qwen35_runtime.cpp:5392-5427, 6634): (role, content) messages ->
+        format_qwen35_chat_prompt with the generation prompt -> gguf_encode_text
+        (specials parsed) -> generate -> gguf_decode_token_text skipping
+        control tokens.  Returns (text, ids, GenerationResult)."""
+        return self._text_turn(tokenizer, tokenizer.encode_chat(messages, True, enable_thinking), max_new_tokens,
+                               generate_kw)
+
+    def complete(self, tokenizer: "Tokenizer", prompt, max_new_tokens, parse_special=False, **generate_kw):
+        """A plain-prompt request (no chat framing): gguf_encode_text(prompt,
+        add_special=False, parse_special) -> generate -> text."""
+        return self._text_turn(tokenizer, tokenizer.encode(prompt, False, parse_special), max_new_tokens,
+                               generate_kw)
+
+    def _text_turn(self, tokenizer, prompt_ids, max_new_tokens, generate_kw):
+        ids, res = self.generate(prompt_ids, max_new_tokens, **generate_kw)
+        return tokenizer.decode([int(i) for i in ids], skip_control=True), ids, res
 
 class PromptCache:
     """Host prefix cache of one model (kib_qwen35_prefix_cache_*)."""
@@ -572,6 +623,118 @@ class PrefixIndex:
         out = np.zeros(6, np.uint64)
         self.lib.kib_prefix_index_stats(self.h, out.ctypes.data)
         return [int(x) for x in out]
+
+
+class Tokenizer:
+    """GGUF byte-level BPE tokenizer + Qwen3.5 chat prompt (host only).
+
+    Mirrors the reference's GgufTokenizer functions
+    (include/toyllm/runtime/gguf_tokenizer.hpp:44-66): load_gguf_tokenizer ->
+    Tokenizer(path), gguf_encode_text -> encode, gguf_decode_token_text ->
+    decode, format_qwen35_chat_prompt -> format_chat,
+    gguf_encode_qwen35_chat_prompt -> encode_chat, gguf_token_id -> token_id,
+    gguf_token_is_control -> is_control.  Errors raise
+    KibError(KIB_ERR_INVALID_ARGUMENT, <the reference's message>).
+    Messages are (role, content) pairs."""
+
+    def __init__(self, path: str):
+        self.lib = load_tools_library()
+        self.h = self.lib.kib_tokenizer_load(path.encode())
+        if not self.h:
+            raise KibError(KIB_ERR_INVALID_ARGUMENT, self.lib.kib_tokenizer_load_error().decode())
+        import numpy as np
+        info = np.zeros(9, np.int64)
+        self.lib.kib_tokenizer_info(self.h, info.ctypes.data)
+        (self.n_tokens, self.n_merges, self.bos_token_id, self.eos_token_id, self.pad_token_id,
+         add_bos, add_eos, self.im_start_id, self.im_end_id) = [int(x) for x in info]
+        self.add_bos_token, self.add_eos_token = bool(add_bos), bool(add_eos)
+        self.model = self._text(lambda b, n: self.lib.kib_tokenizer_meta(self.h, 0, b, n)).decode()
+        self.pre = self._text(lambda b, n: self.lib.kib_tokenizer_meta(self.h, 1, b, n)).decode()
+        self.chat_template = self._text(lambda b, n: self.lib.kib_tokenizer_meta(self.h, 2, b, n)).decode()
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.kib_tokenizer_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def __len__(self):
+        return self.n_tokens
+
+    def _fail(self):
+        raise KibError(KIB_ERR_INVALID_ARGUMENT, self.lib.kib_tokenizer_last_error(self.h).decode())
+
+    def _text(self, call) -> bytes:
+        n = call(None, 0)
+        if n < 0:
+            self._fail()
+        buf = ctypes.create_string_buffer(max(1, n))
+        call(buf, n)
+        return buf.raw[:n]
+
+    def _ids(self, call, bound=0):
+        """bound: a capacity known to suffice (one call instead of two)."""
+        import numpy as np
+        out = np.zeros(max(1, bound), np.int64)
+        n = call(out.ctypes.data, bound) if bound else call(None, 0)
+        if n < 0:
+            self._fail()
+        if n > bound:
+            out = np.zeros(n, np.int64)
+            call(out.ctypes.data, n)
+        return [int(x) for x in out[:n]]
+
+    @staticmethod
+    def _raw(text):
+        return text if isinstance(text, bytes) else text.encode("utf-8")
+
+    def encode(self, text, add_special: bool = False, parse_special: bool = False):
+        b = self._raw(text)
+        # every id covers at least one byte, plus BOS and EOS
+        return self._ids(lambda o, n: self.lib.kib_tokenizer_encode(self.h, b, len(b), int(add_special),
+                                                                    int(parse_special), o, n), len(b) + 2)
+
+    def decode_bytes(self, ids, skip_control: bool = False) -> bytes:
+        import numpy as np
+        a = np.ascontiguousarray(ids, dtype=np.int64)
+        return self._text(lambda o, n: self.lib.kib_tokenizer_decode(self.h, a.ctypes.data, len(a),
+                                                                     int(skip_control), o, n))
+
+    def decode(self, ids, skip_control: bool = False) -> str:
+        return self.decode_bytes(ids, skip_control).decode("utf-8", errors="replace")
+
+    def _messages(self, messages):
+        roles = [self._raw(r) for r, _ in messages]
+        contents = [self._raw(c) for _, c in messages]
+        n = len(messages)
+        return (c_char_p * max(1, n))(*roles), (c_char_p * max(1, n))(*contents), n
+
+    def format_chat(self, messages, add_generation_prompt: bool = True, enable_thinking: bool = False) -> str:
+        r, c, n = self._messages(messages)
+        return self._text(lambda o, k: self.lib.kib_tokenizer_format_chat(
+            self.h, r, c, n, int(add_generation_prompt), int(enable_thinking), o, k)).decode("utf-8", "replace")
+
+    def encode_chat(self, messages, add_generation_prompt: bool = True, enable_thinking: bool = False):
+        r, c, n = self._messages(messages)
+        return self._ids(lambda o, k: self.lib.kib_tokenizer_encode_chat(
+            self.h, r, c, n, int(add_generation_prompt), int(enable_thinking), o, k))
+
+    def token_id(self, text):
+        """The id of a token's exact text, or None."""
+        b = self._raw(text)
+        i = self.lib.kib_tokenizer_token_id(self.h, b, len(b))
+        return None if i < 0 else int(i)
+
+    def token_text(self, id_: int) -> bytes:
+        return self._text(lambda o, n: self.lib.kib_tokenizer_token_text(self.h, id_, o, n))
+
+    def token_type(self, id_: int) -> int:
+        return int(self.lib.kib_tokenizer_token_type(self.h, id_))
+
+    def is_control(self, id_: int) -> bool:
+        return bool(self.lib.kib_tokenizer_is_control(self.h, id_))
 
 
 def quantize(qtype: int, x):

@@ -10,6 +10,9 @@
 #include KIB_STR(KIB_REF_RUNTIME_TU)
 
 #include <cstring>
+#include <map>
+
+#include "toyllm/runtime/gguf_tokenizer.hpp"
 
 extern "C" {
 
@@ -125,6 +128,109 @@ int ref_prefix_script(unsigned long long block_tokens, unsigned long long capaci
   stats6[4] = st.evicted_blocks;
   stats6[5] = st.block_tokens;
   return 0;
+}
+
+// ---- GgufTokenizer (src/runtime/gguf_tokenizer.cpp) over a GGUF file, to pin
+// the repository's tokenizer against the reference's own.  ref_tok_load reads
+// (or re-reads) the file and keeps the tokenizer for the other calls on the
+// same path.  Each call returns its element count or -1 with err filled.
+namespace {
+std::map<std::string, toyllm::GgufTokenizer> g_ref_toks;
+
+int ref_fail(char* err, int err_len, const std::string& m) {
+  if (err && err_len > 0) {
+    std::strncpy(err, m.c_str(), static_cast<size_t>(err_len - 1));
+    err[err_len - 1] = 0;
+  }
+  return -1;
+}
+
+const toyllm::GgufTokenizer* ref_tok(const char* path, char* err, int err_len, bool reload) {
+  auto it = g_ref_toks.find(path);
+  if (it != g_ref_toks.end() && !reload) return &it->second;
+  auto gguf = toyllm::read_gguf_file(path);
+  if (!gguf.is_ok()) {
+    ref_fail(err, err_len, gguf.status().message());
+    return nullptr;
+  }
+  auto tok = toyllm::load_gguf_tokenizer(gguf.value());
+  if (!tok.is_ok()) {
+    ref_fail(err, err_len, tok.status().message());
+    return nullptr;
+  }
+  g_ref_toks[path] = tok.value();
+  return &g_ref_toks[path];
+}
+
+std::vector<toyllm::ChatMessage> ref_messages(const char* const* roles, const char* const* contents, int n) {
+  std::vector<toyllm::ChatMessage> m;
+  for (int i = 0; i < n; ++i) m.emplace_back(roles[i], contents[i]);
+  return m;
+}
+
+long long ref_put_ids(const std::vector<std::int64_t>& ids, long long* out, unsigned long long cap) {
+  for (size_t i = 0; i < ids.size() && i < cap; ++i) out[i] = ids[i];
+  return static_cast<long long>(ids.size());
+}
+
+long long ref_put_text(const std::string& s, char* out, unsigned long long cap) {
+  if (s.size() <= cap) std::memcpy(out, s.data(), s.size());
+  return static_cast<long long>(s.size());
+}
+}  // namespace
+
+// info9: tokens, merges, bos, eos, pad, add_bos, add_eos, <|im_start|>, <|im_end|> (-1 when absent)
+int ref_tok_load(const char* path, long long* info9, char* err, int err_len) {
+  const auto* t = ref_tok(path, err, err_len, true);
+  if (!t) return -1;
+  const auto im_s = toyllm::gguf_token_id(*t, "<|im_start|>");
+  const auto im_e = toyllm::gguf_token_id(*t, "<|im_end|>");
+  const long long v[9] = {static_cast<long long>(t->tokens.size()), static_cast<long long>(t->merges.size()),
+                          t->bos_token_id, t->eos_token_id, t->pad_token_id, t->add_bos_token, t->add_eos_token,
+                          im_s ? *im_s : -1, im_e ? *im_e : -1};
+  for (int i = 0; i < 9; ++i) info9[i] = v[i];
+  return 0;
+}
+
+long long ref_tok_encode(const char* path, const char* text, unsigned long long len, int add_special,
+                         int parse_special, long long* out, unsigned long long cap, char* err, int err_len) {
+  const auto* t = ref_tok(path, err, err_len, false);
+  if (!t) return -1;
+  auto r = toyllm::gguf_encode_text(*t, std::string_view(text, len), add_special != 0, parse_special != 0);
+  if (!r.is_ok()) return ref_fail(err, err_len, r.status().message());
+  return ref_put_ids(r.value(), out, cap);
+}
+
+long long ref_tok_decode(const char* path, const long long* ids, unsigned long long n, int skip_control, char* out,
+                         unsigned long long cap, char* err, int err_len) {
+  const auto* t = ref_tok(path, err, err_len, false);
+  if (!t) return -1;
+  std::vector<std::int64_t> v(ids, ids + n);
+  auto r = toyllm::gguf_decode_token_text(*t, v, skip_control != 0);
+  if (!r.is_ok()) return ref_fail(err, err_len, r.status().message());
+  return ref_put_text(r.value(), out, cap);
+}
+
+long long ref_tok_format_chat(const char* path, const char* const* roles, const char* const* contents, int n,
+                              int add_generation_prompt, int enable_thinking, char* out, unsigned long long cap,
+                              char* err, int err_len) {
+  const auto* t = ref_tok(path, err, err_len, false);
+  if (!t) return -1;
+  auto r = toyllm::format_qwen35_chat_prompt(*t, ref_messages(roles, contents, n), add_generation_prompt != 0,
+                                             enable_thinking != 0);
+  if (!r.is_ok()) return ref_fail(err, err_len, r.status().message());
+  return ref_put_text(r.value(), out, cap);
+}
+
+long long ref_tok_encode_chat(const char* path, const char* const* roles, const char* const* contents, int n,
+                              int add_generation_prompt, int enable_thinking, long long* out,
+                              unsigned long long cap, char* err, int err_len) {
+  const auto* t = ref_tok(path, err, err_len, false);
+  if (!t) return -1;
+  auto r = toyllm::gguf_encode_qwen35_chat_prompt(*t, ref_messages(roles, contents, n), add_generation_prompt != 0,
+                                                  enable_thinking != 0);
+  if (!r.is_ok()) return ref_fail(err, err_len, r.status().message());
+  return ref_put_ids(r.value(), out, cap);
 }
 
 }  // extern "C"

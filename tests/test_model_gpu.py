@@ -222,3 +222,27 @@ def test_forward_one_token_argmax_matches_decode(ctx, small_model):
     assert m.position == 20 + 16
     m.close()
     assert got == toks
+
+
+def test_chat_text_end_to_end_matches_oracle(ctx, oracle, small_model, tmp_path):
+    """Messages -> chat prompt ids (the GGUF tokenizer) -> GPU generate ->
+    text: the ids are the oracle's greedy continuation of the encoded prompt
+    and the text is their decoding with control tokens skipped."""
+    import tok_fixtures as tf
+    tokens, types, merges = tf.fuzz_vocab(4, complete=True)
+    assert len(tokens) < SMALL["vocab"]
+    types += [tf.NORMAL] * (SMALL["vocab"] - len(tokens))  # every id the model can emit decodes
+    tokens += [f"<fill_{i}>" for i in range(len(tokens), SMALL["vocab"])]
+    tok = kib.Tokenizer(tf.write_kv_gguf(str(tmp_path / "tok.gguf"), tf.tokenizer_kv(tokens, types, merges)))
+    msgs = [("system", "be brief"), ("user", "hello world, abc dea bad cab?")]
+    m = kib.Qwen35(ctx, small_model, context_tokens=256, decode_tokens=96)
+    text, ids, res = m.chat(tok, msgs, 24, ignore_eos=True)
+    p = np.array(tok.encode_chat(msgs, True, False), np.int32)
+    assert res.prompt_tokens == len(p) and p[0] == tok.im_start_id
+    om = oracle_lib.OracleModel(oracle, small_model, m.plan.attention_capacity_tokens)
+    _, _, lg = om.forward(p, 0)
+    ot, _ = om.generate_from(len(p), int(np.argmax(lg[-1])), 24)
+    assert list(ids) == list(ot)
+    assert text == tok.decode([int(i) for i in ids], skip_control=True)
+    om.close()
+    m.close()
