@@ -48,12 +48,14 @@ cudaError_t kq_skinny_launch(int type, const void* w, int rows, int cols, const 
                              int y_ld, const float* resid, float* ws, int num_sms, cudaStream_t st, bool xsplit);
 cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const int* ids, int T, float* out,
                             int out_ld, cudaStream_t st);
-cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st);
+// out16: also the rows rounded to half (the prefill GEMMs' input), or null
+cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st,
+                            __half* out16 = nullptr);
 cudaError_t norm_gate_launch(float* v, const float* w, const float* gate, int T, int heads, int d, float eps,
-                             float* out, cudaStream_t st);
+                             float* out, cudaStream_t st, __half* out16 = nullptr);
 cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w, int K, int C, int T, float* out,
                         int out_ld, int silu, cudaStream_t st);
-cudaError_t silu_mul_launch(float* g, const float* u, size_t n, cudaStream_t st);
+cudaError_t silu_mul_launch(float* g, const float* u, size_t n, cudaStream_t st, __half* out16 = nullptr);
 }  // namespace kib
 
 using namespace kib;
@@ -440,12 +442,15 @@ void main_layers_small(Enq& q, int T, const int* pos) {
 // ---- prefill (T > 8) blocks ----------------------------------------------------
 
 // same_x: x is the input of the previous gemm() call, unchanged since (its f16
-// copy is reused).
+// copy is reused).  x16_ready: the kernel that wrote x also wrote its half
+// copy into d_x16 ([T][cols] packed), used as is above 8 tokens (the 4..8
+// bucket splits x itself).
 void gemm(Enq& q, const DevT& w, const float* x, int x_ld, int T, float* y, int y_ld, const float* resid = nullptr,
-          bool same_x = false) {
+          bool same_x = false, bool x16_ready = false) {
   if (q.m->d_w16 && w.cols() % 64 == 0 && x_ld % 4 == 0)
     q.run(gemm_f16w_launch(w.type, w.p, w.h, w.rows(), w.cols(), x, x_ld, T, y, y_ld, resid, q.m->d_w16, q.m->d_x16,
-                           !same_x, q.m->ctx->num_sms, q.st, q.m->ctx->d_err),
+                           !same_x && !(x16_ready && T > 8 && x_ld == w.cols()), q.m->ctx->num_sms, q.st,
+                           q.m->ctx->d_err),
           "gemm_f16w");
   else
     q.run(gemm_f16_launch(w.type, w.p, w.rows(), w.cols(), x, x_ld, T, y, y_ld, resid, q.st), "gemm");
@@ -454,8 +459,8 @@ void gemm(Enq& q, const DevT& w, const float* x, int x_ld, int T, float* y, int 
 void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, float* x_mid) {
   kib_qwen35* m = q.m;
   const int li = L.cache_index;
-  q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
-  gemm(q, L.qkv, m->d_norm, m->H, T, m->d_qkv, m->C);
+  q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st, m->d_x16), "rms");
+  gemm(q, L.qkv, m->d_norm, m->H, T, m->d_qkv, m->C, nullptr, false, true);
   q.run(conv_launch(m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1), m->d_qkv, m->C, L.conv1d.f(), m->convk,
                     m->C, T, m->d_qkv, m->C, 1, q.st),
         "conv");
@@ -491,6 +496,9 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
       q.run(cudaFuncSetAttribute(gdn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kGcScanSmem)),
             "gdn_chunk_attr");
+      q.run(cudaFuncSetAttribute(gdn_chunk_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kGcScanTcSmem)),
+            "gdn_chunk_attr");
       chunk_cfg = true;
     }
     GdnChunkParams gc;
@@ -507,8 +515,16 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
     gc.value_heads = m->lvh;
     q.run(launch_pdl(gdn_chunk_prep_kernel, dim3(m->lvh, (T + kGc - 1) / kGc), dim3(256), kGcPrepSmem, q.st, gc),
           "gdn_chunk_prep");
-    q.run(launch_pdl(gdn_chunk_scan_kernel, dim3(m->lvh, kGcD / kGcRows), dim3(256), kGcScanSmem, q.st, gc),
-          "gdn_chunk_scan");
+    static const bool scan_tc = [] {
+      const char* v = std::getenv("KIB_GDN_SCAN_TC");
+      return !(v && v[0] == '0');
+    }();
+    if (scan_tc)
+      q.run(launch_pdl(gdn_chunk_scan_tc_kernel, dim3(m->lvh, kGcD / kGcRows), dim3(256), kGcScanTcSmem, q.st, gc),
+            "gdn_chunk_scan_tc");
+    else
+      q.run(launch_pdl(gdn_chunk_scan_kernel, dim3(m->lvh, kGcD / kGcRows), dim3(256), kGcScanSmem, q.st, gc),
+            "gdn_chunk_scan");
   } else if (m->lhd == 128 && m->lkh <= m->lvh && m->C % 4 == 0) {
     // token-parallel norms and gate/beta first, then the sequential scan alone
     q.run(launch_pdl(gdn_prep_kernel, dim3(T, m->lkh), dim3(128), 0, q.st, m->d_qkv, m->C, m->d_alpha, m->d_beta, m->lvh,
@@ -525,15 +541,16 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
   } else {
     q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
   }
-  q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, T, m->lvh, m->lhd, m->eps, m->d_norm2, q.st), "norm_gate");
-  gemm(q, L.ssm_out, m->d_norm2, m->VD, T, x_mid, m->H, x_in);
+  q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, T, m->lvh, m->lhd, m->eps, m->d_norm2, q.st, m->d_x16),
+        "norm_gate");
+  gemm(q, L.ssm_out, m->d_norm2, m->VD, T, x_mid, m->H, x_in, false, true);
 }
 
 void attention_block_prefill(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc, const int* pos, int T,
                              const float* x_in, float* x_mid) {
   kib_qwen35* m = q.m;
-  q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
-  gemm(q, L.q, m->d_norm, m->H, T, m->d_qg, 2 * m->AD);
+  q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st, m->d_x16), "rms");
+  gemm(q, L.q, m->d_norm, m->H, T, m->d_qg, 2 * m->AD, nullptr, false, true);
   gemm(q, L.k, m->d_norm, m->H, T, m->d_kp, m->KD, nullptr, true);
   gemm(q, L.v, m->d_norm, m->H, T, m->d_vp, m->KD, nullptr, true);
   const AttnParams a = attn_params(m, L, kc, vc, pos, T);
@@ -556,11 +573,11 @@ void attention_block_prefill(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc
 
 void ffn_prefill(Enq& q, const LayerW& L, int T, const float* x_mid, float* x_out) {
   kib_qwen35* m = q.m;
-  q.run(rms_rows_launch(x_mid, L.post_norm.f(), T, m->H, m->eps, m->d_norm, q.st), "rms");
-  gemm(q, L.ffn_gate, m->d_norm, m->H, T, m->d_act, m->I);
+  q.run(rms_rows_launch(x_mid, L.post_norm.f(), T, m->H, m->eps, m->d_norm, q.st, m->d_x16), "rms");
+  gemm(q, L.ffn_gate, m->d_norm, m->H, T, m->d_act, m->I, nullptr, false, true);
   gemm(q, L.ffn_up, m->d_norm, m->H, T, m->d_act2, m->I, nullptr, true);
-  q.run(silu_mul_launch(m->d_act, m->d_act2, static_cast<size_t>(T) * m->I, q.st), "silu_mul");
-  gemm(q, L.ffn_down, m->d_act, m->I, T, x_out, m->H, x_mid);
+  q.run(silu_mul_launch(m->d_act, m->d_act2, static_cast<size_t>(T) * m->I, q.st, m->d_x16), "silu_mul");
+  gemm(q, L.ffn_down, m->d_act, m->I, T, x_out, m->H, x_mid, false, true);
 }
 
 void main_layers_prefill(Enq& q, int T, const int* pos) {

@@ -30,7 +30,11 @@ namespace kib {
 constexpr int kGc = 64;     // tokens per chunk
 constexpr int kGcD = 128;   // head dimension (keys and values)
 constexpr int kGcRows = 16; // value rows per scan CTA
-constexpr int kGcWs = kGc * kGc * 2 + kGc * kGcD + kGc;  // workspace floats per (head, chunk)
+// workspace per (head, chunk): Tb [64][64], P [64][64], Kt [64][128], G [64],
+// then the decayed operands Qg = e^{G_i} q_i and Kd = e^{G_C - G_j} k_j [64][128]
+constexpr int kGcWsQg = kGc * kGc * 2 + kGc * kGcD + kGc;
+constexpr int kGcWsKd = kGcWsQg + kGc * kGcD;
+constexpr int kGcWs = kGcWsKd + kGc * kGcD;  // workspace floats per (head, chunk)
 
 struct GdnChunkParams {
   const float* conv_out;  // [T][C]: q | k (L2-normalised) | v
@@ -193,6 +197,19 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const __grid_consta
       *reinterpret_cast<float4*>(o + 4) = make_float4(acc[a][4], acc[a][5], acc[a][6], acc[a][7]);
     }
   }
+  // the scan's decayed operands: q rows by e^{G_i}, k rows by e^{G_C - G_j}
+  {
+    float* wQg = ws + kGcWsQg;
+    float* wKd = ws + kGcWsKd;
+    const float gend = G[kGc - 1];
+    for (int i = tid; i < kGc * kGcD / 4; i += 256) {
+      const int t = i >> 5;
+      const float fq = expf(G[t]), fk = expf(gend - G[t]);
+      const float4 qv = reinterpret_cast<const float4*>(qr)[i], kv = reinterpret_cast<const float4*>(kr)[i];
+      reinterpret_cast<float4*>(wQg)[i] = make_float4(qv.x * fq, qv.y * fq, qv.z * fq, qv.w * fq);
+      reinterpret_cast<float4*>(wKd)[i] = make_float4(kv.x * fk, kv.y * fk, kv.z * fk, kv.w * fk);
+    }
+  }
 }
 
 // ---------------------------------------------------------------- scan
@@ -338,6 +355,309 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_kernel(const __grid_consta
   for (int i = tid; i < kGcRows * kGcD / 4; i += 256) {
     const int rr = i >> 5, d4 = i & 31;
     reinterpret_cast<float4*>(S + rr * kGcD)[d4] = *reinterpret_cast<const float4*>(sS + rr * kGcSr + 4 * d4);
+  }
+}
+
+// ---------------------------------------------------------------- scan on the tensor cores
+// The same per-chunk products as gdn_chunk_scan_kernel on mma.sync m16n8k8
+// TF32 at fp32 accuracy: every operand is split into a TF32 high part and a
+// TF32 remainder, and a product is accumulated as lo*hi + hi*lo + hi*hi
+// (the remainder-by-remainder term is below fp32 rounding), in fp32.
+// One CTA per (value head, 16 value rows), 8 warps.  Warp w = (m-tile
+// mt = w & 3 of the chunk's 64 tokens, k-half kh = w >> 2):
+//   X1 = Kt S0^T and X2 = Qg S0^T over its k-half, both n-tiles of the 16
+//        value rows; the halves meet in shared memory, after which warp w owns
+//        n-tile kh of m-tile mt;
+//   U  = Tb V - X1 and Y = X2 + P U for that tile (P lower triangular: k up
+//        to the tile's last row);
+//   S  = e^{G_C} S + U^T Kd for d columns 16w .. 16w + 15, the state kept in
+//        the warp's accumulator registers across chunks (and written back to
+//        shared memory split into high and low parts for the next X products).
+// The next chunk's tiles stream in with cp.async while the current chunk
+// uses the other buffers: Kt / Qg after the X products, Tb / V after U, P /
+// Kd / G after the state update.
+constexpr int kTcLdK = 132;  // Kt, Qg, S rows: (g * 132 + t) mod 32 distinct over a warp
+constexpr int kTcLdKd = 136; // Kd rows read as B (k = token): (t * 136 + g) mod 32 distinct
+constexpr int kTcLdT = 68;   // Tb, P rows
+constexpr int kTcLdV = 24;   // V, U rows (16 value rows + 8)
+constexpr int kTcOffQg = kGc * kTcLdK;
+constexpr int kTcOffKd = kTcOffQg + kGc * kTcLdK;
+constexpr int kTcOffTb = kTcOffKd + kGc * kTcLdKd;
+constexpr int kTcOffP = kTcOffTb + kGc * kTcLdT;
+constexpr int kTcOffV = kTcOffP + kGc * kTcLdT;
+constexpr int kTcOffUh = kTcOffV + kGc * kTcLdV;
+constexpr int kTcOffUl = kTcOffUh + kGc * kTcLdV;
+constexpr int kTcOffSh = kTcOffUl + kGc * kTcLdV;
+constexpr int kTcOffSl = kTcOffSh + kGcRows * kTcLdK;
+constexpr int kTcOffX = kTcOffSl + kGcRows * kTcLdK;
+constexpr int kTcOffG = kTcOffX + 8 * 8 * 32;
+constexpr size_t kGcScanTcSmem = static_cast<size_t>(kTcOffG + kGc) * sizeof(float);
+
+KIB_DEV uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+KIB_DEV void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_rna(x);
+  lo = tf32_rna(x - __uint_as_float(hi));
+}
+KIB_DEV void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// d += A B with split operands: the two cross terms first, then the main one
+KIB_DEV void mma3(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0, uint32_t bh1,
+                  uint32_t bl0, uint32_t bl1) {
+  mma_tf32(d, al, bh0, bh1);
+  mma_tf32(d, ah, bl0, bl1);
+  mma_tf32(d, ah, bh0, bh1);
+}
+// A fragment (16 x 8, row-major source, rows m0.., columns k0..) split in two
+KIB_DEV void gc_lda(const float* s, int ld, int m0, int k0, int g, int t, uint32_t (&h)[4], uint32_t (&l)[4]) {
+  const float* p = s + (m0 + g) * ld + k0 + t;
+  tf32_split(p[0], h[0], l[0]);
+  tf32_split(p[8 * ld], h[1], l[1]);
+  tf32_split(p[4], h[2], l[2]);
+  tf32_split(p[8 * ld + 4], h[3], l[3]);
+}
+// B fragment (8 x 8) from a source stored with k along rows: B[k][n] = s[k * ld + n]
+KIB_DEV void gc_ldb_k(const float* s, int ld, int k0, int n0, int g, int t, uint32_t& h0, uint32_t& h1, uint32_t& l0,
+                      uint32_t& l1) {
+  const float* p = s + (k0 + t) * ld + n0 + g;
+  tf32_split(p[0], h0, l0);
+  tf32_split(p[4 * ld], h1, l1);
+}
+
+__global__ void __launch_bounds__(256) gdn_chunk_scan_tc_kernel(const __grid_constant__ GdnChunkParams p) {
+  extern __shared__ __align__(16) float tc_sm[];
+  float* sKt = tc_sm;
+  float* sQg = tc_sm + kTcOffQg;
+  float* sKd = tc_sm + kTcOffKd;
+  float* sTb = tc_sm + kTcOffTb;
+  float* sP = tc_sm + kTcOffP;
+  float* sV = tc_sm + kTcOffV;
+  float* sUh = tc_sm + kTcOffUh;
+  float* sUl = tc_sm + kTcOffUl;
+  float* sSh = tc_sm + kTcOffSh;
+  float* sSl = tc_sm + kTcOffSl;
+  float* sX = tc_sm + kTcOffX;
+  float* sG = tc_sm + kTcOffG;
+  const int h = blockIdx.x, r0 = blockIdx.y * kGcRows, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const int mt = warp & 3, kh = warp >> 2, m0 = 16 * mt;
+  const int key_dim = p.key_heads * kGcD;
+  const int nchunks = (p.T + kGc - 1) / kGc;
+  float* S = p.state + (static_cast<size_t>(h) * kGcD + r0) * kGcD;
+
+  // state fragment of warp w: rows g, g + 8 of the CTA's 16, columns
+  // 16w + 8nt + 2t (+1)
+  float sreg[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int d = 16 * warp + 8 * nt + 2 * t;
+    const float2 a = *reinterpret_cast<const float2*>(S + g * kGcD + d);
+    const float2 b = *reinterpret_cast<const float2*>(S + (g + 8) * kGcD + d);
+    sreg[nt][0] = a.x;
+    sreg[nt][1] = a.y;
+    sreg[nt][2] = b.x;
+    sreg[nt][3] = b.y;
+  }
+  auto put_state = [&]() {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int d = 16 * warp + 8 * nt + 2 * t;
+      uint32_t hi, lo;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        tf32_split(sreg[nt][e], hi, lo);
+        const int o = (g + 8 * (e >> 1)) * kTcLdK + d + (e & 1);
+        sSh[o] = __uint_as_float(hi);
+        sSl[o] = __uint_as_float(lo);
+      }
+    }
+  };
+  put_state();
+  pdl_wait();
+  pdl_launch_dependents();
+
+  auto ws_of = [&](int c) { return p.ws + (static_cast<size_t>(h) * nchunks + c) * kGcWs; };
+  auto issue_ktqg = [&](int c) {
+    if (c < nchunks) {
+      const float* ws = ws_of(c);
+      for (int i = tid; i < kGc * kGcD / 4; i += 256) {
+        const int tk = i >> 5, d4 = i & 31;
+        gc_cp16(sKt + tk * kTcLdK + 4 * d4, ws + 2 * kGc * kGc + 4 * i, true);
+        gc_cp16(sQg + tk * kTcLdK + 4 * d4, ws + kGcWsQg + 4 * i, true);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  auto issue_tbv = [&](int c) {
+    if (c < nchunks) {
+      const float* ws = ws_of(c);
+      const int t0 = c * kGc, n = min(kGc, p.T - t0);
+      for (int i = tid; i < kGc * kGc / 4; i += 256) {
+        const int r = i >> 4, j4 = i & 15;
+        gc_cp16(sTb + r * kTcLdT + 4 * j4, ws + 4 * i, true);
+      }
+      const int tk = tid >> 2, q4 = tid & 3;  // 64 tokens x 4 pieces of the 16 value rows
+      const bool ok = tk < n;
+      gc_cp16(sV + tk * kTcLdV + 4 * q4,
+              p.conv_out + static_cast<size_t>(t0 + (ok ? tk : 0)) * p.C + 2 * key_dim + h * kGcD + r0 + 4 * q4, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  auto issue_pkd = [&](int c) {
+    if (c < nchunks) {
+      const float* ws = ws_of(c);
+      for (int i = tid; i < kGc * kGc / 4; i += 256) {
+        const int r = i >> 4, j4 = i & 15;
+        gc_cp16(sP + r * kTcLdT + 4 * j4, ws + kGc * kGc + 4 * i, true);
+      }
+      for (int i = tid; i < kGc * kGcD / 4; i += 256) {
+        const int tk = i >> 5, d4 = i & 31;
+        gc_cp16(sKd + tk * kTcLdKd + 4 * d4, ws + kGcWsKd + 4 * i, true);
+      }
+      if (tid < kGc / 4) gc_cp16(sG + 4 * tid, ws + 2 * kGc * kGc + kGc * kGcD + 4 * tid, true);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  issue_ktqg(0);
+  issue_tbv(0);
+  issue_pkd(0);
+
+  const float scale = 1.0f / sqrtf(static_cast<float>(kGcD));
+  const size_t out_ld = static_cast<size_t>(p.value_heads) * kGcD;
+  const int nt_own = kh;  // n-tile this warp owns after the X exchange
+  for (int c = 0; c < nchunks; ++c) {
+    const int t0 = c * kGc, n = min(kGc, p.T - t0);
+    // ---- X1 = Kt S0^T, X2 = Qg S0^T over this warp's k-half
+    asm volatile("cp.async.wait_group 2;" ::: "memory");
+    __syncthreads();
+    float x1[2][4], x2[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x1[nt][e] = x2[nt][e] = 0.0f;
+#pragma unroll 2
+    for (int ks = 0; ks < 8; ++ks) {
+      const int k0 = 64 * kh + 8 * ks;
+      uint32_t bh[2][2], bl[2][2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int o = (8 * nt + g) * kTcLdK + k0 + t;
+        bh[nt][0] = __float_as_uint(sSh[o]);
+        bh[nt][1] = __float_as_uint(sSh[o + 4]);
+        bl[nt][0] = __float_as_uint(sSl[o]);
+        bl[nt][1] = __float_as_uint(sSl[o + 4]);
+      }
+      uint32_t ah[4], al[4];
+      gc_lda(sKt, kTcLdK, m0, k0, g, t, ah, al);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) mma3(x1[nt], ah, al, bh[nt][0], bh[nt][1], bl[nt][0], bl[nt][1]);
+      gc_lda(sQg, kTcLdK, m0, k0, g, t, ah, al);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) mma3(x2[nt], ah, al, bh[nt][0], bh[nt][1], bl[nt][0], bl[nt][1]);
+    }
+    // halves meet: the warp keeps n-tile kh, hands the other to warp w ^ 4
+    {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        sX[(warp * 8 + e) * 32 + lane] = nt_own ? x1[0][e] : x1[1][e];
+        sX[(warp * 8 + 4 + e) * 32 + lane] = nt_own ? x2[0][e] : x2[1][e];
+      }
+    }
+    __syncthreads();
+    float X1[4], X2[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float r1 = sX[((warp ^ 4) * 8 + e) * 32 + lane], r2 = sX[((warp ^ 4) * 8 + 4 + e) * 32 + lane];
+      // k-half 0 + k-half 1, in that order on both warps
+      X1[e] = kh == 0 ? x1[0][e] + r1 : r1 + x1[1][e];
+      X2[e] = kh == 0 ? x2[0][e] + r2 : r2 + x2[1][e];
+    }
+    issue_ktqg(c + 1);
+    // ---- U = Tb V - X1 for (mt, nt_own)
+    asm volatile("cp.async.wait_group 2;" ::: "memory");
+    __syncthreads();
+    float u[4] = {-X1[0], -X1[1], -X1[2], -X1[3]};
+#pragma unroll 2
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t ah[4], al[4], b0h, b1h, b0l, b1l;
+      gc_lda(sTb, kTcLdT, m0, 8 * ks, g, t, ah, al);
+      gc_ldb_k(sV, kTcLdV, 8 * ks, 8 * nt_own, g, t, b0h, b1h, b0l, b1l);
+      mma3(u, ah, al, b0h, b1h, b0l, b1l);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      uint32_t hi, lo;
+      tf32_split(u[e], hi, lo);
+      const int o = (m0 + g + 8 * (e >> 1)) * kTcLdV + 8 * nt_own + 2 * t + (e & 1);
+      sUh[o] = __uint_as_float(hi);
+      sUl[o] = __uint_as_float(lo);
+    }
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // P, Kd, G of this chunk
+    __syncthreads();
+    issue_tbv(c + 1);
+    // ---- Y = (X2 + P U) / sqrt(128) for (mt, nt_own): tokens up to the tile's last row
+    {
+      float y[4] = {X2[0], X2[1], X2[2], X2[3]};
+      for (int ks = 0; ks <= 2 * mt + 1; ++ks) {
+        uint32_t ah[4], al[4];
+        gc_lda(sP, kTcLdT, m0, 8 * ks, g, t, ah, al);
+        const int o = (8 * ks + t) * kTcLdV + 8 * nt_own + g;
+        mma3(y, ah, al, __float_as_uint(sUh[o]), __float_as_uint(sUh[o + 4 * kTcLdV]), __float_as_uint(sUl[o]),
+             __float_as_uint(sUl[o + 4 * kTcLdV]));
+      }
+      const int col = h * kGcD + r0 + 8 * nt_own + 2 * t;
+      const int ra = m0 + g, rb = m0 + g + 8;
+      if (ra < n) *reinterpret_cast<float2*>(p.out + static_cast<size_t>(t0 + ra) * out_ld + col) =
+          make_float2(y[0] * scale, y[1] * scale);
+      if (rb < n) *reinterpret_cast<float2*>(p.out + static_cast<size_t>(t0 + rb) * out_ld + col) =
+          make_float2(y[2] * scale, y[3] * scale);
+    }
+    // ---- S = e^{G_C} S + U^T Kd for columns 16w..16w+15
+    {
+      const float eg = expf(sG[kGc - 1]);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sreg[nt][e] *= eg;
+#pragma unroll 2
+      for (int ks = 0; ks < 8; ++ks) {
+        const int j0 = 8 * ks;
+        uint32_t ah[4], al[4];
+        const int o = (j0 + t) * kTcLdV + g;  // A = U^T: A[r][j] = U[j][r]
+        ah[0] = __float_as_uint(sUh[o]);
+        ah[1] = __float_as_uint(sUh[o + 8]);
+        ah[2] = __float_as_uint(sUh[o + 4 * kTcLdV]);
+        ah[3] = __float_as_uint(sUh[o + 4 * kTcLdV + 8]);
+        al[0] = __float_as_uint(sUl[o]);
+        al[1] = __float_as_uint(sUl[o + 8]);
+        al[2] = __float_as_uint(sUl[o + 4 * kTcLdV]);
+        al[3] = __float_as_uint(sUl[o + 4 * kTcLdV + 8]);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          uint32_t b0h, b1h, b0l, b1l;
+          gc_ldb_k(sKd, kTcLdKd, j0, 16 * warp + 8 * nt, g, t, b0h, b1h, b0l, b1l);
+          mma3(sreg[nt], ah, al, b0h, b1h, b0l, b1l);
+        }
+      }
+      put_state();  // the X products of the next chunk read it after its barrier
+    }
+    __syncthreads();  // P, Kd, U free
+    issue_pkd(c + 1);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int d = 16 * warp + 8 * nt + 2 * t;
+    *reinterpret_cast<float2*>(S + g * kGcD + d) = make_float2(sreg[nt][0], sreg[nt][1]);
+    *reinterpret_cast<float2*>(S + (g + 8) * kGcD + d) = make_float2(sreg[nt][2], sreg[nt][3]);
   }
 }
 

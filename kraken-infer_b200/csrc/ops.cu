@@ -21,12 +21,39 @@ using namespace kib;
 // =========================================================== small kernels
 namespace {
 
-__global__ void rms_norm_rows_kernel(const float* in, const float* w, int n, float eps, float* out) {
+// float4 paths need 16-byte aligned rows (half outputs: 8 bytes)
+__device__ __forceinline__ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+__device__ __forceinline__ bool al8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+// out16 (may be null): the same values rounded to half, [T][n] packed -- the
+// input of the prefill GEMMs, so they need no conversion pass of their own.
+__global__ void rms_norm_rows_kernel(const float* in, const float* w, int n, float eps, float* out, __half* out16) {
   __shared__ float red[32];
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();
   pdl_launch_dependents();
   const float* x = in + static_cast<size_t>(t) * n;
+  float* y = out + static_cast<size_t>(t) * n;
+  __half* y16 = out16 ? out16 + static_cast<size_t>(t) * n : nullptr;
+  if (n == 4 * static_cast<int>(blockDim.x) && al16(in) && al16(w) && al16(out) && (!out16 || al8(out16))) {
+    // one float4 per thread (the model's hidden width)
+    const float4 v = reinterpret_cast<const float4*>(x)[tid];
+    float ss = (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < static_cast<int>(blockDim.x) / 32; ++i) tot += red[i];
+    const float scale = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
+    const float4 g = reinterpret_cast<const float4*>(w)[tid];
+    const float4 r = make_float4(v.x * scale * g.x, v.y * scale * g.y, v.z * scale * g.z, v.w * scale * g.w);
+    reinterpret_cast<float4*>(y)[tid] = r;
+    if (y16) {
+      reinterpret_cast<__half2*>(y16)[2 * tid] = __floats2half2_rn(r.x, r.y);
+      reinterpret_cast<__half2*>(y16)[2 * tid + 1] = __floats2half2_rn(r.z, r.w);
+    }
+    return;
+  }
   float ss = 0.0f;
   for (int i = tid; i < n; i += blockDim.x) ss += x[i] * x[i];
   ss = warp_sum(ss);
@@ -35,26 +62,53 @@ __global__ void rms_norm_rows_kernel(const float* in, const float* w, int n, flo
   float tot = 0.0f;
   for (int i = 0; i < static_cast<int>(blockDim.x) / 32; ++i) tot += red[i];
   const float scale = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
-  float* y = out + static_cast<size_t>(t) * n;
-  for (int i = tid; i < n; i += blockDim.x) y[i] = x[i] * scale * w[i];
+  for (int i = tid; i < n; i += blockDim.x) {
+    const float r = x[i] * scale * w[i];
+    y[i] = r;
+    if (y16) y16[i] = __float2half_rn(r);
+  }
 }
 
-// per-head RMSNorm in place; if gate != null also * silu(gate) (norm_gated)
+// per-head RMSNorm in place; if gate != null also * silu(gate) (norm_gated).
+// One warp per (head, token), four per CTA; out16 as for rms_norm_rows_kernel.
 __global__ void head_norm_kernel(float* v, const float* w, const float* gate, int heads, int d, float eps,
-                                 float* out) {
-  const int h = blockIdx.x, t = blockIdx.y, lane = threadIdx.x;
+                                 float* out, __half* out16) {
+  const int h = blockIdx.x * 4 + (threadIdx.x >> 5), t = blockIdx.y, lane = threadIdx.x & 31;
   pdl_wait();
   pdl_launch_dependents();
+  if (h >= heads) return;
   const size_t base = (static_cast<size_t>(t) * heads + h) * d;
+  float* dst = out ? out : v;
+  if (d == 128 && al16(v) && al16(w) && al16(dst) && (!gate || al16(gate)) && (!out16 || al8(out16))) {
+    const float4 x = reinterpret_cast<const float4*>(v + base)[lane];
+    float ss = (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
+    ss = warp_sum(ss);
+    const float scale = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
+    const float4 g = reinterpret_cast<const float4*>(w)[lane];
+    float4 r;
+    if (gate) {
+      const float4 z = reinterpret_cast<const float4*>(gate + base)[lane];
+      r = make_float4(x.x * scale * g.x * silu_k(z.x), x.y * scale * g.y * silu_k(z.y), x.z * scale * g.z * silu_k(z.z),
+                      x.w * scale * g.w * silu_k(z.w));
+    } else {
+      r = make_float4(x.x * (scale * g.x), x.y * (scale * g.y), x.z * (scale * g.z), x.w * (scale * g.w));
+    }
+    reinterpret_cast<float4*>(dst + base)[lane] = r;
+    if (out16) {
+      reinterpret_cast<__half2*>(out16 + base)[2 * lane] = __floats2half2_rn(r.x, r.y);
+      reinterpret_cast<__half2*>(out16 + base)[2 * lane + 1] = __floats2half2_rn(r.z, r.w);
+    }
+    return;
+  }
   float ss = 0.0f;
   for (int i = lane; i < d; i += 32) ss += v[base + i] * v[base + i];
   ss = warp_sum(ss);
   const float scale = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
-  float* dst = out ? out : v;
   for (int i = lane; i < d; i += 32) {
     // qk_norm: v * (scale * w); norm_gated: v * scale * w * silu(gate)
     const float r = gate ? v[base + i] * scale * w[i] * silu_k(gate[base + i]) : v[base + i] * (scale * w[i]);
     dst[base + i] = r;
+    if (out16) out16[base + i] = __float2half_rn(r);
   }
 }
 
@@ -283,11 +337,25 @@ __global__ void unary_kernel(int op, float* v, size_t n) {
   v[i] = op == 0 ? sigmoid_f(x) : (op == 1 ? softplus20_f(x) : silu_k(x));
 }
 
-__global__ void silu_mul_kernel(float* g, const float* u, size_t n) {
+__global__ void silu_mul_kernel(float* g, const float* u, size_t n, __half* out16) {
   pdl_wait();
   pdl_launch_dependents();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i < n) g[i] = silu_k(g[i]) * u[i];
+  if (n % 4 == 0 && al16(g) && al16(u) && (!out16 || al8(out16))) {  // float4 per thread
+    if (4 * i >= n) return;
+    const float4 a = reinterpret_cast<const float4*>(g)[i], b = reinterpret_cast<const float4*>(u)[i];
+    const float4 r = make_float4(silu_k(a.x) * b.x, silu_k(a.y) * b.y, silu_k(a.z) * b.z, silu_k(a.w) * b.w);
+    reinterpret_cast<float4*>(g)[i] = r;
+    if (out16) {
+      reinterpret_cast<__half2*>(out16)[2 * i] = __floats2half2_rn(r.x, r.y);
+      reinterpret_cast<__half2*>(out16)[2 * i + 1] = __floats2half2_rn(r.z, r.w);
+    }
+    return;
+  }
+  if (i < n) {
+    g[i] = silu_k(g[i]) * u[i];
+    if (out16) out16[i] = __float2half_rn(g[i]);
+  }
 }
 
 __global__ void copy_rows_kernel(const float* src, float* dst_f, uint16_t* dst_h, size_t rows, size_t rv, size_t ss,
@@ -823,13 +891,15 @@ cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const 
   }
 }
 
-cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st) {
-  return launch_pdl(rms_norm_rows_kernel, dim3(T), dim3(256), 0, st, in, w, n, eps, out);
+cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st,
+                            __half* out16 = nullptr) {
+  return launch_pdl(rms_norm_rows_kernel, dim3(T), dim3(256), 0, st, in, w, n, eps, out, out16);
 }
 
 cudaError_t norm_gate_launch(float* v, const float* w, const float* gate, int T, int heads, int d, float eps, float* out,
-                             cudaStream_t st) {
-  return launch_pdl(head_norm_kernel, dim3(heads, T), dim3(32), 0, st, v, w, gate, heads, d, eps, out);
+                             cudaStream_t st, __half* out16 = nullptr) {
+  return launch_pdl(head_norm_kernel, dim3((heads + 3) / 4, T), dim3(128), 0, st, v, w, gate, heads, d, eps, out,
+                    out16);
 }
 
 cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w, int K, int C, int T, float* out,
@@ -845,8 +915,11 @@ cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w
                     out_ld, silu);
 }
 
-cudaError_t silu_mul_launch(float* g, const float* u, size_t n, cudaStream_t st) {
-  return launch_pdl(silu_mul_kernel, dim3(blocks_for(n)), dim3(256), 0, st, g, u, n);
+cudaError_t silu_mul_launch(float* g, const float* u, size_t n, cudaStream_t st, __half* out16 = nullptr) {
+  const bool vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u)) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(out16) % 8 == 0;
+  const size_t threads = vec ? n / 4 : n;
+  return launch_pdl(silu_mul_kernel, dim3(blocks_for(threads)), dim3(256), 0, st, g, u, n, out16);
 }
 
 int finish_op(kib_ctx* ctx, const char* what) {

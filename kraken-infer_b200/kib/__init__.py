@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import weakref
 from ctypes import POINTER, byref, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_uint16, c_uint32, c_uint64, c_void_p
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -289,9 +290,12 @@ class Context:
         if rc != KIB_OK:
             raise KibError(rc, "kib_create failed (no sm_100 device?)")
         self.h = h
+        self.children = weakref.WeakSet()  # models on this context: freed before it
 
     def close(self):
         if getattr(self, "h", None):
+            for c in list(self.children):
+                c.close()
             self.lib.kib_destroy(self.h)
             self.h = None
 
@@ -344,12 +348,16 @@ class Qwen35:
         h = c_void_p()
         ctx.check(self.lib.kib_qwen35_load(ctx.h, gguf_path.encode(), byref(opt), byref(h)))
         self.h = h
+        self.children = weakref.WeakSet()  # batches and prompt caches: freed before the model
+        ctx.children.add(self)
         plan = Qwen35Plan()
         ctx.check(self.lib.kib_qwen35_get_plan(self.h, byref(plan)))
         self.plan = plan
 
     def close(self):
         if getattr(self, "h", None):
+            for c in list(self.children):
+                c.close()
             self.lib.kib_qwen35_free(self.h)
             self.h = None
 
@@ -470,6 +478,7 @@ class PromptCache:
 
     def __init__(self, model: "Qwen35", block_tokens: int, capacity_blocks: int, min_reuse_tokens: int = 0):
         self.model = model
+        model.children.add(self)
         self.lib = model.lib
         h = c_void_p()
         model.ctx.check(self.lib.kib_qwen35_prefix_cache_create(model.h, block_tokens, capacity_blocks,
@@ -477,7 +486,7 @@ class PromptCache:
         self.h = h
 
     def close(self):
-        if self.h:
+        if getattr(self, "h", None):
             self.lib.kib_qwen35_prefix_cache_free(self.h)
             self.h = None
 
@@ -510,6 +519,7 @@ class Qwen35Batch:
 
     def __init__(self, model: "Qwen35", slots: int, context_tokens: int, max_steps: int = 256):
         self.model = model
+        model.children.add(self)
         self.lib = model.lib
         self.slots = slots
         h = c_void_p()
@@ -517,7 +527,7 @@ class Qwen35Batch:
         self.h = h
 
     def close(self):
-        if self.h:
+        if getattr(self, "h", None):
             self.lib.kib_qwen35_batch_free(self.h)
             self.h = None
 
@@ -594,7 +604,7 @@ class PrefixIndex:
         self.h = self.lib.kib_prefix_index_create(block_tokens, capacity_blocks, min_reuse_tokens)
 
     def close(self):
-        if self.h:
+        if getattr(self, "h", None):
             self.lib.kib_prefix_index_free(self.h)
             self.h = None
 

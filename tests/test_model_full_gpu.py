@@ -56,6 +56,10 @@ def test_config2_decode_at_ctx4096_matches_oracle(ctx, oracle, baseline_model):
     m.close()
 
 
+# The KV cache holds half values: projections that agree with the oracle to
+# the fp32 checks' 1e-3 can still round one to three half ulps apart (one ulp
+# is up to 2^-10 of the largest entry), so the cache is compared at 2e-3.
+KV_RTOL = 2e-3
 FULL_WIDTH = dict(hidden=1024, layers=4, intermediate=3584, vocab=8192, heads=8, kv_heads=2, head_dim=256,
                   ssm_heads=16, ssm_head_dim=128, nextn_layers=0, threads=16, seed=77)
 
@@ -85,7 +89,7 @@ def test_config4_full_width_1024_token_chunks_match_oracle(ctx, oracle, tmp_path
     for k in ("k", "v"):
         g = gst[k].view(np.float16).astype(np.float32)
         o = ost[k].view(np.float16).astype(np.float32)
-        assert rel(g, o) < LOGIT_RTOL, k
+        assert rel(g, o) < KV_RTOL, k
     am, glg, _ = m.forward([nxt], advance=True, logits=True)
     _, _, lg1 = om.forward([nxt], T)
     assert rel(glg[0], lg1[0]) < LOGIT_RTOL
