@@ -499,6 +499,9 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
       q.run(cudaFuncSetAttribute(gdn_chunk_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kGcScanTcSmem)),
             "gdn_chunk_attr");
+      q.run(cudaFuncSetAttribute(gdn_chunk_prep_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kGcPrepTcSmem)),
+            "gdn_chunk_attr");
       chunk_cfg = true;
     }
     GdnChunkParams gc;
@@ -513,8 +516,17 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
     gc.T = T;
     gc.key_heads = m->lkh;
     gc.value_heads = m->lvh;
-    q.run(launch_pdl(gdn_chunk_prep_kernel, dim3(m->lvh, (T + kGc - 1) / kGc), dim3(256), kGcPrepSmem, q.st, gc),
-          "gdn_chunk_prep");
+    static const bool prep_tc = [] {
+      const char* v = std::getenv("KIB_GDN_PREP_TC");
+      return !(v && v[0] == '0');
+    }();
+    if (prep_tc)
+      q.run(launch_pdl(gdn_chunk_prep_tc_kernel, dim3(m->lvh, (T + kGc - 1) / kGc), dim3(256), kGcPrepTcSmem, q.st,
+                       gc),
+            "gdn_chunk_prep_tc");
+    else
+      q.run(launch_pdl(gdn_chunk_prep_kernel, dim3(m->lvh, (T + kGc - 1) / kGc), dim3(256), kGcPrepSmem, q.st, gc),
+            "gdn_chunk_prep");
     static const bool scan_tc = [] {
       const char* v = std::getenv("KIB_GDN_SCAN_TC");
       return !(v && v[0] == '0');

@@ -432,6 +432,192 @@ KIB_DEV void gc_ldb_k(const float* s, int ld, int k0, int n0, int g, int t, uint
   tf32_split(p[4 * ld], h1, l1);
 }
 
+// ---------------------------------------------------------------- prep on the tensor cores
+// Same outputs as gdn_chunk_prep_kernel.  K K^T, Q K^T and Kt = Tb diag(e^G) K
+// run as split-TF32 mma.sync products (fp32 accuracy, see mma3); the unit
+// lower-triangular inverse X = (I + L)^{-1} is taken by 16 x 16 blocks: the
+// four diagonal blocks by forward substitution inside one warp each, then
+// block row b (b = 1..3) as X_ba = -X_bb * sum_{a <= k < b} L_bk X_ka -- three
+// CTA-wide steps instead of one barrier per row.
+constexpr int kPtLd = 132;  // q / k rows
+constexpr int kPtLdT = 68;  // L, X, Tb diag(e^G)
+constexpr size_t kGcPrepTcSmem =
+    (2 * kGc * kPtLd + 2 * kGc * kPtLdT + 3 * 16 * 16 + 3 * kGc) * sizeof(float);
+
+__global__ void __launch_bounds__(256) gdn_chunk_prep_tc_kernel(const __grid_constant__ GdnChunkParams p) {
+  extern __shared__ __align__(16) float pt_sm[];
+  float* sK = pt_sm;                    // [64][132]: k rows
+  float* sQ = sK + kGc * kPtLd;         // [64][132]: q rows
+  float* sL = sQ + kGc * kPtLd;         // [64][68]: L, later Tb diag(e^G)
+  float* sX = sL + kGc * kPtLdT;        // [64][68]: X = (I + L)^{-1}
+  float* sW = sX + kGc * kPtLdT;        // [3][16][16]: block-row partial sums
+  float* G = sW + 3 * 16 * 16;          // [64]
+  float* bt = G + kGc;                  // [64]
+  float* eG = bt + kGc;                 // [64]
+  const int h = blockIdx.x, c = blockIdx.y, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const int kh = h % p.key_heads;
+  const int t0 = c * kGc, n = min(kGc, p.T - t0);
+  const int key_dim = p.key_heads * kGcD;
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = tid; i < kGc * kGcD / 4; i += 256) {
+    const int tk = i >> 5, d4 = i & 31;
+    const bool ok = tk < n;
+    const float* row = p.conv_out + static_cast<size_t>(t0 + (ok ? tk : 0)) * p.C;
+    gc_cp16(sQ + tk * kPtLd + 4 * d4, row + kh * kGcD + 4 * d4, ok);
+    gc_cp16(sK + tk * kPtLd + 4 * d4, row + key_dim + kh * kGcD + 4 * d4, ok);
+  }
+  if (tid < kGc) {
+    const bool ok = tid < n;
+    G[tid] = ok ? p.g[static_cast<size_t>(t0 + tid) * p.ld_ba + h] : 0.0f;
+    bt[tid] = ok ? p.beta[static_cast<size_t>(t0 + tid) * p.ld_ba + h] : 0.0f;
+  }
+  gc_cp_wait();
+  __syncthreads();
+  if (tid == 0) {
+    float acc = 0.0f;
+    for (int i = 0; i < kGc; ++i) {
+      acc += G[i];
+      G[i] = acc;
+    }
+  }
+  __syncthreads();
+  if (tid < kGc) eG[tid] = expf(G[tid]);
+  float* ws = p.ws + (static_cast<size_t>(h) * gridDim.y + c) * kGcWs;
+  float* wTb = ws;
+  float* wP = ws + kGc * kGc;
+  float* wKt = wP + kGc * kGc;
+  float* wG = wKt + kGc * kGcD;
+
+  // ---- K K^T and Q K^T: warp (m-tile w & 3, n-tiles 4 (w >> 2) .. + 3); tiles
+  // wholly above the diagonal are zero
+  {
+    const int mt = warp & 3, m0 = 16 * mt, nb = 4 * (warp >> 2);
+    float kk[4][4], qk[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) kk[j][e] = qk[j][e] = 0.0f;
+    const int nlive = max(0, min(4, 2 * mt + 2 - nb));  // n-tiles 8nt <= 16mt + 15
+#pragma unroll 2
+    for (int ks = 0; ks < kGcD / 8; ++ks) {
+      const int k0 = 8 * ks;
+      uint32_t akh[4], akl[4], aqh[4], aql[4];
+      gc_lda(sK, kPtLd, m0, k0, g, t, akh, akl);
+      gc_lda(sQ, kPtLd, m0, k0, g, t, aqh, aql);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j < nlive) {
+          const float* bp = sK + (8 * (nb + j) + g) * kPtLd + k0 + t;  // B[d][j'] = k_j'[d]
+          uint32_t b0h, b0l, b1h, b1l;
+          tf32_split(bp[0], b0h, b0l);
+          tf32_split(bp[4], b1h, b1l);
+          mma3(kk[j], akh, akl, b0h, b1h, b0l, b1l);
+          mma3(qk[j], aqh, aql, b0h, b1h, b0l, b1l);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = m0 + g + 8 * (e >> 1), jj = 8 * (nb + j) + 2 * t + (e & 1);
+        const float dec = jj <= i ? expf(G[i] - G[jj]) : 0.0f;
+        sL[i * kPtLdT + jj] = jj < i ? bt[i] * dec * kk[j][e] : 0.0f;
+        wP[i * kGc + jj] = dec * qk[j][e];
+      }
+  }
+  __syncthreads();
+  // ---- X = (I + L)^{-1}: diagonal blocks (warp b, lanes 0..15 = columns)
+  if (warp < 4) {
+    const int b0 = 16 * warp, col = lane & 15;
+    for (int i = 0; i < 16; ++i) {
+      float s = 0.0f;
+      for (int j = col; j < i; ++j) s = fmaf(sL[(b0 + i) * kPtLdT + b0 + j], sX[(b0 + j) * kPtLdT + b0 + col], s);
+      if (lane < 16) sX[(b0 + i) * kPtLdT + b0 + col] = col == i ? 1.0f : (col < i ? -s : 0.0f);
+      __syncwarp();
+    }
+  } else {
+    // zeros above the diagonal blocks
+    for (int e = tid - 128; e < kGc * kGc; e += 128) {
+      const int i = e >> 6, j = e & 63;
+      if ((j >> 4) > (i >> 4)) sX[i * kPtLdT + j] = 0.0f;
+    }
+  }
+  __syncthreads();
+  // block rows 1..3: W_a = sum_{k=a}^{b-1} L_bk X_ka, then X_ba = -X_bb W_a
+  for (int b = 1; b < 4; ++b) {
+    for (int e = tid; e < b * 256; e += 256) {
+      const int a = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      float s = 0.0f;
+      for (int k = a; k < b; ++k)
+#pragma unroll 4
+        for (int q = 0; q < 16; ++q)
+          s = fmaf(sL[(16 * b + r) * kPtLdT + 16 * k + q], sX[(16 * k + q) * kPtLdT + 16 * a + cc], s);
+      sW[e] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < b * 256; e += 256) {
+      const int a = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      float s = 0.0f;
+#pragma unroll 4
+      for (int q = 0; q <= r; ++q) s = fmaf(sX[(16 * b + r) * kPtLdT + 16 * b + q], sW[(a * 16 + q) * 16 + cc], s);
+      sX[(16 * b + r) * kPtLdT + 16 * a + cc] = -s;
+    }
+    __syncthreads();
+  }
+  // ---- Tb = X diag(beta) (to the workspace); Tb diag(e^G) for Kt
+  for (int e = tid; e < kGc * kGc; e += 256) {
+    const int i = e >> 6, j = e & 63;
+    const float v = sX[i * kPtLdT + j] * bt[j];
+    wTb[e] = v;
+    sL[i * kPtLdT + j] = v * eG[j];
+  }
+  if (tid < kGc) wG[tid] = G[tid];
+  __syncthreads();
+  // ---- Kt = (Tb diag(e^G)) K: warp (m-tile w & 3, d columns 64 (w >> 2) ..);
+  // Tb is lower triangular, so tokens up to the tile's last row
+  {
+    const int mt = warp & 3, m0 = 16 * mt, nb = 8 * (warp >> 2);
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
+    for (int ks = 0; ks <= 2 * mt + 1; ++ks) {
+      uint32_t ah[4], al[4];
+      gc_lda(sL, kPtLdT, m0, 8 * ks, g, t, ah, al);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t b0h, b1h, b0l, b1l;
+        gc_ldb_k(sK, kPtLd, 8 * ks, 8 * (nb + j), g, t, b0h, b1h, b0l, b1l);
+        mma3(acc[j], ah, al, b0h, b1h, b0l, b1l);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = 8 * (nb + j) + 2 * t;
+      *reinterpret_cast<float2*>(wKt + (m0 + g) * kGcD + d) = make_float2(acc[j][0], acc[j][1]);
+      *reinterpret_cast<float2*>(wKt + (m0 + g + 8) * kGcD + d) = make_float2(acc[j][2], acc[j][3]);
+    }
+  }
+  // ---- the scan's decayed operands
+  {
+    float* wQg = ws + kGcWsQg;
+    float* wKd = ws + kGcWsKd;
+    const float gend = G[kGc - 1];
+    for (int i = tid; i < kGc * kGcD / 4; i += 256) {
+      const int tk = i >> 5, d4 = i & 31;
+      const float fq = expf(G[tk]), fk = expf(gend - G[tk]);
+      const float4 qv = *reinterpret_cast<const float4*>(sQ + tk * kPtLd + 4 * d4);
+      const float4 kv = *reinterpret_cast<const float4*>(sK + tk * kPtLd + 4 * d4);
+      reinterpret_cast<float4*>(wQg)[i] = make_float4(qv.x * fq, qv.y * fq, qv.z * fq, qv.w * fq);
+      reinterpret_cast<float4*>(wKd)[i] = make_float4(kv.x * fk, kv.y * fk, kv.z * fk, kv.w * fk);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) gdn_chunk_scan_tc_kernel(const __grid_constant__ GdnChunkParams p) {
   extern __shared__ __align__(16) float tc_sm[];
   float* sKt = tc_sm;
