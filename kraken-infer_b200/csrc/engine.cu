@@ -116,6 +116,7 @@ struct kib_qwen35 {
   float *d_att = nullptr, *d_qout = nullptr, *d_norm = nullptr, *d_norm2 = nullptr, *d_hn = nullptr;
   float *d_logits = nullptr, *d_e = nullptr, *d_cat = nullptr, *d_hm = nullptr, *d_hm1 = nullptr, *d_mtp_h = nullptr;
   float *d_part = nullptr;
+  float* d_fa_part = nullptr;  // prefill attention key splits: [split][T][heads][256 + 2]
   __half *d_w16 = nullptr, *d_x16 = nullptr;  // prefill GEMM scratch: one f16 weight matrix, one f16 x
   void* d_w16_all = nullptr;                  // resident f16 prefill weights (DevT::h points inside)
   float* d_gdn_ws = nullptr;                  // chunked delta rule: Tb, P, Kt, G per (value head, 64-token chunk)
@@ -567,7 +568,34 @@ void attention_block_prefill(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc
   gemm(q, L.v, m->d_norm, m->H, T, m->d_vp, m->KD, nullptr, true);
   const AttnParams a = attn_params(m, L, kc, vc, pos, T);
   q.run(launch_pdl(attn_prep_kernel, dim3(T), dim3(256), 8 * kHd * sizeof(float), q.st, a), "attn_prep");
-  if (a.round_q && m->heads % m->kvh == 0) {
+  static const bool fa2_on = [] {
+    const char* v = std::getenv("KIB_FA2");
+    return !(v && v[0] == '0');
+  }();
+  if (a.round_q && fa2_on && m->heads % m->kvh == 0 && (m->heads / m->kvh) % 2 == 0) {
+    static bool fa2_cfg = false;
+    if (!fa2_cfg) {
+      q.run(cudaFuncSetAttribute(attn_prefill_mma2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kFa2Smem)),
+            "attn_prefill_mma2_attr");
+      fa2_cfg = true;
+    }
+    // key splits so that the (query tile, head pair) CTAs cover the GPU about twice
+    const int ctas = ((T + kFa2Q - 1) / kFa2Q) * (m->heads / 2);
+    static const int env_splits = [] {
+      const char* v = std::getenv("KIB_FA_SPLITS");
+      return v ? std::atoi(v) : 0;
+    }();
+    int ns = env_splits > 0 ? env_splits : (2 * m->ctx->num_sms + ctas - 1) / ctas;
+    ns = std::max(1, std::min(ns, kFa2MaxSplits));
+    AttnParams a2 = a;
+    a2.part = m->d_fa_part;
+    q.run(launch_pdl(attn_prefill_mma2_kernel, dim3((T + kFa2Q - 1) / kFa2Q, m->heads / 2, ns), dim3(256), kFa2Smem,
+                     q.st, a2),
+          "attn_prefill_mma2");
+    if (ns > 1)
+      q.run(launch_pdl(attn_prefill_merge_kernel, dim3(T, m->heads), dim3(kHd), 0, q.st, a2, ns), "attn_prefill_merge");
+  } else if (a.round_q && m->heads % m->kvh == 0) {
     static bool fa_cfg = false;
     if (!fa_cfg) {
       q.run(cudaFuncSetAttribute(attn_prefill_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1355,6 +1383,7 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
             dalloc(&m->d_x16, T * std::max<uint64_t>({2 * H, I, VD, AD})) == cudaSuccess &&
             dalloc(&m->d_gdn_ws, static_cast<size_t>(lvh) * ((T + kGc - 1) / kGc) * kGcWs) == cudaSuccess &&
             dalloc(&m->d_part, static_cast<size_t>(m->nsplit) * kMaxSmallT * m->heads * (kHd + 2)) == cudaSuccess &&
+            dalloc(&m->d_fa_part, static_cast<size_t>(kFa2MaxSplits) * T * m->heads * (kHd + 2)) == cudaSuccess &&
             dalloc(&m->d_attn_cnt, 64) == cudaSuccess && dalloc(&m->d_head_cnt, 4) == cudaSuccess &&
             dalloc(&m->d_cand_max, 1024 * kGemvMaxTok) == cudaSuccess &&
             dalloc(&m->d_cand_sum, 1024 * kGemvMaxTok) == cudaSuccess &&
@@ -1443,7 +1472,7 @@ void kib_qwen35_free(kib_qwen35* m) {
   void* ptrs[] = {m->d_weights, m->d_k, m->d_v, m->d_mk, m->d_mv, m->d_r, m->d_s, m->d_r_snap, m->d_s_snap,
                   m->d_pending_h, m->d_h, m->d_h1, m->d_qkv, m->d_z, m->d_beta, m->d_alpha, m->d_y, m->d_act,
                   m->d_act2, m->d_qg, m->d_kp, m->d_vp, m->d_att, m->d_qout, m->d_norm, m->d_norm2, m->d_hn,
-                  m->d_logits, m->d_e, m->d_cat, m->d_hm, m->d_hm1, m->d_mtp_h, m->d_part, m->d_attn_cnt,
+                  m->d_logits, m->d_e, m->d_cat, m->d_hm, m->d_hm1, m->d_mtp_h, m->d_part, m->d_fa_part, m->d_attn_cnt,
                   m->d_head_cnt, m->d_cand_max, m->d_cand_sum, m->d_cand_idx, m->d_pos, m->d_mtp_pos,
                   m->d_tokens, m->d_argmax, m->d_prob, m->d_log, m->d_step, m->d_mtp_tok, m->d_trace,
                   m->d_w16, m->d_x16, m->d_w16_all, m->d_gdn_ws};

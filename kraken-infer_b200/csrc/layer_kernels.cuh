@@ -1327,4 +1327,221 @@ static __global__ void __launch_bounds__(128, 2) attn_prefill_mma_kernel(const _
   }
 }
 
+// The same attention with two query heads of one KV head per CTA (8 warps:
+// warps 0-3 the even head, 4-7 the odd one, sharing every K/V tile) and the
+// key range split over gridDim.z CTAs, so a 1024-token chunk fills the GPU.
+// With one split the output is final, as above; with several, each CTA writes
+// its unnormalised rows, running max and normaliser to part
+// ([split][T][heads][256 + 2]) and attn_prefill_merge_kernel combines them.
+// A split may start past some rows' last key: those rows keep max -inf and
+// weight 0 until a key of theirs arrives.
+constexpr int kFa2Q = 64;  // queries per head per CTA
+constexpr int kFa2MaxSplits = 4;
+constexpr size_t kFa2Smem = static_cast<size_t>(2 * kFa2Q + 4 * kFaK) * kFaLd * 2;
+
+static __global__ void __launch_bounds__(256, 1) attn_prefill_mma2_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ __align__(16) uint16_t fa2_sm[];
+  uint16_t* qs = fa2_sm;                    // [2][64][264]
+  uint16_t* ks = fa2_sm + 2 * kFa2Q * kFaLd;  // [2][32][264]
+  uint16_t* vs = ks + 2 * kFaK * kFaLd;     // [2][32][264]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hl = warp >> 2, wq = warp & 3;  // head of the pair, 16-row tile of it
+  const int head0 = 2 * blockIdx.y, head = head0 + hl, q0 = blockIdx.x * kFa2Q;
+  const int split = blockIdx.z, nsplit = gridDim.z;
+  const int kvh = head0 / (p.heads / p.kv_heads);
+  const int kvd = p.kv_heads * kHd;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pos0 = *p.pos;
+  const int last_q = min(q0 + kFa2Q, p.T) - 1;
+  const int nkeys = pos0 + last_q + 1;
+  const int nblocks = (nkeys + kFaK - 1) / kFaK;
+  const int b_lo = static_cast<int>(static_cast<long>(nblocks) * split / nsplit);
+  const int b_hi = static_cast<int>(static_cast<long>(nblocks) * (split + 1) / nsplit);
+  const uint16_t* kg = p.kcache + static_cast<size_t>(kvh) * kHd;
+  const uint16_t* vg = p.vcache + static_cast<size_t>(kvh) * kHd;
+  auto load_kv = [&](int b, int stage) {
+    uint16_t* kd = ks + stage * kFaK * kFaLd;
+    uint16_t* vd = vs + stage * kFaK * kFaLd;
+#pragma unroll
+    for (int it = 0; it < kFaK * 32 / 256; ++it) {
+      const int i = tid + 256 * it, r = i >> 5, piece = i & 31;
+      const size_t key = static_cast<size_t>(min(b * kFaK + r, nkeys - 1));
+      gs_cp16(kd + r * kFaLd + 8 * piece, kg + key * kvd + 8 * piece);
+      gs_cp16(vd + r * kFaLd + 8 * piece, vg + key * kvd + 8 * piece);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (b_lo < b_hi) load_kv(b_lo, b_lo & 1);
+  // Q rows of both heads, rounded to half (rows past T are zero and never written out)
+  for (int i = tid; i < 2 * kFa2Q * (kHd / 4); i += 256) {
+    const int r = i / (kHd / 4), c4 = i % (kHd / 4), hh = r / kFa2Q, rr = r % kFa2Q;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + rr < p.T)
+      v = *reinterpret_cast<const float4*>(p.q_out + (static_cast<size_t>(q0 + rr) * p.heads + head0 + hh) * kHd +
+                                           4 * c4);
+    __half2* d = reinterpret_cast<__half2*>(qs + r * kFaLd + 4 * c4);
+    d[0] = __floats2half2_rn(v.x, v.y);
+    d[1] = __floats2half2_rn(v.z, v.w);
+  }
+  const int g = lane >> 2, c = lane & 3;
+  const int qpos0 = pos0 + q0 + 16 * wq + g, qpos1 = qpos0 + 8;
+  const int warp_last = pos0 + q0 + 16 * wq + 15;  // last key any row of this warp sees
+  const float scale = 1.0f / sqrtf(static_cast<float>(kHd));
+  const uint32_t qs_base = smem_u32(qs + hl * kFa2Q * kFaLd), ks_base = smem_u32(ks), vs_base = smem_u32(vs);
+  float o[kHd / 8][4];
+#pragma unroll
+  for (int n = 0; n < kHd / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  // running max starts at a finite floor: a row whose keys all lie beyond this
+  // split's blocks keeps weight e^{-inf - floor} = 0 and scale e^0 = 1, and its
+  // first key zeroes the (empty) history exactly as a -inf start would
+  constexpr float kFloor = -1e30f;
+  float m0 = kFloor, m1 = kFloor, l0 = 0.0f, l1 = 0.0f;  // l: this lane's share
+  for (int b = b_lo; b < b_hi; ++b) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();  // block b landed (and Q, at the first block); the other stage is free
+    if (b + 1 < b_hi) load_kv(b + 1, (b + 1) & 1);
+    if (b * kFaK > warp_last) continue;
+    const uint32_t kst = ks_base + static_cast<uint32_t>((b & 1) * kFaK * kFaLd) * 2;
+    const uint32_t vst = vs_base + static_cast<uint32_t>((b & 1) * kFaK * kFaLd) * 2;
+    float s[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll 4
+    for (int k0 = 0; k0 < kHd; k0 += 16) {
+      uint32_t a[4];
+      ldsm_x4(qs_base + static_cast<uint32_t>((16 * wq + (lane & 15)) * kFaLd + k0 + (lane >> 4) * 8) * 2, a[0], a[1],
+              a[2], a[3]);
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        const int n = 8 * j + (lane & 7) + ((lane >> 4) << 3), col = k0 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kst + static_cast<uint32_t>(n * kFaLd + col) * 2, b0, b1, b2, b3);
+        mma_f16_16816(s[j], a, b0, b1);
+        mma_f16_16816(s[j + 1], a, b2, b3);
+      }
+    }
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int key = b * kFaK + 8 * j + 2 * c;
+      s[j][0] = key <= qpos0 ? s[j][0] * scale : -INFINITY;
+      s[j][1] = key + 1 <= qpos0 ? s[j][1] * scale : -INFINITY;
+      s[j][2] = key <= qpos1 ? s[j][2] * scale : -INFINITY;
+      s[j][3] = key + 1 <= qpos1 ? s[j][3] * scale : -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float ps0 = expf(m0 - mx0), ps1 = expf(m1 - mx1);
+    m0 = mx0;
+    m1 = mx1;
+    float rs0 = 0.0f, rs1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      s[j][0] = expf(s[j][0] - m0);
+      s[j][1] = expf(s[j][1] - m0);
+      s[j][2] = expf(s[j][2] - m1);
+      s[j][3] = expf(s[j][3] - m1);
+      rs0 += s[j][0] + s[j][1];
+      rs1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * ps0 + rs0;
+    l1 = l1 * ps1 + rs1;
+#pragma unroll
+    for (int n = 0; n < kHd / 8; ++n) {
+      o[n][0] *= ps0;
+      o[n][1] *= ps0;
+      o[n][2] *= ps1;
+      o[n][3] *= ps1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t ahi[4], alo[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float x = s[2 * kk + (h >> 1)][(h & 1) * 2], y = s[2 * kk + (h >> 1)][(h & 1) * 2 + 1];
+        const __half2 hi = __floats2half2_rn(x, y);
+        const float2 hf = __half22float2(hi);
+        ahi[h] = h2_bits(hi);
+        alo[h] = h2_bits(__floats2half2_rn(x - hf.x, y - hf.y));
+      }
+      const int key = 16 * kk + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int nd = 0; nd < kHd / 16; ++nd) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vst + static_cast<uint32_t>(key * kFaLd + 16 * nd + (lane >> 4) * 8) * 2, b0, b1, b2, b3);
+        mma_f16_16816(o[2 * nd], ahi, b0, b1);
+        mma_f16_16816(o[2 * nd + 1], ahi, b2, b3);
+        mma_f16_16816(o[2 * nd], alo, b0, b1);
+        mma_f16_16816(o[2 * nd + 1], alo, b2, b3);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const int t0 = q0 + 16 * wq + g, t1 = t0 + 8;
+  if (nsplit == 1) {
+    const float inv0 = l0 == 0.0f ? 0.0f : 1.0f / l0, inv1 = l1 == 0.0f ? 0.0f : 1.0f / l1;
+#pragma unroll
+    for (int n = 0; n < kHd / 8; ++n) {
+      const int d = 8 * n + 2 * c;
+      if (t0 < p.T) {
+        const float* gt = p.qg + (static_cast<size_t>(t0) * p.heads + head) * 2 * kHd + kHd + d;
+        *reinterpret_cast<float2*>(p.out + static_cast<size_t>(t0) * p.heads * kHd + head * kHd + d) =
+            make_float2(o[n][0] * inv0 * sigmoid_f(gt[0]), o[n][1] * inv0 * sigmoid_f(gt[1]));
+      }
+      if (t1 < p.T) {
+        const float* gt = p.qg + (static_cast<size_t>(t1) * p.heads + head) * 2 * kHd + kHd + d;
+        *reinterpret_cast<float2*>(p.out + static_cast<size_t>(t1) * p.heads * kHd + head * kHd + d) =
+            make_float2(o[n][2] * inv1 * sigmoid_f(gt[0]), o[n][3] * inv1 * sigmoid_f(gt[1]));
+      }
+    }
+    return;
+  }
+  float* part = p.part + static_cast<size_t>(split) * p.T * p.heads * (kHd + 2);
+  float* r0p = part + (static_cast<size_t>(t0) * p.heads + head) * (kHd + 2);
+  float* r1p = part + (static_cast<size_t>(t1) * p.heads + head) * (kHd + 2);
+#pragma unroll
+  for (int n = 0; n < kHd / 8; ++n) {
+    const int d = 8 * n + 2 * c;
+    if (t0 < p.T) *reinterpret_cast<float2*>(r0p + d) = make_float2(o[n][0], o[n][1]);
+    if (t1 < p.T) *reinterpret_cast<float2*>(r1p + d) = make_float2(o[n][2], o[n][3]);
+  }
+  if (c == 0) {
+    if (t0 < p.T) *reinterpret_cast<float2*>(r0p + kHd) = make_float2(m0, l0);
+    if (t1 < p.T) *reinterpret_cast<float2*>(r1p + kHd) = make_float2(m1, l1);
+  }
+}
+
+// Combines the splits of attn_prefill_mma2_kernel: weights e^{m_s - max m},
+// output = sum_s w_s O_s / sum_s w_s l_s, times sigmoid(gate).  One CTA per
+// (token, head), one thread per output element.
+static __global__ void __launch_bounds__(256) attn_prefill_merge_kernel(const __grid_constant__ AttnParams p,
+                                                                        int nsplit) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
+  const size_t stride = static_cast<size_t>(p.T) * p.heads * (kHd + 2);
+  const float* base = p.part + (static_cast<size_t>(t) * p.heads + head) * (kHd + 2);
+  float mx = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, base[s * stride + kHd]);
+  float o = 0.0f, l = 0.0f;
+  for (int s = 0; s < nsplit; ++s) {
+    // a split that held none of the row's keys reports the floor max and l = 0
+    const float ms = base[s * stride + kHd], ls = base[s * stride + kHd + 1];
+    const float w = expf(ms - mx);
+    o += w * base[s * stride + d];
+    l += w * ls;
+  }
+  const float gt = p.qg[(static_cast<size_t>(t) * p.heads + head) * 2 * kHd + kHd + d];
+  p.out[static_cast<size_t>(t) * p.heads * kHd + head * kHd + d] = (l == 0.0f ? 0.0f : o / l) * sigmoid_f(gt);
+}
+
 }  // namespace kib
