@@ -52,7 +52,8 @@ cudaError_t get_rows_launch(int type, const void* w, int nrows, int cols, const 
 cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float eps, float* out, cudaStream_t st,
                             __half* out16 = nullptr);
 cudaError_t norm_gate_launch(float* v, const float* w, const float* gate, int T, int heads, int d, float eps,
-                             float* out, cudaStream_t st, __half* out16 = nullptr);
+                             float* out, cudaStream_t st, __half* out16 = nullptr, int gate_ld = 0);
+cudaError_t silu_mul_cat_launch(const float* gu, int T, int I, float* act, cudaStream_t st, __half* out16);
 cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w, int K, int C, int T, float* out,
                         int out_ld, int silu, cudaStream_t st);
 cudaError_t silu_mul_launch(float* g, const float* u, size_t n, cudaStream_t st, __half* out16 = nullptr);
@@ -116,7 +117,8 @@ struct kib_qwen35 {
   float *d_att = nullptr, *d_qout = nullptr, *d_norm = nullptr, *d_norm2 = nullptr, *d_hn = nullptr;
   float *d_logits = nullptr, *d_e = nullptr, *d_cat = nullptr, *d_hm = nullptr, *d_hm1 = nullptr, *d_mtp_h = nullptr;
   float *d_part = nullptr;
-  float* d_fa_part = nullptr;  // prefill attention key splits: [split][T][heads][256 + 2]
+  float* d_fa_part = nullptr;
+  float* d_proj = nullptr;  // prefill: outputs of one GEMM over concatenated weights [T][sum of rows]  // prefill attention key splits: [split][T][heads][256 + 2]
   __half *d_w16 = nullptr, *d_x16 = nullptr;  // prefill GEMM scratch: one f16 weight matrix, one f16 x
   void* d_w16_all = nullptr;                  // resident f16 prefill weights (DevT::h points inside)
   float* d_gdn_ws = nullptr;                  // chunked delta rule: Tb, P, Kt, G per (value head, 64-token chunk)
@@ -457,23 +459,64 @@ void gemm(Enq& q, const DevT& w, const float* x, int x_ld, int T, float* y, int 
     q.run(gemm_f16_launch(w.type, w.p, w.rows(), w.cols(), x, x_ld, T, y, y_ld, resid, q.st), "gemm");
 }
 
+// Several weights with the same input as ONE GEMM above 64 tokens: their
+// resident f16 copies were laid out back to back at load time, so rows
+// [w0 | w1 | ...] are one matrix; the outputs land side by side in d_proj
+// ([T][sum of rows]).  Returns the row stride, or 0 when the copies are not
+// contiguous (the caller then runs them one by one).
+int gemm_cat(Enq& q, std::initializer_list<const DevT*> ws, const float* x, int x_ld, int T, bool x16_ready) {
+  kib_qwen35* m = q.m;
+  static const bool on = [] {
+    const char* v = std::getenv("KIB_GEMM_CAT");
+    return !(v && v[0] == '0');
+  }();
+  if (!on || T <= 64 || !m->d_w16) return 0;
+  const DevT* first = *ws.begin();
+  int rows = 0;
+  const __half* next = first->h;
+  for (const DevT* w : ws) {
+    if (!w->h || w->h != next || w->cols() != first->cols() || w->cols() % 64) return 0;
+    rows += w->rows();
+    const size_t bytes = (static_cast<size_t>(w->rows()) * w->cols() * 2 + 255) & ~static_cast<size_t>(255);
+    next = reinterpret_cast<const __half*>(reinterpret_cast<const uint8_t*>(w->h) + bytes);
+    if (bytes != static_cast<size_t>(w->rows()) * w->cols() * 2 && w != *(ws.end() - 1)) return 0;  // padding gap
+  }
+  const int ld = (rows + 3) & ~3;
+  q.run(gemm_f16w_launch(first->type, first->p, first->h, rows, first->cols(), x, x_ld, T, m->d_proj, ld, nullptr,
+                         m->d_w16, m->d_x16, !(x16_ready && x_ld == first->cols()), m->ctx->num_sms, q.st,
+                         m->ctx->d_err),
+        "gemm_cat");
+  return ld;
+}
+
 void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, float* x_mid) {
   kib_qwen35* m = q.m;
   const int li = L.cache_index;
   q.run(rms_rows_launch(x_in, L.attn_norm.f(), T, m->H, m->eps, m->d_norm, q.st, m->d_x16), "rms");
-  gemm(q, L.qkv, m->d_norm, m->H, T, m->d_qkv, m->C, nullptr, false, true);
-  q.run(conv_launch(m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1), m->d_qkv, m->C, L.conv1d.f(), m->convk,
-                    m->C, T, m->d_qkv, m->C, 1, q.st),
+  // qkv | z | beta | alpha: one GEMM when their copies are contiguous
+  float *qkv = m->d_qkv, *z = m->d_z, *beta = m->d_beta, *alpha = m->d_alpha;
+  int qkv_ld = m->C, z_ld = m->VD, ld_ba = m->lvh;
+  if (const int ld = gemm_cat(q, {&L.qkv, &L.zgate, &L.beta, &L.alpha}, m->d_norm, m->H, T, true)) {
+    qkv = m->d_proj;
+    z = qkv + L.qkv.rows();
+    beta = z + L.zgate.rows();
+    alpha = beta + L.beta.rows();
+    qkv_ld = z_ld = ld_ba = ld;
+  } else {
+    gemm(q, L.qkv, m->d_norm, m->H, T, qkv, qkv_ld, nullptr, false, true);
+    gemm(q, L.zgate, m->d_norm, m->H, T, z, z_ld, nullptr, true);
+    gemm(q, L.beta, m->d_norm, m->H, T, beta, ld_ba, nullptr, true);
+    gemm(q, L.alpha, m->d_norm, m->H, T, alpha, ld_ba, nullptr, true);
+  }
+  q.run(conv_launch(m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1), qkv, qkv_ld, L.conv1d.f(), m->convk,
+                    m->C, T, qkv, qkv_ld, 1, q.st),
         "conv");
-  gemm(q, L.zgate, m->d_norm, m->H, T, m->d_z, m->VD, nullptr, true);
-  gemm(q, L.beta, m->d_norm, m->H, T, m->d_beta, m->lvh, nullptr, true);
-  gemm(q, L.alpha, m->d_norm, m->H, T, m->d_alpha, m->lvh, nullptr, true);
   GdnParams g = {};
-  g.conv_out = m->d_qkv;
-  g.C = m->C;
-  g.beta_raw = m->d_beta;
-  g.alpha_raw = m->d_alpha;
-  g.ld_ba = m->lvh;
+  g.conv_out = qkv;
+  g.C = qkv_ld;
+  g.beta_raw = beta;
+  g.alpha_raw = alpha;
+  g.ld_ba = ld_ba;
   g.dt_bias = L.dt_bias.f();
   g.ssm_a = L.ssm_a.f();
   g.state = m->d_s + static_cast<size_t>(li) * m->lvh * m->lhd * m->lhd;
@@ -486,7 +529,7 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
   if (m->lhd == 128 && m->lkh <= m->lvh && m->C % 4 == 0 && T >= kGc && gdn_chunked_enabled()) {
     // token-parallel norms and gate/beta, then the chunked delta rule: the
     // per-chunk matrices for every chunk at once, then the scan over chunks
-    q.run(launch_pdl(gdn_prep_kernel, dim3(T, m->lkh), dim3(128), 0, q.st, m->d_qkv, m->C, m->d_alpha, m->d_beta, m->lvh,
+    q.run(launch_pdl(gdn_prep_kernel, dim3(T, m->lkh), dim3(128), 0, q.st, qkv, qkv_ld, alpha, beta, ld_ba,
                      L.dt_bias.f(), L.ssm_a.f(), m->lkh, m->lvh, m->eps),
           "gdn_prep");
     static bool chunk_cfg = false;
@@ -506,11 +549,11 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
       chunk_cfg = true;
     }
     GdnChunkParams gc;
-    gc.conv_out = m->d_qkv;
-    gc.C = m->C;
-    gc.g = m->d_alpha;
-    gc.beta = m->d_beta;
-    gc.ld_ba = m->lvh;
+    gc.conv_out = qkv;
+    gc.C = qkv_ld;
+    gc.g = alpha;
+    gc.beta = beta;
+    gc.ld_ba = ld_ba;
     gc.state = g.state;
     gc.out = m->d_y;
     gc.ws = m->d_gdn_ws;
@@ -540,7 +583,7 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
             "gdn_chunk_scan");
   } else if (m->lhd == 128 && m->lkh <= m->lvh && m->C % 4 == 0) {
     // token-parallel norms and gate/beta first, then the sequential scan alone
-    q.run(launch_pdl(gdn_prep_kernel, dim3(T, m->lkh), dim3(128), 0, q.st, m->d_qkv, m->C, m->d_alpha, m->d_beta, m->lvh,
+    q.run(launch_pdl(gdn_prep_kernel, dim3(T, m->lkh), dim3(128), 0, q.st, qkv, qkv_ld, alpha, beta, ld_ba,
                      L.dt_bias.f(), L.ssm_a.f(), m->lkh, m->lvh, m->eps),
           "gdn_prep");
     static bool scan_cfg = false;
@@ -554,7 +597,7 @@ void linear_block_prefill(Enq& q, const LayerW& L, int T, const float* x_in, flo
   } else {
     q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows), dim3(128), 0, q.st, g), "gdn_core");
   }
-  q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, T, m->lvh, m->lhd, m->eps, m->d_norm2, q.st, m->d_x16),
+  q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), z, T, m->lvh, m->lhd, m->eps, m->d_norm2, q.st, m->d_x16, z_ld),
         "norm_gate");
   gemm(q, L.ssm_out, m->d_norm2, m->VD, T, x_mid, m->H, x_in, false, true);
 }
@@ -614,9 +657,13 @@ void attention_block_prefill(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc
 void ffn_prefill(Enq& q, const LayerW& L, int T, const float* x_mid, float* x_out) {
   kib_qwen35* m = q.m;
   q.run(rms_rows_launch(x_mid, L.post_norm.f(), T, m->H, m->eps, m->d_norm, q.st, m->d_x16), "rms");
-  gemm(q, L.ffn_gate, m->d_norm, m->H, T, m->d_act, m->I, nullptr, false, true);
-  gemm(q, L.ffn_up, m->d_norm, m->H, T, m->d_act2, m->I, nullptr, true);
-  q.run(silu_mul_launch(m->d_act, m->d_act2, static_cast<size_t>(T) * m->I, q.st, m->d_x16), "silu_mul");
+  if (gemm_cat(q, {&L.ffn_gate, &L.ffn_up}, m->d_norm, m->H, T, true) == 2 * m->I) {
+    q.run(silu_mul_cat_launch(m->d_proj, T, m->I, m->d_act, q.st, m->d_x16), "silu_mul_cat");
+  } else {
+    gemm(q, L.ffn_gate, m->d_norm, m->H, T, m->d_act, m->I, nullptr, false, true);
+    gemm(q, L.ffn_up, m->d_norm, m->H, T, m->d_act2, m->I, nullptr, true);
+    q.run(silu_mul_launch(m->d_act, m->d_act2, static_cast<size_t>(T) * m->I, q.st, m->d_x16), "silu_mul");
+  }
   gemm(q, L.ffn_down, m->d_act, m->I, T, x_out, m->H, x_mid, false, true);
 }
 
@@ -1384,6 +1431,7 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
             dalloc(&m->d_gdn_ws, static_cast<size_t>(lvh) * ((T + kGc - 1) / kGc) * kGcWs) == cudaSuccess &&
             dalloc(&m->d_part, static_cast<size_t>(m->nsplit) * kMaxSmallT * m->heads * (kHd + 2)) == cudaSuccess &&
             dalloc(&m->d_fa_part, static_cast<size_t>(kFa2MaxSplits) * T * m->heads * (kHd + 2)) == cudaSuccess &&
+            dalloc(&m->d_proj, T * std::max<uint64_t>({C + VD + 2 * lvh, 2 * I, 2 * AD + 2 * KD})) == cudaSuccess &&
             dalloc(&m->d_attn_cnt, 64) == cudaSuccess && dalloc(&m->d_head_cnt, 4) == cudaSuccess &&
             dalloc(&m->d_cand_max, 1024 * kGemvMaxTok) == cudaSuccess &&
             dalloc(&m->d_cand_sum, 1024 * kGemvMaxTok) == cudaSuccess &&
@@ -1472,7 +1520,7 @@ void kib_qwen35_free(kib_qwen35* m) {
   void* ptrs[] = {m->d_weights, m->d_k, m->d_v, m->d_mk, m->d_mv, m->d_r, m->d_s, m->d_r_snap, m->d_s_snap,
                   m->d_pending_h, m->d_h, m->d_h1, m->d_qkv, m->d_z, m->d_beta, m->d_alpha, m->d_y, m->d_act,
                   m->d_act2, m->d_qg, m->d_kp, m->d_vp, m->d_att, m->d_qout, m->d_norm, m->d_norm2, m->d_hn,
-                  m->d_logits, m->d_e, m->d_cat, m->d_hm, m->d_hm1, m->d_mtp_h, m->d_part, m->d_fa_part, m->d_attn_cnt,
+                  m->d_logits, m->d_e, m->d_cat, m->d_hm, m->d_hm1, m->d_mtp_h, m->d_part, m->d_fa_part, m->d_proj, m->d_attn_cnt,
                   m->d_head_cnt, m->d_cand_max, m->d_cand_sum, m->d_cand_idx, m->d_pos, m->d_mtp_pos,
                   m->d_tokens, m->d_argmax, m->d_prob, m->d_log, m->d_step, m->d_mtp_tok, m->d_trace,
                   m->d_w16, m->d_x16, m->d_w16_all, m->d_gdn_ws};

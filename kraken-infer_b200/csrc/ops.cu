@@ -71,13 +71,15 @@ __global__ void rms_norm_rows_kernel(const float* in, const float* w, int n, flo
 
 // per-head RMSNorm in place; if gate != null also * silu(gate) (norm_gated).
 // One warp per (head, token), four per CTA; out16 as for rms_norm_rows_kernel.
+// gate rows are gate_ld floats apart (0: heads * d, packed).
 __global__ void head_norm_kernel(float* v, const float* w, const float* gate, int heads, int d, float eps,
-                                 float* out, __half* out16) {
+                                 float* out, __half* out16, int gate_ld) {
   const int h = blockIdx.x * 4 + (threadIdx.x >> 5), t = blockIdx.y, lane = threadIdx.x & 31;
   pdl_wait();
   pdl_launch_dependents();
   if (h >= heads) return;
   const size_t base = (static_cast<size_t>(t) * heads + h) * d;
+  if (gate) gate += static_cast<size_t>(t) * (gate_ld ? gate_ld : heads * d) + static_cast<size_t>(h) * d - base;
   float* dst = out ? out : v;
   if (d == 128 && al16(v) && al16(w) && al16(dst) && (!gate || al16(gate)) && (!out16 || al8(out16))) {
     const float4 x = reinterpret_cast<const float4*>(v + base)[lane];
@@ -897,9 +899,9 @@ cudaError_t rms_rows_launch(const float* in, const float* w, int T, int n, float
 }
 
 cudaError_t norm_gate_launch(float* v, const float* w, const float* gate, int T, int heads, int d, float eps, float* out,
-                             cudaStream_t st, __half* out16 = nullptr) {
+                             cudaStream_t st, __half* out16 = nullptr, int gate_ld = 0) {
   return launch_pdl(head_norm_kernel, dim3((heads + 3) / 4, T), dim3(128), 0, st, v, w, gate, heads, d, eps, out,
-                    out16);
+                    out16, gate_ld);
 }
 
 cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w, int K, int C, int T, float* out,
@@ -913,6 +915,32 @@ cudaError_t conv_launch(float* state, const float* in, int in_ld, const float* w
                       out, out_ld, silu);
   return launch_pdl(conv_stateful_kernel, dim3((C + 31) / 32), dim3(32, ntiles), 0, st, state, in, in_ld, w, K, C, T, out,
                     out_ld, silu);
+}
+
+// act[t][i] = silu(gu[t][i]) * gu[t][I + i] over a [T][2I] gate | up buffer
+// (one GEMM over the concatenated weights); also in half for the next GEMM.
+__global__ void silu_mul_cat_kernel(const float* gu, int I, size_t n4, float* act, __half* out16) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // float4 of act
+  if (i >= n4) return;
+  const size_t t = (4 * i) / I, c = (4 * i) % I;
+  const float4 a = *reinterpret_cast<const float4*>(gu + t * 2 * I + c);
+  const float4 b = *reinterpret_cast<const float4*>(gu + t * 2 * I + I + c);
+  const float4 r = make_float4(silu_k(a.x) * b.x, silu_k(a.y) * b.y, silu_k(a.z) * b.z, silu_k(a.w) * b.w);
+  reinterpret_cast<float4*>(act)[i] = r;
+  if (out16) {
+    reinterpret_cast<__half2*>(out16)[2 * i] = __floats2half2_rn(r.x, r.y);
+    reinterpret_cast<__half2*>(out16)[2 * i + 1] = __floats2half2_rn(r.z, r.w);
+  }
+}
+
+cudaError_t silu_mul_cat_launch(const float* gu, int T, int I, float* act, cudaStream_t st, __half* out16) {
+  if (I % 4 || reinterpret_cast<uintptr_t>(gu) % 16 || reinterpret_cast<uintptr_t>(act) % 16 ||
+      reinterpret_cast<uintptr_t>(out16) % 8)
+    return cudaErrorInvalidValue;
+  const size_t n4 = static_cast<size_t>(T) * I / 4;
+  return launch_pdl(silu_mul_cat_kernel, dim3(blocks_for(n4)), dim3(256), 0, st, gu, I, n4, act, out16);
 }
 
 cudaError_t silu_mul_launch(float* g, const float* u, size_t n, cudaStream_t st, __half* out16 = nullptr) {
