@@ -295,7 +295,7 @@ def prefill_bench(ctx, path):
     peak, kind = (float(json.load(open(pk))["bf16_tflops_sustained"]), "measured sustained bf16") if os.path.exists(pk) \
         else (1400.0, "fallback")
     return {"workload": "BASELINE config 4: 8192-token prefill in 1024-token chunks (tcgen05 GEMMs with TMEM "
-                        "accumulators on resident f16 weights, mma.sync flash attention, sequential delta-rule scan)", "tokens": PREFILL_TOKENS, "ms": round(ms, 2),
+                        "accumulators on resident f16 weights, split-key mma.sync flash attention, chunked delta rule on split-TF32 mma.sync)", "tokens": PREFILL_TOKENS, "ms": round(ms, 2),
             "tok_per_s": round(PREFILL_TOKENS / (ms * 1e-3), 1), "bound": "tensor", "achieved": round(tflops, 2),
             "peak": peak, "unit": "TFLOP/s", "frac": round(tflops / peak, 4), "peak_kind": kind,
             "flop": PREFILL_FLOP, "next_token": int(nxt)}
