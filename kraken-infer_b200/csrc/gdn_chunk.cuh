@@ -402,8 +402,10 @@ KIB_DEV void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
   hi = tf32_rna(x);
   lo = tf32_rna(x - __uint_as_float(hi));
 }
+// not volatile: a pure function of its operands, so the compiler may move
+// the next k-step's loads and splits ahead of it
 KIB_DEV void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -415,6 +417,18 @@ KIB_DEV void mma3(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4
   mma_tf32(d, al, bh0, bh1);
   mma_tf32(d, ah, bl0, bl1);
   mma_tf32(d, ah, bh0, bh1);
+}
+// The same with the cross terms in their own accumulator c (added to d by the
+// caller once the k loop is done): two shorter dependent chains instead of one
+KIB_DEV void mma3s(float (&d)[4], float (&c)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0,
+                   uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+  mma_tf32(c, al, bh0, bh1);
+  mma_tf32(c, ah, bl0, bl1);
+  mma_tf32(d, ah, bh0, bh1);
+}
+KIB_DEV void acc_add(float (&d)[4], const float (&c)[4]) {
+#pragma unroll
+  for (int e = 0; e < 4; ++e) d[e] += c[e];
 }
 // A fragment (16 x 8, row-major source, rows m0.., columns k0..) split in two
 KIB_DEV void gc_lda(const float* s, int ld, int m0, int k0, int g, int t, uint32_t (&h)[4], uint32_t (&l)[4]) {
@@ -494,11 +508,11 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_tc_kernel(const __grid_con
   // wholly above the diagonal are zero
   {
     const int mt = warp & 3, m0 = 16 * mt, nb = 4 * (warp >> 2);
-    float kk[4][4], qk[4][4];
+    float kk[4][4], qk[4][4], ck[4][4], cq[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) kk[j][e] = qk[j][e] = 0.0f;
+      for (int e = 0; e < 4; ++e) kk[j][e] = qk[j][e] = ck[j][e] = cq[j][e] = 0.0f;
     const int nlive = max(0, min(4, 2 * mt + 2 - nb));  // n-tiles 8nt <= 16mt + 15
 #pragma unroll 2
     for (int ks = 0; ks < kGcD / 8; ++ks) {
@@ -513,10 +527,15 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_tc_kernel(const __grid_con
           uint32_t b0h, b0l, b1h, b1l;
           tf32_split(bp[0], b0h, b0l);
           tf32_split(bp[4], b1h, b1l);
-          mma3(kk[j], akh, akl, b0h, b1h, b0l, b1l);
-          mma3(qk[j], aqh, aql, b0h, b1h, b0l, b1l);
+          mma3s(kk[j], ck[j], akh, akl, b0h, b1h, b0l, b1l);
+          mma3s(qk[j], cq[j], aqh, aql, b0h, b1h, b0l, b1l);
         }
       }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc_add(kk[j], ck[j]);
+      acc_add(qk[j], cq[j]);
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -580,11 +599,11 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_tc_kernel(const __grid_con
   // Tb is lower triangular, so tokens up to the tile's last row
   {
     const int mt = warp & 3, m0 = 16 * mt, nb = 8 * (warp >> 2);
-    float acc[8][4];
+    float acc[8][4], cacc[8][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
+      for (int e = 0; e < 4; ++e) acc[j][e] = cacc[j][e] = 0.0f;
     for (int ks = 0; ks <= 2 * mt + 1; ++ks) {
       uint32_t ah[4], al[4];
       gc_lda(sL, kPtLdT, m0, 8 * ks, g, t, ah, al);
@@ -592,9 +611,11 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_tc_kernel(const __grid_con
       for (int j = 0; j < 8; ++j) {
         uint32_t b0h, b1h, b0l, b1l;
         gc_ldb_k(sK, kPtLd, 8 * ks, 8 * (nb + j), g, t, b0h, b1h, b0l, b1l);
-        mma3(acc[j], ah, al, b0h, b1h, b0l, b1l);
+        mma3s(acc[j], cacc[j], ah, al, b0h, b1h, b0l, b1l);
       }
     }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc_add(acc[j], cacc[j]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int d = 8 * (nb + j) + 2 * t;
@@ -724,12 +745,12 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_tc_kernel(const __grid_con
     // ---- X1 = Kt S0^T, X2 = Qg S0^T over this warp's k-half
     asm volatile("cp.async.wait_group 2;" ::: "memory");
     __syncthreads();
-    float x1[2][4], x2[2][4];
+    float x1[2][4], x2[2][4], c1[2][4], c2[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) x1[nt][e] = x2[nt][e] = 0.0f;
-#pragma unroll 2
+      for (int e = 0; e < 4; ++e) x1[nt][e] = x2[nt][e] = c1[nt][e] = c2[nt][e] = 0.0f;
+#pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       const int k0 = 64 * kh + 8 * ks;
       uint32_t bh[2][2], bl[2][2];
@@ -744,10 +765,15 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_tc_kernel(const __grid_con
       uint32_t ah[4], al[4];
       gc_lda(sKt, kTcLdK, m0, k0, g, t, ah, al);
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma3(x1[nt], ah, al, bh[nt][0], bh[nt][1], bl[nt][0], bl[nt][1]);
+      for (int nt = 0; nt < 2; ++nt) mma3s(x1[nt], c1[nt], ah, al, bh[nt][0], bh[nt][1], bl[nt][0], bl[nt][1]);
       gc_lda(sQg, kTcLdK, m0, k0, g, t, ah, al);
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma3(x2[nt], ah, al, bh[nt][0], bh[nt][1], bl[nt][0], bl[nt][1]);
+      for (int nt = 0; nt < 2; ++nt) mma3s(x2[nt], c2[nt], ah, al, bh[nt][0], bh[nt][1], bl[nt][0], bl[nt][1]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      acc_add(x1[nt], c1[nt]);
+      acc_add(x2[nt], c2[nt]);
     }
     // halves meet: the warp keeps n-tile kh, hands the other to warp w ^ 4
     {
@@ -770,14 +796,15 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_tc_kernel(const __grid_con
     // ---- U = Tb V - X1 for (mt, nt_own)
     asm volatile("cp.async.wait_group 2;" ::: "memory");
     __syncthreads();
-    float u[4] = {-X1[0], -X1[1], -X1[2], -X1[3]};
-#pragma unroll 2
+    float u[4] = {-X1[0], -X1[1], -X1[2], -X1[3]}, cu[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       uint32_t ah[4], al[4], b0h, b1h, b0l, b1l;
       gc_lda(sTb, kTcLdT, m0, 8 * ks, g, t, ah, al);
       gc_ldb_k(sV, kTcLdV, 8 * ks, 8 * nt_own, g, t, b0h, b1h, b0l, b1l);
-      mma3(u, ah, al, b0h, b1h, b0l, b1l);
+      mma3s(u, cu, ah, al, b0h, b1h, b0l, b1l);
     }
+    acc_add(u, cu);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       uint32_t hi, lo;
@@ -791,14 +818,15 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_tc_kernel(const __grid_con
     issue_tbv(c + 1);
     // ---- Y = (X2 + P U) / sqrt(128) for (mt, nt_own): tokens up to the tile's last row
     {
-      float y[4] = {X2[0], X2[1], X2[2], X2[3]};
+      float y[4] = {X2[0], X2[1], X2[2], X2[3]}, cy[4] = {0.f, 0.f, 0.f, 0.f};
       for (int ks = 0; ks <= 2 * mt + 1; ++ks) {
         uint32_t ah[4], al[4];
         gc_lda(sP, kTcLdT, m0, 8 * ks, g, t, ah, al);
         const int o = (8 * ks + t) * kTcLdV + 8 * nt_own + g;
-        mma3(y, ah, al, __float_as_uint(sUh[o]), __float_as_uint(sUh[o + 4 * kTcLdV]), __float_as_uint(sUl[o]),
-             __float_as_uint(sUl[o + 4 * kTcLdV]));
+        mma3s(y, cy, ah, al, __float_as_uint(sUh[o]), __float_as_uint(sUh[o + 4 * kTcLdV]), __float_as_uint(sUl[o]),
+              __float_as_uint(sUl[o + 4 * kTcLdV]));
       }
+      acc_add(y, cy);
       const int col = h * kGcD + r0 + 8 * nt_own + 2 * t;
       const int ra = m0 + g, rb = m0 + g + 8;
       if (ra < n) *reinterpret_cast<float2*>(p.out + static_cast<size_t>(t0 + ra) * out_ld + col) =
@@ -809,11 +837,15 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_tc_kernel(const __grid_con
     // ---- S = e^{G_C} S + U^T Kd for columns 16w..16w+15
     {
       const float eg = expf(sG[kGc - 1]);
+      float cs[2][4];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sreg[nt][e] *= eg;
-#pragma unroll 2
+        for (int e = 0; e < 4; ++e) {
+          sreg[nt][e] *= eg;
+          cs[nt][e] = 0.0f;
+        }
+#pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const int j0 = 8 * ks;
         uint32_t ah[4], al[4];
@@ -830,9 +862,11 @@ __global__ void __launch_bounds__(256) gdn_chunk_scan_tc_kernel(const __grid_con
         for (int nt = 0; nt < 2; ++nt) {
           uint32_t b0h, b1h, b0l, b1l;
           gc_ldb_k(sKd, kTcLdKd, j0, 16 * warp + 8 * nt, g, t, b0h, b1h, b0l, b1l);
-          mma3(sreg[nt], ah, al, b0h, b1h, b0l, b1l);
+          mma3s(sreg[nt], cs[nt], ah, al, b0h, b1h, b0l, b1l);
         }
       }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) acc_add(sreg[nt], cs[nt]);
       put_state();  // the X products of the next chunk read it after its barrier
     }
     __syncthreads();  // P, Kd, U free
