@@ -416,6 +416,17 @@ void kib_qwen35_prefix_cache_stats(const kib_qwen35_prefix_cache* cache, uint64_
 int kib_qwen35_prefill_cached(kib_qwen35* model, kib_qwen35_prefix_cache* cache, const int32_t* tokens,
                               uint64_t count, int32_t* next_token, uint64_t* hit_tokens);
 
+/* Streaming generate (the reference's per-token stream_token callback,
+ * emit_generated_token in qwen35_runtime.cpp:6128-6139, which feeds the
+ * gateway's SSE responses): as kib_generate_qwen35, and every committed token is passed
+ * to cb(user, token, index) as soon as the host has it; a nonzero return
+ * cancels (finish_reason_stop stays 0).  cache (may be NULL): prefill through
+ * the host prompt cache, its hit length in *cached_tokens. */
+typedef int (*kib_token_callback)(void* user, int32_t token, uint64_t index);
+int kib_generate_qwen35_stream(kib_qwen35* model, const kib_generation_request* request,
+                               kib_qwen35_prefix_cache* cache, kib_token_callback cb, void* user, int32_t* out_tokens,
+                               uint64_t out_capacity, kib_generation_result* result, uint64_t* cached_tokens);
+
 /* Synthetic BASELINE-shaped Qwen3.5 GGUF writer (random-init weights, Q4_K_M mix). */
 typedef struct kib_synth_config {
   uint64_t hidden, layers, intermediate, vocab, heads, kv_heads, head_dim;

@@ -32,6 +32,10 @@ def _stale():
     t = os.path.getmtime(LIB)
     deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
     deps.append(os.path.join(HERE, "..", "include", "kib.h"))
+    gw = os.path.join(HERE, "gateway")
+    deps += [os.path.join(gw, f) for f in ("gw_core.cpp", "gw_abi.cpp", "gw_server.cpp", "gw_core.hpp", "gw_json.hpp")]
+    if not os.path.exists(os.path.join(gw, "_build", "kib_gateway")):
+        return True
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
@@ -66,6 +70,8 @@ def build(force=False, verbose=False, ptxas_info=False):
     if verbose:
         print(" ".join(cmd))
     subprocess.check_call(cmd)
+    # the OpenAI-compatible gateway (host C++ over libkib.so)
+    subprocess.check_call(["make", "-s", "-C", os.path.join(HERE, "gateway")])
     return LIB
 
 

@@ -1825,10 +1825,19 @@ int kib_qwen35_mtp_forward(kib_qwen35* m, const int32_t* tokens, const float* h_
 }
 
 // generate_qwen35_metal (qwen35_runtime.cpp:5239-6714), greedy decoding.
-int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t* out, uint64_t cap_out,
-                        kib_generation_result* res) {
+int kib_qwen35_prefill_cached(kib_qwen35* m, kib_qwen35_prefix_cache* cache, const int32_t* tokens, uint64_t count,
+                              int32_t* next_token, uint64_t* hit_tokens);
+
+// The generate loop behind kib_generate_qwen35 and its streaming form: every
+// committed token goes through emit (cb may cancel), and the prompt is
+// prefilled through the host prefix cache when one is given.
+static int generate_impl(kib_qwen35* m, const kib_generation_request* rq, kib_qwen35_prefix_cache* cache,
+                         kib_token_callback cb, void* user, int32_t* out, uint64_t cap_out, kib_generation_result* res,
+                         uint64_t* cached_tokens) {
   if (!m || !rq || !rq->prompt_tokens || rq->prompt_count == 0 || !res) return KIB_ERR_INVALID_ARGUMENT;
   std::memset(res, 0, sizeof(*res));
+  if (cached_tokens) *cached_tokens = 0;
+  bool cancelled = false;
   if (int rc = check_tokens(m, rq->prompt_tokens, rq->prompt_count)) return rc;
   const uint64_t max_new = std::min<uint64_t>(rq->max_new_tokens, cap_out);
   if (rq->prompt_count + max_new + 8 > static_cast<uint64_t>(m->cap))
@@ -1847,12 +1856,25 @@ int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t
   if (rc) return rc;
   cudaEventRecord(e0, st);
   int32_t next = 0;
-  rc = kib_qwen35_prefill(m, rq->prompt_tokens, rq->prompt_count, rq->prefill_chunk_tokens, &next);
+  if (cache) {
+    uint64_t hit = 0;
+    rc = kib_qwen35_prefill_cached(m, cache, rq->prompt_tokens, rq->prompt_count, &next, &hit);
+    if (cached_tokens) *cached_tokens = hit;
+  } else {
+    rc = kib_qwen35_prefill(m, rq->prompt_tokens, rq->prompt_count, rq->prefill_chunk_tokens, &next);
+  }
   if (rc) return rc;
   cudaEventRecord(e1, st);
   res->prompt_tokens = rq->prompt_count;
   uint64_t n = 0;
   bool stop = false;
+  // a committed token: stored, then handed to the callback (false: cancelled)
+  auto emit = [&](int32_t t) {
+    out[n] = t;
+    ++n;
+    if (cb && cb(user, t, n - 1) != 0) cancelled = true;
+    return !cancelled;
+  };
   const bool mtp = rq->enable_mtp && m->has_mtp && rq->mtp_draft_tokens > 0;
   kib_mtp_report& R = res->mtp;
   R.available = m->has_mtp ? 1 : 0;
@@ -1865,21 +1887,21 @@ int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t
     int32_t tok = next;
     if (is_eos(tok)) {
       stop = true;
-    } else if (max_new > 0) {
-      out[n++] = tok;
+    } else if (max_new > 0 && !emit(tok)) {
+      stop = true;
     }
     std::vector<int32_t> buf;
     while (!stop && n < max_new) {
-      const uint64_t batch = std::min<uint64_t>(32, max_new - n);
+      // (smaller device batches when streaming, so tokens reach the client sooner)
+      const uint64_t batch = std::min<uint64_t>(cb ? 4 : 32, max_new - n);
       buf.resize(batch);
       rc = kib_qwen35_decode_greedy(m, tok, batch, buf.data());
       if (rc) return rc;
       for (uint64_t i = 0; i < batch; ++i) {
-        if (is_eos(buf[i])) {
+        if (is_eos(buf[i]) || !emit(buf[i])) {
           stop = true;
           break;
         }
-        out[n++] = buf[i];
       }
       tok = buf[batch - 1];
     }
@@ -1894,7 +1916,10 @@ int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t
         stop = true;
         break;
       }
-      out[n++] = next_token;
+      if (!emit(next_token)) {
+        stop = true;
+        break;
+      }
       if (n >= max_new) break;
       const uint64_t vpos = m->pos;
       const uint64_t b = std::min<uint64_t>(budget, max_new - n);
@@ -1946,8 +1971,11 @@ int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t
           break;
         }
         if (targets[i] != drafts[i]) break;
-        out[n++] = drafts[i];
         ++acc;
+        if (!emit(drafts[i])) {
+          stop = true;
+          break;
+        }
         ++R.accepted_tokens;
         if (i < 8) ++R.accepted_by_position[i];
         if (n >= max_new) break;
@@ -2010,9 +2038,20 @@ int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t
   res->prefill_ms = pf;
   res->decode_ms = dc;
   res->generated_tokens = n;
-  res->finish_reason_stop = stop ? 1 : 0;
+  res->finish_reason_stop = stop && !cancelled ? 1 : 0;
   res->kv_used_tokens = m->pos;
   return KIB_OK;
+}
+
+int kib_generate_qwen35(kib_qwen35* m, const kib_generation_request* rq, int32_t* out, uint64_t cap_out,
+                        kib_generation_result* res) {
+  return generate_impl(m, rq, nullptr, nullptr, nullptr, out, cap_out, res, nullptr);
+}
+
+int kib_generate_qwen35_stream(kib_qwen35* m, const kib_generation_request* rq, kib_qwen35_prefix_cache* cache,
+                               kib_token_callback cb, void* user, int32_t* out, uint64_t cap_out,
+                               kib_generation_result* res, uint64_t* cached_tokens) {
+  return generate_impl(m, rq, cache, cb, user, out, cap_out, res, cached_tokens);
 }
 
 }  // extern "C"

@@ -255,3 +255,27 @@ def fuzz_text(rng: random.Random, specials=("<|im_start|>", "<|im_end|>", "<thin
         else:
             parts.append(rng.choice(ALPHABET).encode("utf-8"))
     return b"".join(parts)
+
+
+def ascii_vocab(size: int):
+    """(tokens, types, merges) of a size-entry vocabulary whose every token
+    decodes to ASCII: the byte symbols of bytes 9, 10 and 32..126, merges that
+    build a few words, the chat control tokens, fillers.  For end-to-end tests
+    that decode model output chosen at random."""
+    _, enc = byte_symbols()
+    tokens = [enc[b] for b in [9, 10] + list(range(32, 127))]
+    types = [NORMAL] * len(tokens)
+    merges = []
+    for word in [" abc", " dea", " bad", " cab", "hello", " world", "\n\n", " ee"]:
+        e = encoded(word, enc)
+        for k in range(2, len(e) + 1):
+            merges.append(e[:k - 1] + " " + e[k - 1])
+            if e[:k] not in tokens:
+                tokens.append(e[:k])
+                types.append(NORMAL)
+    for special in ("<|im_start|>", "<|im_end|>"):
+        tokens.append(special)
+        types.append(CONTROL)
+    types += [NORMAL] * (size - len(tokens))
+    tokens += [f"<fill_{i}>" for i in range(len(tokens), size)]
+    return tokens, types, merges
