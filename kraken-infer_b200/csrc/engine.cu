@@ -2087,8 +2087,8 @@ namespace {
 void linear_block_batch(Enq& q, kib_qwen35_batch* b, const LayerW& L, int S) {
   kib_qwen35* m = q.m;
   const int li = L.cache_index;
-  q.run(rms_rows_launch(m->d_h, L.attn_norm.f(), S, m->H, m->eps, m->d_norm, q.st), "rms");
-  gemm(q, L.qkv, m->d_norm, m->H, S, m->d_qkv, m->C);
+  q.run(rms_rows_launch(m->d_h, L.attn_norm.f(), S, m->H, m->eps, m->d_norm, q.st, m->d_x16), "rms");
+  gemm(q, L.qkv, m->d_norm, m->H, S, m->d_qkv, m->C, nullptr, false, true);
   q.run(launch_pdl(conv_batched_kernel<4>, dim3((m->C + 255) / 256, S), dim3(256), 0, q.st,
                    b->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1), b->r_slot,
                    static_cast<const float*>(m->d_qkv), m->C, L.conv1d.f(), m->C, m->d_qkv, m->C),
@@ -2113,14 +2113,15 @@ void linear_block_batch(Enq& q, kib_qwen35_batch* b, const LayerW& L, int S) {
   g.batched = 1;
   g.state_slot_stride = b->s_slot;
   q.run(launch_pdl(gdn_core_kernel, dim3(m->lvh, m->lhd / kGdnRows, S), dim3(128), 0, q.st, g), "gdn_batched");
-  q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, S, m->lvh, m->lhd, m->eps, m->d_norm2, q.st), "norm_gate");
-  gemm(q, L.ssm_out, m->d_norm2, m->VD, S, m->d_h1, m->H, m->d_h);
+  q.run(norm_gate_launch(m->d_y, L.ssm_norm.f(), m->d_z, S, m->lvh, m->lhd, m->eps, m->d_norm2, q.st, m->d_x16),
+        "norm_gate");
+  gemm(q, L.ssm_out, m->d_norm2, m->VD, S, m->d_h1, m->H, m->d_h, false, true);
 }
 
 void attention_block_batch(Enq& q, kib_qwen35_batch* b, const LayerW& L, int S) {
   kib_qwen35* m = q.m;
-  q.run(rms_rows_launch(m->d_h, L.attn_norm.f(), S, m->H, m->eps, m->d_norm, q.st), "rms");
-  gemm(q, L.q, m->d_norm, m->H, S, m->d_qg, 2 * m->AD);
+  q.run(rms_rows_launch(m->d_h, L.attn_norm.f(), S, m->H, m->eps, m->d_norm, q.st, m->d_x16), "rms");
+  gemm(q, L.q, m->d_norm, m->H, S, m->d_qg, 2 * m->AD, nullptr, false, true);
   gemm(q, L.k, m->d_norm, m->H, S, m->d_kp, m->KD, nullptr, true);
   gemm(q, L.v, m->d_norm, m->H, S, m->d_vp, m->KD, nullptr, true);
   const size_t off = static_cast<size_t>(L.cache_index) * b->cap * m->KD;
@@ -2153,12 +2154,10 @@ void batch_step(Enq& q, kib_qwen35_batch* b) {
     else attention_block_batch(q, b, L, S);
     ffn_prefill(q, L, S, m->d_h1, m->d_h);
   }
-  q.run(rms_rows_launch(m->d_h, m->output_norm.f(), S, m->H, m->eps, m->d_hn, q.st), "head_norm");
+  // the head's skinny GEMM reads the half rows the norm writes
+  q.run(rms_rows_launch(m->d_h, m->output_norm.f(), S, m->H, m->eps, m->d_hn, q.st, m->d_x16), "head_norm");
   const DevT& hw = head_weight(m);
   if (S <= 64) {
-    q.run(launch_pdl(x_to_f16_kernel, dim3(std::max(1, S * m->H / 1024)), dim3(256), 0, q.st,
-                     static_cast<const float*>(m->d_hn), m->H, S, m->H, m->d_x16),
-          "head_x16");
     q.run(kq_skinny_launch(hw.type, hw.p, m->V, m->H, m->d_x16, S, b->d_logits, m->V, nullptr,
                            reinterpret_cast<float*>(m->d_w16), m->ctx->num_sms, q.st, false),
           "lm_head");

@@ -20,6 +20,8 @@
 // kq_skinny_reduce_kernel sums in split order.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "kquant.cuh"
 #include "layer_kernels.cuh"
 
@@ -41,6 +43,7 @@ struct SkinnyParams {
   int kb_per_split;
   int xrows;          // rows of x in the shared tile (T, or 16 with xsplit)
   int xsplit;         // x rows 0..7 = half(x), 8..15 = half(x - half(x)): the 4..8 bucket
+  int cluster;        // the splits of a row tile are one cluster: partials meet in shared memory
 };
 
 template <int NT>
@@ -141,6 +144,36 @@ __global__ void __launch_bounds__(128) kq_skinny_gemm_kernel(const __grid_consta
     // low-half row (tile 1)
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc[0][c] += acc[1 % NT][c];
+  }
+  if (split && p.cluster) {
+    // partial tile [NTOK tokens][64 rows] in this CTA's shared memory (the A
+    // tile is no longer read), then every CTA of the cluster sums a slice of
+    // the tile over the splits, in split order
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    __syncthreads();
+    float* part = reinterpret_cast<float*>(A);
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        part[(8 * j + 2 * q + (c & 1)) * kSkRows + 16 * warp + g + (c >> 1) * 8] = acc[j][c];
+    cl.sync();
+    const int nsplit = static_cast<int>(gridDim.y), rank = static_cast<int>(cl.block_rank());
+    const int ntok = p.xsplit ? 8 : NTOK, total = ntok * kSkRows;
+    const int e0 = total * rank / nsplit, e1 = total * (rank + 1) / nsplit;
+    for (int e = e0 + tid; e < e1; e += 128) {
+      const int t = e / kSkRows, row = row0 + e % kSkRows;
+      float v = 0.0f;
+      for (int s = 0; s < nsplit; ++s) v += cl.map_shared_rank(part, s)[e];
+      if (row < p.rows && t < p.T) {
+        const size_t o = static_cast<size_t>(t) * p.y_ld + row;
+        if (p.resid) v += p.resid[o];
+        p.y[o] = v;
+      }
+    }
+    cl.sync();  // the peers' partials stay in place until every slice is summed
+    return;
   }
 #pragma unroll
   for (int j = 0; j < NT; ++j)

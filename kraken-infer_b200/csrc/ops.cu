@@ -745,6 +745,8 @@ cudaError_t launch(const SkinnyParams& p, dim3 grid, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     cfg = true;
   }
+  if (p.cluster && grid.y > 1)
+    return launch_pdl_cluster(kq_skinny_gemm_kernel<QT, NT>, grid, dim3(128), smem, st, dim3(1, grid.y, 1), p);
   return launch_pdl(kq_skinny_gemm_kernel<QT, NT>, grid, dim3(128), smem, st, p);
 }
 template <int QT>
@@ -761,6 +763,10 @@ cudaError_t launch_t(const SkinnyParams& p, dim3 grid, cudaStream_t st) {
 // in split order by a second kernel.
 cudaError_t kq_skinny_launch(int type, const void* w, int rows, int cols, const __half* x16, int T, float* y,
                              int y_ld, const float* resid, float* ws, int num_sms, cudaStream_t st, bool xsplit) {
+  static const bool cluster_on = [] {
+    const char* v = std::getenv("KIB_SKINNY_CLUSTER");
+    return !(v && v[0] == '0');
+  }();
   const int bpr = cols / 256;
   const int tiles = (rows + kSkRows - 1) / kSkRows;
   int nsplit = std::min(bpr, std::max(1, (2 * num_sms + tiles - 1) / tiles));
@@ -780,6 +786,12 @@ cudaError_t kq_skinny_launch(int type, const void* w, int rows, int cols, const 
   p.kb_per_split = kps;
   p.xsplit = xsplit ? 1 : 0;
   p.xrows = xsplit ? 16 : T;
+  // the 4..8-token bucket (MTP verify) reduces its splits inside one portable
+  // cluster through shared memory (measured ~1 % faster there); elsewhere the
+  // workspace and the reduce kernel win (batched decode, 32 tokens: 2.65 ms a
+  // step against 2.71 ms with clusters, whose co-scheduling leaves SMs idle)
+  const bool cluster = cluster_on && xsplit && nsplit <= 8;
+  p.cluster = cluster ? 1 : 0;
   const dim3 grid(tiles, nsplit);
   cudaError_t e;
   switch (type) {
@@ -787,7 +799,7 @@ cudaError_t kq_skinny_launch(int type, const void* w, int rows, int cols, const 
     case kTypeQ5K: e = skinny_host::launch_t<kTypeQ5K>(p, grid, st); break;
     default: e = skinny_host::launch_t<kTypeQ6K>(p, grid, st); break;
   }
-  if (e != cudaSuccess || nsplit == 1) return e;
+  if (e != cudaSuccess || nsplit == 1 || cluster) return e;
   const size_t n = static_cast<size_t>(T) * rows;
   const int rg = static_cast<int>(std::min<size_t>((n + 255) / 256, static_cast<size_t>(num_sms) * 4));
   return launch_pdl(kq_skinny_reduce_kernel, dim3(rg), dim3(256), 0, st, static_cast<const float*>(ws), nsplit, rows, T,
