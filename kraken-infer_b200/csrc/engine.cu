@@ -126,6 +126,9 @@ struct kib_qwen35 {
   float *d_cand_max = nullptr, *d_cand_sum = nullptr;
   int* d_cand_idx = nullptr;
   unsigned* d_head_cnt = nullptr;
+  // d_pos, d_step and d_tokens live in one block d_io (pos at 0, step at 1,
+  // tokens from 4), so a decode step's host inputs reach it in one copy
+  int* d_io = nullptr;
   int *d_pos = nullptr, *d_mtp_pos = nullptr, *d_tokens = nullptr, *d_argmax = nullptr, *d_log = nullptr,
       *d_step = nullptr, *d_mtp_tok = nullptr;
   float* d_prob = nullptr;
@@ -1435,13 +1438,18 @@ int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* op
             dalloc(&m->d_attn_cnt, 64) == cudaSuccess && dalloc(&m->d_head_cnt, 4) == cudaSuccess &&
             dalloc(&m->d_cand_max, 1024 * kGemvMaxTok) == cudaSuccess &&
             dalloc(&m->d_cand_sum, 1024 * kGemvMaxTok) == cudaSuccess &&
-            dalloc(&m->d_cand_idx, 1024 * kGemvMaxTok) == cudaSuccess && dalloc(&m->d_pos, 4) == cudaSuccess &&
-            dalloc(&m->d_mtp_pos, 4) == cudaSuccess && dalloc(&m->d_tokens, T) == cudaSuccess &&
+            dalloc(&m->d_cand_idx, 1024 * kGemvMaxTok) == cudaSuccess && dalloc(&m->d_io, T + 8) == cudaSuccess &&
+            dalloc(&m->d_mtp_pos, 4) == cudaSuccess && 
             dalloc(&m->d_argmax, kMaxSmallT) == cudaSuccess && dalloc(&m->d_prob, 4096) == cudaSuccess &&
-            dalloc(&m->d_log, 1 << 20) == cudaSuccess && dalloc(&m->d_step, 4) == cudaSuccess &&
+            dalloc(&m->d_log, 1 << 20) == cudaSuccess && 
             dalloc(&m->d_mtp_tok, 4) == cudaSuccess &&
             cudaMallocHost(&m->h_pin, 4096 * sizeof(int)) == cudaSuccess &&
             cudaMallocHost(&m->h_pinf, 4096 * sizeof(float)) == cudaSuccess;
+  if (ok) {
+    m->d_pos = m->d_io;
+    m->d_step = m->d_io + 1;
+    m->d_tokens = m->d_io + 4;
+  }
   if (!ok) {
     kib_qwen35_free(mp.release());
     return set_error(ctx, KIB_ERR_INTERNAL, "cache/activation allocation failed");
@@ -1521,8 +1529,8 @@ void kib_qwen35_free(kib_qwen35* m) {
                   m->d_pending_h, m->d_h, m->d_h1, m->d_qkv, m->d_z, m->d_beta, m->d_alpha, m->d_y, m->d_act,
                   m->d_act2, m->d_qg, m->d_kp, m->d_vp, m->d_att, m->d_qout, m->d_norm, m->d_norm2, m->d_hn,
                   m->d_logits, m->d_e, m->d_cat, m->d_hm, m->d_hm1, m->d_mtp_h, m->d_part, m->d_fa_part, m->d_proj, m->d_attn_cnt,
-                  m->d_head_cnt, m->d_cand_max, m->d_cand_sum, m->d_cand_idx, m->d_pos, m->d_mtp_pos,
-                  m->d_tokens, m->d_argmax, m->d_prob, m->d_log, m->d_step, m->d_mtp_tok, m->d_trace,
+                  m->d_head_cnt, m->d_cand_max, m->d_cand_sum, m->d_cand_idx, m->d_io, m->d_mtp_pos,
+                  m->d_argmax, m->d_prob, m->d_log, m->d_mtp_tok, m->d_trace,
                   m->d_w16, m->d_x16, m->d_w16_all, m->d_gdn_ws};
   for (void* p : ptrs)
     if (p) cudaFree(p);
@@ -1588,6 +1596,16 @@ static int check_tokens(kib_qwen35* m, const int32_t* t, uint64_t n) {
   return KIB_OK;
 }
 
+// position, step counter 0 and the token of a decode step: one copy into d_io
+static cudaError_t put_step_inputs(kib_qwen35* m, int32_t token, cudaStream_t st) {
+  int* h = m->h_pin + 48;
+  h[0] = static_cast<int>(m->pos);
+  h[1] = 0;
+  h[2] = h[3] = 0;
+  h[4] = token;
+  return cudaMemcpyAsync(m->d_io, h, 5 * sizeof(int), cudaMemcpyHostToDevice, st);
+}
+
 int kib_qwen35_forward(kib_qwen35* m, const int32_t* tokens, uint64_t n, int advance, int32_t* argmax_out,
                        float* logits, float* normed_hidden) {
   if (!m || !tokens || n < 1 || n > kMaxSmallT) return KIB_ERR_INVALID_ARGUMENT;
@@ -1599,12 +1617,7 @@ int kib_qwen35_forward(kib_qwen35* m, const int32_t* tokens, uint64_t n, int adv
     // argmax to the token log and advances the device position)
     int rc = ensure_pk_graph(m);
     if (rc) return rc;
-    m->h_pin[0] = static_cast<int>(m->pos);
-    m->h_pin[1] = tokens[0];
-    m->h_pin[2] = 0;
-    ENG_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, st));
-    ENG_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_pin + 1, sizeof(int), cudaMemcpyHostToDevice, st));
-    ENG_CUDA(cudaMemcpyAsync(m->d_step, m->h_pin + 2, sizeof(int), cudaMemcpyHostToDevice, st));
+    ENG_CUDA(put_step_inputs(m, tokens[0], st));
     ENG_CUDA(cudaGraphLaunch(m->pk_graph, st));
     ENG_CUDA(cudaMemcpyAsync(m->h_pin + 32, m->d_log, sizeof(int), cudaMemcpyDeviceToHost, st));
     rc = sync_check(m, "forward");
@@ -1710,12 +1723,7 @@ int kib_qwen35_decode_greedy(kib_qwen35* m, int32_t first_token, uint64_t steps,
   }
   if (m->trace_on && m->d_trace) ENG_CUDA(cudaMemsetAsync(m->d_trace, 0, 4096 * 8 * sizeof(unsigned long long), st));
   if (m->trace_on && m->d_pk_trace) ENG_CUDA(cudaMemsetAsync(m->d_pk_trace, 0, 16 * 4096 * sizeof(unsigned long long), st));
-  m->h_pin[0] = static_cast<int>(m->pos);
-  m->h_pin[1] = first_token;
-  m->h_pin[2] = 0;
-  ENG_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, st));
-  ENG_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_pin + 1, sizeof(int), cudaMemcpyHostToDevice, st));
-  ENG_CUDA(cudaMemcpyAsync(m->d_step, m->h_pin + 2, sizeof(int), cudaMemcpyHostToDevice, st));
+  ENG_CUDA(put_step_inputs(m, first_token, st));
   cudaGraphExec_t g = use_pk ? m->pk_graph : m->decode_graph;
   for (uint64_t i = 0; i < steps; ++i) ENG_CUDA(cudaGraphLaunch(g, st));
   if (tokens_out) ENG_CUDA(cudaMemcpyAsync(tokens_out, m->d_log, steps * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
