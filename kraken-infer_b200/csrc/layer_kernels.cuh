@@ -1337,13 +1337,14 @@ static __global__ void __launch_bounds__(128, 2) attn_prefill_mma_kernel(const _
 // weight 0 until a key of theirs arrives.
 constexpr int kFa2Q = 64;  // queries per head per CTA
 constexpr int kFa2MaxSplits = 4;
-constexpr size_t kFa2Smem = static_cast<size_t>(2 * kFa2Q + 4 * kFaK) * kFaLd * 2;
+constexpr int kFa2Blk = 2 * kFaK;  // keys per staged block: two 32-key softmax steps per barrier
+constexpr size_t kFa2Smem = static_cast<size_t>(2 * kFa2Q + 4 * kFa2Blk) * kFaLd * 2;
 
 static __global__ void __launch_bounds__(256, 1) attn_prefill_mma2_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) uint16_t fa2_sm[];
   uint16_t* qs = fa2_sm;                    // [2][64][264]
   uint16_t* ks = fa2_sm + 2 * kFa2Q * kFaLd;  // [2][32][264]
-  uint16_t* vs = ks + 2 * kFaK * kFaLd;     // [2][32][264]
+  uint16_t* vs = ks + 2 * kFa2Blk * kFaLd;  // [2][64][264]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hl = warp >> 2, wq = warp & 3;  // head of the pair, 16-row tile of it
   const int head0 = 2 * blockIdx.y, head = head0 + hl, q0 = blockIdx.x * kFa2Q;
@@ -1355,18 +1356,18 @@ static __global__ void __launch_bounds__(256, 1) attn_prefill_mma2_kernel(const 
   const int pos0 = *p.pos;
   const int last_q = min(q0 + kFa2Q, p.T) - 1;
   const int nkeys = pos0 + last_q + 1;
-  const int nblocks = (nkeys + kFaK - 1) / kFaK;
+  const int nblocks = (nkeys + kFa2Blk - 1) / kFa2Blk;
   const int b_lo = static_cast<int>(static_cast<long>(nblocks) * split / nsplit);
   const int b_hi = static_cast<int>(static_cast<long>(nblocks) * (split + 1) / nsplit);
   const uint16_t* kg = p.kcache + static_cast<size_t>(kvh) * kHd;
   const uint16_t* vg = p.vcache + static_cast<size_t>(kvh) * kHd;
   auto load_kv = [&](int b, int stage) {
-    uint16_t* kd = ks + stage * kFaK * kFaLd;
-    uint16_t* vd = vs + stage * kFaK * kFaLd;
+    uint16_t* kd = ks + stage * kFa2Blk * kFaLd;
+    uint16_t* vd = vs + stage * kFa2Blk * kFaLd;
 #pragma unroll
-    for (int it = 0; it < kFaK * 32 / 256; ++it) {
+    for (int it = 0; it < kFa2Blk * 32 / 256; ++it) {
       const int i = tid + 256 * it, r = i >> 5, piece = i & 31;
-      const size_t key = static_cast<size_t>(min(b * kFaK + r, nkeys - 1));
+      const size_t key = static_cast<size_t>(min(b * kFa2Blk + r, nkeys - 1));
       gs_cp16(kd + r * kFaLd + 8 * piece, kg + key * kvd + 8 * piece);
       gs_cp16(vd + r * kFaLd + 8 * piece, vg + key * kvd + 8 * piece);
     }
@@ -1397,13 +1398,16 @@ static __global__ void __launch_bounds__(256, 1) attn_prefill_mma2_kernel(const 
   // first key zeroes the (empty) history exactly as a -inf start would
   constexpr float kFloor = -1e30f;
   float m0 = kFloor, m1 = kFloor, l0 = 0.0f, l1 = 0.0f;  // l: this lane's share
-  for (int b = b_lo; b < b_hi; ++b) {
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();  // block b landed (and Q, at the first block); the other stage is free
-    if (b + 1 < b_hi) load_kv(b + 1, (b + 1) & 1);
-    if (b * kFaK > warp_last) continue;
-    const uint32_t kst = ks_base + static_cast<uint32_t>((b & 1) * kFaK * kFaLd) * 2;
-    const uint32_t vst = vs_base + static_cast<uint32_t>((b & 1) * kFaK * kFaLd) * 2;
+  for (int bb = 2 * b_lo; bb < 2 * b_hi; ++bb) {
+    const int b = bb >> 1;  // staged block; bb: its 32-key half
+    if ((bb & 1) == 0) {
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncthreads();  // block b landed (and Q, at the first block); the other stage is free
+      if (b + 1 < b_hi) load_kv(b + 1, (b + 1) & 1);
+    }
+    if (bb * kFaK > warp_last) continue;
+    const uint32_t kst = ks_base + static_cast<uint32_t>(((b & 1) * kFa2Blk + (bb & 1) * kFaK) * kFaLd) * 2;
+    const uint32_t vst = vs_base + static_cast<uint32_t>(((b & 1) * kFa2Blk + (bb & 1) * kFaK) * kFaLd) * 2;
     float s[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
@@ -1424,7 +1428,7 @@ static __global__ void __launch_bounds__(256, 1) attn_prefill_mma2_kernel(const 
     float mx0 = m0, mx1 = m1;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int key = b * kFaK + 8 * j + 2 * c;
+      const int key = bb * kFaK + 8 * j + 2 * c;
       s[j][0] = key <= qpos0 ? s[j][0] * scale : -INFINITY;
       s[j][1] = key + 1 <= qpos0 ? s[j][1] * scale : -INFINITY;
       s[j][2] = key <= qpos1 ? s[j][2] * scale : -INFINITY;
