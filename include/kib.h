@@ -362,6 +362,11 @@ int kib_qwen35_set_position(kib_qwen35* model, uint64_t position);
  * KIB_ERR_TIMEOUT and the model stays usable (state of the aborted step is
  * undefined; reset and prefill again).  stage = -1 restores the stage list. */
 int kib_qwen35_debug_stall(kib_qwen35* model, uint32_t poll_limit, int stage);
+/* No counterpart in the reference: which bs1 decode path the model runs.
+ * Returns the persistent kernel's stage count (> 0), or 0 when decode runs as
+ * the per-kernel graph, with the reason (e.g. a matrix type or shape outside
+ * the persistent kernel's limits) copied into why (may be null). */
+int kib_qwen35_persistent_stages(const kib_qwen35* model, char* why, int why_len);
 /* Copies cache state out of (write_into_model = 0) or into (1) the engine: any
  * pointer may be null.  Host buffers; sizes from kib_qwen35_plan. */
 int kib_qwen35_state_io(kib_qwen35* model, int write_into_model, uint16_t* k_cache, uint16_t* v_cache,
@@ -436,6 +441,7 @@ typedef struct kib_synth_config {
   double rope_theta, rms_eps;
   int64_t eos_token_id;
   int threads;
+  uint32_t qkv_type; /* GDN attn_qkv type; 0: proj_type (Q4_K_M files store it as Q5_K, 13) */
 } kib_synth_config;
 void kib_synth_default(kib_synth_config* cfg);
 int kib_write_synthetic_qwen35(const char* path, const kib_synth_config* cfg, char* err, int err_len);

@@ -187,7 +187,7 @@ struct __align__(16) PkStage {
   int gate_tag;
   int resid_tag;
   int src_tag;        // GDN / attention / merge: the stage that wrote their inputs
-  int src2_tag;       // merge: the q|gate projection
+  int src2_tag;       // merge: the q|gate projection; GDN: the beta/alpha rows (0: src_tag)
   int pad0;
   PkSeg seg[kPkMaxSegs];
   const void* in;      // cells (in_tag) or floats
@@ -620,7 +620,7 @@ struct PkX {
   float s[4];
 };
 
-// x values of unit u of block blk from the padded stage input.  Q4_K: quarter q = elements
+// x values of unit u of block blk from the padded stage input.  Q4_K/Q5_K: quarter q = elements
 // 16q..16q+15 of the 64 contiguous columns; Q6_K: quarter k = the 16-column
 // run of group k.
 KIB_DEV void pk_load_x(int type, const float* xs, int blk, int u, PkX& x) {
@@ -650,16 +650,15 @@ KIB_DEV void pk_load_x(int type, const float* xs, int blk, int u, PkX& x) {
 
 // Codes (16 words of 4 byte-codes, element order as unit_col) and per-quarter
 // affine coefficients (value = A*code + B) of unit u of one row's block.
-KIB_DEV void pk_decode(int type, const uint8_t* blk, int u, uint32_t (&q)[16], float (&A)[4], float (&B)[4]) {
-  if (type == kTypeQ6K) {
-    const RawUnit<kTypeQ6K> raw = load_raw<kTypeQ6K>(blk, u);
-    codes_from_raw<kTypeQ6K>(raw, u, q);
-    coeffs_from_raw<kTypeQ6K>(raw, u, A, B);
+template <int QT>
+KIB_DEV void pk_decode_t(const uint8_t* blk, int u, uint32_t (&q)[16], float (&A)[4], float (&B)[4]) {
+  const RawUnit<QT> raw = load_raw<QT>(blk, u);
+  codes_from_raw<QT>(raw, u, q);
+  if (QT == kTypeQ6K) {
+    coeffs_from_raw<QT>(raw, u, A, B);
   } else {
-    const RawUnit<kTypeQ4K> raw = load_raw<kTypeQ4K>(blk, u);
-    codes_from_raw<kTypeQ4K>(raw, u, q);
     float a2[4], b2[4];
-    coeffs_from_raw<kTypeQ4K>(raw, u, a2, b2);
+    coeffs_from_raw<QT>(raw, u, a2, b2);
     A[0] = A[1] = a2[0];
     A[2] = A[3] = a2[1];
     B[0] = B[1] = b2[0];
@@ -675,8 +674,20 @@ template <int R>
 KIB_DEV void pk_dot_rows(int type, const uint8_t* const (&blk)[R], int u, const PkX& x, float (&out)[R]) {
   uint32_t q[R][16];
   float A[R][4], B[R][4];
+  // one type's decodes together: the code a stage runs stays contiguous
+  // Q5_K (in Q4_K_M files only the GDN in-projection) runs on the two-row
+  // passes alone, laid out off the hot path: the four-row passes (quad stages,
+  // the LM head) carry no code for it
+  if (R == 2 && __builtin_expect(type == kTypeQ5K, 0)) {
 #pragma unroll
-  for (int k = 0; k < R; ++k) pk_decode(type, blk[k], u, q[k], A[k], B[k]);
+    for (int k = 0; k < R; ++k) pk_decode_t<kTypeQ5K>(blk[k], u, q[k], A[k], B[k]);
+  } else if (type == kTypeQ6K) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) pk_decode_t<kTypeQ6K>(blk[k], u, q[k], A[k], B[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < R; ++k) pk_decode_t<kTypeQ4K>(blk[k], u, q[k], A[k], B[k]);
+  }
 #pragma unroll
   for (int k = 0; k < R; ++k) {
     float2 acc[4][2];
@@ -886,8 +897,8 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
   // columns runs as one pass of four rows per lane (the LM head's dot code)
   // instead of two passes of two
   const int nr0 = min(tile_rows, rows - cta * tile_rows);
-  const bool quad = S.kind == kPkGemv && rg_log2 == 4 && !paired && ntiles <= grid && nr0 > groups * R &&
-                    nr0 <= 4 * groups;
+  const bool quad = S.kind == kPkGemv && type != kTypeQ5K && rg_log2 == 4 && !paired && ntiles <= grid &&
+                    nr0 > groups * R && nr0 <= 4 * groups;
   const bool q_owner = (gl & 3) == 0;
   const int q_off = ((gl & 15) >> 2) * groups + group;
   // the first pass's epilogue inputs go out before the prologue's wait
@@ -927,7 +938,7 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
     cs.release_warp();
     return true;
   }
-  if (S.kind == kPkHead && rg_log2 == 4 && tile_rows == groups * R) {
+  if (S.kind == kPkHead && type != kTypeQ5K && rg_log2 == 4 && tile_rows == groups * R) {
     // LM head: two tiles per pass (a lane dots rows of both), so each pass has
     // twice the independent work between its waits
     PkArgmax am2;
@@ -935,10 +946,14 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
     #pragma unroll 1
     for (int t = cta; t < ntiles; t += 2 * grid) {
       const bool two = t + grid < ntiles;
+      unsigned long long* ttr = nullptr;  // per-pass times of CTA 0, thread 0 (trace only)
+      if (cs.tr && (t - cta) / (2 * grid) < 500) ttr = cs.tr - 16 * (P.nstages - 1) + 8192 + 4 * ((t - cta) / (2 * grid));
+      pk_mark(ttr, 0);
       const uint8_t* ta = cs.take();
       if (!ta) return false;
       const uint8_t* tb = two ? cs.take_next() : ta;
       if (!tb) return false;
+      pk_mark(ttr, 1);
       const int na = min(tile_rows, rows - t * tile_rows);
       const int nb = two ? min(tile_rows, rows - (t + grid) * tile_rows) : 0;
       const uint8_t* b[4];
@@ -960,8 +975,10 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
         const int rl = group + (own2 & 1) * groups;
         if (rl < (own2 < 2 ? na : nb)) am2.push(v * scale, tt * tile_rows + rl);
       }
+      pk_mark(ttr, 2);
       cs.release_warp();
       if (two) cs.release_warp();
+      pk_mark(ttr, 3);
     }
     pk_head_finish(P, cs.sh, am2, epoch);
     return true;
@@ -1066,6 +1083,7 @@ __device__ __noinline__ bool pk_gdn(const PkStage& S, PkCons& cs) {
   const int key_dim = S.key_heads * D;
   const float scale = 1.0f / sqrtf(static_cast<float>(D));
   const uint32_t in_tag = cs.tag(S.src_tag), otag = cs.tag(S.tag);
+  const uint32_t ba_tag = S.src2_tag ? cs.tag(S.src2_tag) : in_tag;
   #pragma unroll 1
   for (int it = static_cast<int>(blockIdx.x); it < items; it += static_cast<int>(gridDim.x)) {
     const int h = it / (D / kPkGdnRows), grp = it % (D / kPkGdnRows);
@@ -1089,8 +1107,8 @@ __device__ __noinline__ bool pk_gdn(const PkStage& S, PkCons& cs) {
       vv[r] = pk_cell(S.conv_out + 2 * key_dim + h * D + grp * kPkGdnRows + r, in_tag, cs.err, ok);
     } else if (tid == D + kPkGdnRows) {
       const uint64_t ac = cell_ld1(S.alpha_raw + h), bc = cell_ld1(S.beta_raw + h);
-      const float a = pk_cell_chk(S.alpha_raw + h, ac, in_tag, cs.err, ok);
-      const float b = pk_cell_chk(S.beta_raw + h, bc, in_tag, cs.err, ok);
+      const float a = pk_cell_chk(S.alpha_raw + h, ac, ba_tag, cs.err, ok);
+      const float b = pk_cell_chk(S.beta_raw + h, bc, ba_tag, cs.err, ok);
       cs.sh->gb[0] = softplus20_f(a + S.dt_bias[h]) * S.ssm_a[h];
       cs.sh->gb[1] = pk_sigmoid(b);
     }
@@ -1506,9 +1524,9 @@ __global__ void __launch_bounds__(kPkThreads, 1) decode_persistent_kernel(const 
     const int kind = S.kind;
     bool ok = true;
     if (kind == kPkGemv || kind == kPkHead) {
-      // CTAs without a tile of this stage skip its input entirely.  Q4_K and
-      // Q6_K only: the host routes models with Q5_K projections to the
-      // per-kernel path.
+      // CTAs without a tile of this stage skip its input entirely.  One
+      // K-quant type per stage (Q4_K, Q5_K or Q6_K): the host splits a
+      // projection group of mixed types into one stage per type.
       // (the LM head's finish runs inside pk_gemv; a CTA without a head tile
       // still takes part in the last-CTA ticket)
       if (static_cast<int>(blockIdx.x) < S.ntiles) ok = pk_gemv(S, cs, P, epoch);

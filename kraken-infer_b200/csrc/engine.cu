@@ -882,8 +882,8 @@ struct PkSegIn {
 static bool pk_gemv_stage(kib_qwen35* m, PkStage& S, int kind, const std::vector<PkSegIn>& segs, int grid) {
   const int type = segs[0].w->type;
   const int cols = segs[0].w->cols();
-  if (type != kTypeQ4K && type != kTypeQ6K) {
-    m->pk_why = "matrix type other than Q4_K / Q6_K";
+  if (type != kTypeQ4K && type != kTypeQ5K && type != kTypeQ6K) {
+    m->pk_why = "matrix type other than Q4_K / Q5_K / Q6_K";
     return false;
   }
   if (cols % 256 || cols > kPkMaxCols || static_cast<int>(segs.size()) > kPkMaxSegs) {
@@ -1024,28 +1024,43 @@ static int build_pk(kib_qwen35* m) {
       uint64_t* c_z = cells(L.zgate.rows());
       uint64_t* c_beta = cells(L.beta.rows());
       uint64_t* c_alpha = cells(L.alpha.rows());
-      PkStage a = {};
-      if (!pk_gemv_stage(m, a, kPkGemv,
-                         {{&L.qkv, nullptr, c_qkv, kEpiConv},
-                          {&L.zgate, nullptr, c_z, kEpiStore},
-                          {&L.beta, nullptr, c_beta, kEpiStore},
-                          {&L.alpha, nullptr, c_alpha, kEpiStore}},
-                         grid))
+      // the in-projection group (qkv with the conv epilogue, z, beta, alpha):
+      // one stage, or -- when the matrices differ in K-quant type, as the
+      // Q4_K_M files' Q5_K attn_qkv does -- one stage per type, all reading
+      // the same normed input
+      const std::vector<PkSegIn> in_segs = {{&L.qkv, nullptr, c_qkv, kEpiConv},
+                                            {&L.zgate, nullptr, c_z, kEpiStore},
+                                            {&L.beta, nullptr, c_beta, kEpiStore},
+                                            {&L.alpha, nullptr, c_alpha, kEpiStore}};
+      int seg_tag[4] = {0, 0, 0, 0};
+      for (size_t i0 = 0; i0 < in_segs.size();) {
+        size_t i1 = i0 + 1;
+        while (i1 < in_segs.size() && in_segs[i1].w->type == in_segs[i0].w->type) ++i1;
+        PkStage a = {};
+        if (!pk_gemv_stage(m, a, kPkGemv, std::vector<PkSegIn>(in_segs.begin() + i0, in_segs.begin() + i1), grid))
+          return KIB_OK;
+        a.prologue = kProRms;
+        a.in = h_in;
+        a.in_tag = h_tag;
+        a.norm_w = L.attn_norm.f();
+        a.conv_state = m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1);
+        a.conv_w = L.conv1d.f();
+        const int tg = add(a);
+        for (size_t i = i0; i < i1; ++i) seg_tag[i] = tg;
+        i0 = i1;
+      }
+      if (seg_tag[2] != seg_tag[3]) {
+        m->pk_why = "ssm beta and alpha types differ";
         return KIB_OK;
-      a.prologue = kProRms;
-      a.in = h_in;
-      a.in_tag = h_tag;
-      a.norm_w = L.attn_norm.f();
-      a.conv_state = m->d_r + static_cast<size_t>(li) * m->C * (m->convk - 1);
-      a.conv_w = L.conv1d.f();
-      const int a_tag = add(a);
+      }
       PkStage g = {};
       g.kind = kPkGdn;
       g.conv_out = c_qkv;
       g.C = m->C;
       g.beta_raw = c_beta;
       g.alpha_raw = c_alpha;
-      g.src_tag = a_tag;
+      g.src_tag = seg_tag[0];
+      g.src2_tag = seg_tag[2] == seg_tag[0] ? 0 : seg_tag[2];
       g.dt_bias = L.dt_bias.f();
       g.ssm_a = L.ssm_a.f();
       g.state = m->d_s + static_cast<size_t>(li) * m->lvh * m->lhd * m->lhd;
@@ -1061,7 +1076,7 @@ static int build_pk(kib_qwen35* m) {
       o.in = g.gdn_out;
       o.in_tag = g_tag;
       o.gate = c_z;
-      o.gate_tag = a_tag;
+      o.gate_tag = seg_tag[1];
       o.norm_w = L.ssm_norm.f();
       o.head_dim = m->lhd;
       o.resid = h_in;
@@ -1563,6 +1578,15 @@ int kib_qwen35_reset(kib_qwen35* m) {
 }
 
 uint64_t kib_qwen35_position(const kib_qwen35* m) { return m ? m->pos : 0; }
+
+int kib_qwen35_persistent_stages(const kib_qwen35* m, char* why, int why_len) {
+  if (!m) return 0;
+  if (why && why_len > 0) {
+    std::strncpy(why, m->pk_on ? "" : m->pk_why.c_str(), static_cast<size_t>(why_len - 1));
+    why[why_len - 1] = 0;
+  }
+  return m->pk_on ? m->pk_n : 0;
+}
 
 int kib_qwen35_debug_stall(kib_qwen35* m, uint32_t poll_limit, int stage) {
   if (!m) return KIB_ERR_INVALID_ARGUMENT;

@@ -423,7 +423,7 @@ bool write_synthetic_qwen35(const std::string& path, const SynthQwen35Config& cf
       add(p + "attn_q_norm.weight", {u(hd)}, 0, 1);
       add(p + "attn_k_norm.weight", {u(hd)}, 0, 1);
     } else {
-      add(p + "attn_qkv.weight", {u(H), u(conv_dim)}, cfg.proj_type, 0);
+      add(p + "attn_qkv.weight", {u(H), u(conv_dim)}, cfg.qkv_type ? cfg.qkv_type : cfg.proj_type, 0);
       add(p + "attn_gate.weight", {u(H), u(value_dim)}, cfg.proj_type, 0);
       add(p + "ssm_conv1d.weight", {u(cfg.conv_kernel), u(conv_dim)}, 0, 2);
       add(p + "ssm_dt.bias", {u(sh)}, 0, 2);

@@ -80,6 +80,7 @@ struct SynthQwen35Config {
   double rms_eps = 1e-6;
   int64_t eos_token_id = -1;    // -1: no EOS key
   int threads = 8;
+  uint32_t qkv_type = 0;        // GDN attn_qkv; 0: proj_type (the Q4_K_M files store it as Q5_K)
 };
 
 // Writes a GGUF whose metadata and tensor names/shapes are those the reference's

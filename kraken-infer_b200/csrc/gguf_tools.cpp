@@ -38,6 +38,7 @@ void kib_synth_default(kib_synth_config* c) {
   c->rms_eps = d.rms_eps;
   c->eos_token_id = d.eos_token_id;
   c->threads = d.threads;
+  c->qkv_type = d.qkv_type;
 }
 
 int kib_write_synthetic_qwen35(const char* path, const kib_synth_config* c, char* err, int err_len) {
@@ -63,6 +64,7 @@ int kib_write_synthetic_qwen35(const char* path, const kib_synth_config* c, char
   d.rms_eps = c->rms_eps;
   d.eos_token_id = c->eos_token_id;
   d.threads = c->threads > 0 ? c->threads : 8;
+  d.qkv_type = c->qkv_type;
   std::string e;
   if (!write_synthetic_qwen35(path, d, &e)) {
     if (err && err_len > 0) {

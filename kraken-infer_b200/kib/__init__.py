@@ -162,7 +162,8 @@ class SynthConfig(ctypes.Structure):
         "hidden", "layers", "intermediate", "vocab", "heads", "kv_heads", "head_dim", "ssm_heads", "ssm_head_dim",
         "conv_kernel", "full_attention_interval", "nextn_layers")] + [
         ("proj_type", c_uint32), ("down_type", c_uint32), ("embd_type", c_uint32), ("seed", c_uint64),
-        ("rope_theta", c_double), ("rms_eps", c_double), ("eos_token_id", c_int64), ("threads", c_int)]
+        ("rope_theta", c_double), ("rms_eps", c_double), ("eos_token_id", c_int64), ("threads", c_int),
+        ("qkv_type", c_uint32)]
 
 
 _U64 = c_uint64
@@ -231,6 +232,7 @@ def _declare(lib):
         "kib_qwen35_position": (c_uint64, [_P]),
         "kib_qwen35_set_position": (c_int, [_P, _U64]),
         "kib_qwen35_debug_stall": (c_int, [_P, c_uint32, c_int]),
+        "kib_qwen35_persistent_stages": (c_int, [_P, ctypes.c_char_p, c_int]),
         "kib_qwen35_batch_create": (c_int, [_P, _U64, _U64, _U64, POINTER(c_void_p)]),
         "kib_qwen35_batch_free": (None, [_P]),
         "kib_qwen35_batch_prefill": (c_int, [_P, _U64, _P, _U64, _P]),
@@ -370,6 +372,13 @@ class Qwen35:
     @property
     def position(self):
         return int(self.lib.kib_qwen35_position(self.h))
+
+    def persistent_stages(self):
+        """(stage count of the one-launch-per-token decode kernel, or 0; the
+        reason when decode runs as the per-kernel graph)."""
+        why = ctypes.create_string_buffer(256)
+        n = int(self.lib.kib_qwen35_persistent_stages(self.h, why, 256))
+        return n, why.value.decode()
 
     def set_position(self, pos):
         self.ctx.check(self.lib.kib_qwen35_set_position(self.h, pos))

@@ -204,6 +204,34 @@ def test_persistent_decode_full_width_matches_oracle(ctx, oracle, full_width_mod
     assert toks == list(otoks[1:25])
 
 
+@pytest.fixture(scope="module")
+def q4km_mix_model(tmp_path_factory):
+    """FULL_WIDTH with the Q4_K_M files' type mix: the GDN in-projection
+    attn_qkv stored as Q5_K next to Q4_K attn_gate / ssm_beta / ssm_alpha."""
+    path = str(tmp_path_factory.mktemp("mix") / "q4km_mix.gguf")
+    kib.write_synthetic_qwen35(path, qkv_type=13, **FULL_WIDTH)
+    return path
+
+
+def test_persistent_decode_q5k_in_projection_matches_oracle(ctx, oracle, q4km_mix_model, monkeypatch):
+    """A model whose GDN attn_qkv is Q5_K stays on the one-launch-per-token
+    decode (the in-projection group becomes one stage per K-quant type) and
+    decodes the oracle's greedy tokens."""
+    monkeypatch.setenv("KIB_PERSISTENT", "1")
+    m = kib.Qwen35(ctx, q4km_mix_model, context_tokens=512, decode_tokens=64)
+    n, why = m.persistent_stages()
+    m.close()
+    assert n > 0, why
+    p = prompt(160, FULL_WIDTH["vocab"], 5)
+    nxt, toks = _decode_tokens(ctx, q4km_mix_model, p, 24, True, monkeypatch, context_tokens=512, decode_tokens=64)
+    om = oracle_lib.OracleModel(oracle, q4km_mix_model, 512)
+    _, _, lg = om.forward(p, 0)
+    assert nxt == int(np.argmax(lg[-1]))
+    otoks, _ = om.generate_from(160, nxt, 25, mtp_draft_tokens=0)
+    om.close()
+    assert toks == list(otoks[1:25])
+
+
 def test_forward_one_token_argmax_matches_decode(ctx, small_model):
     """kib_qwen35_forward with one token and only the argmax requested (the
     per-token host loop) gives the same tokens as the device-side greedy loop."""
