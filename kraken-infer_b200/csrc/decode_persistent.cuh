@@ -670,7 +670,7 @@ KIB_DEV void pk_decode_t(const uint8_t* blk, int u, uint32_t (&q)[16], float (&A
 // decoded first and their FMA chains are independent, so loads and arithmetic
 // of different rows overlap.  Codes are the floats 0.5 + b/256 (one PRMT);
 // sum(b*x) over a quarter is 256*acc - 128*sum(x), exact up to fp32 rounding.
-template <int R>
+template <int R, int ONLY = 0>  // ONLY: the one K-quant type this call site decodes (0: any)
 KIB_DEV void pk_dot_rows(int type, const uint8_t* const (&blk)[R], int u, const PkX& x, float (&out)[R]) {
   uint32_t q[R][16];
   float A[R][4], B[R][4];
@@ -678,7 +678,13 @@ KIB_DEV void pk_dot_rows(int type, const uint8_t* const (&blk)[R], int u, const 
   // Q5_K (in Q4_K_M files only the GDN in-projection) runs on the two-row
   // passes alone, laid out off the hot path: the four-row passes (quad stages,
   // the LM head) carry no code for it
-  if (R == 2 && __builtin_expect(type == kTypeQ5K, 0)) {
+  if (ONLY == kTypeQ6K) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) pk_decode_t<kTypeQ6K>(blk[k], u, q[k], A[k], B[k]);
+  } else if (ONLY == kTypeQ4K) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) pk_decode_t<kTypeQ4K>(blk[k], u, q[k], A[k], B[k]);
+  } else if (R == 2 && __builtin_expect(type == kTypeQ5K, 0)) {
 #pragma unroll
     for (int k = 0; k < R; ++k) pk_decode_t<kTypeQ5K>(blk[k], u, q[k], A[k], B[k]);
   } else if (type == kTypeQ6K) {
@@ -897,7 +903,8 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
   // columns runs as one pass of four rows per lane (the LM head's dot code)
   // instead of two passes of two
   const int nr0 = min(tile_rows, rows - cta * tile_rows);
-  const bool quad = S.kind == kPkGemv && type != kTypeQ5K && rg_log2 == 4 && !paired && ntiles <= grid &&
+  // (Q4_K only: the four-row code carries one type's decode)
+  const bool quad = S.kind == kPkGemv && type == kTypeQ4K && rg_log2 == 4 && !paired && ntiles <= grid &&
                     nr0 > groups * R && nr0 <= 4 * groups;
   const bool q_owner = (gl & 3) == 0;
   const int q_off = ((gl & 15) >> 2) * groups + group;
@@ -926,7 +933,7 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
 #pragma unroll
     for (int k = 0; k < 4; ++k) b[k] = tile + static_cast<size_t>(min(k * groups + group, nr0 - 1)) * row_bytes + blk_off;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    if (active) pk_dot_rows<4>(type, b, u, ux, acc);
+    if (active) pk_dot_rows<4, kTypeQ4K>(type, b, u, ux, acc);
     // lanes 0-3 / 4-7 / 8-11 / 12-15 of the group end with rows 0..3
     const bool h1 = gl & 8, h2 = gl & 4;
     const float a0 = (h1 ? acc[2] : acc[0]) + __shfl_xor_sync(0xffffffffu, h1 ? acc[0] : acc[2], 8);
@@ -938,7 +945,7 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
     cs.release_warp();
     return true;
   }
-  if (S.kind == kPkHead && type != kTypeQ5K && rg_log2 == 4 && tile_rows == groups * R) {
+  if (S.kind == kPkHead && type == kTypeQ6K && rg_log2 == 4 && tile_rows == groups * R) {
     // LM head: two tiles per pass (a lane dots rows of both), so each pass has
     // twice the independent work between its waits
     PkArgmax am2;
@@ -962,7 +969,7 @@ KIB_DEV bool pk_gemv(const PkStage& S, PkCons& cs, const PkProgram& P, uint32_t 
       b[2] = tb + static_cast<size_t>(min(group, max(nb, 1) - 1)) * row_bytes + blk_off;
       b[3] = tb + static_cast<size_t>(min(group + groups, max(nb, 1) - 1)) * row_bytes + blk_off;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      if (active) pk_dot_rows<4>(type, b, u, ux, acc);
+      if (active) pk_dot_rows<4, kTypeQ6K>(type, b, u, ux, acc);
       // lanes 0-3 / 4-7 / 8-11 / 12-15 of the group end with rows 0..3
       const bool h1 = gl & 8, h2 = gl & 4;
       const float a0 = (h1 ? acc[2] : acc[0]) + __shfl_xor_sync(0xffffffffu, h1 ? acc[0] : acc[2], 8);
