@@ -788,6 +788,17 @@ int sync_check(kib_qwen35* m, const char* what) {
   return KIB_OK;
 }
 
+// As sync_check, with the error flag already copied (in stream order) to *h_err.
+int sync_check_flag(kib_qwen35* m, const char* what, const int* h_err) {
+  cudaError_t e = cudaStreamSynchronize(m->ctx->stream);
+  if (e != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, std::string(what) + ": " + cudaGetErrorString(e));
+  if (*reinterpret_cast<const volatile int*>(h_err)) {
+    cudaMemset(m->ctx->d_err, 0, sizeof(int));
+    return fail(m, KIB_ERR_TIMEOUT, std::string(what) + ": a bounded device wait gave up");
+  }
+  return KIB_OK;
+}
+
 int set_pos(kib_qwen35* m, int* dptr, uint64_t value) {
   m->h_pin[0] = static_cast<int>(value);
   ENG_CUDA(cudaMemcpyAsync(dptr, m->h_pin, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
@@ -1644,7 +1655,9 @@ int kib_qwen35_forward(kib_qwen35* m, const int32_t* tokens, uint64_t n, int adv
     ENG_CUDA(put_step_inputs(m, tokens[0], st));
     ENG_CUDA(cudaGraphLaunch(m->pk_graph, st));
     ENG_CUDA(cudaMemcpyAsync(m->h_pin + 32, m->d_log, sizeof(int), cudaMemcpyDeviceToHost, st));
-    rc = sync_check(m, "forward");
+    // the error flag travels with the token (no second, blocking copy after the sync)
+    ENG_CUDA(cudaMemcpyAsync(m->h_pin + 33, m->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    rc = sync_check_flag(m, "forward", m->h_pin + 33);
     if (rc) {
       pk_reset_after_error(m);
       return rc;
