@@ -558,8 +558,8 @@ def main():
                            "layers": int(m.plan.main_layers), "vocab": int(m.plan.vocab_size),
                            "reduced_model_for_profiling": bool(MODEL_OVERRIDES),
                            "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (weights 513 MB)"},
-                "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 20, "d2h_bytes_per_step": 4,
-                        "api": "kib_qwen35_forward (position, step counter and token H2D in one 20-byte copy, argmax D2H, per-token sync)"},
+                "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 20, "d2h_bytes_per_step": 8,
+                        "api": "kib_qwen35_forward (one graph launch per token: position, step counter and token H2D in one 20-byte copy, argmax and error flag D2H, per-token sync)"},
                 "roofline": roof,
                 "matvec_config1": mv,
                 "mtp_verify_config3": mtp,

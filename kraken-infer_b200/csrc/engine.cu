@@ -162,6 +162,7 @@ struct kib_qwen35 {
   unsigned long long* d_pk_trace = nullptr;
   bool pk_coop = true;
   cudaGraphExec_t pk_graph = nullptr;
+  cudaGraphExec_t pk_fwd_graph = nullptr;  // one-token forward: step inputs in, embedding, persistent kernel, token + error flag out
 };
 
 namespace {
@@ -1265,6 +1266,22 @@ static int ensure_pk_graph(kib_qwen35* m) {
   return rc;
 }
 
+// The one-token forward of kib_qwen35_forward as a single graph launch: the
+// host-to-device copy of the step inputs (pinned h_pin[48..52]), the step, and
+// the copies of the token (h_pin[32]) and of the error flag (h_pin[33]).
+static int ensure_pk_fwd_graph(kib_qwen35* m) {
+  if (m->pk_fwd_graph) return KIB_OK;
+  int rc = ensure_pk_graph(m);  // settles the cooperative attribute
+  if (rc) return rc;
+  return capture(m, &m->pk_fwd_graph, [&](Enq& q) {
+    q.run(cudaMemcpyAsync(m->d_io, m->h_pin + 48, 5 * sizeof(int), cudaMemcpyHostToDevice, q.st), "step_inputs");
+    q.run(get_rows_launch(m->tok_embd.type, m->tok_embd.p, m->V, m->H, m->d_tokens, 1, m->d_h, m->H, q.st), "embed");
+    q.run(pk_launch(m, q.st), "decode_persistent");
+    q.run(cudaMemcpyAsync(m->h_pin + 32, m->d_log, sizeof(int), cudaMemcpyDeviceToHost, q.st), "token_out");
+    q.run(cudaMemcpyAsync(m->h_pin + 33, m->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, q.st), "err_out");
+  });
+}
+
 int kib_qwen35_load(kib_ctx* ctx, const char* path, const kib_qwen35_options* opt, kib_qwen35** out) {
   if (!ctx || !path || !out) return KIB_ERR_INVALID_ARGUMENT;
   *out = nullptr;
@@ -1548,6 +1565,7 @@ void kib_qwen35_free(kib_qwen35* m) {
   if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
   if (m->mtp_graph) cudaGraphExecDestroy(m->mtp_graph);
   if (m->pk_graph) cudaGraphExecDestroy(m->pk_graph);
+  if (m->pk_fwd_graph) cudaGraphExecDestroy(m->pk_fwd_graph);
   void* pk_ptrs[] = {m->d_pk, m->d_pk_ctr, m->d_pk_cells, m->d_pk_rope, m->d_pk_cmax, m->d_pk_cidx, m->d_pk_trace};
   for (void* p : pk_ptrs)
     if (p) cudaFree(p);
@@ -1650,13 +1668,16 @@ int kib_qwen35_forward(kib_qwen35* m, const int32_t* tokens, uint64_t n, int adv
   if (n == 1 && !logits && !normed_hidden && m->pk_on) {
     // one token, argmax only: the persistent decode path (its head writes the
     // argmax to the token log and advances the device position)
-    int rc = ensure_pk_graph(m);
+    int rc = ensure_pk_fwd_graph(m);
     if (rc) return rc;
-    ENG_CUDA(put_step_inputs(m, tokens[0], st));
-    ENG_CUDA(cudaGraphLaunch(m->pk_graph, st));
-    ENG_CUDA(cudaMemcpyAsync(m->h_pin + 32, m->d_log, sizeof(int), cudaMemcpyDeviceToHost, st));
-    // the error flag travels with the token (no second, blocking copy after the sync)
-    ENG_CUDA(cudaMemcpyAsync(m->h_pin + 33, m->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    int* h = m->h_pin + 48;  // step inputs, read by the graph's first node
+    h[0] = static_cast<int>(m->pos);
+    h[1] = 0;
+    h[2] = h[3] = 0;
+    h[4] = tokens[0];
+    // one launch: inputs in, the step, token and error flag out (the flag
+    // travels with the token instead of a blocking copy after the sync)
+    ENG_CUDA(cudaGraphLaunch(m->pk_fwd_graph, st));
     rc = sync_check_flag(m, "forward", m->h_pin + 33);
     if (rc) {
       pk_reset_after_error(m);
