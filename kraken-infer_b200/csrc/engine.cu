@@ -347,7 +347,11 @@ void attention_block_small(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc, 
              {{&L.q, m->d_qg, 2 * m->AD, kEpiStore}, {&L.k, m->d_kp, m->KD, kEpiStore}, {&L.v, m->d_vp, m->KD, kEpiStore}});
   AttnParams a = attn_params(m, L, kc, vc, pos, T);
   a.trace = q.slot("attn_decode");
-  q.run(T == 1 ? launch_attn_decode<1>(a, m->kvh, m->nsplit, q.st) : launch_attn_decode<8>(a, m->kvh, m->nsplit, q.st),
+  // register arrays sized to the token count (verify: 2..5 tokens)
+  q.run(T == 1   ? launch_attn_decode<1>(a, m->kvh, m->nsplit, q.st)
+        : T == 2 ? launch_attn_decode<2>(a, m->kvh, m->nsplit, q.st)
+        : T <= 4 ? launch_attn_decode<4>(a, m->kvh, m->nsplit, q.st)
+                 : launch_attn_decode<8>(a, m->kvh, m->nsplit, q.st),
         "attn_decode");
   GemvDesc o = base_desc(m, L.o.type, m->AD, T);
   o.prologue = kProPlain;
