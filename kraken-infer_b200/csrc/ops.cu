@@ -494,8 +494,12 @@ cudaError_t gemv_launch(const GemvDesc& d, int num_sms, cudaStream_t st, std::st
   const int mult = paired ? 2 : 1;
   bool has_conv = false;
   for (int i = 0; i < d.nseg; ++i) has_conv = has_conv || d.seg[i].epilogue == kEpiConv;
+  // Two or three tokens (MTP verify) with a norm prologue take the kernel that
+  // stages x in shared memory once per CTA: per-lane units would redo the
+  // prologue (silu(gate), the RMS sums) once per row group and token.
   const bool compact = d.ntok <= 3 && p.rg <= 128 &&
-                       (d.prologue != kProNormGate || (units == p.rg && d.head_dim == 128)) &&
+                       (d.prologue != kProNormGate || (d.ntok == 1 && units == p.rg && d.head_dim == 128)) &&
+                       (d.prologue != kProRms || d.ntok == 1) &&
                        (!has_conv || d.conv_k == 4);
   const int km1 = d.conv_k - 1;
   auto count_tiles = [&](int tr) {
