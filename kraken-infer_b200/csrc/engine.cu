@@ -729,7 +729,8 @@ void attention_block_mid(Enq& q, const LayerW& L, uint16_t* kc, uint16_t* vc, co
   gemm(q, L.k, m->d_norm, m->H, T, m->d_kp, m->KD, nullptr, true);
   gemm(q, L.v, m->d_norm, m->H, T, m->d_vp, m->KD, nullptr, true);
   AttnParams a = attn_params(m, L, kc, vc, pos, T);
-  q.run(launch_attn_decode<8>(a, m->kvh, m->nsplit, q.st), "attn_decode");
+  q.run(T <= 4 ? launch_attn_decode<4>(a, m->kvh, m->nsplit, q.st) : launch_attn_decode<8>(a, m->kvh, m->nsplit, q.st),
+        "attn_decode");
   gemm(q, L.o, m->d_att, m->AD, T, x_mid, m->H, x_in);
 }
 

@@ -238,41 +238,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) kquant_gemv_kernel(const __gr
     mbar_wait_bounded(&full_bar[st], static_cast<uint32_t>((local / S) & 1), p.err);
     const uint8_t* tile = stage_base + static_cast<size_t>(st) * p.stage_bytes;
     const int passes = (nrows + groups - 1) / groups;
-    for (int pass = 0; pass < passes; ++pass) {
-      const int rl = pass * groups + group;
-      const bool row_ok = rl < nrows;
-      float acc[NT], acc2[NT];
-#pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] = acc2[t] = 0.0f;
-      if (row_ok && active) {
-        const uint8_t* b0 = tile + static_cast<size_t>(rl) * p.row_bytes + blk * BB;
-        if constexpr (F16W) {
-          // weights rounded to half (two per register), x read as float4 runs
-          // of unit_col, products accumulated in two fp32 lanes (FFMA2)
-          __half2 wh[32];
-#pragma unroll 1
-          for (int hh = 0; hh <= static_cast<int>(paired); ++hh) {
-            unit_dequant_h2<QT>(b0 + hh * (p.stage_bytes / 2), unit, wh);
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              if (t >= p.ntok) break;  // xs holds ntok rows only
-              const float* xb = xs + t * p.cols + 256 * blk;
-              float2 s2 = make_float2(0.0f, 0.0f);
-#pragma unroll
-              for (int e = 0; e < 64; e += 4) {
-                const float4 x4 = *reinterpret_cast<const float4*>(xb + unit_col<QT>(unit, e));
-                s2 = ffma2(__half22float2(wh[e / 2]), make_float2(x4.x, x4.y), s2);
-                s2 = ffma2(__half22float2(wh[e / 2 + 1]), make_float2(x4.z, x4.w), s2);
-              }
-              if (hh == 0) acc[t] = s2.x + s2.y;
-              else acc2[t] = s2.x + s2.y;
-            }
-          }
-        } else {
-          unit_dot<QT, NT>(b0, unit, ux, acc);
-          if (paired) unit_dot<QT, NT>(b0 + p.stage_bytes / 2, unit, ux, acc2);
-        }
-      }
+    // F16W: two rows per pass, so every x value read from shared memory
+    // serves both (the x of 4..8 tokens does not fit in registers)
+    constexpr int PR = F16W ? 2 : 1;
+    auto finish = [&](float (&acc)[NT], float (&acc2)[NT], const int rl, const bool row_ok) {
       // ---- reduce across the group
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
@@ -359,6 +328,58 @@ __global__ void __launch_bounds__(kGemvThreads, 1) kquant_gemv_kernel(const __gr
           }
         }
       }
+        };
+#pragma unroll 1
+    for (int pass = 0; pass < passes; pass += PR) {
+      const int rl = pass * groups + group, rlb = rl + groups;
+      const bool row_ok = rl < nrows, rowb_ok = PR == 2 && rlb < nrows;
+      float acc[NT], acc2[NT], accb[NT], accb2[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t] = acc2[t] = accb[t] = accb2[t] = 0.0f;
+      if constexpr (F16W) {
+        if (row_ok && active) {
+          // weights rounded to half (two per register), x read as float4 runs
+          // of unit_col, products accumulated in two fp32 lanes (FFMA2)
+          const uint8_t* b0 = tile + static_cast<size_t>(rl) * p.row_bytes + blk * BB;
+          const uint8_t* b1 = tile + static_cast<size_t>(rowb_ok ? rlb : rl) * p.row_bytes + blk * BB;
+          __half2 wh[32], wh2[32];
+#pragma unroll 1
+          for (int hh = 0; hh <= static_cast<int>(paired); ++hh) {
+            unit_dequant_h2<QT>(b0 + hh * (p.stage_bytes / 2), unit, wh);
+            unit_dequant_h2<QT>(b1 + hh * (p.stage_bytes / 2), unit, wh2);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              if (t >= p.ntok) break;  // xs holds ntok rows only
+              const float* xb = xs + t * p.cols + 256 * blk;
+              float2 s2 = make_float2(0.0f, 0.0f), s2b = make_float2(0.0f, 0.0f);
+#pragma unroll
+              for (int e = 0; e < 64; e += 4) {
+                const float4 x4 = *reinterpret_cast<const float4*>(xb + unit_col<QT>(unit, e));
+                const float2 xa = make_float2(x4.x, x4.y), xc = make_float2(x4.z, x4.w);
+                s2 = ffma2(__half22float2(wh[e / 2]), xa, s2);
+                s2 = ffma2(__half22float2(wh[e / 2 + 1]), xc, s2);
+                s2b = ffma2(__half22float2(wh2[e / 2]), xa, s2b);
+                s2b = ffma2(__half22float2(wh2[e / 2 + 1]), xc, s2b);
+              }
+              if (hh == 0) {
+                acc[t] = s2.x + s2.y;
+                accb[t] = s2b.x + s2b.y;
+              } else {
+                acc2[t] = s2.x + s2.y;
+                accb2[t] = s2b.x + s2b.y;
+              }
+            }
+          }
+        }
+      } else {
+        if (row_ok && active) {
+          const uint8_t* b0 = tile + static_cast<size_t>(rl) * p.row_bytes + blk * BB;
+          unit_dot<QT, NT>(b0, unit, ux, acc);
+          if (paired) unit_dot<QT, NT>(b0 + p.stage_bytes / 2, unit, ux, acc2);
+        }
+      }
+      finish(acc, acc2, rl, row_ok);
+      if (PR == 2) finish(accb, accb2, rlb, rowb_ok);
     }
     __syncthreads();  // stage consumed by every group
     if (tid == 0 && local + S < my_tiles) issue(local + S);
