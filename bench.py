@@ -416,8 +416,10 @@ def main():
     ap.add_argument("--no-mtp", action="store_true", help="skip the config-3 MTP verify measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
     ap.add_argument("--no-batch", action="store_true", help="skip the config-5 batched decode measurement")
-    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "prefill", "batch"],
-                    help="matvec: BASELINE config 1 only (Q4_K 3584x1024 GEMV roofline)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "prefill", "batch", "verify"],
+                    help="matvec: BASELINE config 1 only (Q4_K 3584x1024 GEMV roofline); verify: one MTP verify "
+                         "forward of --verify-tokens tokens at ctx 2048 inside cudaProfilerStart/Stop (profiling)")
+    ap.add_argument("--verify-tokens", type=int, default=2)
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: fewer layers than the BASELINE model (the JSON line says so)")
     ap.add_argument("--vocab", type=int, default=None, help="profiling only: smaller vocabulary")
@@ -452,6 +454,34 @@ def main():
         r = prefill_bench(ctx, path)
         print(json.dumps({"metric": "Qwen3.5-0.8B-shape 8192-token chunked prefill tok/s", "value": r["tok_per_s"],
                           "unit": "tok/s", "prefill_config4": r}), flush=True)
+        ctx.close()
+        return
+    if args.workload == "verify":
+        import numpy as np
+        import torch
+        import kib
+        torch.cuda.set_device(local)
+        ctx = kib.Context(local)
+        d = os.environ.get("KIB_BENCH_DIR", os.path.join(tempfile.gettempdir(), "kib_bench"))
+        os.makedirs(d, exist_ok=True)
+        path = os.path.join(d, "qwen35_0p8b_shape_q4_k_m_nextn1_seed1234.gguf")
+        if not os.path.exists(path):
+            kib.write_synthetic_qwen35(path + ".tmp", threads=min(os.cpu_count() or 8, 64), seed=1234, nextn_layers=1)
+            os.replace(path + ".tmp", path)
+        m = kib.Qwen35(ctx, path, context_tokens=MTP_CONTEXT + 256, decode_tokens=64, prefill_chunk=1024,
+                       enable_mtp=True)
+        rng = np.random.default_rng(2048)
+        m.prefill(rng.integers(0, m.plan.vocab_size, MTP_CONTEXT).astype(np.int32), 1024)
+        toks = rng.integers(0, m.plan.vocab_size, args.verify_tokens).astype(np.int32)
+        for _ in range(3):
+            m.forward(toks, advance=False)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        m.forward(toks, advance=False)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"workload": "verify", "tokens": args.verify_tokens}), flush=True)
+        m.close()
         ctx.close()
         return
     if args.workload == "batch":
