@@ -117,6 +117,16 @@ KIB_DEV void cp_async_cg16(void* sdst, const void* gsrc) {
 KIB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 KIB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// Tensor copy (no multicast) of the box at (x, y, 0) of a rank-3 map (the
+// instruction's dimension must be the map's rank) into shared memory.
+KIB_DEV void pk_tma_kv(void* dst, const void* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(0), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Out-of-line poll of one cell: re-loads until it carries `tag`.  Returns the
 // cell, or 0 (tag 0 is never a stage tag) when the poll limit runs out or
 // another CTA raised the error flag.
@@ -225,6 +235,8 @@ struct __align__(16) PkStage {
   int n_dims;
   int nsplit;         // splits per kv head (kv_heads * nsplit <= grid)
   int pad2;
+  const void* tk;     // rank-3 CUtensorMaps (device memory) over kcache / vcache: [1][cap][kv_heads*256],
+  const void* tv;     // boxes of 256 columns (one KV head) x 32 positions x 1
 };
 
 struct PkProgram {
@@ -391,17 +403,15 @@ __device__ __noinline__ void pk_produce(const PkProgram& P, PkProducer& pr) {
       int kb, ke;
       pk_split_range(pos + 1, S.nsplit, split, kb, ke);
       const int old_end = min(ke, pos);
-      const int kvd = S.kv_heads * kHd;
+      // one tensor copy per 32-key chunk for K and one for V (per-key bulk
+      // copies of 512 B are issue-bound); rows past the split are not read
       #pragma unroll 1
       for (int k0 = kb; k0 < old_end; k0 += kAttnChunk) {
-        const int nk = min(kAttnChunk, old_end - k0);
-        uint8_t* dst = pr.acquire(static_cast<uint32_t>(nk) * 2u * kHd * 2u);
+        uint8_t* dst = pr.acquire(static_cast<uint32_t>(kAttnChunk) * 2u * kHd * 2u);
         if (!dst) return;
-        if (lane < nk) {
-          const size_t src = static_cast<size_t>(k0 + lane) * kvd + kvh * kHd;
-          uint8_t* d = dst + static_cast<size_t>(lane) * 2 * kHd * 2;
-          bulk_g2s(d, S.kcache + src, kHd * 2, pr.bar());
-          bulk_g2s(d + kHd * 2, S.vcache + src, kHd * 2, pr.bar());
+        if (lane == 0) {
+          pk_tma_kv(dst, S.tk, kvh * kHd, k0, pr.bar());
+          pk_tma_kv(dst + static_cast<size_t>(kAttnChunk) * kHd * 2, S.tv, kvh * kHd, k0, pr.bar());
         }
         pr.advance();
       }
@@ -1284,7 +1294,7 @@ __device__ __noinline__ bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
   for (int k0 = kb; k0 < old_end; k0 += kAttnChunk) {
     const uint8_t* tile = cs.take();
     if (!tile) return false;
-    const uint16_t* kvbuf = reinterpret_cast<const uint16_t*>(tile);
+    const uint16_t* kvbuf = reinterpret_cast<const uint16_t*>(tile);  // [K: 32 keys x 256][V: 32 keys x 256]
     const int nk = min(kAttnChunk, old_end - k0);
     #pragma unroll 1
     for (int kk0 = kh2 * KB; kk0 < nk; kk0 += 2 * KB) {
@@ -1292,7 +1302,7 @@ __device__ __noinline__ bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
 #pragma unroll
       for (int e = 0; e < KB; ++e) {
         const int kk = min(kk0 + e, nk - 1);
-        const uint4 kr = *reinterpret_cast<const uint4*>(kvbuf + static_cast<size_t>(kk) * 2 * kHd + 8 * lane);
+        const uint4 kr = *reinterpret_cast<const uint4*>(kvbuf + static_cast<size_t>(kk) * kHd + 8 * lane);
         const __half2* kh = reinterpret_cast<const __half2*>(&kr);
         float d = 0.0f;
 #pragma unroll
@@ -1318,7 +1328,8 @@ __device__ __noinline__ bool pk_attn(const PkStage& S, PkCons& cs, int pos) {
       uint4 vr[KB];
 #pragma unroll
       for (int e = 0; e < KB; ++e)
-        vr[e] = *reinterpret_cast<const uint4*>(kvbuf + static_cast<size_t>(min(kk0 + e, nk - 1)) * 2 * kHd + kHd + 8 * lane);
+        vr[e] = *reinterpret_cast<const uint4*>(kvbuf + static_cast<size_t>(kAttnChunk + min(kk0 + e, nk - 1)) * kHd +
+                                                8 * lane);
 #pragma unroll
       for (int e = 0; e < KB; ++e) {
         const float w = kk0 + e < nk ? expf(sc[e] - mx) : 0.0f;

@@ -16,6 +16,7 @@
 // chained with programmatic dependent launch, the sampled token and the
 // position stay on the device.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
@@ -157,6 +158,7 @@ struct kib_qwen35 {
   unsigned* d_pk_ctr = nullptr;  // [1] LM-head ticket, [2] cell tag epoch
   uint64_t* d_pk_cells = nullptr;
   float* d_pk_rope = nullptr;  // [kPkRopePairs] rotary inverse frequencies
+  CUtensorMap* d_pk_tmaps = nullptr;  // per attention layer: K and V cache tensor maps of the persistent kernel
   float* d_pk_cmax = nullptr;
   int* d_pk_cidx = nullptr;
   unsigned long long* d_pk_trace = nullptr;
@@ -982,6 +984,30 @@ static size_t pk_cells_needed(const kib_qwen35* m, int nsplit) {
   return n;
 }
 
+// Tensor map over one attention layer's K or V cache, [positions][kv_dim]
+// halves, as a rank-3 map [1][positions][kv_dim] (the persistent kernel issues
+// 3-D copies): boxes of one KV head's 256 columns x 32 positions, unswizzled,
+// rows past the cache read as zeros.
+static bool kv_cache_tensor_map(CUtensorMap* map, const uint16_t* base, int kv_dim, int positions) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || kv_dim % kHd) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kv_dim), static_cast<cuuint64_t>(positions), 1};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kv_dim) * 2,
+                                 static_cast<cuuint64_t>(kv_dim) * static_cast<cuuint64_t>(positions) * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kHd), static_cast<cuuint32_t>(kAttnChunk), 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static int build_pk(kib_qwen35* m) {
   m->pk_on = false;
   if (const char* e = std::getenv("KIB_PERSISTENT"); e && e[0] == '0') {
@@ -1011,6 +1037,23 @@ static int build_pk(kib_qwen35* m) {
     }
     if (dalloc(&m->d_pk_rope, kPkRopePairs) != cudaSuccess) return fail(m, KIB_ERR_INTERNAL, "pk rope alloc");
     ENG_CUDA(cudaMemcpy(m->d_pk_rope, fr.data(), fr.size() * sizeof(float), cudaMemcpyHostToDevice));
+  }
+  if (!m->d_pk_tmaps) {
+    // the attention stages stream their K/V rows by tensor copies of 32
+    // positions x 256 columns (one KV head)
+    const size_t na = m->plan.full_attention_layers;
+    std::vector<CUtensorMap> maps(2 * std::max<size_t>(na, 1));
+    for (size_t ai = 0; ai < na; ++ai) {
+      const size_t off = ai * static_cast<size_t>(m->cap) * m->KD;
+      if (!kv_cache_tensor_map(&maps[2 * ai], m->d_k + off, m->KD, m->cap) ||
+          !kv_cache_tensor_map(&maps[2 * ai + 1], m->d_v + off, m->KD, m->cap)) {
+        m->pk_why = "KV cache tensor maps unavailable";
+        return KIB_OK;
+      }
+    }
+    if (cudaMalloc(&m->d_pk_tmaps, maps.size() * sizeof(CUtensorMap)) != cudaSuccess)
+      return fail(m, KIB_ERR_INTERNAL, "pk tensor map alloc");
+    ENG_CUDA(cudaMemcpy(m->d_pk_tmaps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
   }
   const size_t ncells = pk_cells_needed(m, nsplit);
   if (!m->d_pk_cells) {
@@ -1133,6 +1176,8 @@ static int build_pk(kib_qwen35* m) {
       t.theta = m->theta;
       t.n_dims = n_dims;
       t.rope_freq = m->d_pk_rope;
+      t.tk = m->d_pk_tmaps + 2 * li;
+      t.tv = m->d_pk_tmaps + 2 * li + 1;
       t.nsplit = nsplit;
       t.part = cells(static_cast<size_t>(nsplit) * m->heads * (kHd + 2));
       const int t_tag = add(t);
@@ -1571,7 +1616,8 @@ void kib_qwen35_free(kib_qwen35* m) {
   if (m->mtp_graph) cudaGraphExecDestroy(m->mtp_graph);
   if (m->pk_graph) cudaGraphExecDestroy(m->pk_graph);
   if (m->pk_fwd_graph) cudaGraphExecDestroy(m->pk_fwd_graph);
-  void* pk_ptrs[] = {m->d_pk, m->d_pk_ctr, m->d_pk_cells, m->d_pk_rope, m->d_pk_cmax, m->d_pk_cidx, m->d_pk_trace};
+  void* pk_ptrs[] = {m->d_pk, m->d_pk_ctr, m->d_pk_cells, m->d_pk_rope, m->d_pk_cmax, m->d_pk_cidx, m->d_pk_trace,
+                     m->d_pk_tmaps};
   for (void* p : pk_ptrs)
     if (p) cudaFree(p);
   void* ptrs[] = {m->d_weights, m->d_k, m->d_v, m->d_mk, m->d_mv, m->d_r, m->d_s, m->d_r_snap, m->d_s_snap,
